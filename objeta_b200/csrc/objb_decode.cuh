@@ -1,0 +1,364 @@
+// objb_decode.cuh -- in-register block decoders for the batch-1 GEMV.
+//
+// Each format defines a "lane tile": the run of consecutive 32-weight blocks
+// one lane owns within a row, sized so the tile is a whole number of 32-bit
+// words and the word stride between lanes is odd (bank-conflict-free shared
+// memory reads).  A lane keeps the x values of its tile in registers for the
+// whole kernel and, for every row that streams through shared memory, returns
+// its partial dot product.  Per block the decoders form sum_l (q_l - off) x_l
+// in fp32 and multiply by the block scale once, which is the reference's
+// arithmetic (w = (q - off) * scale; sum += w * x, quant.rs:928-1019) with the
+// scale factored out of the block sum.
+//
+// Q4_0 uses an exact "magic number" decode: OR-ing a nibble that sits at bit
+// 4k of a word into the mantissa of 2^23 gives the float 2^23 + q*16^k, and
+// subtracting 2^23 + 8*16^k leaves (q - 8)*16^k exactly.  The matching x
+// register holds x * 16^-k (an exact power-of-two scaling), so the product is
+// (q - 8) * x rounded once.  Pairs of lanes of that arithmetic run as
+// sm_100 packed fp32x2 add / fma (__fadd2_rn, __ffma2_rn).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+
+#include <cstdint>
+
+#include "../../include/objeta_b200.h"
+#include "objb_pipe.cuh"
+
+namespace objb {
+namespace dev {
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// IEEE half -> float, exact for every finite and infinite code; equals the
+// reference's f16_to_f32_bits (quant.rs:1021-1044) on all non-NaN inputs.
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t bits16) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
+}
+
+// E8M0 -> float (quant.rs:886-892 / deepseek.rs:831-850): raw 0 is 2^-127.
+__device__ __forceinline__ float e8m0_to_f32(uint32_t raw) {
+  return raw == 0 ? u2f(1u << 22) : u2f(raw << 23);
+}
+
+// Small unsigned integer q (< 2^23) minus `off`, as an exact float.
+__device__ __forceinline__ float qf(uint32_t q, float off) {
+  return u2f(0x4B000000u | q) - (8388608.0f + off);
+}
+
+// Byte `i` (compile-time after unrolling) of a little-endian word array.
+template <int N>
+__device__ __forceinline__ uint32_t byte_at(const uint32_t (&w)[N], int i) {
+  return (w[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+}
+
+template <int FMT>
+struct Tile;
+
+// ---------------------------------------------------------------- Q4_0
+// Tile = 2 blocks = 36 bytes = 9 words:
+//   w0 = [s0 lo, s0 hi, qs0[0], qs0[1]]  w1..w3 = qs0[2..13]
+//   w4 = [qs0[14], qs0[15], s1 lo, s1 hi]  w5..w8 = qs1[0..15]
+// Byte j of qs holds element 2j (low nibble) and 2j+1 (high nibble), so in an
+// aligned quant word nibble position p is element (word base + p).
+template <>
+struct Tile<OBJB_Q4_0> {
+  static constexpr int P = 2;
+  static constexpr int BB = 18;
+  static constexpr int TB = P * BB;
+  static constexpr int XR = 64;
+
+  // Decode word u (0..7), nibble position p (0..7) -> element within the tile.
+  __device__ __forceinline__ static int elem(int u, int p) {
+    if (u == 0) return p < 4 ? 28 + p : p - 4;  // merged word (see dot)
+    if (u < 4) return 4 + 8 * (u - 1) + p;
+    return 32 + 8 * (u - 4) + p;
+  }
+  // Power-of-16 exponent of nibble position p in the decode.
+  __device__ __forceinline__ static int kexp(int p) { return p < 5 ? p : p - 3; }
+
+  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
+                                                float (&xr)[XR]) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        float v = active ? __ldg(x + col0 + elem(u, p)) : 0.0f;
+        xr[u * 8 + p] = v * u2f(static_cast<uint32_t>(127 - 4 * kexp(p)) << 23);
+      }
+    }
+  }
+
+  __device__ __forceinline__ static float2 word(uint32_t d, const float* xr, float2 acc) {
+    constexpr uint32_t M = 0x4B000000u;
+    // 2^23 + 8 * 16^k for k = 0..4
+    constexpr float C0 = 8388616.0f, C1 = 8388736.0f, C2 = 8390656.0f, C3 = 8421376.0f,
+                    C4 = 8912896.0f;
+    const uint32_t dh = d >> 12;
+    float2 v;
+    v = __fadd2_rn(make_float2(u2f((d & 0xFu) | M), u2f((d & 0xF0u) | M)), make_float2(-C0, -C1));
+    acc = __ffma2_rn(v, make_float2(xr[0], xr[1]), acc);
+    v = __fadd2_rn(make_float2(u2f((d & 0xF00u) | M), u2f((d & 0xF000u) | M)),
+                   make_float2(-C2, -C3));
+    acc = __ffma2_rn(v, make_float2(xr[2], xr[3]), acc);
+    v = __fadd2_rn(make_float2(u2f((d & 0xF0000u) | M), u2f((dh & 0xF00u) | M)),
+                   make_float2(-C4, -C2));
+    acc = __ffma2_rn(v, make_float2(xr[4], xr[5]), acc);
+    v = __fadd2_rn(make_float2(u2f((dh & 0xF000u) | M), u2f((dh & 0xF0000u) | M)),
+                   make_float2(-C3, -C4));
+    acc = __ffma2_rn(v, make_float2(xr[6], xr[7]), acc);
+    return acc;
+  }
+
+  // t: 4-byte aligned pointer to the lane tile in shared memory.
+  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) w[i] = lds32(t + 4 * i);
+    const float s0 = f16_bits_to_f32(w[0]);
+    const float s1 = f16_bits_to_f32(w[4] >> 16);
+    const uint32_t m = __byte_perm(w[0], w[4], 0x3254);
+    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+    a0 = word(m, xr + 0, a0);
+    a0 = word(w[1], xr + 8, a0);
+    a0 = word(w[2], xr + 16, a0);
+    a0 = word(w[3], xr + 24, a0);
+    a1 = word(w[5], xr + 32, a1);
+    a1 = word(w[6], xr + 40, a1);
+    a1 = word(w[7], xr + 48, a1);
+    a1 = word(w[8], xr + 56, a1);
+    float2 r = __fmul2_rn(a0, make_float2(s0, s0));
+    r = __ffma2_rn(a1, make_float2(s1, s1), r);
+    return r.x + r.y;
+  }
+};
+
+// ---------------------------------------------------------------- Q5_0
+// Block = [s (2)][qh (4)][qs (16)] (quant.rs:831-858); q = low | high << 4,
+// weight (q - 16) * s.  Tile = 2 blocks = 44 bytes = 11 words.
+template <>
+struct Tile<OBJB_Q5_0> {
+  static constexpr int P = 2;
+  static constexpr int BB = 22;
+  static constexpr int TB = P * BB;
+  static constexpr int XR = 64;
+
+  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
+                                                float (&xr)[XR]) {
+#pragma unroll
+    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+  }
+
+  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+    uint32_t w[11];
+#pragma unroll
+    for (int i = 0; i < 11; ++i) w[i] = lds32(t + 4 * i);
+    float total = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const int base = b * BB;
+      const float s = f16_bits_to_f32(byte_at(w, base) | (byte_at(w, base + 1) << 8));
+      const uint32_t qh = byte_at(w, base + 2) | (byte_at(w, base + 3) << 8) |
+                          (byte_at(w, base + 4) << 16) | (byte_at(w, base + 5) << 24);
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t by = byte_at(w, base + 6 + j);
+        const uint32_t q0 = (by & 0xFu) | (((qh >> (2 * j)) & 1u) << 4);
+        const uint32_t q1 = (by >> 4) | (((qh >> (2 * j + 1)) & 1u) << 4);
+        const float2 v = make_float2(qf(q0, 16.0f), qf(q1, 16.0f));
+        acc = __ffma2_rn(v, make_float2(xr[b * 32 + 2 * j], xr[b * 32 + 2 * j + 1]), acc);
+      }
+      total = fmaf(acc.x + acc.y, s, total);
+    }
+    return total;
+  }
+};
+
+// ---------------------------------------------------------------- IQ3_0
+// Block = [s (2)][2-bit lows (8)][1-bit highs (4)] (quant.rs:860-879);
+// q = low | high << 2, weight (q - 4) * s.  Tile = 2 blocks = 28 bytes.
+template <>
+struct Tile<OBJB_IQ3_0> {
+  static constexpr int P = 2;
+  static constexpr int BB = 14;
+  static constexpr int TB = P * BB;
+  static constexpr int XR = 64;
+
+  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
+                                                float (&xr)[XR]) {
+#pragma unroll
+    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+  }
+
+  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+    uint32_t w[7];
+#pragma unroll
+    for (int i = 0; i < 7; ++i) w[i] = lds32(t + 4 * i);
+    float total = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const int base = b * BB;
+      const float s = f16_bits_to_f32(byte_at(w, base) | (byte_at(w, base + 1) << 8));
+      uint32_t lo0 = 0, lo1 = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo0 |= byte_at(w, base + 2 + j) << (8 * j);
+        lo1 |= byte_at(w, base + 6 + j) << (8 * j);
+        hi |= byte_at(w, base + 10 + j) << (8 * j);
+      }
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const uint32_t lw = e < 16 ? lo0 : lo1;
+        const int sh = 2 * (e & 15);
+        const uint32_t qa = ((lw >> sh) & 3u) | (((hi >> e) & 1u) << 2);
+        const uint32_t qb = ((lw >> (sh + 2)) & 3u) | (((hi >> (e + 1)) & 1u) << 2);
+        const float2 v = make_float2(qf(qa, 4.0f), qf(qb, 4.0f));
+        acc = __ffma2_rn(v, make_float2(xr[b * 32 + e], xr[b * 32 + e + 1]), acc);
+      }
+      total = fmaf(acc.x + acc.y, s, total);
+    }
+    return total;
+  }
+};
+
+// ------------------------------------------------- FP4 E2M1, interleaved
+// Block = [E8M0 scale (1)][16 packed bytes] (quant.rs:908-926).  Tile = 2
+// blocks = 34 bytes, read as 17 half-words (2-byte aligned).  The E2M1 pairs
+// go through the sm_100a hardware e2m1x2 -> f16x2 conversion, which is exact
+// (code 8 -> -0.0, as quant.rs's FP4_TABLE).
+__device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
+  __half2_raw h = __nv_cvt_fp4x2_to_halfraw2(static_cast<__nv_fp4x2_storage_t>(byte), __NV_E2M1);
+  return __half22float2(*reinterpret_cast<__half2*>(&h));
+}
+
+template <>
+struct Tile<OBJB_FP4_E2M1> {
+  static constexpr int P = 2;
+  static constexpr int BB = 17;
+  static constexpr int TB = P * BB;
+  static constexpr int XR = 64;
+
+  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
+                                                float (&xr)[XR]) {
+#pragma unroll
+    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+  }
+
+  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+    uint32_t h[17];
+#pragma unroll
+    for (int i = 0; i < 17; ++i) h[i] = *reinterpret_cast<const uint16_t*>(t + 2 * i);
+    float total = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const int base = b * BB;
+#define OBJB_FP4_BYTE(i) ((h[(i) >> 1] >> (((i) & 1) * 8)) & 0xFFu)
+      const float s = e8m0_to_f32(OBJB_FP4_BYTE(base));
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float2 v = e2m1x2_to_float2(OBJB_FP4_BYTE(base + 1 + j));
+        acc = __ffma2_rn(v, make_float2(xr[b * 32 + 2 * j], xr[b * 32 + 2 * j + 1]), acc);
+      }
+#undef OBJB_FP4_BYTE
+      total = fmaf(acc.x + acc.y, s, total);
+    }
+    return total;
+  }
+};
+
+// ------------------------------------------------------ FP4 E2M1, split
+// DeepSeek layout (moe.rs:27-35, quant.rs:368-408): weight [rows, cols/2],
+// scale [rows, cols/32].  A lane owns blocks (seg * lpr * P + j * lpr + ll),
+// j < P, so consecutive lanes read consecutive 16-byte blocks (conflict-free
+// 128-bit shared loads).
+struct SplitFp4 {
+  static constexpr int P = 2;
+  static constexpr int XR = 64;
+
+  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int b0, int stride,
+                                                int nblocks, float (&xr)[XR]) {
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int b = b0 + j * stride;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) xr[j * 32 + e] = b < nblocks ? __ldg(x + b * 32 + e) : 0.0f;
+    }
+  }
+
+  __device__ __forceinline__ static float dot(const uint8_t* wrow, const uint8_t* srow, int b0,
+                                              int stride, int nblocks, const float (&xr)[XR]) {
+    float total = 0.0f;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int b = b0 + j * stride;
+      if (b < nblocks) {
+        const uint4 q = *reinterpret_cast<const uint4*>(wrow + 16 * b);
+        const float s = e8m0_to_f32(srow[b]);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float2 v = e2m1x2_to_float2((qw[k >> 2] >> ((k & 3) * 8)) & 0xFFu);
+          acc = __ffma2_rn(v, make_float2(xr[j * 32 + 2 * k], xr[j * 32 + 2 * k + 1]), acc);
+        }
+        total = fmaf(acc.x + acc.y, s, total);
+      }
+    }
+    return total;
+  }
+};
+
+// ------------------------------------------- generic block dot (fallback)
+// Reads one block straight from global memory (any alignment) and returns
+// sum_l (q_l - off) x_l times the block scale.  Used by the fallback kernel
+// for shapes or pointers the TMA path cannot take.
+template <int FMT>
+__device__ __forceinline__ float block_dot_global(const uint8_t* __restrict__ blk,
+                                                  const float* __restrict__ x32) {
+  float acc = 0.0f;
+  if constexpr (FMT == OBJB_Q4_0) {
+    const float s = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t by = blk[2 + j];
+      acc = fmaf(qf(by & 0xFu, 8.0f), __ldg(x32 + 2 * j), acc);
+      acc = fmaf(qf(by >> 4, 8.0f), __ldg(x32 + 2 * j + 1), acc);
+    }
+    return acc * s;
+  } else if constexpr (FMT == OBJB_Q5_0) {
+    const float s = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+    const uint32_t qh = blk[2] | (blk[3] << 8) | (blk[4] << 16) | (static_cast<uint32_t>(blk[5]) << 24);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const uint32_t by = blk[6 + e / 2];
+      const uint32_t q = ((e & 1) ? (by >> 4) : (by & 0xFu)) | (((qh >> e) & 1u) << 4);
+      acc = fmaf(qf(q, 16.0f), __ldg(x32 + e), acc);
+    }
+    return acc * s;
+  } else if constexpr (FMT == OBJB_IQ3_0) {
+    const float s = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const uint32_t low = (blk[2 + e / 4] >> (2 * (e % 4))) & 3u;
+      const uint32_t high = (blk[10 + e / 8] >> (e % 8)) & 1u;
+      acc = fmaf(qf(low | (high << 2), 4.0f), __ldg(x32 + e), acc);
+    }
+    return acc * s;
+  } else {
+    const float s = e8m0_to_f32(blk[0]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 v = e2m1x2_to_float2(blk[1 + j]);
+      acc = fmaf(v.x, __ldg(x32 + 2 * j), acc);
+      acc = fmaf(v.y, __ldg(x32 + 2 * j + 1), acc);
+    }
+    return acc * s;
+  }
+}
+
+}  // namespace dev
+}  // namespace objb

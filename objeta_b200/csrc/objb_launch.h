@@ -1,0 +1,49 @@
+// objb_launch.h -- host-side planning of the pipelined row-streaming kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace objb {
+
+// Mirror of dev::RowLayout (same field order; the device struct is passed by
+// value as a kernel argument).
+struct RowLayoutHost {
+  int rows, cols;
+  int nblocks;
+  int row_bytes;
+  int srow_bytes;
+  int nseg;
+  int lpr;
+  int rpw;
+  int ngrp;
+  int tstage;
+  int nslots;
+  int stage_bytes;
+};
+
+struct DeviceProps {
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  size_t l2_bytes = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+
+// Cached per-device properties (queried once per device).
+int device_props(int device, DeviceProps* out);
+int current_device(int* dev);
+
+// Plans the row streaming of a rows x cols matrix whose packed rows are
+// `row_bytes` (+ `srow_bytes` of split scales) long, with lane tiles covering
+// `blocks_per_lane` blocks.  `dual` doubles the per-stage bytes (two matrices
+// per stage).  Returns false when the shape cannot use the bulk-copy path.
+bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
+               int max_consumer_warps, RowLayoutHost* L);
+
+size_t pipe_smem_bytes(const RowLayoutHost& L);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace objb
