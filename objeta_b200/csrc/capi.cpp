@@ -2,7 +2,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -124,6 +126,48 @@ int device_error_word(int device, unsigned** out) {
     g_err_words[device] = w;
   }
   *out = g_err_words[device];
+  return OBJB_OK;
+}
+
+namespace {
+std::mutex g_ws_mu;
+struct WsKey {
+  int device;
+  cudaStream_t stream;
+  bool operator<(const WsKey& o) const {
+    return device != o.device ? device < o.device : stream < o.stream;
+  }
+};
+struct WsBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<WsKey, WsBuf> g_ws;
+}  // namespace
+
+int workspace_get(int device, cudaStream_t stream, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  WsBuf& b = g_ws[WsKey{device, stream}];
+  if (b.bytes >= bytes && b.ptr) {
+    *out = b.ptr;
+    return OBJB_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  OBJB_CUDA(cudaStreamIsCapturing(stream, &cs), "query stream capture state");
+  if (cs != cudaStreamCaptureStatusNone)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "allocate stream workspace",
+                     "the per-stream workspace must be allocated before stream capture: make one "
+                     "uncaptured call with this shape on this stream first");
+  if (b.ptr) {
+    OBJB_CUDA(cudaStreamSynchronize(stream), "drain stream before growing its workspace");
+    cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+  }
+  const size_t want = std::max<size_t>(bytes, kWorkspaceMinBytes);
+  OBJB_CUDA(cudaMalloc(&b.ptr, want), "allocate stream workspace");
+  b.bytes = want;
+  *out = b.ptr;
   return OBJB_OK;
 }
 

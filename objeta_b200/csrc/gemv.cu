@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -16,12 +17,6 @@ namespace objb {
 
 static_assert(sizeof(RowLayoutHost) == sizeof(dev::RowLayout), "layout mirror mismatch");
 
-static int next_pow2(int v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
-
 bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
                int max_consumer_warps, RowLayoutHost* L) {
   if (rows <= 0 || cols <= 0 || cols % 32) return false;
@@ -30,16 +25,24 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
   const int lanes = (nblocks + blocks_per_lane - 1) / blocks_per_lane;
   const int nseg = (lanes + 31) / 32;
   if (nseg > max_consumer_warps) return false;
-  const int lpr = nseg > 1 ? 32 : next_pow2(lanes);
-  const int rpw = 32 / lpr;
+  const int lpr = 32;  // one row per warp; idle lanes when the row is narrow
+  const int rpw = 1;
   const int ngrp = std::max(1, max_consumer_warps / nseg);
   int per_row = row_bytes + srow_bytes;
   if (dual) per_row *= 2;
-  constexpr int kStageTarget = 32 * 1024;
+  constexpr int kStageTarget = 48 * 1024;
   constexpr int kSmemBudget = 200 * 1024;
-  int T = std::max(1, std::min(dev::kMaxRowsPerStage, kStageTarget / per_row));
-  const int quantum = ngrp * rpw;
-  if (T >= quantum) T = T / quantum * quantum;
+  // One stage gives every row group one 4-row batch when that fits; small rows
+  // get several batches per stage.
+  const int quantum = ngrp * 4;
+  int T;
+  if (quantum * per_row <= kStageTarget) {
+    T = quantum;
+    while (T + quantum <= dev::kMaxRowsPerStage && (T + quantum) * per_row <= kStageTarget) T += quantum;
+  } else {
+    T = std::max(1, std::min(quantum, (kSmemBudget / 2 - 4096) / per_row));
+  }
+  T = std::min(T, dev::kMaxRowsPerStage);
   const int stage_bytes = ((T * per_row) + 127) / 128 * 128;
   const int red_bytes = dev::kMaxSlots * T * nseg * 2 * 4;
   const int fixed = 2 * dev::kMaxSlots * 8 + red_bytes + 128;
@@ -67,52 +70,98 @@ size_t pipe_smem_bytes(const RowLayoutHost& L) {
   return off + static_cast<size_t>(L.nslots) * L.stage_bytes;
 }
 
-namespace {
-
-// Opt a kernel into large dynamic shared memory once per device.
-template <class K>
-int ensure_smem_attr(K kernel, int device, size_t bytes) {
+// Opts a kernel into large dynamic shared memory, once per (kernel, device).
+int ensure_smem_attr_ptr(const void* kernel, int device, size_t bytes) {
   static std::mutex mu;
-  static uint64_t done_mask = 0;
-  static size_t done_bytes[64] = {};
+  static std::map<std::pair<const void*, int>, size_t> done;
   std::lock_guard<std::mutex> lk(mu);
-  if (device < 64 && (done_mask >> device) & 1u && done_bytes[device] >= bytes) return OBJB_OK;
+  auto key = std::make_pair(kernel, device);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return OBJB_OK;
+  const size_t want = std::max<size_t>(bytes, 200 * 1024);
   OBJB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(std::max<size_t>(bytes, 200 * 1024))),
+                                 static_cast<int>(want)),
             "opt kernel into large shared memory");
-  if (device < 64) {
-    done_mask |= (1ull << device);
-    done_bytes[device] = std::max<size_t>(bytes, 200 * 1024);
-  }
+  done[key] = want;
   return OBJB_OK;
 }
+
+namespace {
+
+template <class K>
+int ensure_smem_attr(K kernel, int device, size_t bytes) {
+  return ensure_smem_attr_ptr(reinterpret_cast<const void*>(kernel), device, bytes);
+}
+
+}  // namespace
+
+// Launches the x-image prep kernel for `nvec` vectors into `img`, then lets
+// the caller launch the consumer kernel with programmatic serialization.
+template <class RD>
+int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int nvec, uint4* img,
+                  size_t img_stride_quads, cudaStream_t stream) {
+  dev::RowLayout dl;
+  std::memcpy(&dl, &L, sizeof(dl));
+  const int n = L.nseg * 32 * nvec;
+  const int grid = std::max(1, std::min((n + 127) / 128, 1024));
+  dev::ximage_kernel<RD><<<grid, 128, 0, stream>>>(dl, x, x_stride, nvec, img, img_stride_quads);
+  OBJB_CUDA(cudaGetLastError(), "launch x-image kernel");
+  return OBJB_OK;
+}
+
+template <class RD>
+size_t ximage_quads(const RowLayoutHost& L) {
+  return static_cast<size_t>(RD::XRegs::kQuads) * L.nseg * 32;
+}
+
+// Launches `kernel` with programmatic stream serialization (it may start while
+// the previous kernel in the stream, the x-image prep, is still running).
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cudaStream_t stream,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OBJB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...), "launch pipelined kernel");
+  return OBJB_OK;
+}
+
+namespace {
 
 template <class RD>
 int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s, const float* x,
                      float* y, cudaStream_t stream, int device, const DeviceProps& props) {
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
+  void* ws = nullptr;
+  OBJB_TRY(workspace_get(device, stream, ximage_quads<RD>(L) * 16, &ws));
+  uint4* img = static_cast<uint4*>(ws);
+  OBJB_TRY(launch_ximage<RD>(L, x, 0, 1, img, 0, stream));
   const int nst = (L.rows + L.tstage - 1) / L.tstage;
   int grid = std::min(nst, props.sm_count);
   const int st_per_cta = (nst + grid - 1) / grid;
   grid = (nst + st_per_cta - 1) / st_per_cta;
   dev::GemvProg prog;
   prog.src = dev::StageSource{w, s, nullptr, nullptr};
-  prog.x = x;
+  prog.ximg = img;
   prog.y = y;
   prog.rows = L.rows;
   prog.rows_per_cta = st_per_cta * L.tstage;
-  prog.dual = false;
   prog.err = err;
   const size_t smem = pipe_smem_bytes(L);
-  auto kernel = dev::pipe_kernel<RD, dev::GemvProg>;
+  auto kernel = dev::pipe_kernel<RD, dev::GemvProg, false>;
   OBJB_TRY(ensure_smem_attr(kernel, device, smem));
   dev::RowLayout dl;
   std::memcpy(&dl, &L, sizeof(dl));
   const int threads = (L.nseg * L.ngrp + 1) * 32;
-  kernel<<<grid, threads, smem, stream>>>(dl, prog);
-  OBJB_CUDA(cudaGetLastError(), "launch pipelined GEMV kernel");
-  return OBJB_OK;
+  return launch_pdl(kernel, grid, threads, smem, stream, dl, prog);
 }
 
 template <int FMT>
@@ -126,7 +175,7 @@ int gemv_device_fmt(const uint8_t* w, const float* x, float* y, int rows, int co
   const int row_bytes = cols / 32 * T::BB;
   RowLayoutHost L;
   const bool fast = aligned16(w) && (cols / 32) % T::P == 0 &&
-                    plan_rows(rows, cols, row_bytes, 0, T::P, false, 8, &L);
+                    plan_rows(rows, cols, row_bytes, 0, T::P, false, dev::kMaxConsumerWarps, &L);
   if (fast) return launch_gemv_pipe<dev::RowDot<FMT>>(L, w, nullptr, x, y, stream, device, props);
   const int grid = (rows + 7) / 8;
   dev::gemv_fallback_kernel<FMT><<<grid, 256, 0, stream>>>(w, x, y, rows, cols,
@@ -170,7 +219,7 @@ int gemv_fp4_split_device(const void* w, const void* s, const float* x, float* y
   const uint8_t* sb = static_cast<const uint8_t*>(s);
   RowLayoutHost L;
   const bool fast = aligned16(wb) && aligned16(sb) &&
-                    plan_rows(r, c, c / 2, c / 32, dev::SplitFp4::P, false, 8, &L);
+                    plan_rows(r, c, c / 2, c / 32, dev::SplitFp4::P, false, dev::kMaxConsumerWarps, &L);
   if (fast) return launch_gemv_pipe<dev::RowDotSplitFp4>(L, wb, sb, x, y, stream, device, props);
   dev::gemv_fp4_split_fallback_kernel<<<(r + 7) / 8, 256, 0, stream>>>(wb, sb, x, y, r, c);
   OBJB_CUDA(cudaGetLastError(), "launch split FP4 fallback kernel");

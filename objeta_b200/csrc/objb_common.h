@@ -55,4 +55,10 @@ int validate_gemv_shape(int fmt, size_t rows, size_t cols);
 // Lazily created per-device error word used by kernels with bounded waits.
 int device_error_word(int device, unsigned int** out);
 
+// Per-(device, stream) device workspace, grow-only, at least
+// kWorkspaceMinBytes.  Work on one stream is ordered, so one buffer per stream
+// is race-free; it cannot be allocated while the stream is being captured.
+constexpr size_t kWorkspaceMinBytes = 1u << 20;
+int workspace_get(int device, cudaStream_t stream, size_t bytes, void** out);
+
 }  // namespace objb

@@ -53,6 +53,39 @@ __device__ __forceinline__ uint32_t byte_at(const uint32_t (&w)[N], int i) {
   return (w[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
 }
 
+// A lane's x registers as N 128-bit quads.  Indexed with compile-time
+// constants only (after unrolling), so the array stays in registers.
+template <int N>
+struct Words {
+  static constexpr int kQuads = N;
+  uint4 q[N];
+  __device__ __forceinline__ uint32_t w(int i) const {
+    const uint4& v = q[i >> 2];
+    switch (i & 3) {
+      case 0: return v.x;
+      case 1: return v.y;
+      case 2: return v.z;
+      default: return v.w;
+    }
+  }
+  __device__ __forceinline__ void set(int i, uint32_t val) {
+    uint4& v = q[i >> 2];
+    switch (i & 3) {
+      case 0: v.x = val; break;
+      case 1: v.y = val; break;
+      case 2: v.z = val; break;
+      default: v.w = val; break;
+    }
+  }
+  __device__ __forceinline__ float2 f2(int i) const {
+    return make_float2(__uint_as_float(w(2 * i)), __uint_as_float(w(2 * i + 1)));
+  }
+  __device__ __forceinline__ void set_f2(int i, float2 v) {
+    set(2 * i, __float_as_uint(v.x));
+    set(2 * i + 1, __float_as_uint(v.y));
+  }
+};
+
 template <int FMT>
 struct Tile;
 
@@ -60,77 +93,110 @@ struct Tile;
 // Tile = 2 blocks = 36 bytes = 9 words:
 //   w0 = [s0 lo, s0 hi, qs0[0], qs0[1]]  w1..w3 = qs0[2..13]
 //   w4 = [qs0[14], qs0[15], s1 lo, s1 hi]  w5..w8 = qs1[0..15]
-// Byte j of qs holds element 2j (low nibble) and 2j+1 (high nibble), so in an
-// aligned quant word nibble position p is element (word base + p).
+// Byte j of qs holds element 2j (low nibble) and 2j+1 (high nibble).  The
+// eight "decode words" are m = [qs0[14], qs0[15], qs0[0], qs0[1]] (one byte
+// permute), w1..w3, w5..w8; nibble position p of decode word u is element
+// elem(u, p) of the tile.
+//
+// Block sums are exact integer dot products: each x of a block is held as
+// X = rint(x * 2^(20-E)) (2^E > max|x| of the block), split into three
+// signed 7-bit digits, and sum_l q_l X_l is formed with dp4a on the unpacked
+// nibbles (q in 0..15) against the digit bytes, then
+//   sum_l (q_l - 8) x_l = (sum_l q_l X_l - 8 sum_l X_l) * 2^(E-20).
+// The only rounding before the fp32 accumulation across blocks is that of X
+// (at most 2^-21 of the block's largest |x|) and one int -> f32 conversion.
 template <>
 struct Tile<OBJB_Q4_0> {
   static constexpr int P = 2;
   static constexpr int BB = 18;
   static constexpr int TB = P * BB;
-  static constexpr int XR = 64;
 
-  // Decode word u (0..7), nibble position p (0..7) -> element within the tile.
+  // Words 0..47: digit word (u, h, k) at u * 6 + h * 3 + k  ([decode word]
+  // [low/high nibble half][digit]); 48..49: 2^(E-20) per block (NaN for a
+  // non-finite block); 50..51: -8 * sum X per block.
+  using XRegs = Words<13>;
+  __device__ __forceinline__ static int dgi(int u, int h, int k) { return u * 6 + h * 3 + k; }
+
   __device__ __forceinline__ static int elem(int u, int p) {
-    if (u == 0) return p < 4 ? 28 + p : p - 4;  // merged word (see dot)
+    if (u == 0) return p < 4 ? 28 + p : p - 4;
     if (u < 4) return 4 + 8 * (u - 1) + p;
     return 32 + 8 * (u - 4) + p;
   }
-  // Power-of-16 exponent of nibble position p in the decode.
-  __device__ __forceinline__ static int kexp(int p) { return p < 5 ? p : p - 3; }
 
   __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                float (&xr)[XR]) {
+                                                XRegs& xr) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int b = 0; b < 2; ++b) {
+      float xv[32];
+      float m = 0.0f;
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        float v = active ? __ldg(x + col0 + elem(u, p)) : 0.0f;
-        xr[u * 8 + p] = v * u2f(static_cast<uint32_t>(127 - 4 * kexp(p)) << 23);
+      for (int e = 0; e < 32; ++e) {
+        xv[e] = active ? __ldg(x + col0 + 32 * b + e) : 0.0f;
+        m = fmaxf(m, fabsf(xv[e]));
+      }
+      int E = 0;
+      frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
+      int X[32];
+      int sx = 0;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        X[e] = __float2int_rn(ldexpf(xv[e], 20 - E));
+        sx += X[e];
+      }
+      xr.set(48 + b, __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000)));
+      xr.set(50 + b, static_cast<uint32_t>(-8 * sx));
+#pragma unroll
+      for (int uu = 0; uu < 4; ++uu) {
+        const int u = 4 * b + uu;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[3] = {0u, 0u, 0u};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int v = X[elem(u, 2 * j + h) - 32 * b];
+            const int d0 = ((v + 64) & 127) - 64;
+            const int v1 = (v - d0) / 128;
+            const int d1 = ((v1 + 64) & 127) - 64;
+            const int d2 = (v1 - d1) / 128;
+            pk[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * j);
+            pk[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
+            pk[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * j);
+          }
+          xr.set(dgi(u, h, 0), pk[0]);
+          xr.set(dgi(u, h, 1), pk[1]);
+          xr.set(dgi(u, h, 2), pk[2]);
+        }
       }
     }
   }
 
-  __device__ __forceinline__ static float2 word(uint32_t d, const float* xr, float2 acc) {
-    constexpr uint32_t M = 0x4B000000u;
-    // 2^23 + 8 * 16^k for k = 0..4
-    constexpr float C0 = 8388616.0f, C1 = 8388736.0f, C2 = 8390656.0f, C3 = 8421376.0f,
-                    C4 = 8912896.0f;
-    const uint32_t dh = d >> 12;
-    float2 v;
-    v = __fadd2_rn(make_float2(u2f((d & 0xFu) | M), u2f((d & 0xF0u) | M)), make_float2(-C0, -C1));
-    acc = __ffma2_rn(v, make_float2(xr[0], xr[1]), acc);
-    v = __fadd2_rn(make_float2(u2f((d & 0xF00u) | M), u2f((d & 0xF000u) | M)),
-                   make_float2(-C2, -C3));
-    acc = __ffma2_rn(v, make_float2(xr[2], xr[3]), acc);
-    v = __fadd2_rn(make_float2(u2f((d & 0xF0000u) | M), u2f((dh & 0xF00u) | M)),
-                   make_float2(-C4, -C2));
-    acc = __ffma2_rn(v, make_float2(xr[4], xr[5]), acc);
-    v = __fadd2_rn(make_float2(u2f((dh & 0xF000u) | M), u2f((dh & 0xF0000u) | M)),
-                   make_float2(-C3, -C4));
-    acc = __ffma2_rn(v, make_float2(xr[6], xr[7]), acc);
-    return acc;
-  }
-
   // t: 4-byte aligned pointer to the lane tile in shared memory.
-  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+  __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) w[i] = lds32(t + 4 * i);
-    const float s0 = f16_bits_to_f32(w[0]);
-    const float s1 = f16_bits_to_f32(w[4] >> 16);
-    const uint32_t m = __byte_perm(w[0], w[4], 0x3254);
-    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-    a0 = word(m, xr + 0, a0);
-    a0 = word(w[1], xr + 8, a0);
-    a0 = word(w[2], xr + 16, a0);
-    a0 = word(w[3], xr + 24, a0);
-    a1 = word(w[5], xr + 32, a1);
-    a1 = word(w[6], xr + 40, a1);
-    a1 = word(w[7], xr + 48, a1);
-    a1 = word(w[8], xr + 56, a1);
-    float2 r = __fmul2_rn(a0, make_float2(s0, s0));
-    r = __ffma2_rn(a1, make_float2(s1, s1), r);
-    return r.x + r.y;
+    const float s[2] = {f16_bits_to_f32(w[0]), f16_bits_to_f32(w[4] >> 16)};
+    const uint32_t D[8] = {__byte_perm(w[0], w[4], 0x3254), w[1], w[2], w[3], w[5], w[6], w[7], w[8]};
+    float r = 0.0f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      int q0 = 0, q1 = 0, q2 = 0;
+#pragma unroll
+      for (int uu = 0; uu < 4; ++uu) {
+        const int u = 4 * b + uu;
+        const int lo = static_cast<int>(D[u] & 0x0F0F0F0Fu);
+        const int hi = static_cast<int>((D[u] >> 4) & 0x0F0F0F0Fu);
+        q0 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 0))), q0);
+        q1 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 1))), q1);
+        q2 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 2))), q2);
+        q0 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 0))), q0);
+        q1 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 1))), q1);
+        q2 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 2))), q2);
+      }
+      const int T = q0 + (q1 + q2 * 128) * 128 + static_cast<int>(xr.w(50 + b));
+      r = fmaf(__int2float_rn(T), s[b] * __uint_as_float(xr.w(48 + b)), r);
+    }
+    return r;
   }
 };
 
@@ -142,15 +208,17 @@ struct Tile<OBJB_Q5_0> {
   static constexpr int P = 2;
   static constexpr int BB = 22;
   static constexpr int TB = P * BB;
-  static constexpr int XR = 64;
+  using XRegs = Words<16>;  // x of the tile as 32 float pairs
 
   __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                float (&xr)[XR]) {
+                                                XRegs& xr) {
 #pragma unroll
-    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+    for (int i = 0; i < 32; ++i)
+      xr.set_f2(i, active ? make_float2(__ldg(x + col0 + 2 * i), __ldg(x + col0 + 2 * i + 1))
+                          : make_float2(0.f, 0.f));
   }
 
-  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+  __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[11];
 #pragma unroll
     for (int i = 0; i < 11; ++i) w[i] = lds32(t + 4 * i);
@@ -168,7 +236,7 @@ struct Tile<OBJB_Q5_0> {
         const uint32_t q0 = (by & 0xFu) | (((qh >> (2 * j)) & 1u) << 4);
         const uint32_t q1 = (by >> 4) | (((qh >> (2 * j + 1)) & 1u) << 4);
         const float2 v = make_float2(qf(q0, 16.0f), qf(q1, 16.0f));
-        acc = __ffma2_rn(v, make_float2(xr[b * 32 + 2 * j], xr[b * 32 + 2 * j + 1]), acc);
+        acc = __ffma2_rn(v, xr.f2(b * 16 + j), acc);
       }
       total = fmaf(acc.x + acc.y, s, total);
     }
@@ -184,15 +252,17 @@ struct Tile<OBJB_IQ3_0> {
   static constexpr int P = 2;
   static constexpr int BB = 14;
   static constexpr int TB = P * BB;
-  static constexpr int XR = 64;
+  using XRegs = Words<16>;  // x of the tile as 32 float pairs
 
   __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                float (&xr)[XR]) {
+                                                XRegs& xr) {
 #pragma unroll
-    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+    for (int i = 0; i < 32; ++i)
+      xr.set_f2(i, active ? make_float2(__ldg(x + col0 + 2 * i), __ldg(x + col0 + 2 * i + 1))
+                          : make_float2(0.f, 0.f));
   }
 
-  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+  __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[7];
 #pragma unroll
     for (int i = 0; i < 7; ++i) w[i] = lds32(t + 4 * i);
@@ -216,7 +286,7 @@ struct Tile<OBJB_IQ3_0> {
         const uint32_t qa = ((lw >> sh) & 3u) | (((hi >> e) & 1u) << 2);
         const uint32_t qb = ((lw >> (sh + 2)) & 3u) | (((hi >> (e + 1)) & 1u) << 2);
         const float2 v = make_float2(qf(qa, 4.0f), qf(qb, 4.0f));
-        acc = __ffma2_rn(v, make_float2(xr[b * 32 + e], xr[b * 32 + e + 1]), acc);
+        acc = __ffma2_rn(v, xr.f2(b * 16 + e / 2), acc);
       }
       total = fmaf(acc.x + acc.y, s, total);
     }
@@ -239,15 +309,17 @@ struct Tile<OBJB_FP4_E2M1> {
   static constexpr int P = 2;
   static constexpr int BB = 17;
   static constexpr int TB = P * BB;
-  static constexpr int XR = 64;
+  using XRegs = Words<16>;  // x of the tile as 32 float pairs
 
   __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                float (&xr)[XR]) {
+                                                XRegs& xr) {
 #pragma unroll
-    for (int i = 0; i < XR; ++i) xr[i] = active ? __ldg(x + col0 + i) : 0.0f;
+    for (int i = 0; i < 32; ++i)
+      xr.set_f2(i, active ? make_float2(__ldg(x + col0 + 2 * i), __ldg(x + col0 + 2 * i + 1))
+                          : make_float2(0.f, 0.f));
   }
 
-  __device__ __forceinline__ static float dot(const uint8_t* t, const float (&xr)[XR]) {
+  __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t h[17];
 #pragma unroll
     for (int i = 0; i < 17; ++i) h[i] = *reinterpret_cast<const uint16_t*>(t + 2 * i);
@@ -261,7 +333,7 @@ struct Tile<OBJB_FP4_E2M1> {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const float2 v = e2m1x2_to_float2(OBJB_FP4_BYTE(base + 1 + j));
-        acc = __ffma2_rn(v, make_float2(xr[b * 32 + 2 * j], xr[b * 32 + 2 * j + 1]), acc);
+        acc = __ffma2_rn(v, xr.f2(b * 16 + j), acc);
       }
 #undef OBJB_FP4_BYTE
       total = fmaf(acc.x + acc.y, s, total);
@@ -277,20 +349,22 @@ struct Tile<OBJB_FP4_E2M1> {
 // 128-bit shared loads).
 struct SplitFp4 {
   static constexpr int P = 2;
-  static constexpr int XR = 64;
+  using XRegs = Words<16>;
 
   __device__ __forceinline__ static void load_x(const float* __restrict__ x, int b0, int stride,
-                                                int nblocks, float (&xr)[XR]) {
+                                                int nblocks, XRegs& xr) {
 #pragma unroll
     for (int j = 0; j < P; ++j) {
       const int b = b0 + j * stride;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) xr[j * 32 + e] = b < nblocks ? __ldg(x + b * 32 + e) : 0.0f;
+      for (int e = 0; e < 16; ++e)
+        xr.set_f2(j * 16 + e, b < nblocks ? make_float2(__ldg(x + b * 32 + 2 * e), __ldg(x + b * 32 + 2 * e + 1))
+                                          : make_float2(0.f, 0.f));
     }
   }
 
   __device__ __forceinline__ static float dot(const uint8_t* wrow, const uint8_t* srow, int b0,
-                                              int stride, int nblocks, const float (&xr)[XR]) {
+                                              int stride, int nblocks, const XRegs& xr) {
     float total = 0.0f;
 #pragma unroll
     for (int j = 0; j < P; ++j) {
@@ -303,7 +377,7 @@ struct SplitFp4 {
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const float2 v = e2m1x2_to_float2((qw[k >> 2] >> ((k & 3) * 8)) & 0xFFu);
-          acc = __ffma2_rn(v, make_float2(xr[j * 32 + 2 * k], xr[j * 32 + 2 * k + 1]), acc);
+          acc = __ffma2_rn(v, xr.f2(j * 16 + k), acc);
         }
         total = fmaf(acc.x + acc.y, s, total);
       }

@@ -22,7 +22,7 @@ namespace objb {
 namespace dev {
 
 constexpr int kMaxSlots = 4;
-constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxConsumerWarps = 15;  // + 1 producer = 16 warps: 4 per SM sub-partition, 128 registers each
 constexpr int kMaxRowsPerStage = 64;
 
 // Geometry of one streamed matrix, decided on the host.
@@ -59,41 +59,91 @@ __device__ __forceinline__ SmemPlan carve_smem(uint8_t* base, const RowLayout& L
   return p;
 }
 
-// Per-format adapter: x registers and the lane-partial dot of one row.
+// Per-format adapter: x registers and the lane-partial dot of one row.  Lane
+// `lane` of column segment `seg` owns lane tile lt = seg * 32 + lane.  The x
+// registers of every lane tile are built once per x vector by
+// ximage_kernel ("x image", quad q of tile lt at img[q * nseg * 32 + lt]) and
+// loaded by each consumer lane with coalesced 128-bit loads.
 template <int FMT>
 struct RowDot {
   using T = Tile<FMT>;
-  static constexpr int XR = T::XR;
+  using XRegs = typename T::XRegs;
   int tile_off;  // byte offset of this lane's tile inside a row
   bool active;
-  __device__ __forceinline__ void init(const RowLayout& L, int seg, int ll, const float* x,
-                                       float (&xr)[XR]) {
-    const int lt = seg * L.lpr + ll;
+  __device__ __forceinline__ static void build(const RowLayout& L, int lt, const float* x, XRegs& xr) {
+    T::load_x(x, lt * T::P * 32, (lt * T::P) < L.nblocks, xr);
+  }
+  __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
+    const int lt = seg * 32 + lane;
     active = (lt * T::P) < L.nblocks;
     tile_off = lt * T::TB;
-    T::load_x(x, lt * T::P * 32, active, xr);
   }
-  __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t*,
-                                       const float (&xr)[XR]) const {
+  __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t*, const XRegs& xr) const {
     return active ? T::dot(wrow + tile_off, xr) : 0.0f;
   }
 };
 
 struct RowDotSplitFp4 {
-  static constexpr int XR = SplitFp4::XR;
-  int b0, stride, nblocks;
-  __device__ __forceinline__ void init(const RowLayout& L, int seg, int ll, const float* x,
-                                       float (&xr)[XR]) {
-    b0 = seg * L.lpr * SplitFp4::P + ll;
-    stride = L.lpr;
-    nblocks = L.nblocks;
-    SplitFp4::load_x(x, b0, stride, nblocks, xr);
+  using XRegs = SplitFp4::XRegs;
+  int b0, nblocks;
+  __device__ __forceinline__ static void build(const RowLayout& L, int lt, const float* x, XRegs& xr) {
+    const int seg = lt / 32, lane = lt % 32;
+    SplitFp4::load_x(x, seg * 32 * SplitFp4::P + lane, 32, L.nblocks, xr);
   }
-  __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t* srow,
-                                       const float (&xr)[XR]) const {
-    return SplitFp4::dot(wrow, srow, b0, stride, nblocks, xr);
+  __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
+    b0 = seg * 32 * SplitFp4::P + lane;
+    nblocks = L.nblocks;
+  }
+  __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t* srow, const XRegs& xr) const {
+    return SplitFp4::dot(wrow, srow, b0, 32, nblocks, xr);
   }
 };
+
+template <class XR>
+__device__ __forceinline__ void load_ximage(const uint4* __restrict__ img, int ntp, int lt, XR& xr) {
+#pragma unroll
+  for (int q = 0; q < XR::kQuads; ++q) xr.q[q] = __ldg(img + q * ntp + lt);
+}
+
+// Builds the x images of `nvec` vectors (x + v * x_stride) for layout L.
+// Starts dependents immediately: the consumer kernel is launched with
+// programmatic stream serialization and waits (griddepcontrol.wait) before
+// it reads the image, so its launch and first weight copies overlap this.
+template <class RD>
+__global__ void __launch_bounds__(128) ximage_kernel(const RowLayout L, const float* __restrict__ x,
+                                                     size_t x_stride, int nvec, uint4* __restrict__ img,
+                                                     size_t img_stride_quads) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int ntp = L.nseg * 32;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < ntp * nvec; idx += gridDim.x * blockDim.x) {
+    const int v = idx / ntp, lt = idx % ntp;
+    typename RD::XRegs xr;
+    RD::build(L, lt, x + v * x_stride, xr);
+    uint4* out = img + v * img_stride_quads;
+#pragma unroll
+    for (int q = 0; q < RD::XRegs::kQuads; ++q) out[q * ntp + lt] = xr.q[q];
+  }
+}
+
+// Reduces NV per-lane values over the 32 lanes of a warp with a transposed
+// butterfly: log2(NV) exchange steps that halve the value set, then plain
+// xor-shuffle steps.  Afterwards v[0] of lane L holds the full sum of value
+// index (L / (32 / NV)).  NV - 1 + (5 - log2 NV) shuffles instead of 5 * NV.
+template <int NV>
+__device__ __forceinline__ void butterfly(float (&v)[NV], int lane) {
+#pragma unroll
+  for (int n = NV, off = 16; n > 1; n >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float keep = upper ? v[i + n / 2] : v[i];
+      const float send = upper ? v[i] : v[i + n / 2];
+      v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = 16 / NV; off > 0; off >>= 1) v[0] += __shfl_xor_sync(0xFFFFFFFFu, v[0], off);
+}
 
 // The producer side: issues the bulk copies of `nst` stages of up to two
 // matrices (A and, when dual, B) into the ring.  Stage i covers rows
@@ -136,20 +186,21 @@ __device__ __forceinline__ void issue_stage(const RowLayout& L, const SmemPlan& 
 // One job = a row range of one matrix (or a matching pair) against one x.
 struct Job {
   StageSource src;
-  const float* x;
+  const uint4* ximg;  // x image of this job's vector
   int row_begin, row_end;
 };
 
 // Consumer warps: nseg * ngrp (<= kMaxConsumerWarps); one producer warp more.
-constexpr int kPipeThreads = (8 + 1) * 32;
+constexpr int kPipeThreads = (kMaxConsumerWarps + 1) * 32;
 
 // The pipelined kernel.  `Prog` supplies, for this CTA, a list of jobs and an
 // epilogue that receives each finished row (va for matrix A, vb for B):
 //   int njobs(int cta) const;   Job job(int cta, int j) const;
 //   void epilogue(int cta, int j, int row, float va, float vb) const;
 //   void finalize(int cta, int tid, int nthreads) const;   // after all jobs
-//   bool dual;  unsigned* err;
-template <class RD, class Prog>
+//   unsigned* err;
+// DUAL streams a second matrix of the same shape through the same stages.
+template <class RD, class Prog, bool DUAL>
 __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L, const Prog prog) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const SmemPlan sp = carve_smem(smem_raw, L, 2);
@@ -189,7 +240,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
             }
           }
           const int nr = min(T, J.row_end - r0);
-          issue_stage(L, sp, slot, J.src, prog.dual, r0, nr, pol);
+          issue_stage(L, sp, slot, J.src, DUAL, r0, nr, pol);
           ++it;
         }
       }
@@ -202,21 +253,26 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
   }
 
   // ---------------- consumers
+  // Warp (seg, grp) computes, for batches of RB rows, the partial dot of its
+  // column segment; rows of a stage are dealt to row groups RB at a time.
+  constexpr int RB = 4;
+  constexpr int NV = DUAL ? 2 * RB : RB;
+  constexpr int W = 32 / NV;
   const int seg = warp % L.nseg;
   const int grp = warp / L.nseg;
-  const int sub = lane / L.lpr;
-  const int ll = lane % L.lpr;
   const int nthr = ncw * 32;
-  const uint32_t shfl_mask = 0xFFFFFFFFu;
   bool ok = true;
   uint32_t it = 0;
   RD rd;
-  float xr[RD::XR];
+  rd.init(L, seg, lane);
+  typename RD::XRegs xr;
   const int part = slot_part_bytes(L);
+  // x images are written by the preceding ximage_kernel (programmatic launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   for (int j = 0; j < njobs; ++j) {
     const Job J = prog.job(cta, j);
-    rd.init(L, seg, ll, J.x, xr);
+    load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
       if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout);
@@ -224,22 +280,21 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
       const uint8_t* stg = sp.stage + static_cast<size_t>(slot) * L.stage_bytes;
       const uint8_t* sca = stg + static_cast<size_t>(T) * L.row_bytes;
       float* red = sp.red + static_cast<size_t>(slot) * T * L.nseg * 2;
-      for (int step = grp; step * L.rpw < nr; step += L.ngrp) {
-        const int t = step * L.rpw + sub;
-        const bool have = t < nr;
-        const int tt = have ? t : 0;
-        float pa = have ? rd.dot(stg + tt * L.row_bytes, sca + tt * L.srow_bytes, xr) : 0.0f;
-        float pb = 0.0f;
-        if (prog.dual)
-          pb = have ? rd.dot(stg + part + tt * L.row_bytes, stg + part + static_cast<size_t>(T) * L.row_bytes + tt * L.srow_bytes, xr)
-                    : 0.0f;
-        for (int o = L.lpr >> 1; o > 0; o >>= 1) {
-          pa += __shfl_xor_sync(shfl_mask, pa, o);
-          if (prog.dual) pb += __shfl_xor_sync(shfl_mask, pb, o);
+      for (int bt = grp * RB; bt < nr; bt += L.ngrp * RB) {
+        float v[NV];
+#pragma unroll
+        for (int i = 0; i < RB; ++i) {
+          const int t = min(bt + i, nr - 1);
+          v[i] = rd.dot(stg + t * L.row_bytes, sca + t * L.srow_bytes, xr);
+          if constexpr (DUAL)
+            v[RB + i] = rd.dot(stg + part + t * L.row_bytes,
+                               stg + part + static_cast<size_t>(T) * L.row_bytes + t * L.srow_bytes, xr);
         }
-        if (ll == 0 && have) {
-          red[(t * L.nseg + seg) * 2] = pa;
-          red[(t * L.nseg + seg) * 2 + 1] = pb;
+        butterfly<NV>(v, lane);
+        if ((lane & (W - 1)) == 0) {
+          const int idx = lane / W;
+          const int t = bt + (idx % RB);
+          if (t < nr) red[(t * L.nseg + seg) * 2 + idx / RB] = v[0];
         }
       }
       __syncwarp();
@@ -249,7 +304,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
         float va = 0.0f, vb = 0.0f;
         for (int s2 = 0; s2 < L.nseg; ++s2) {
           va += red[(t * L.nseg + s2) * 2];
-          vb += red[(t * L.nseg + s2) * 2 + 1];
+          if constexpr (DUAL) vb += red[(t * L.nseg + s2) * 2 + 1];
         }
         prog.epilogue(cta, j, r0 + t, va, vb);
       }
@@ -263,17 +318,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
 // Plain GEMV: each CTA owns `rows_per_cta` consecutive rows.
 struct GemvProg {
   StageSource src;
-  const float* x;
+  const uint4* ximg;
   float* y;
   int rows;
   int rows_per_cta;
-  bool dual;
   unsigned* err;
   __device__ __forceinline__ int njobs(int) const { return 1; }
   __device__ __forceinline__ Job job(int cta, int) const {
     Job J;
     J.src = src;
-    J.x = x;
+    J.ximg = ximg;
     J.row_begin = cta * rows_per_cta;
     J.row_end = min(rows, J.row_begin + rows_per_cta);
     return J;

@@ -44,6 +44,9 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
 
 size_t pipe_smem_bytes(const RowLayoutHost& L);
 
+// Opts a kernel into large dynamic shared memory once per (kernel, device).
+int ensure_smem_attr_ptr(const void* kernel, int device, size_t bytes);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace objb

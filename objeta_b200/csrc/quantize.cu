@@ -194,8 +194,15 @@ __global__ void fp4_decode_split_kernel(const uint8_t* __restrict__ w, const uin
     // f8e8m0_to_f32 (deepseek.rs:831-850): 0 -> 2^-127, 255 -> +inf.
     const float sc = raw == 0 ? __uint_as_float(1u << 22)
                               : (raw == 255 ? __uint_as_float(0x7F800000u) : __uint_as_float(raw << 23));
-    out[r * cols + lo] = __fmul_rn(kFp4ParserTable[b & 0xFu], sc);
-    out[r * cols + lo + 1] = __fmul_rn(kFp4ParserTable[(b >> 4) & 0xFu], sc);
+    // 0 * inf (codes 0 / 8 with scale byte 255) is NaN; the reference decode
+    // runs on x86 hosts, whose SSE multiply returns the default NaN 0xFFC00000,
+    // so that exact pattern is written instead of the GPU's canonical NaN.
+    float v0 = __fmul_rn(kFp4ParserTable[b & 0xFu], sc);
+    float v1 = __fmul_rn(kFp4ParserTable[(b >> 4) & 0xFu], sc);
+    if (v0 != v0) v0 = __uint_as_float(0xFFC00000u);
+    if (v1 != v1) v1 = __uint_as_float(0xFFC00000u);
+    out[r * cols + lo] = v0;
+    out[r * cols + lo + 1] = v1;
   }
 }
 
