@@ -8,6 +8,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "objb_common.h"
 #include "objb_gemv.cuh"
@@ -102,9 +103,16 @@ int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int n
                   size_t img_stride_quads, cudaStream_t stream) {
   dev::RowLayout dl;
   std::memcpy(&dl, &L, sizeof(dl));
-  const int n = L.nseg * 32 * nvec;
-  const int grid = std::max(1, std::min((n + 127) / 128, 1024));
-  dev::ximage_kernel<RD><<<grid, 128, 0, stream>>>(dl, x, x_stride, nvec, img, img_stride_quads);
+  if constexpr (dev::IsDigitRD<RD>::value) {
+    const int warps = L.nseg * 32 * 2 * nvec;
+    const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
+    dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img,
+                                                                                 img_stride_quads);
+  } else {
+    const int n = L.nseg * 32 * RD::XRegs::kQuads * nvec;
+    const int grid = std::max(1, std::min((n + 255) / 256, 2048));
+    dev::ximage_f32_kernel<RD><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img, img_stride_quads);
+  }
   OBJB_CUDA(cudaGetLastError(), "launch x-image kernel");
   return OBJB_OK;
 }

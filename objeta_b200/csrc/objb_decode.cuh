@@ -89,112 +89,97 @@ struct Words {
 template <int FMT>
 struct Tile;
 
+// ------------------------------------------- integer formats: the digit image
+// Q4_0, Q5_0 and IQ3_0 form each block sum exactly in integers.  Every x of a
+// block is held as X = rint(x * 2^(20-E)) (2^E > max|x| of the block), split
+// into three signed 7-bit digits; a lane keeps, per block, 8 "groups" of four
+// elements x 3 digit words (one byte per element) plus the block's 2^(E-20)
+// and -off * sum X:  words (b*8 + g)*3 + k, 48 + b, 50 + b of a 13-quad image.
+// The row decode unpacks the codes of a group into four bytes (q in 0..31)
+// and dp4a-multiplies them with the digit words, so
+//   sum_l (q_l - off) x_l = (sum_l q_l X_l - off * sum_l X_l) * 2^(E-20)
+// with |sum_l q_l X_l| < 2^30.  The only roundings before the fp32
+// accumulation across blocks are that of X (<= 2^-21 of the block's largest
+// |x|) and one int -> f32 conversion.  Each format names, for group g and
+// byte j, the element of its block (elem) and its offset (kOffset).
+using DigitRegs = Words<13>;
+__device__ __forceinline__ int dg_word(int b, int g, int k) { return (b * 8 + g) * 3 + k; }
+
+// Block sum for one group set: 8 groups' code bytes against the digits.
+__device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const DigitRegs& xr, int b,
+                                             float scale) {
+  int q0 = 0, q1 = 0, q2 = 0;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const int a = static_cast<int>(qb[g]);
+    q0 = __dp4a(a, static_cast<int>(xr.w(dg_word(b, g, 0))), q0);
+    q1 = __dp4a(a, static_cast<int>(xr.w(dg_word(b, g, 1))), q1);
+    q2 = __dp4a(a, static_cast<int>(xr.w(dg_word(b, g, 2))), q2);
+  }
+  const int T = q0 + (q1 + q2 * 128) * 128 + static_cast<int>(xr.w(50 + b));
+  return __int2float_rn(T) * (scale * __uint_as_float(xr.w(48 + b)));
+}
+
+// Four bits (positions 0, 2, 4, 6 of hb) to the low bit of four bytes: the
+// product puts bit 2j at 8j; the other partial products land off the byte
+// boundaries and never carry into them.
+__device__ __forceinline__ uint32_t spread_even4(uint32_t hb) {
+  return ((hb & 0x55u) * 0x41041u) & 0x01010101u;
+}
+// 16 bits to the even bits of a word (bit i -> bit 2i).
+__device__ __forceinline__ uint32_t spread2_16(uint32_t v) {
+  v &= 0xFFFFu;
+  v = (v | (v << 8)) & 0x00FF00FFu;
+  v = (v | (v << 4)) & 0x0F0F0F0Fu;
+  v = (v | (v << 2)) & 0x33333333u;
+  v = (v | (v << 1)) & 0x55555555u;
+  return v;
+}
+
+// Nibble formats (Q4_0 / Q5_0) share the decode-word layout: in a tile the
+// eight decode words are m = [qs0[14], qs0[15], qs0[0], qs0[1]] (a byte
+// permute of the two words straddling block 0's scale) and the aligned quant
+// words; nibble position p of decode word u is element nib_elem(u, p) of the
+// tile, and group g = 2 * uu + h holds the low (h = 0) or high nibbles.
+__device__ __forceinline__ int nib_elem(int u, int p) {
+  if (u == 0) return p < 4 ? 28 + p : p - 4;
+  if (u < 4) return 4 + 8 * (u - 1) + p;
+  return 32 + 8 * (u - 4) + p;
+}
+
 // ---------------------------------------------------------------- Q4_0
 // Tile = 2 blocks = 36 bytes = 9 words:
 //   w0 = [s0 lo, s0 hi, qs0[0], qs0[1]]  w1..w3 = qs0[2..13]
 //   w4 = [qs0[14], qs0[15], s1 lo, s1 hi]  w5..w8 = qs1[0..15]
-// Byte j of qs holds element 2j (low nibble) and 2j+1 (high nibble).  The
-// eight "decode words" are m = [qs0[14], qs0[15], qs0[0], qs0[1]] (one byte
-// permute), w1..w3, w5..w8; nibble position p of decode word u is element
-// elem(u, p) of the tile.
-//
-// Block sums are exact integer dot products: each x of a block is held as
-// X = rint(x * 2^(20-E)) (2^E > max|x| of the block), split into three
-// signed 7-bit digits, and sum_l q_l X_l is formed with dp4a on the unpacked
-// nibbles (q in 0..15) against the digit bytes, then
-//   sum_l (q_l - 8) x_l = (sum_l q_l X_l - 8 sum_l X_l) * 2^(E-20).
-// The only rounding before the fp32 accumulation across blocks is that of X
-// (at most 2^-21 of the block's largest |x|) and one int -> f32 conversion.
+// Byte j of qs holds element 2j (low nibble) and 2j+1 (high nibble).
 template <>
 struct Tile<OBJB_Q4_0> {
   static constexpr int P = 2;
   static constexpr int BB = 18;
   static constexpr int TB = P * BB;
-
-  // Words 0..47: digit word (u, h, k) at u * 6 + h * 3 + k  ([decode word]
-  // [low/high nibble half][digit]); 48..49: 2^(E-20) per block (NaN for a
-  // non-finite block); 50..51: -8 * sum X per block.
-  using XRegs = Words<13>;
-  __device__ __forceinline__ static int dgi(int u, int h, int k) { return u * 6 + h * 3 + k; }
-
-  __device__ __forceinline__ static int elem(int u, int p) {
-    if (u == 0) return p < 4 ? 28 + p : p - 4;
-    if (u < 4) return 4 + 8 * (u - 1) + p;
-    return 32 + 8 * (u - 4) + p;
+  static constexpr int kOffset = 8;
+  using XRegs = DigitRegs;
+  __device__ __forceinline__ static int elem(int b, int g, int j) {
+    return nib_elem(4 * b + g / 2, 2 * j + (g & 1)) - 32 * b;
   }
 
-  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                XRegs& xr) {
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      float xv[32];
-      float m = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        xv[e] = active ? __ldg(x + col0 + 32 * b + e) : 0.0f;
-        m = fmaxf(m, fabsf(xv[e]));
-      }
-      int E = 0;
-      frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
-      int X[32];
-      int sx = 0;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        X[e] = __float2int_rn(ldexpf(xv[e], 20 - E));
-        sx += X[e];
-      }
-      xr.set(48 + b, __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000)));
-      xr.set(50 + b, static_cast<uint32_t>(-8 * sx));
-#pragma unroll
-      for (int uu = 0; uu < 4; ++uu) {
-        const int u = 4 * b + uu;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t pk[3] = {0u, 0u, 0u};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int v = X[elem(u, 2 * j + h) - 32 * b];
-            const int d0 = ((v + 64) & 127) - 64;
-            const int v1 = (v - d0) / 128;
-            const int d1 = ((v1 + 64) & 127) - 64;
-            const int d2 = (v1 - d1) / 128;
-            pk[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * j);
-            pk[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
-            pk[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * j);
-          }
-          xr.set(dgi(u, h, 0), pk[0]);
-          xr.set(dgi(u, h, 1), pk[1]);
-          xr.set(dgi(u, h, 2), pk[2]);
-        }
-      }
-    }
-  }
-
-  // t: 4-byte aligned pointer to the lane tile in shared memory.
   __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) w[i] = lds32(t + 4 * i);
-    const float s[2] = {f16_bits_to_f32(w[0]), f16_bits_to_f32(w[4] >> 16)};
     const uint32_t D[8] = {__byte_perm(w[0], w[4], 0x3254), w[1], w[2], w[3], w[5], w[6], w[7], w[8]};
+    const float s0 = f16_bits_to_f32(w[0]), s1 = f16_bits_to_f32(w[4] >> 16);
     float r = 0.0f;
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
-      int q0 = 0, q1 = 0, q2 = 0;
+      uint32_t qb[8];
 #pragma unroll
       for (int uu = 0; uu < 4; ++uu) {
-        const int u = 4 * b + uu;
-        const int lo = static_cast<int>(D[u] & 0x0F0F0F0Fu);
-        const int hi = static_cast<int>((D[u] >> 4) & 0x0F0F0F0Fu);
-        q0 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 0))), q0);
-        q1 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 1))), q1);
-        q2 = __dp4a(lo, static_cast<int>(xr.w(dgi(u, 0, 2))), q2);
-        q0 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 0))), q0);
-        q1 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 1))), q1);
-        q2 = __dp4a(hi, static_cast<int>(xr.w(dgi(u, 1, 2))), q2);
+        const uint32_t d = D[4 * b + uu];
+        qb[2 * uu] = d & 0x0F0F0F0Fu;
+        qb[2 * uu + 1] = (d >> 4) & 0x0F0F0F0Fu;
       }
-      const int T = q0 + (q1 + q2 * 128) * 128 + static_cast<int>(xr.w(50 + b));
-      r = fmaf(__int2float_rn(T), s[b] * __uint_as_float(xr.w(48 + b)), r);
+      r += digit_block(qb, xr, b, b ? s1 : s0);
     }
     return r;
   }
@@ -202,95 +187,92 @@ struct Tile<OBJB_Q4_0> {
 
 // ---------------------------------------------------------------- Q5_0
 // Block = [s (2)][qh (4)][qs (16)] (quant.rs:831-858); q = low | high << 4,
-// weight (q - 16) * s.  Tile = 2 blocks = 44 bytes = 11 words.
+// weight (q - 16) * s.  Tile = 2 blocks = 44 bytes = 11 words:
+//   w0 = [s0, qh0 b0 b1]  w1 = [qh0 b2 b3, qs0 b0 b1]  w2..w4 = qs0 b2..b13
+//   w5 = [qs0 b14 b15, s1]  w6 = qh1  w7..w10 = qs1
+// The decode words match Q4_0's element layout; the high bits of a decode
+// word's elements are the byte of qh starting at its first element (a funnel
+// shift for the merged word), spread onto bit 4 of the nibble bytes.
 template <>
 struct Tile<OBJB_Q5_0> {
   static constexpr int P = 2;
   static constexpr int BB = 22;
   static constexpr int TB = P * BB;
-  using XRegs = Words<16>;  // x of the tile as 32 float pairs
-
-  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                XRegs& xr) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      xr.set_f2(i, active ? make_float2(__ldg(x + col0 + 2 * i), __ldg(x + col0 + 2 * i + 1))
-                          : make_float2(0.f, 0.f));
+  static constexpr int kOffset = 16;
+  using XRegs = DigitRegs;
+  __device__ __forceinline__ static int elem(int b, int g, int j) {
+    return nib_elem(4 * b + g / 2, 2 * j + (g & 1)) - 32 * b;
   }
 
   __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[11];
 #pragma unroll
     for (int i = 0; i < 11; ++i) w[i] = lds32(t + 4 * i);
-    float total = 0.0f;
+    const uint32_t qh[2] = {__byte_perm(w[0], w[1], 0x5432), w[6]};
+    const uint32_t D[8] = {__byte_perm(w[1], w[5], 0x3254), w[2], w[3], w[4], w[7], w[8], w[9], w[10]};
+    const float s0 = f16_bits_to_f32(w[0]), s1 = f16_bits_to_f32(w[5] >> 16);
+    float r = 0.0f;
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
-      const int base = b * BB;
-      const float s = f16_bits_to_f32(byte_at(w, base) | (byte_at(w, base + 1) << 8));
-      const uint32_t qh = byte_at(w, base + 2) | (byte_at(w, base + 3) << 8) |
-                          (byte_at(w, base + 4) << 16) | (byte_at(w, base + 5) << 24);
-      float2 acc = make_float2(0.f, 0.f);
+      uint32_t qb[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const uint32_t by = byte_at(w, base + 6 + j);
-        const uint32_t q0 = (by & 0xFu) | (((qh >> (2 * j)) & 1u) << 4);
-        const uint32_t q1 = (by >> 4) | (((qh >> (2 * j + 1)) & 1u) << 4);
-        const float2 v = make_float2(qf(q0, 16.0f), qf(q1, 16.0f));
-        acc = __ffma2_rn(v, xr.f2(b * 16 + j), acc);
+      for (int uu = 0; uu < 4; ++uu) {
+        const uint32_t d = D[4 * b + uu];
+        // high bits of the 8 elements of this decode word, element order
+        const uint32_t hb = (b == 0 && uu == 0) ? __funnelshift_r(qh[0], qh[0], 28)
+                                                : (qh[b] >> (b == 0 ? 4 + 8 * (uu - 1) : 8 * uu));
+        qb[2 * uu] = (d & 0x0F0F0F0Fu) + (spread_even4(hb) << 4);
+        qb[2 * uu + 1] = ((d >> 4) & 0x0F0F0F0Fu) + (spread_even4(hb >> 1) << 4);
       }
-      total = fmaf(acc.x + acc.y, s, total);
+      r += digit_block(qb, xr, b, b ? s1 : s0);
     }
-    return total;
+    return r;
   }
 };
 
 // ---------------------------------------------------------------- IQ3_0
 // Block = [s (2)][2-bit lows (8)][1-bit highs (4)] (quant.rs:860-879);
-// q = low | high << 2, weight (q - 4) * s.  Tile = 2 blocks = 28 bytes.
+// q = low | high << 2, weight (q - 4) * s.  Tile = 2 blocks = 28 bytes:
+//   w0 = [s0, L0 b0 b1]  w1 = L0 b2..b5  w2 = [L0 b6 b7, H0 b0 b1]
+//   w3 = [H0 b2 b3, s1]  w4, w5 = L1  w6 = H1
+// A 32-bit word of lows holds 16 elements; (lw >> 2c) & 0x03030303 are
+// elements 4j + c.  The highs are first spread to even bits (element e at
+// bit 2e) so the same shift brings them next to their lows.  Group
+// g = 4 * hh + c (hh: which 16 elements).
 template <>
 struct Tile<OBJB_IQ3_0> {
   static constexpr int P = 2;
   static constexpr int BB = 14;
   static constexpr int TB = P * BB;
-  using XRegs = Words<16>;  // x of the tile as 32 float pairs
-
-  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int col0, bool active,
-                                                XRegs& xr) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-      xr.set_f2(i, active ? make_float2(__ldg(x + col0 + 2 * i), __ldg(x + col0 + 2 * i + 1))
-                          : make_float2(0.f, 0.f));
-  }
+  static constexpr int kOffset = 4;
+  using XRegs = DigitRegs;
+  __device__ __forceinline__ static int elem(int, int g, int j) { return 16 * (g / 4) + 4 * j + (g & 3); }
 
   __device__ __forceinline__ static float dot(const uint8_t* t, const XRegs& xr) {
     uint32_t w[7];
 #pragma unroll
     for (int i = 0; i < 7; ++i) w[i] = lds32(t + 4 * i);
-    float total = 0.0f;
+    const uint32_t L[2][2] = {{__byte_perm(w[0], w[1], 0x5432), __byte_perm(w[1], w[2], 0x5432)},
+                              {w[4], w[5]}};
+    const uint32_t H[2] = {__byte_perm(w[2], w[3], 0x5432), w[6]};
+    const float s0 = f16_bits_to_f32(w[0]), s1 = f16_bits_to_f32(w[3] >> 16);
+    float r = 0.0f;
 #pragma unroll
     for (int b = 0; b < 2; ++b) {
-      const int base = b * BB;
-      const float s = f16_bits_to_f32(byte_at(w, base) | (byte_at(w, base + 1) << 8));
-      uint32_t lo0 = 0, lo1 = 0, hi = 0;
+      uint32_t qb[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        lo0 |= byte_at(w, base + 2 + j) << (8 * j);
-        lo1 |= byte_at(w, base + 6 + j) << (8 * j);
-        hi |= byte_at(w, base + 10 + j) << (8 * j);
-      }
-      float2 acc = make_float2(0.f, 0.f);
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t h2 = spread2_16(H[b] >> (16 * hh));  // element e's high at bit 2e
 #pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        const uint32_t lw = e < 16 ? lo0 : lo1;
-        const int sh = 2 * (e & 15);
-        const uint32_t qa = ((lw >> sh) & 3u) | (((hi >> e) & 1u) << 2);
-        const uint32_t qb = ((lw >> (sh + 2)) & 3u) | (((hi >> (e + 1)) & 1u) << 2);
-        const float2 v = make_float2(qf(qa, 4.0f), qf(qb, 4.0f));
-        acc = __ffma2_rn(v, xr.f2(b * 16 + e / 2), acc);
+        for (int c = 0; c < 4; ++c) {
+          // high of element 4j + c sits at bit 8j + 2c; move it to bit 8j + 2
+          const uint32_t hc = c == 0 ? (h2 << 2) : (h2 >> (2 * c - 2));
+          qb[4 * hh + c] = ((L[b][hh] >> (2 * c)) & 0x03030303u) | (hc & 0x04040404u);
+        }
       }
-      total = fmaf(acc.x + acc.y, s, total);
+      r += digit_block(qb, xr, b, b ? s1 : s0);
     }
-    return total;
+    return r;
   }
 };
 

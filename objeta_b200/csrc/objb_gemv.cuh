@@ -70,29 +70,42 @@ struct RowDot {
   using XRegs = typename T::XRegs;
   int tile_off;  // byte offset of this lane's tile inside a row
   bool active;
-  __device__ __forceinline__ static void build(const RowLayout& L, int lt, const float* x, XRegs& xr) {
-    T::load_x(x, lt * T::P * 32, (lt * T::P) < L.nblocks, xr);
-  }
   __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
     const int lt = seg * 32 + lane;
     active = (lt * T::P) < L.nblocks;
     tile_off = lt * T::TB;
+  }
+  // First x column of quad q of tile lt (natural order tiles), -1 if idle.
+  __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
+    return (lt * T::P) < L.nblocks ? lt * T::P * 32 + 4 * q : -1;
   }
   __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t*, const XRegs& xr) const {
     return active ? T::dot(wrow + tile_off, xr) : 0.0f;
   }
 };
 
+template <class RD>
+struct IsDigitRD {
+  static constexpr bool value = false;
+  static constexpr int fmt = -1;
+};
+template <int FMT>
+struct IsDigitRD<RowDot<FMT>> {
+  static constexpr bool value = FMT != OBJB_FP4_E2M1;
+  static constexpr int fmt = FMT;
+};
+
 struct RowDotSplitFp4 {
   using XRegs = SplitFp4::XRegs;
   int b0, nblocks;
-  __device__ __forceinline__ static void build(const RowLayout& L, int lt, const float* x, XRegs& xr) {
-    const int seg = lt / 32, lane = lt % 32;
-    SplitFp4::load_x(x, seg * 32 * SplitFp4::P + lane, 32, L.nblocks, xr);
-  }
   __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
     b0 = seg * 32 * SplitFp4::P + lane;
     nblocks = L.nblocks;
+  }
+  __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
+    const int seg = lt / 32, lane = lt % 32;
+    const int b = seg * 32 * SplitFp4::P + lane + (q / 8) * 32;
+    return b < L.nblocks ? b * 32 + 4 * (q % 8) : -1;
   }
   __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t* srow, const XRegs& xr) const {
     return SplitFp4::dot(wrow, srow, b0, 32, nblocks, xr);
@@ -105,23 +118,94 @@ __device__ __forceinline__ void load_ximage(const uint4* __restrict__ img, int n
   for (int q = 0; q < XR::kQuads; ++q) xr.q[q] = __ldg(img + q * ntp + lt);
 }
 
-// Builds the x images of `nvec` vectors (x + v * x_stride) for layout L.
-// Starts dependents immediately: the consumer kernel is launched with
-// programmatic stream serialization and waits (griddepcontrol.wait) before
-// it reads the image, so its launch and first weight copies overlap this.
+// x-image builders.  The image of vector v is quads img[v * img_stride_quads +
+// q * ntp + lt] (ntp = nseg * 32 lane tiles).  Both kernels start their
+// dependents immediately: the consumer kernel is launched with programmatic
+// stream serialization and waits (griddepcontrol.wait) before reading the
+// image, so its launch and first weight copies overlap the build.
+//
+// Float tiles: one thread per (vector, tile, quad); quad q of a tile is four
+// consecutive x values whose first column RD::quad_col gives (-1: zeros).
 template <class RD>
-__global__ void __launch_bounds__(128) ximage_kernel(const RowLayout L, const float* __restrict__ x,
-                                                     size_t x_stride, int nvec, uint4* __restrict__ img,
-                                                     size_t img_stride_quads) {
+__global__ void __launch_bounds__(256) ximage_f32_kernel(const RowLayout L, const float* __restrict__ x,
+                                                         size_t x_stride, int nvec, uint4* __restrict__ img,
+                                                         size_t img_stride_quads) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  constexpr int NQ = RD::XRegs::kQuads;
   const int ntp = L.nseg * 32;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < ntp * nvec; idx += gridDim.x * blockDim.x) {
-    const int v = idx / ntp, lt = idx % ntp;
-    typename RD::XRegs xr;
-    RD::build(L, lt, x + v * x_stride, xr);
-    uint4* out = img + v * img_stride_quads;
+  const int total = nvec * ntp * NQ;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int v = idx / (ntp * NQ);
+    const int r = idx % (ntp * NQ);
+    const int q = r / ntp, lt = r % ntp;
+    const int c = RD::quad_col(L, lt, q);
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c >= 0) {
+      const float* src = x + v * x_stride + c;
+      f = make_float4(__ldg(src), __ldg(src + 1), __ldg(src + 2), __ldg(src + 3));
+    }
+    img[v * img_stride_quads + static_cast<size_t>(q) * ntp + lt] =
+        make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+  }
+}
+
+// Digit images (Q4_0 / Q5_0 / IQ3_0): one warp per 32-value block.  Lane e
+// holds x_e; the warp forms the block's exponent, X_e = rint(x_e * 2^(20-E)),
+// its three signed 7-bit digits and sum X; lanes 0..23 then assemble the 24
+// digit words of the block (group g, digit k -> word (b*8 + g)*3 + k, byte j
+// = element Tile::elem(b, g, j)) and lanes 24 / 25 the block's 2^(E-20) and
+// -offset * sum X.
+template <int FMT>
+__global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, const float* __restrict__ x,
+                                                            size_t x_stride, int nvec, uint4* __restrict__ img,
+                                                            size_t img_stride_quads) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  using T = Tile<FMT>;
+  const int ntp = L.nseg * 32;
+  const int nb_img = ntp * T::P;  // blocks covered by the image (incl. idle lanes)
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb_img; wi += warps) {
+    const int v = wi / nb_img, gb = wi % nb_img;
+    const float xe = gb < L.nblocks ? __ldg(x + v * x_stride + gb * 32 + lane) : 0.0f;
+    float m = fabsf(xe);
 #pragma unroll
-    for (int q = 0; q < RD::XRegs::kQuads; ++q) out[q * ntp + lt] = xr.q[q];
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    int E = 0;
+    frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
+    const int X = __float2int_rn(ldexpf(xe, 20 - E));
+    const int d0 = ((X + 64) & 127) - 64;
+    const int X1 = (X - d0) / 128;
+    const int d1 = ((X1 + 64) & 127) - 64;
+    const int d2 = (X1 - d1) / 128;
+    const int sx = __reduce_add_sync(0xFFFFFFFFu, X);
+    const int lt = gb / T::P, b = gb % T::P;
+    const int t = lane < 24 ? lane : 0;  // word t = g * 3 + k of this block
+    const int g = t / 3, k = t % 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int el = T::elem(b, g, j);
+      const int s0 = __shfl_sync(0xFFFFFFFFu, d0, el);
+      const int s1 = __shfl_sync(0xFFFFFFFFu, d1, el);
+      const int s2 = __shfl_sync(0xFFFFFFFFu, d2, el);
+      const int dk = k == 0 ? s0 : (k == 1 ? s1 : s2);
+      word |= (static_cast<uint32_t>(dk) & 0xFFu) << (8 * j);
+    }
+    uint32_t* out = reinterpret_cast<uint32_t*>(img + v * img_stride_quads);
+    int widx = -1;
+    uint32_t val = 0;
+    if (lane < 24) {
+      widx = dg_word(b, g, k);
+      val = word;
+    } else if (lane == 24) {
+      widx = 48 + b;
+      val = __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000));
+    } else if (lane == 25) {
+      widx = 50 + b;
+      val = static_cast<uint32_t>(-T::kOffset * sx);
+    }
+    if (widx >= 0) out[(static_cast<size_t>(widx >> 2) * ntp + lt) * 4 + (widx & 3)] = val;
   }
 }
 
