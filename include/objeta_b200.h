@@ -172,6 +172,229 @@ int objb_fp4_decode_split_device(const void *d_weight, const void *d_scale,
                                  size_t rows, size_t cols, float *d_out,
                                  objb_stream_t stream);
 
+/* ------------------------------------------------ selected-expert MoE */
+
+/* objb_moe_layer.flags */
+enum {
+  /* Some expert tensor pointer is not 16-byte aligned (or a row is not a
+   * multiple of 16 bytes): run the generic path instead of the bulk-copy
+   * pipeline. */
+  OBJB_MOE_UNALIGNED = 1
+};
+
+/* One MoE layer resident on the device.  The expert tensors keep the
+ * reference's layouts: ExpertWeights (moe.rs:13-18) -- Q4_0 (or Q5_0 / IQ3_0 /
+ * interleaved FP4) gate / up [intermediate x hidden] and down
+ * [out_dim x intermediate] -- or DeepSeekFp4ExpertWeights (moe.rs:27-35),
+ * fmt = OBJB_FP4_E2M1 with the three scale tables set: split weight
+ * [rows, cols/2] + E8M0 scale [rows, cols/32].  d_gate / d_up / d_down (and
+ * the scale tables) are DEVICE arrays of num_experts device pointers. */
+typedef struct {
+  int fmt;
+  uint32_t flags;
+  size_t hidden, intermediate, out_dim, num_experts;
+  const void *const *d_gate;
+  const void *const *d_up;
+  const void *const *d_down;
+  const void *const *d_gate_scale;
+  const void *const *d_up_scale;
+  const void *const *d_down_scale;
+} objb_moe_layer;
+
+/* cpu_router (crates/objeta-cuda/src/bin/deepseek_single_layer_moe.rs:
+ * 720-740) on the device: softmax of the logits, the top_k of a stable
+ * descending sort (ties keep the lower expert index), weights = the kept
+ * probabilities, divided by their sum when renormalize != 0. */
+int objb_router_topk_device(const float *d_logits, size_t num_experts, size_t top_k,
+                            int renormalize, int32_t *d_ids, float *d_weights,
+                            objb_stream_t stream);
+
+/* Bytes of device scratch objb_moe_selected_device uses for top_k experts
+ * (it takes them from a per-(device, stream) workspace allocated on first
+ * use, so make the first call on a stream outside graph capture). */
+int objb_moe_scratch_bytes(const objb_moe_layer *layer, size_t top_k, size_t *bytes);
+
+/* The selected-expert MoE FFN of MoeExecutor::execute_selected_moe_cuda /
+ * execute_selected_moe_native_fp4_cuda (moe.rs:352-751, 816-1280) for one
+ * token, with the selection (d_ids, d_weights: top_k entries) and x already
+ * on the device: out = sum_k w_k * down_k(silu(gate_k x) * up_k x), summed in
+ * selection order.  swiglu_limit > 0 clamps as silu_mul does (moe.cu:2-22).
+ * Two pipelined launches (gate+up with SwiGLU fused; down with the weighted
+ * combine fused) plus two small x-image builds; asynchronous on `stream`. */
+int objb_moe_selected_device(const objb_moe_layer *layer, const int32_t *d_ids,
+                             const float *d_weights, size_t top_k, const float *d_x,
+                             float *d_out, float swiglu_limit, objb_stream_t stream);
+
+/* Router + selected-expert MoE in one call: logits -> (d_ids, d_weights) ->
+ * out.  d_ids / d_weights receive the selection. */
+int objb_moe_forward_device(const objb_moe_layer *layer, const float *d_logits,
+                            size_t top_k, int renormalize, int32_t *d_ids, float *d_weights,
+                            const float *d_x, float *d_out, float swiglu_limit,
+                            objb_stream_t stream);
+
+/* ------------------------------------------------------- expert cache */
+
+/* ExpertCacheKey (moe.rs:56-62): tensor_kind = OBJB_KIND_*, quant_format =
+ * OBJB_Q4_0 ... */
+typedef struct {
+  size_t layer_id;
+  size_t expert_id;
+  int32_t tensor_kind;
+  int32_t quant_format;
+} objb_expert_cache_key;
+
+/* The public counters of CudaExpertCache (moe.rs:70-89), same names, plus the
+ * number of tensors that did not fit the cache's slab and were allocated on
+ * their own. */
+typedef struct {
+  size_t capacity_bytes, resident_bytes, pinned_bytes;
+  size_t hit_count, miss_count, eviction_count;
+  int32_t bypass_oversized_experts;
+  size_t cache_insert_attempt_count, cache_insert_accept_count, cache_insert_bypass_count;
+  size_t oversized_tensor_bypass_count, oversized_expert_bypass_count, self_eviction_risk_count;
+  size_t overflow_allocations;
+} objb_expert_cache_stats;
+
+typedef struct objb_expert_cache objb_expert_cache;
+
+/* CudaExpertCache::new (moe.rs:92-111): a byte-capacity LRU cache of expert
+ * tensors resident on `device`. */
+int objb_expert_cache_new(int device, size_t capacity_bytes, objb_expert_cache **out);
+void objb_expert_cache_free(objb_expert_cache *cache);
+
+/* get (moe.rs:113-122): on a hit counts it, moves the key to most-recent
+ * and returns the device pointer; on a miss counts it and returns NULL. */
+int objb_expert_cache_get(objb_expert_cache *cache, const objb_expert_cache_key *key,
+                          const void **d_ptr);
+
+/* insert (moe.rs:124-154): uploads `bytes` from host_src and makes it
+ * resident (evicting least-recent non-pinned tensors until it fits), or, when
+ * bytes > capacity, counts an oversized bypass and returns a buffer that is
+ * not cached (*resident = 0), valid until the next release point.  The upload
+ * runs on the cache's side stream; `stream` is made to wait for it. */
+int objb_expert_cache_insert(objb_expert_cache *cache, const objb_expert_cache_key *key,
+                             const void *host_src, size_t bytes, objb_stream_t stream,
+                             const void **d_ptr, int *resident);
+
+/* The README's get_or_insert (README.md:121-124): get, and on a miss insert;
+ * counters move exactly as the executor's inline get/insert (moe.rs:508-518). */
+int objb_expert_cache_get_or_insert(objb_expert_cache *cache, const objb_expert_cache_key *key,
+                                    const void *host_src, size_t bytes, objb_stream_t stream,
+                                    const void **d_ptr, int *hit);
+
+/* touch / evict_lru / pin / insert_pinned / clear / reset_counters
+ * (moe.rs:156-226). evict_lru reports the evicted key in *evicted. */
+int objb_expert_cache_touch(objb_expert_cache *cache, const objb_expert_cache_key *key);
+int objb_expert_cache_evict_lru(objb_expert_cache *cache, objb_expert_cache_key *evicted, int *found);
+int objb_expert_cache_pin(objb_expert_cache *cache, const objb_expert_cache_key *key);
+int objb_expert_cache_insert_pinned(objb_expert_cache *cache, const objb_expert_cache_key *key,
+                                    const void *host_src, size_t bytes, objb_stream_t stream,
+                                    const void **d_ptr);
+int objb_expert_cache_clear(objb_expert_cache *cache);
+int objb_expert_cache_reset_counters(objb_expert_cache *cache);
+
+/* The public fields of the reference struct. */
+int objb_expert_cache_stats_get(objb_expert_cache *cache, objb_expert_cache_stats *out);
+int objb_expert_cache_set_bypass_oversized_experts(objb_expert_cache *cache, int bypass);
+/* Executor-side admission counters (moe.rs:483-494, the executor bumps the
+ * cache's public fields directly in the reference). which: 0 =
+ * oversized_expert_bypass, 1 = self_eviction_risk, 2 = insert attempt +
+ * bypass (one bypassed tensor of a bypassed expert). */
+int objb_expert_cache_count(objb_expert_cache *cache, int which);
+
+/* Membership and LRU order (least recent first), for inspection. */
+int objb_expert_cache_contains(objb_expert_cache *cache, const objb_expert_cache_key *key, int *found);
+int objb_expert_cache_lru_keys(objb_expert_cache *cache, objb_expert_cache_key *out, size_t cap,
+                               size_t *n);
+
+/* Release point: every pointer handed out so far has had all of its reads
+ * enqueued on `stream`.  Slots evicted before this call become reusable once
+ * `stream` reaches this point, and bypass buffers are freed in stream order.
+ * (No reference counterpart: the reference keeps evicted buffers alive with
+ * Arc reference counts.) */
+int objb_expert_cache_release(objb_expert_cache *cache, objb_stream_t stream);
+
+/* --------------------------------------------------------- MoeExecutor */
+
+/* ExpertWeights (moe.rs:13-18): host slices of one expert. */
+typedef struct {
+  const uint8_t *w_gate;
+  size_t w_gate_len;
+  const uint8_t *w_up;
+  size_t w_up_len;
+  const uint8_t *w_down;
+  size_t w_down_len;
+} objb_expert_weights;
+
+/* DeepSeekFp4ExpertWeights (moe.rs:27-35). */
+typedef struct {
+  const uint8_t *gate_weight;
+  size_t gate_weight_len;
+  const uint8_t *gate_scale;
+  size_t gate_scale_len;
+  const uint8_t *up_weight;
+  size_t up_weight_len;
+  const uint8_t *up_scale;
+  size_t up_scale_len;
+  const uint8_t *down_weight;
+  size_t down_weight_len;
+  const uint8_t *down_scale;
+  size_t down_scale_len;
+} objb_fp4_expert_weights;
+
+/* MoeTelemetry (moe.rs:236-276), same fields (bytes_by_tensor_kind flattened
+ * into bytes_gate / bytes_up / bytes_down). */
+typedef struct {
+  size_t selected_expert_count;
+  size_t logical_expert_bytes_requested;
+  size_t actual_expert_bytes_loaded;
+  size_t resident_cache_bytes_reused;
+  size_t weight_bytes_loaded, weight_bytes_reused, scale_bytes_loaded, scale_bytes_reused;
+  size_t resident_cache_resident_bytes, resident_cache_capacity_bytes;
+  size_t resident_cache_hit_count, resident_cache_miss_count, resident_cache_eviction_count;
+  size_t resident_cache_insert_attempt_count, resident_cache_insert_accept_count;
+  size_t resident_cache_insert_bypass_count, resident_cache_oversized_tensor_bypass_count;
+  size_t resident_cache_oversized_expert_bypass_count, resident_cache_self_eviction_risk_count;
+  size_t dequantized_scratch_bytes;
+  float h2d_ms, gate_up_qgemv_ms, activation_ms, down_qgemv_ms, accum_ms, unaccounted_ms, total_ms,
+      shared_expert_ms;
+  size_t bytes_gate, bytes_up, bytes_down;
+  size_t bytes_per_expert, selected_working_set_bytes;
+  size_t routed_fp4_bytes_loaded, routed_fp4_bytes_reused, shared_fp8_bytes_loaded, shared_fp8_bytes_reused;
+  size_t total_logical_bytes, total_loaded_bytes, total_reused_bytes;
+} objb_moe_telemetry;
+
+typedef struct objb_moe_executor objb_moe_executor;
+
+/* MoeExecutor::new / compile (moe.rs:292-307). */
+int objb_moe_executor_new(int device, objb_moe_executor **out);
+void objb_moe_executor_free(objb_moe_executor *ex);
+int objb_moe_executor_compile(objb_moe_executor *ex);
+
+/* MoeExecutor::execute_selected_moe_cuda (moe.rs:352-751): host experts,
+ * host selection (expert index, weight) in order, host x; writes out[out_dim]
+ * and the telemetry.  fmt is OBJB_Q4_0 for the reference path (Q5_0 / IQ3_0
+ * run the same way).  With a cache, tensors are looked up / uploaded / evicted
+ * with the reference's counters and byte accounting; without one every tensor
+ * is uploaded for this call.  Fails with InvalidInput on the reference's
+ * validation errors and Internal if the byte invariant logical == loaded +
+ * reused does not hold. */
+int objb_moe_execute_selected(objb_moe_executor *ex, objb_stream_t stream, int fmt,
+                              const objb_expert_weights *experts, size_t num_experts,
+                              const int64_t *selected_ids, const float *selected_weights,
+                              size_t num_selected, const float *x, size_t x_len, size_t hidden,
+                              size_t intermediate, size_t out_dim, size_t layer_id,
+                              objb_expert_cache *cache, float *out, objb_moe_telemetry *telemetry);
+
+/* MoeExecutor::execute_selected_moe_native_fp4_cuda (moe.rs:816-1280). */
+int objb_moe_execute_selected_native_fp4(objb_moe_executor *ex, objb_stream_t stream,
+                                         const objb_fp4_expert_weights *experts, size_t num_experts,
+                                         const int64_t *selected_ids, const float *selected_weights,
+                                         size_t num_selected, const float *x, size_t x_len,
+                                         size_t hidden, size_t intermediate, size_t out_dim,
+                                         size_t layer_id, objb_expert_cache *cache, float *out,
+                                         objb_moe_telemetry *telemetry);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,8 +13,36 @@
 #include "objb_common.h"
 #include "objb_gemv.cuh"
 #include "objb_launch.h"
+#include "objb_host_launch.cuh"
 
 namespace objb {
+namespace dev {
+
+// Split-layout FP4 fallback (any alignment).
+__global__ void __launch_bounds__(256) gemv_fp4_split_fallback_kernel(
+    const uint8_t* __restrict__ w, const uint8_t* __restrict__ s, const float* __restrict__ x,
+    float* __restrict__ y, int rows, int cols) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nb = cols / 32;
+  const uint8_t* rw = w + static_cast<size_t>(row) * (cols / 2);
+  const uint8_t* rs = s + static_cast<size_t>(row) * nb;
+  float acc = 0.0f;
+  for (int b = lane; b < nb; b += 32) {
+    float a = 0.0f;
+    for (int j = 0; j < 16; ++j) {
+      const float2 v = e2m1x2_to_float2(rw[b * 16 + j]);
+      a = fmaf(v.x, __ldg(x + b * 32 + 2 * j), a);
+      a = fmaf(v.y, __ldg(x + b * 32 + 2 * j + 1), a);
+    }
+    acc += a * e8m0_to_f32(rs[b]);
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+  if (lane == 0) y[row] = acc;
+}
+
+}  // namespace dev
 
 static_assert(sizeof(RowLayoutHost) == sizeof(dev::RowLayout), "layout mirror mismatch");
 
@@ -84,60 +112,6 @@ int ensure_smem_attr_ptr(const void* kernel, int device, size_t bytes) {
                                  static_cast<int>(want)),
             "opt kernel into large shared memory");
   done[key] = want;
-  return OBJB_OK;
-}
-
-namespace {
-
-template <class K>
-int ensure_smem_attr(K kernel, int device, size_t bytes) {
-  return ensure_smem_attr_ptr(reinterpret_cast<const void*>(kernel), device, bytes);
-}
-
-}  // namespace
-
-// Launches the x-image prep kernel for `nvec` vectors into `img`, then lets
-// the caller launch the consumer kernel with programmatic serialization.
-template <class RD>
-int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int nvec, uint4* img,
-                  size_t img_stride_quads, cudaStream_t stream) {
-  dev::RowLayout dl;
-  std::memcpy(&dl, &L, sizeof(dl));
-  if constexpr (dev::IsDigitRD<RD>::value) {
-    const int warps = L.nseg * 32 * 2 * nvec;
-    const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
-    dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img,
-                                                                                 img_stride_quads);
-  } else {
-    const int n = L.nseg * 32 * RD::XRegs::kQuads * nvec;
-    const int grid = std::max(1, std::min((n + 255) / 256, 2048));
-    dev::ximage_f32_kernel<RD><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img, img_stride_quads);
-  }
-  OBJB_CUDA(cudaGetLastError(), "launch x-image kernel");
-  return OBJB_OK;
-}
-
-template <class RD>
-size_t ximage_quads(const RowLayoutHost& L) {
-  return static_cast<size_t>(RD::XRegs::kQuads) * L.nseg * 32;
-}
-
-// Launches `kernel` with programmatic stream serialization (it may start while
-// the previous kernel in the stream, the x-image prep, is still running).
-template <class... KArgs, class... Args>
-int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cudaStream_t stream,
-               Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  OBJB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...), "launch pipelined kernel");
   return OBJB_OK;
 }
 

@@ -1,0 +1,368 @@
+// moe.cu -- the selected-expert MoE layer on the device: router, fused
+// gate/up + SwiGLU, fused down + weighted combine, and the C ABI for it.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "objb_common.h"
+#include "objb_host_launch.cuh"
+#include "objb_moe.cuh"
+#include "objb_moe_launch.h"
+
+namespace objb {
+namespace dev {
+
+// ---- generic path (any shape / alignment): one warp per (selected expert,
+// row); blocks read straight from global memory.
+
+// Block dot of the split FP4 layout (weight [rows, cols/2], scale [rows, cols/32]).
+__device__ __forceinline__ float split_block_dot_global(const uint8_t* __restrict__ wrow,
+                                                        const uint8_t* __restrict__ srow, int b,
+                                                        const float* __restrict__ x32) {
+  float a = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float2 v = e2m1x2_to_float2(wrow[b * 16 + j]);
+    a = fmaf(v.x, __ldg(x32 + 2 * j), a);
+    a = fmaf(v.y, __ldg(x32 + 2 * j + 1), a);
+  }
+  return a * e8m0_to_f32(srow[b]);
+}
+
+template <int FMT, bool SPLIT>
+__device__ __forceinline__ float row_dot_global(const uint8_t* w, const uint8_t* s, int row, int cols,
+                                                const float* x, int lane) {
+  const int nb = cols / 32;
+  float acc = 0.0f;
+  if constexpr (SPLIT) {
+    const uint8_t* rw = w + static_cast<size_t>(row) * (cols / 2);
+    const uint8_t* rs = s + static_cast<size_t>(row) * nb;
+    for (int b = lane; b < nb; b += 32) acc += split_block_dot_global(rw, rs, b, x + b * 32);
+  } else {
+    constexpr int BB = FMT == OBJB_Q4_0 ? 18 : FMT == OBJB_Q5_0 ? 22 : FMT == OBJB_IQ3_0 ? 14 : 17;
+    const uint8_t* rw = w + static_cast<size_t>(row) * nb * BB;
+    for (int b = lane; b < nb; b += 32) acc += block_dot_global<FMT>(rw + static_cast<size_t>(b) * BB, x + b * 32);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+  return acc;
+}
+
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(256) moe_generic_gateup_kernel(ExpertTables t, const int32_t* ids, int K, int I,
+                                                                 int H, const float* __restrict__ x,
+                                                                 float* __restrict__ act, float limit,
+                                                                 unsigned* err) {
+  const int wi = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wi >= K * I) return;
+  const int k = wi / I, row = wi % I;
+  const int e = checked_expert(ids, k, t.num_experts, err);
+  const int lane = threadIdx.x & 31;
+  const float g = row_dot_global<FMT, SPLIT>(t.gate[e], SPLIT ? t.gate_scale[e] : nullptr, row, H, x, lane);
+  const float u = row_dot_global<FMT, SPLIT>(t.up[e], SPLIT ? t.up_scale[e] : nullptr, row, H, x, lane);
+  if (lane == 0) act[static_cast<size_t>(k) * I + row] = swiglu(g, u, limit);
+}
+
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(256) moe_generic_down_kernel(ExpertTables t, const int32_t* ids,
+                                                               const float* __restrict__ weights, int K, int I,
+                                                               int O, const float* __restrict__ act,
+                                                               float* __restrict__ out, unsigned* err) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= O) return;
+  const int lane = threadIdx.x & 31;
+  float acc = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    const int e = checked_expert(ids, k, t.num_experts, err);
+    const float d = row_dot_global<FMT, SPLIT>(t.down[e], SPLIT ? t.down_scale[e] : nullptr, row, I,
+                                               act + static_cast<size_t>(k) * I, lane);
+    acc = __fadd_rn(acc, __fmul_rn(weights[k], d));
+  }
+  if (lane == 0) out[row] = acc;
+}
+
+}  // namespace dev
+
+namespace {
+
+struct MoeShape {
+  int H, I, O, E, K;
+};
+
+dev::ExpertTables tables_of(const objb_moe_layer& l) {
+  dev::ExpertTables t;
+  t.gate = reinterpret_cast<const uint8_t* const*>(l.d_gate);
+  t.up = reinterpret_cast<const uint8_t* const*>(l.d_up);
+  t.down = reinterpret_cast<const uint8_t* const*>(l.d_down);
+  t.gate_scale = reinterpret_cast<const uint8_t* const*>(l.d_gate_scale);
+  t.up_scale = reinterpret_cast<const uint8_t* const*>(l.d_up_scale);
+  t.down_scale = reinterpret_cast<const uint8_t* const*>(l.d_down_scale);
+  t.num_experts = static_cast<int>(l.num_experts);
+  return t;
+}
+
+// Row byte sizes of one matrix with `cols` columns.
+void row_bytes(int fmt, bool split, int cols, int* rb, int* srb) {
+  if (split) {
+    *rb = cols / 2;
+    *srb = cols / 32;
+  } else {
+    *rb = cols / 32 * block_bytes(fmt);
+    *srb = 0;
+  }
+}
+
+template <class RD>
+struct MoePlan {
+  bool fast = false;
+  RowLayoutHost lg, ld;
+  size_t act_bytes = 0, imgx_quads = 0, imga_quads = 0;
+  size_t scratch_bytes() const {
+    return fast ? act_bytes + (imgx_quads + imga_quads) * 16 + 256 : act_bytes;
+  }
+};
+
+template <class RD>
+MoePlan<RD> plan_moe(const MoeShape& s, int fmt, bool split, bool aligned) {
+  MoePlan<RD> p;
+  p.act_bytes = (static_cast<size_t>(s.K) * s.I * 4 + 255) / 256 * 256;
+  int rbh, srbh, rbi, srbi;
+  row_bytes(fmt, split, s.H, &rbh, &srbh);
+  row_bytes(fmt, split, s.I, &rbi, &srbi);
+  const int P = 2;
+  const bool blocks_ok = split || ((s.H / 32) % P == 0 && (s.I / 32) % P == 0);
+  p.fast = aligned && blocks_ok &&
+           plan_rows(s.I, s.H, rbh, srbh, P, true, dev::kMaxConsumerWarps, &p.lg) &&
+           plan_rows(s.O, s.I, rbi, srbi, P, false, dev::kMaxConsumerWarps, &p.ld);
+  if (p.fast) {
+    p.imgx_quads = ximage_quads<RD>(p.lg);
+    p.imga_quads = ximage_quads<RD>(p.ld);
+    p.imga_quads *= 1;  // per vector; K vectors below
+  }
+  return p;
+}
+
+template <class RD, int FMT, bool SPLIT>
+int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, const float* weights,
+            const float* x, float* out, float limit, cudaStream_t stream, void* scratch, size_t scratch_bytes,
+            bool aligned, cudaEvent_t mid) {
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  unsigned* err = nullptr;
+  OBJB_TRY(device_error_word(device, &err));
+  MoePlan<RD> p = plan_moe<RD>(s, FMT, SPLIT, aligned);
+  const size_t need = p.fast ? p.act_bytes + (p.imgx_quads + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
+  if (scratch_bytes < need)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run selected-expert MoE",
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(need));
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  float* act = reinterpret_cast<float*>(sc);
+  const dev::ExpertTables t = tables_of(l);
+  if (!p.fast) {
+    const int g1 = (s.K * s.I + 7) / 8;
+    dev::moe_generic_gateup_kernel<FMT, SPLIT><<<g1, 256, 0, stream>>>(t, ids, s.K, s.I, s.H, x, act, limit, err);
+    OBJB_CUDA(cudaGetLastError(), "launch generic gate/up kernel");
+    if (mid) OBJB_CUDA(cudaEventRecord(mid, stream), "record gate/up end");
+    dev::moe_generic_down_kernel<FMT, SPLIT><<<(s.O + 7) / 8, 256, 0, stream>>>(t, ids, weights, s.K, s.I, s.O, act,
+                                                                               out, err);
+    OBJB_CUDA(cudaGetLastError(), "launch generic down kernel");
+    return OBJB_OK;
+  }
+  uint4* imgx = reinterpret_cast<uint4*>(sc + p.act_bytes);
+  uint4* imga = imgx + p.imgx_quads;
+  // gate/up
+  OBJB_TRY(launch_ximage<RD>(p.lg, x, 0, 1, imgx, 0, stream));
+  {
+    const int total = s.K * s.I;
+    const int T = p.lg.tstage;
+    int R = (total + props.sm_count - 1) / props.sm_count;
+    R = (R + T - 1) / T * T;
+    const int grid = (total + R - 1) / R;
+    dev::GateUpProg prog;
+    prog.t = t;
+    prog.ids = ids;
+    prog.ximg = imgx;
+    prog.act = act;
+    prog.K = s.K;
+    prog.I = s.I;
+    prog.rows_per_cta = R;
+    prog.swiglu_limit = limit;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(p.lg);
+    auto kernel = dev::pipe_kernel<RD, dev::GateUpProg, true>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.lg, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  if (mid) OBJB_CUDA(cudaEventRecord(mid, stream), "record gate/up end");
+  // down + combine
+  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), s.K, imga, p.imga_quads, stream));
+  {
+    const int T = p.ld.tstage;
+    int R = (s.O + props.sm_count - 1) / props.sm_count;
+    R = (R + T - 1) / T * T;
+    const int grid = (s.O + R - 1) / R;
+    dev::DownProg prog;
+    prog.t = t;
+    prog.ids = ids;
+    prog.weights = weights;
+    prog.ximg = imga;
+    prog.img_stride = p.imga_quads;
+    prog.out = out;
+    prog.K = s.K;
+    prog.O = s.O;
+    prog.rows_per_cta = R;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(p.ld);
+    auto kernel = dev::pipe_kernel<RD, dev::DownProg, false>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.ld, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (p.ld.nseg * p.ld.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  return OBJB_OK;
+}
+
+int validate_layer(const objb_moe_layer* l, size_t top_k, MoeShape* s, bool* split) {
+  if (!l) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "null layer descriptor");
+  if (!valid_format(l->fmt))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "unknown QuantFormat ordinal " + std::to_string(l->fmt));
+  if (l->hidden % 32 || l->intermediate % 32)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer",
+                     "hidden " + std::to_string(l->hidden) + " and intermediate " + std::to_string(l->intermediate) +
+                         " must be multiples of block_size 32");
+  if (!l->d_gate || !l->d_up || !l->d_down)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "null expert pointer table");
+  *split = l->fmt == OBJB_FP4_E2M1 && l->d_gate_scale && l->d_up_scale && l->d_down_scale;
+  if (l->fmt == OBJB_FP4_E2M1 && !*split && (l->d_gate_scale || l->d_up_scale || l->d_down_scale))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "split FP4 needs all three scale tables");
+  if (top_k == 0 || top_k > 1024)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "top_k must be in 1..1024");
+  if (l->num_experts == 0 || l->num_experts > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "num_experts must be in 1..2^20");
+  if (l->hidden > (1u << 20) || l->intermediate > (1u << 20) || l->out_dim > (1u << 24) || l->out_dim == 0)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "shape exceeds the supported range");
+  if (static_cast<size_t>(top_k) * l->intermediate > (1u << 30))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "top_k * intermediate too large");
+  s->H = static_cast<int>(l->hidden);
+  s->I = static_cast<int>(l->intermediate);
+  s->O = static_cast<int>(l->out_dim);
+  s->E = static_cast<int>(l->num_experts);
+  s->K = static_cast<int>(top_k);
+  return OBJB_OK;
+}
+
+}  // namespace
+
+int moe_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_layer(l, top_k, &s, &split));
+  size_t need = 0;
+  auto calc = [&](auto tag) {
+    using RD = decltype(tag);
+    MoePlan<RD> p = plan_moe<RD>(s, l->fmt, split, true);
+    need = p.fast ? p.act_bytes + (p.imgx_quads + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
+  };
+  if (split) calc(dev::RowDotSplitFp4{});
+  else if (l->fmt == OBJB_Q4_0) calc(dev::RowDot<OBJB_Q4_0>{});
+  else if (l->fmt == OBJB_Q5_0) calc(dev::RowDot<OBJB_Q5_0>{});
+  else if (l->fmt == OBJB_IQ3_0) calc(dev::RowDot<OBJB_IQ3_0>{});
+  else calc(dev::RowDot<OBJB_FP4_E2M1>{});
+  *out = need;
+  return OBJB_OK;
+}
+
+// Alignment of every expert pointer is not visible to the host (the tables
+// live in device memory); the caller states it.  Unaligned layers run the
+// generic path.
+int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weights, size_t top_k,
+                 const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
+                 size_t scratch_bytes, cudaEvent_t mid) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_layer(l, top_k, &s, &split));
+  if (!ids || !weights || !x || !out)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run selected-expert MoE", "null device pointer");
+  const bool aligned = (l->flags & OBJB_MOE_UNALIGNED) == 0;
+  if (split)
+    return run_moe<dev::RowDotSplitFp4, OBJB_FP4_E2M1, true>(*l, s, ids, weights, x, out, limit, stream, scratch,
+                                                              scratch_bytes, aligned, mid);
+  switch (l->fmt) {
+    case OBJB_Q4_0:
+      return run_moe<dev::RowDot<OBJB_Q4_0>, OBJB_Q4_0, false>(*l, s, ids, weights, x, out, limit, stream, scratch,
+                                                                scratch_bytes, aligned, mid);
+    case OBJB_Q5_0:
+      return run_moe<dev::RowDot<OBJB_Q5_0>, OBJB_Q5_0, false>(*l, s, ids, weights, x, out, limit, stream, scratch,
+                                                                scratch_bytes, aligned, mid);
+    case OBJB_IQ3_0:
+      return run_moe<dev::RowDot<OBJB_IQ3_0>, OBJB_IQ3_0, false>(*l, s, ids, weights, x, out, limit, stream,
+                                                                  scratch, scratch_bytes, aligned, mid);
+    default:
+      return run_moe<dev::RowDot<OBJB_FP4_E2M1>, OBJB_FP4_E2M1, false>(*l, s, ids, weights, x, out, limit, stream,
+                                                                        scratch, scratch_bytes, aligned, mid);
+  }
+}
+
+int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
+                cudaStream_t stream) {
+  if (!logits || !ids || !weights)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_router_topk_device", "null device pointer");
+  if (n == 0 || n > 8192 || top_k == 0 || top_k > n)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_router_topk_device",
+                     "need 1 <= top_k <= num_experts <= 8192 (got top_k " + std::to_string(top_k) +
+                         ", num_experts " + std::to_string(n) + ")");
+  const int threads = static_cast<int>(std::min<size_t>(1024, (n + 31) / 32 * 32));
+  dev::router_topk_kernel<<<1, threads, n * sizeof(float), stream>>>(logits, static_cast<int>(n),
+                                                                     static_cast<int>(top_k), renorm, ids, weights);
+  OBJB_CUDA(cudaGetLastError(), "launch router kernel");
+  return OBJB_OK;
+}
+
+}  // namespace objb
+
+extern "C" {
+
+int objb_moe_scratch_bytes(const objb_moe_layer* layer, size_t top_k, size_t* bytes) {
+  objb::clear_error();
+  if (!bytes) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_scratch_bytes", "null output pointer");
+  return objb::moe_scratch_bytes(layer, top_k, bytes);
+}
+
+int objb_router_topk_device(const float* d_logits, size_t num_experts, size_t top_k, int renormalize,
+                            int32_t* d_ids, float* d_weights, objb_stream_t stream) {
+  objb::clear_error();
+  return objb::router_topk(d_logits, num_experts, top_k, renormalize, d_ids, d_weights,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int objb_moe_selected_device(const objb_moe_layer* layer, const int32_t* d_ids, const float* d_weights,
+                             size_t top_k, const float* d_x, float* d_out, float swiglu_limit,
+                             objb_stream_t stream_) {
+  objb::clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  OBJB_TRY(objb::moe_scratch_bytes(layer, top_k, &need));
+  int device = 0;
+  OBJB_TRY(objb::current_device(&device));
+  void* ws = nullptr;
+  OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
+  return objb::moe_selected(layer, d_ids, d_weights, top_k, d_x, d_out, swiglu_limit, stream, ws, need, nullptr);
+}
+
+int objb_moe_forward_device(const objb_moe_layer* layer, const float* d_logits, size_t top_k, int renormalize,
+                            int32_t* d_ids, float* d_weights, const float* d_x, float* d_out, float swiglu_limit,
+                            objb_stream_t stream) {
+  objb::clear_error();
+  if (!layer) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_forward_device", "null layer descriptor");
+  OBJB_TRY(objb::router_topk(d_logits, layer->num_experts, top_k, renormalize, d_ids, d_weights,
+                             static_cast<cudaStream_t>(stream)));
+  return objb_moe_selected_device(layer, d_ids, d_weights, top_k, d_x, d_out, swiglu_limit, stream);
+}
+
+}  // extern "C"

@@ -247,8 +247,17 @@ __device__ __forceinline__ int slot_part_bytes(const RowLayout& L) {
 // Issues stage `i` (row range [r0, r0 + nr)) into `slot`.
 __device__ __forceinline__ void issue_stage(const RowLayout& L, const SmemPlan& sp, int slot,
                                             const StageSource& src, bool dual, int r0, int nr,
-                                            uint64_t pol) {
+                                            uint64_t pol, unsigned* err) {
   uint8_t* dst = sp.stage + static_cast<size_t>(slot) * L.stage_bytes;
+  // Bulk copies need 16-byte aligned sources: a misaligned expert pointer is
+  // recorded and its stage completed without data instead of faulting.
+  const uintptr_t mis = (reinterpret_cast<uintptr_t>(src.wa) | reinterpret_cast<uintptr_t>(src.sa) |
+                         (dual ? (reinterpret_cast<uintptr_t>(src.wb) | reinterpret_cast<uintptr_t>(src.sb)) : 0)) & 15u;
+  if (mis || src.wa == nullptr || (dual && src.wb == nullptr)) {
+    if (err) atomicOr(err, kErrMisaligned);
+    mbar_arrive(&sp.full[slot]);
+    return;
+  }
   const uint32_t wbytes = static_cast<uint32_t>(nr) * L.row_bytes;
   const uint32_t sbytes = static_cast<uint32_t>(nr) * L.srow_bytes;
   const uint32_t per = wbytes + sbytes;
@@ -324,7 +333,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
             }
           }
           const int nr = min(T, J.row_end - r0);
-          issue_stage(L, sp, slot, J.src, DUAL, r0, nr, pol);
+          issue_stage(L, sp, slot, J.src, DUAL, r0, nr, pol, err);
           ++it;
         }
       }
@@ -435,30 +444,6 @@ __global__ void __launch_bounds__(256) gemv_fallback_kernel(const uint8_t* __res
   const uint8_t* rw = w + static_cast<size_t>(row) * row_bytes;
   float acc = 0.0f;
   for (int b = lane; b < nb; b += 32) acc += block_dot_global<FMT>(rw + static_cast<size_t>(b) * BB, x + b * 32);
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-  if (lane == 0) y[row] = acc;
-}
-
-// Split-layout FP4 fallback (any alignment).
-__global__ void __launch_bounds__(256) gemv_fp4_split_fallback_kernel(
-    const uint8_t* __restrict__ w, const uint8_t* __restrict__ s, const float* __restrict__ x,
-    float* __restrict__ y, int rows, int cols) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int nb = cols / 32;
-  const uint8_t* rw = w + static_cast<size_t>(row) * (cols / 2);
-  const uint8_t* rs = s + static_cast<size_t>(row) * nb;
-  float acc = 0.0f;
-  for (int b = lane; b < nb; b += 32) {
-    float a = 0.0f;
-    for (int j = 0; j < 16; ++j) {
-      const float2 v = e2m1x2_to_float2(rw[b * 16 + j]);
-      a = fmaf(v.x, __ldg(x + b * 32 + 2 * j), a);
-      a = fmaf(v.y, __ldg(x + b * 32 + 2 * j + 1), a);
-    }
-    acc += a * e8m0_to_f32(rs[b]);
-  }
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
   if (lane == 0) y[row] = acc;
 }

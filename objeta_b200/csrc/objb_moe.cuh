@@ -1,0 +1,192 @@
+// objb_moe.cuh -- programs for the selected-expert MoE on the row-streaming
+// pipeline (objb_gemv.cuh), plus the router.
+//
+// One token's MoE layer runs as
+//   [router]  -> x image -> gate/up (both matrices of every selected expert
+//   streamed through the same stages, SwiGLU in the epilogue) -> act images
+//   -> down (all selected experts of an output row block in one CTA, the
+//   weighted combine in the epilogue, in selection order).
+#pragma once
+
+#include <cstdint>
+
+#include "objb_gemv.cuh"
+
+namespace objb {
+namespace dev {
+
+// silu_mul (crates/objeta-cuda/kernels/moe.cu:2-22): with limit > 0 the up
+// value is clamped to [-limit, limit] and the gate to <= limit; then
+// act = g / (1 + exp(-g)) * u.
+__device__ __forceinline__ float swiglu(float g, float u, float limit) {
+  if (limit > 0.0f) {
+    u = fminf(limit, fmaxf(-limit, u));
+    g = fminf(limit, g);
+  }
+  const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  return __fmul_rn(silu, u);
+}
+
+// Expert tables as the kernels see them.
+struct ExpertTables {
+  const uint8_t* const* gate;
+  const uint8_t* const* up;
+  const uint8_t* const* down;
+  const uint8_t* const* gate_scale;  // split FP4 only
+  const uint8_t* const* up_scale;
+  const uint8_t* const* down_scale;
+  int num_experts;
+};
+
+__device__ __forceinline__ int checked_expert(const int32_t* ids, int k, int num_experts, unsigned* err) {
+  int e = ids[k];
+  if (e < 0 || e >= num_experts) {
+    if (err) atomicOr(err, 8u);  // out-of-range expert id: computed as expert 0, flagged
+    e = 0;
+  }
+  return e;
+}
+
+// gate/up: CTA c covers rows [c * R, (c + 1) * R) of the K * I rows of all
+// selected experts concatenated; one job per expert the range touches.
+struct GateUpProg {
+  ExpertTables t;
+  const int32_t* ids;
+  const uint4* ximg;
+  float* act;  // [K][I]
+  int K, I;
+  int rows_per_cta;
+  float swiglu_limit;
+  unsigned* err;
+
+  __device__ __forceinline__ int first_k(int cta) const { return (cta * rows_per_cta) / I; }
+  __device__ __forceinline__ int njobs(int cta) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(K * I, a + rows_per_cta);
+    if (a >= b) return 0;
+    return (b - 1) / I - a / I + 1;
+  }
+  __device__ __forceinline__ Job job(int cta, int j) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(K * I, a + rows_per_cta);
+    const int k = a / I + j;
+    Job J;
+    const int e = checked_expert(ids, k, t.num_experts, err);
+    J.src.wa = t.gate[e];
+    J.src.wb = t.up[e];
+    J.src.sa = t.gate_scale ? t.gate_scale[e] : nullptr;
+    J.src.sb = t.up_scale ? t.up_scale[e] : nullptr;
+    J.ximg = ximg;
+    J.row_begin = max(a, k * I) - k * I;
+    J.row_end = min(b, (k + 1) * I) - k * I;
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int cta, int j, int row, float va, float vb) const {
+    const int k = first_k(cta) + j;
+    act[static_cast<size_t>(k) * I + row] = swiglu(va, vb, swiglu_limit);
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
+// down + combine: CTA c owns output rows [c * R, (c + 1) * R); job j is
+// selected expert j.  The epilogue thread of a row is the same for every job
+// (identical stage split), so out[row] accumulates in selection order exactly
+// as the reference does (moe.rs:1319-1321, 650): out = 0; out += w * down.
+struct DownProg {
+  ExpertTables t;
+  const int32_t* ids;
+  const float* weights;
+  const uint4* ximg;  // K images, img_stride quads apart
+  size_t img_stride;
+  float* out;
+  int K, O;
+  int rows_per_cta;
+  unsigned* err;
+
+  __device__ __forceinline__ int njobs(int cta) const { return cta * rows_per_cta < O ? K : 0; }
+  __device__ __forceinline__ Job job(int cta, int j) const {
+    Job J;
+    const int e = checked_expert(ids, j, t.num_experts, err);
+    J.src.wa = t.down[e];
+    J.src.sa = t.down_scale ? t.down_scale[e] : nullptr;
+    J.src.wb = nullptr;
+    J.src.sb = nullptr;
+    J.ximg = ximg + j * img_stride;
+    J.row_begin = cta * rows_per_cta;
+    J.row_end = min(O, J.row_begin + rows_per_cta);
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int, int j, int row, float va, float) const {
+    const float p = __fmul_rn(weights[j], va);
+    out[row] = __fadd_rn(j == 0 ? 0.0f : out[row], p);
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
+// Router (crates/objeta-cuda/src/bin/deepseek_single_layer_moe.rs:720-740):
+// max-subtracted softmax, then the first top_k of a stable descending sort
+// (ties keep the lower expert index); optional renormalisation of the kept
+// weights by their sequential sum.  One CTA; the sequential f32 sum of the
+// reference is kept (thread 0 sums in expert order).  exp is evaluated in
+// double precision and rounded to f32.
+__global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int n, int top_k,
+                                                           int renorm, int32_t* __restrict__ ids,
+                                                           float* __restrict__ weights) {
+  extern __shared__ float sp[];  // [n] exp values, then probs
+  __shared__ float s_max, s_sum;
+  if (threadIdx.x == 0) {
+    float m = -__int_as_float(0x7F800000);
+    for (int e = 0; e < n; ++e) m = fmaxf(m, logits[e]);
+    s_max = m;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n; e += blockDim.x)
+    sp[e] = __double2float_rn(exp(static_cast<double>(__fsub_rn(logits[e], s_max))));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int e = 0; e < n; ++e) s = __fadd_rn(s, sp[e]);
+    s_sum = s;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n; e += blockDim.x) sp[e] = __fdiv_rn(sp[e], s_sum);
+  __syncthreads();
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const float pe = sp[e];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const float pj = sp[j];
+      rank += (pj > pe) || (pj == pe && j < e);
+    }
+    if (rank < top_k) {
+      ids[rank] = e;
+      weights[rank] = pe;
+    }
+  }
+  if (renorm) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.0f;
+      for (int k = 0; k < top_k; ++k) s = __fadd_rn(s, weights[k]);
+      if (s > 0.0f)
+        for (int k = 0; k < top_k; ++k) weights[k] = __fdiv_rn(weights[k], s);
+    }
+  }
+}
+
+// Elementwise kernels of the generic (unaligned-shape) MoE path, same
+// arithmetic as silu_mul / weighted_accum (moe.cu:2-34).
+__global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                float* __restrict__ act, int n, float limit) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) act[i] = swiglu(gate[i], up[i], limit);
+}
+
+__global__ void weighted_accum_kernel(const float* __restrict__ down, float* __restrict__ out,
+                                      const float* __restrict__ weights, int k, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __fadd_rn(k == 0 ? 0.0f : out[i], __fmul_rn(weights[k], down[i]));
+}
+
+}  // namespace dev
+}  // namespace objb

@@ -16,6 +16,8 @@ namespace dev {
 constexpr unsigned kErrFullWaitTimeout = 1u;
 constexpr unsigned kErrEmptyWaitTimeout = 2u;
 constexpr unsigned kErrDrainTimeout = 4u;
+constexpr unsigned kErrBadExpertId = 8u;
+constexpr unsigned kErrMisaligned = 16u;
 
 // mbarrier.try_wait may suspend the thread for a hardware time slice, so the
 // wall-clock bound is kMaxSpins times that slice (well under a few seconds).

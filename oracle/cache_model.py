@@ -54,8 +54,13 @@ class CacheModel:
             self.resident_bytes -= self.sizes.pop(key)
             if key in self.order:
                 self.order.remove(key)
+        # The reference loops while the order is non-empty; when only pinned
+        # keys remain it would spin forever -- the model (like the product)
+        # stops there.  A stale key dropped from the order still counts as
+        # progress.
         while self.resident_bytes + size > self.capacity_bytes and self.order:
-            self.evict_lru()
+            if self.evict_lru() is None and not any(k not in self.pinned for k in self.order):
+                break
         self.sizes[key] = size
         self.resident_bytes += size
         self.order.append(key)
