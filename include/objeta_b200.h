@@ -225,6 +225,27 @@ int objb_moe_selected_device(const objb_moe_layer *layer, const int32_t *d_ids,
                              const float *d_weights, size_t top_k, const float *d_x,
                              float *d_out, float swiglu_limit, objb_stream_t stream);
 
+/* No counterpart in the reference.  The same launch as
+ * objb_moe_selected_device for callers that cannot let a library allocate
+ * device memory (a host framework that reserves all HBM up front and forbids
+ * allocation on its hot path, or whose allocator must see every byte): the
+ * scratch comes from a fixed 4 MiB array in the library's device image (held
+ * on every GPU that loads the library until the process exits) instead of a
+ * cudaMalloc'd workspace; nothing is allocated.  Layers whose scratch
+ * (objb_moe_scratch_bytes) exceeds 4 MiB - 256 bytes are rejected with
+ * OBJB_ERR_INVALID_INPUT.  The first call on a device looks up the array's
+ * device address (once per device, with that device current); make that
+ * first call before any stream capture.  All calls on a device share the one
+ * array: calls that overlap on the GPU (different streams, or host threads
+ * racing) race on it.  Each call clears the error word at the array's start
+ * and overwrites the scratch it reads; nothing needs clearing between calls.
+ * A device-side error (an out-of-range expert id, a pipeline wait that ran
+ * out) is not reported through objb_device_error_take: it turns every element
+ * of d_out into NaN. */
+int objb_moe_selected_device_noalloc(const objb_moe_layer *layer, const int32_t *d_ids,
+                                     const float *d_weights, size_t top_k, const float *d_x,
+                                     float *d_out, float swiglu_limit, objb_stream_t stream);
+
 /* Router + selected-expert MoE in one call: logits -> (d_ids, d_weights) ->
  * out.  d_ids / d_weights receive the selection. */
 int objb_moe_forward_device(const objb_moe_layer *layer, const float *d_logits,

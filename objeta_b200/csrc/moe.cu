@@ -147,13 +147,13 @@ MoePlan<RD> plan_moe(const MoeShape& s, int fmt, bool split, bool aligned) {
 template <class RD, int FMT, bool SPLIT>
 int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, const float* weights,
             const float* x, float* out, float limit, cudaStream_t stream, void* scratch, size_t scratch_bytes,
-            bool aligned, cudaEvent_t mid) {
+            bool aligned, cudaEvent_t mid, unsigned* err_word) {
   int device = 0;
   OBJB_TRY(current_device(&device));
   DeviceProps props;
   OBJB_TRY(device_props(device, &props));
-  unsigned* err = nullptr;
-  OBJB_TRY(device_error_word(device, &err));
+  unsigned* err = err_word;
+  if (!err) OBJB_TRY(device_error_word(device, &err));
   MoePlan<RD> p = plan_moe<RD>(s, FMT, SPLIT, aligned);
   const size_t need = p.fast ? p.act_bytes + (p.imgx_quads + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
   if (scratch_bytes < need)
@@ -283,7 +283,7 @@ int moe_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out) {
 // generic path.
 int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weights, size_t top_k,
                  const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
-                 size_t scratch_bytes, cudaEvent_t mid) {
+                 size_t scratch_bytes, cudaEvent_t mid, unsigned* err_word) {
   MoeShape s;
   bool split = false;
   OBJB_TRY(validate_layer(l, top_k, &s, &split));
@@ -292,20 +292,20 @@ int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weigh
   const bool aligned = (l->flags & OBJB_MOE_UNALIGNED) == 0;
   if (split)
     return run_moe<dev::RowDotSplitFp4, OBJB_FP4_E2M1, true>(*l, s, ids, weights, x, out, limit, stream, scratch,
-                                                              scratch_bytes, aligned, mid);
+                                                              scratch_bytes, aligned, mid, err_word);
   switch (l->fmt) {
     case OBJB_Q4_0:
       return run_moe<dev::RowDot<OBJB_Q4_0>, OBJB_Q4_0, false>(*l, s, ids, weights, x, out, limit, stream, scratch,
-                                                                scratch_bytes, aligned, mid);
+                                                                scratch_bytes, aligned, mid, err_word);
     case OBJB_Q5_0:
       return run_moe<dev::RowDot<OBJB_Q5_0>, OBJB_Q5_0, false>(*l, s, ids, weights, x, out, limit, stream, scratch,
-                                                                scratch_bytes, aligned, mid);
+                                                                scratch_bytes, aligned, mid, err_word);
     case OBJB_IQ3_0:
       return run_moe<dev::RowDot<OBJB_IQ3_0>, OBJB_IQ3_0, false>(*l, s, ids, weights, x, out, limit, stream,
-                                                                  scratch, scratch_bytes, aligned, mid);
+                                                                  scratch, scratch_bytes, aligned, mid, err_word);
     default:
       return run_moe<dev::RowDot<OBJB_FP4_E2M1>, OBJB_FP4_E2M1, false>(*l, s, ids, weights, x, out, limit, stream,
-                                                                        scratch, scratch_bytes, aligned, mid);
+                                                                        scratch, scratch_bytes, aligned, mid, err_word);
   }
 }
 

@@ -19,7 +19,7 @@ int moe_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out);
 // One token through the layer with caller-provided scratch.
 int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weights, size_t top_k,
                  const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
-                 size_t scratch_bytes, cudaEvent_t mid = nullptr);
+                 size_t scratch_bytes, cudaEvent_t mid = nullptr, unsigned* err_word = nullptr);
 
 int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream);

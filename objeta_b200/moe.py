@@ -152,6 +152,8 @@ _lib.register_signatures({
                                          c_void_p, ctypes.c_float, c_void_p]),
     "objb_moe_forward_device": (c_int, [ctypes.POINTER(_LayerC), c_void_p, c_size, c_int, c_void_p, c_void_p,
                                         c_void_p, c_void_p, ctypes.c_float, c_void_p]),
+    "objb_moe_selected_device_noalloc": (c_int, [ctypes.POINTER(_LayerC), c_void_p, c_void_p, c_size, c_void_p,
+                                                 c_void_p, ctypes.c_float, c_void_p]),
 })
 
 
@@ -478,6 +480,15 @@ class MoeLayer:
         if d_out is None:
             d_out = torch.empty(self.out_dim, dtype=torch.float32, device=self.device)
         _lib.call("objb_moe_selected_device", ctypes.byref(self._c), _dev_ptr(d_ids), _dev_ptr(d_weights),
+                  d_ids.numel(), _dev_ptr(d_x), _dev_ptr(d_out), float(swiglu_limit), _lib.stream_handle(stream))
+        return d_out
+
+    def forward_selected_noalloc(self, d_ids, d_weights, d_x, d_out, swiglu_limit: float = 0.0, stream=None):
+        """The same launch for callers that cannot let the library allocate
+        device memory: scratch comes from the library's fixed 4 MiB array
+        (objb_moe_selected_device_noalloc); ``d_out`` must be given.  Calls
+        that overlap on the GPU share that array and race."""
+        _lib.call("objb_moe_selected_device_noalloc", ctypes.byref(self._c), _dev_ptr(d_ids), _dev_ptr(d_weights),
                   d_ids.numel(), _dev_ptr(d_x), _dev_ptr(d_out), float(swiglu_limit), _lib.stream_handle(stream))
         return d_out
 
