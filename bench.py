@@ -2,6 +2,11 @@
 """Benchmark of the objeta-cuda hot path on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --case q4_0:151936x2048 [--steps K] [--warmup W]
+
+`--case` runs one GEMV of the sweep alone (W + K plain launches, rotating
+over its weight copies, no graph) and prints its mean launch time; it is the
+command the ncu captures are taken on.
 
 Workload: the block-quant GEMV format/shape sweep,
 Q4_0, Q5_0 and IQ3_0 at rows x cols in {4096x4096, 14336x4096, 4096x14336,
@@ -122,12 +127,15 @@ def read_peaks():
 
 
 def read_traffic(kernel_key):
+    """DRAM bytes (read + write) per launch of `kernel_key` from the committed
+    ncu summary profiles/traffic.json, or None."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
-            return json.load(f).get(kernel_key)
+            v = json.load(f).get(kernel_key)
     except (OSError, ValueError):
         return None
+    return v.get("dram_bytes_per_launch") if isinstance(v, dict) else v
 
 
 # --------------------------------------------------------------- our arm
@@ -240,23 +248,21 @@ def run_ours(args, world, rank, local):
     per_case_ms = per_head + per_extra
     cases = headline + extra
 
-    # dominant kernel: the format whose launches take the largest share
-    share = {}
-    for i, c in enumerate(cases):
-        if c["fmt"] in HEADLINE_FORMATS:
-            share.setdefault(c["fmt"], [0.0, 0])
-            share[c["fmt"]][0] += per_case_ms[i]
-            share[c["fmt"]][1] += c["bytes"]
-    dom = max(share, key=lambda f: share[f][0])
-    dom_ms, dom_bytes = share[dom]
+    # dominant kernel: the sweep case with the largest share of the step.  Its
+    # per-launch time (CUDA events around the GEMV inside the graph) covers the
+    # GEMV's two kernels, the x-image prep and the pipelined GEMV.
+    dom = max(range(len(headline)), key=lambda i: per_case_ms[i])
+    dc = headline[dom]
     peak, peak_kind = read_peaks()
-    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
-    dom_launches = len(SHAPES)
-    traffic = read_traffic(f"gemv_{FMT_NAMES[dom]}")
-    roofline = {"bound": "hbm", "kernel": f"pipe_kernel<RowDot<{FMT_NAMES[dom]}>> (GEMV, {dom_launches} shapes)",
-                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind,
+    achieved = dc["bytes"] / (per_case_ms[dom] / 1e3) / 1e9
+    dom_name = f"{FMT_NAMES[dc['fmt']]}_{dc['rows']}x{dc['cols']}"
+    roofline = {"bound": "hbm",
+                "kernel": f"ximage + pipe_kernel<RowDot<{FMT_NAMES[dc['fmt']]}>> GEMV {dc['rows']}x{dc['cols']}",
+                "achieved": round(achieved, 1), "peak": peak, "peak_source": f"{peak_kind} (hbm_gbs)",
                 "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "traffic": traffic}
+                "algorithmic_bytes_per_launch": dc["bytes"],
+                "us_per_launch": round(per_case_ms[dom] * 1e3, 2),
+                "traffic": read_traffic(f"gemv_{dom_name}")}
     case_out = {}
     for i, c in enumerate(cases):
         gbs = c["bytes"] / (per_case_ms[i] / 1e3) / 1e9
@@ -281,7 +287,7 @@ def run_ours(args, world, rank, local):
                        "l2_defeat": "weights rotated over >= 4x L2 per case",
                        "bytes_per_step": step_bytes, "cuda_graph": True},
             "roofline": roofline, "cases": case_out, "e2e": e2e,
-            "gpu_launches": args.steps * len(headline),
+            "gpu_launches": args.steps * len(headline) * 2,  # x-image prep + GEMV per case
             "clocks": sampler.summary(),
         }
         cb = cpu_baseline(cases, headline, args)
@@ -404,17 +410,58 @@ def run_reference(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_case(args, local):
+    """One sweep case alone: W + K launches of GEMV `fmt:RxC` (weights rotated
+    over >= 4x L2 copies), timed with CUDA events on the launching stream."""
+    import torch
+    from objeta_b200 import QGemvShape, QuantBackend, QuantFormat
+    from objeta_b200.quant import gemv_device
+    name, _, dims = args.case.partition(":")
+    fmt = {v: k for k, v in FMT_NAMES.items()}[name]
+    rows, cols = (int(v) for v in dims.split("x"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    qb = QuantBackend(local)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    shape = QGemvShape.new(QuantFormat(fmt), rows, cols)
+    m = torch.randn(rows, cols, device=dev, generator=gen) * 0.02
+    q0 = qb.quantize_matrix_device(QuantFormat(fmt), m, shape)
+    del m
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    copies = [q0] + [q0.clone() for _ in range(max(2, math.ceil(4 * l2 / q0.numel())) - 1)]
+    x = torch.randn(cols, device=dev, generator=gen)
+    y = torch.empty(rows, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    for i in range(args.warmup):
+        gemv_device(fmt, copies[i % len(copies)], x, y, rows, cols, stream)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        gemv_device(fmt, copies[(args.warmup + i) % len(copies)], x, y, rows, cols, stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) * 1e3 / args.steps
+    return {"case": args.case, "launches": args.steps, "us_per_gemv": round(us, 2),
+            "GB/s": round(algo_bytes(fmt, rows, cols) / us / 1e3, 1), "copies": len(copies)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--case", default=None, help="fmt:RxC, e.g. q4_0:151936x2048 (one GEMV alone)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
         args.warmup = 3
     world, rank, local = dist_env()
+    if args.case:
+        print(json.dumps(run_case(args, local)), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, world, rank)
     else:
