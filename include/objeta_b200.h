@@ -246,6 +246,40 @@ int objb_moe_selected_device_noalloc(const objb_moe_layer *layer, const int32_t 
                                      const float *d_weights, size_t top_k, const float *d_x,
                                      float *d_out, float swiglu_limit, objb_stream_t stream);
 
+/* ---- multi-token MoE (no counterpart in the reference, which runs one token
+ * per execute_selected_moe_cuda call; the per-pair arithmetic is the same).
+ *
+ * objb_moe_pairs_device runs the layer over num_pairs (expert, token) pairs:
+ * for pair p, e = d_pair_expert[p] and t = d_pair_token[p] (0 <= t <
+ * num_tokens, x row t of d_x [num_tokens][hidden]); the unweighted down
+ * output down_e(SwiGLU(gate_e x_t, up_e x_t)) is written to row
+ * d_pair_out[p] of d_v [v_rows][out_dim] (row p when d_pair_out is NULL).
+ * Pairs are computed in the given order: group them by expert so each
+ * expert's weights are streamed once while they sit in L2.  Every output row
+ * is bit-identical to the value the single-token launch computes for the same
+ * expert and x.  Out-of-range ids or rows are clamped to 0 and flagged in the
+ * device error word (bit 8).  Scratch comes from the per-stream workspace. */
+int objb_moe_pairs_scratch_bytes(const objb_moe_layer *layer, size_t num_pairs,
+                                 size_t num_tokens, size_t *bytes);
+int objb_moe_pairs_device(const objb_moe_layer *layer, size_t num_pairs,
+                          const int32_t *d_pair_expert, const int32_t *d_pair_token,
+                          const int32_t *d_pair_out, size_t num_tokens, const float *d_x,
+                          float *d_v, size_t v_rows, float swiglu_limit, objb_stream_t stream);
+
+/* The weighted top-k combine (moe.rs:1319-1321) for num_tokens tokens:
+ * d_out[t][i] = sum over j = 0..top_k-1, in slot order, of
+ * d_weights[t][j] * d_v[d_slot_row[t][j]][i], starting from 0 -- the exact
+ * arithmetic of the single-token fused combine. */
+int objb_moe_combine_device(const float *d_v, size_t v_rows, const int32_t *d_slot_row,
+                            const float *d_weights, size_t num_tokens, size_t top_k,
+                            size_t out_dim, float *d_out, objb_stream_t stream);
+
+/* objb_router_topk_device for num_tokens rows of logits [num_tokens][num_experts]
+ * (one CTA per token); ids / weights are [num_tokens][top_k]. */
+int objb_router_topk_batched_device(const float *d_logits, size_t num_tokens,
+                                    size_t num_experts, size_t top_k, int renormalize,
+                                    int32_t *d_ids, float *d_weights, objb_stream_t stream);
+
 /* Router + selected-expert MoE in one call: logits -> (d_ids, d_weights) ->
  * out.  d_ids / d_weights receive the selection. */
 int objb_moe_forward_device(const objb_moe_layer *layer, const float *d_logits,

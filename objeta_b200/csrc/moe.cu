@@ -83,6 +83,42 @@ __global__ void __launch_bounds__(256) moe_generic_down_kernel(ExpertTables t, c
   if (lane == 0) out[row] = acc;
 }
 
+// Generic pair kernels: one warp per (pair, row).
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(256) moe_generic_pairs_gateup_kernel(ExpertTables t, const int32_t* pair_expert,
+                                                                       const int32_t* pair_token, int P, int I,
+                                                                       int H, int T, const float* __restrict__ x,
+                                                                       float* __restrict__ act, float limit,
+                                                                       unsigned* err) {
+  const int wi = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wi >= P * I) return;
+  const int p = wi / I, row = wi % I;
+  const int e = checked_expert(pair_expert, p, t.num_experts, err);
+  const float* xp = x + static_cast<size_t>(checked_index(pair_token, p, T, err)) * H;
+  const int lane = threadIdx.x & 31;
+  const float g = row_dot_global<FMT, SPLIT>(t.gate[e], SPLIT ? t.gate_scale[e] : nullptr, row, H, xp, lane);
+  const float u = row_dot_global<FMT, SPLIT>(t.up[e], SPLIT ? t.up_scale[e] : nullptr, row, H, xp, lane);
+  if (lane == 0) act[static_cast<size_t>(p) * I + row] = swiglu(g, u, limit);
+}
+
+template <int FMT, bool SPLIT>
+__global__ void __launch_bounds__(256) moe_generic_pairs_down_kernel(ExpertTables t, const int32_t* pair_expert,
+                                                                     const int32_t* pair_out, int P, int I, int O,
+                                                                     int v_rows, const float* __restrict__ act,
+                                                                     float* __restrict__ v, unsigned* err) {
+  const int wi = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wi >= P * O) return;
+  const int p = wi / O, row = wi % O;
+  const int e = checked_expert(pair_expert, p, t.num_experts, err);
+  const int lane = threadIdx.x & 31;
+  const float d = row_dot_global<FMT, SPLIT>(t.down[e], SPLIT ? t.down_scale[e] : nullptr, row, I,
+                                             act + static_cast<size_t>(p) * I, lane);
+  if (lane == 0) {
+    const int r = pair_out ? checked_index(pair_out, p, v_rows, err) : p;
+    v[static_cast<size_t>(r) * O + row] = d;
+  }
+}
+
 }  // namespace dev
 
 namespace {
@@ -228,6 +264,99 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
   return OBJB_OK;
 }
 
+// Pairs: s.K is the pair count P; T token vectors of H floats.
+template <class RD>
+size_t pairs_need(const MoePlan<RD>& p, const MoeShape& s, int T) {
+  return p.fast ? p.act_bytes + (p.imgx_quads * T + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
+}
+
+template <class RD, int FMT, bool SPLIT>
+int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* pair_expert,
+              const int32_t* pair_token, const int32_t* pair_out, const float* x, float* v, int v_rows,
+              float limit, cudaStream_t stream, void* scratch, size_t scratch_bytes, bool aligned,
+              unsigned* err_word) {
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  unsigned* err = err_word;
+  if (!err) OBJB_TRY(device_error_word(device, &err));
+  MoePlan<RD> p = plan_moe<RD>(s, FMT, SPLIT, aligned);
+  const size_t need = pairs_need(p, s, T);
+  if (scratch_bytes < need)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run multi-token MoE pairs",
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(need));
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  float* act = reinterpret_cast<float*>(sc);
+  const dev::ExpertTables t = tables_of(l);
+  const int P = s.K;
+  if (!p.fast) {
+    dev::moe_generic_pairs_gateup_kernel<FMT, SPLIT><<<(P * s.I + 7) / 8, 256, 0, stream>>>(
+        t, pair_expert, pair_token, P, s.I, s.H, T, x, act, limit, err);
+    OBJB_CUDA(cudaGetLastError(), "launch generic pair gate/up kernel");
+    dev::moe_generic_pairs_down_kernel<FMT, SPLIT><<<(P * s.O + 7) / 8, 256, 0, stream>>>(
+        t, pair_expert, pair_out, P, s.I, s.O, v_rows, act, v, err);
+    OBJB_CUDA(cudaGetLastError(), "launch generic pair down kernel");
+    return OBJB_OK;
+  }
+  uint4* imgx = reinterpret_cast<uint4*>(sc + p.act_bytes);
+  uint4* imga = imgx + p.imgx_quads * T;
+  OBJB_TRY(launch_ximage<RD>(p.lg, x, static_cast<size_t>(s.H), T, imgx, p.imgx_quads, stream));
+  {
+    const int total = P * s.I;
+    const int TS = p.lg.tstage;
+    int R = (total + props.sm_count - 1) / props.sm_count;
+    R = (R + TS - 1) / TS * TS;
+    const int grid = (total + R - 1) / R;
+    dev::GateUpPairsProg prog;
+    prog.t = t;
+    prog.pair_expert = pair_expert;
+    prog.pair_token = pair_token;
+    prog.ximg = imgx;
+    prog.img_stride = p.imgx_quads;
+    prog.act = act;
+    prog.P = P;
+    prog.I = s.I;
+    prog.T = T;
+    prog.rows_per_cta = R;
+    prog.swiglu_limit = limit;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(p.lg);
+    auto kernel = dev::pipe_kernel<RD, dev::GateUpPairsProg, true>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.lg, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream));
+  {
+    const int total = P * s.O;
+    const int TS = p.ld.tstage;
+    int R = (total + props.sm_count - 1) / props.sm_count;
+    R = (R + TS - 1) / TS * TS;
+    const int grid = (total + R - 1) / R;
+    dev::DownPairsProg prog;
+    prog.t = t;
+    prog.pair_expert = pair_expert;
+    prog.pair_out = pair_out;
+    prog.ximg = imga;
+    prog.img_stride = p.imga_quads;
+    prog.v = v;
+    prog.P = P;
+    prog.O = s.O;
+    prog.v_rows = v_rows;
+    prog.rows_per_cta = R;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(p.ld);
+    auto kernel = dev::pipe_kernel<RD, dev::DownPairsProg, false>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.ld, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (p.ld.nseg * p.ld.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  return OBJB_OK;
+}
+
 int validate_layer(const objb_moe_layer* l, size_t top_k, MoeShape* s, bool* split) {
   if (!l) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE layer", "null layer descriptor");
   if (!valid_format(l->fmt))
@@ -309,6 +438,102 @@ int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weigh
   }
 }
 
+namespace {
+
+int validate_pairs(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, MoeShape* s, bool* split) {
+  OBJB_TRY(validate_layer(l, 1, s, split));
+  if (num_pairs == 0 || num_pairs > (1u << 20) || num_tokens == 0 || num_tokens > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE pairs",
+                     "need 1 <= num_pairs, num_tokens <= 2^20 (got " + std::to_string(num_pairs) + ", " +
+                         std::to_string(num_tokens) + ")");
+  if (num_pairs * std::max(l->intermediate, l->out_dim) > (1u << 30) || num_tokens * l->hidden > (1ull << 34))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate MoE pairs", "num_pairs * rows too large");
+  s->K = static_cast<int>(num_pairs);
+  return OBJB_OK;
+}
+
+}  // namespace
+
+int moe_pairs_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_pairs(l, num_pairs, num_tokens, &s, &split));
+  const int T = static_cast<int>(num_tokens);
+  auto calc = [&](auto tag) {
+    using RD = decltype(tag);
+    *out = pairs_need(plan_moe<RD>(s, l->fmt, split, true), s, T);
+  };
+  if (split) calc(dev::RowDotSplitFp4{});
+  else if (l->fmt == OBJB_Q4_0) calc(dev::RowDot<OBJB_Q4_0>{});
+  else if (l->fmt == OBJB_Q5_0) calc(dev::RowDot<OBJB_Q5_0>{});
+  else if (l->fmt == OBJB_IQ3_0) calc(dev::RowDot<OBJB_IQ3_0>{});
+  else calc(dev::RowDot<OBJB_FP4_E2M1>{});
+  return OBJB_OK;
+}
+
+int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_expert, const int32_t* pair_token,
+              const int32_t* pair_out, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
+              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_pairs(l, num_pairs, num_tokens, &s, &split));
+  if (!pair_expert || !pair_token || !x || !v)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run multi-token MoE pairs", "null device pointer");
+  if (v_rows < (pair_out ? 1 : num_pairs) || v_rows > (1u << 30))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run multi-token MoE pairs",
+                     "v_rows " + std::to_string(v_rows) + " cannot hold the pair outputs");
+  const bool aligned = (l->flags & OBJB_MOE_UNALIGNED) == 0;
+  const int T = static_cast<int>(num_tokens);
+  const int VR = static_cast<int>(v_rows);
+#define OBJB_PAIRS(RDT, F, SP)                                                                                   \
+  return run_pairs<RDT, F, SP>(*l, s, T, pair_expert, pair_token, pair_out, x, v, VR, limit, stream, scratch, \
+                               scratch_bytes, aligned, err_word)
+  if (split) OBJB_PAIRS(dev::RowDotSplitFp4, OBJB_FP4_E2M1, true);
+  switch (l->fmt) {
+    case OBJB_Q4_0: OBJB_PAIRS(dev::RowDot<OBJB_Q4_0>, OBJB_Q4_0, false);
+    case OBJB_Q5_0: OBJB_PAIRS(dev::RowDot<OBJB_Q5_0>, OBJB_Q5_0, false);
+    case OBJB_IQ3_0: OBJB_PAIRS(dev::RowDot<OBJB_IQ3_0>, OBJB_IQ3_0, false);
+    default: OBJB_PAIRS(dev::RowDot<OBJB_FP4_E2M1>, OBJB_FP4_E2M1, false);
+  }
+#undef OBJB_PAIRS
+}
+
+int moe_combine(const float* v, size_t v_rows, const int32_t* slot_row, const float* weights, size_t num_tokens,
+                size_t top_k, size_t out_dim, float* out, cudaStream_t stream, unsigned* err_word) {
+  if (!v || !slot_row || !weights || !out)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_combine_device", "null device pointer");
+  if (num_tokens == 0 || num_tokens > 65535 || top_k == 0 || top_k > 1024 || out_dim == 0 ||
+      out_dim > (1u << 24) || v_rows == 0 || v_rows > (1u << 30))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_combine_device",
+                     "need 1 <= num_tokens <= 65535, 1 <= top_k <= 1024, 1 <= out_dim <= 2^24");
+  unsigned* err = err_word;
+  if (!err) {
+    int device = 0;
+    OBJB_TRY(current_device(&device));
+    OBJB_TRY(device_error_word(device, &err));
+  }
+  const dim3 grid(static_cast<unsigned>((out_dim + 255) / 256), static_cast<unsigned>(num_tokens));
+  dev::combine_kernel<<<grid, 256, 0, stream>>>(v, slot_row, weights, static_cast<int>(top_k),
+                                                 static_cast<int>(out_dim), static_cast<int>(v_rows), out, err);
+  OBJB_CUDA(cudaGetLastError(), "launch combine kernel");
+  return OBJB_OK;
+}
+
+int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t top_k, int renorm, int32_t* ids,
+                        float* weights, cudaStream_t stream) {
+  if (!logits || !ids || !weights)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_router_topk_batched_device", "null device pointer");
+  if (num_tokens == 0 || num_tokens > 65535 || n == 0 || n > 8192 || top_k == 0 || top_k > n)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_router_topk_batched_device",
+                     "need 1 <= num_tokens <= 65535 and 1 <= top_k <= num_experts <= 8192 (got top_k " +
+                         std::to_string(top_k) + ", num_experts " + std::to_string(n) + ")");
+  const int threads = static_cast<int>(std::min<size_t>(1024, (n + 31) / 32 * 32));
+  dev::router_topk_kernel<<<static_cast<unsigned>(num_tokens), threads, n * sizeof(float), stream>>>(
+      logits, static_cast<int>(n), static_cast<int>(top_k), renorm, ids, weights);
+  OBJB_CUDA(cudaGetLastError(), "launch batched router kernel");
+  return OBJB_OK;
+}
+
 int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream) {
   if (!logits || !ids || !weights)
@@ -363,6 +588,41 @@ int objb_moe_forward_device(const objb_moe_layer* layer, const float* d_logits, 
   OBJB_TRY(objb::router_topk(d_logits, layer->num_experts, top_k, renormalize, d_ids, d_weights,
                              static_cast<cudaStream_t>(stream)));
   return objb_moe_selected_device(layer, d_ids, d_weights, top_k, d_x, d_out, swiglu_limit, stream);
+}
+
+int objb_moe_pairs_scratch_bytes(const objb_moe_layer* layer, size_t num_pairs, size_t num_tokens, size_t* bytes) {
+  objb::clear_error();
+  if (!bytes) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_pairs_scratch_bytes", "null output pointer");
+  return objb::moe_pairs_scratch_bytes(layer, num_pairs, num_tokens, bytes);
+}
+
+int objb_moe_pairs_device(const objb_moe_layer* layer, size_t num_pairs, const int32_t* d_pair_expert,
+                          const int32_t* d_pair_token, const int32_t* d_pair_out, size_t num_tokens,
+                          const float* d_x, float* d_v, size_t v_rows, float swiglu_limit, objb_stream_t stream_) {
+  objb::clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  OBJB_TRY(objb::moe_pairs_scratch_bytes(layer, num_pairs, num_tokens, &need));
+  int device = 0;
+  OBJB_TRY(objb::current_device(&device));
+  void* ws = nullptr;
+  OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
+  return objb::moe_pairs(layer, num_pairs, d_pair_expert, d_pair_token, d_pair_out, num_tokens, d_x, d_v, v_rows,
+                         swiglu_limit, stream, ws, need, nullptr);
+}
+
+int objb_moe_combine_device(const float* d_v, size_t v_rows, const int32_t* d_slot_row, const float* d_weights,
+                            size_t num_tokens, size_t top_k, size_t out_dim, float* d_out, objb_stream_t stream) {
+  objb::clear_error();
+  return objb::moe_combine(d_v, v_rows, d_slot_row, d_weights, num_tokens, top_k, out_dim, d_out,
+                           static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int objb_router_topk_batched_device(const float* d_logits, size_t num_tokens, size_t num_experts, size_t top_k,
+                                    int renormalize, int32_t* d_ids, float* d_weights, objb_stream_t stream) {
+  objb::clear_error();
+  return objb::router_topk_batched(d_logits, num_tokens, num_experts, top_k, renormalize, d_ids, d_weights,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

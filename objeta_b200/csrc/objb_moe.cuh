@@ -123,6 +123,124 @@ struct DownProg {
   __device__ __forceinline__ void finalize(int, int, int) const {}
 };
 
+// ---- multi-token MoE over (expert, token) pairs.  Pair p runs the expert
+// pair_expert[p] on token pair_token[p]; its unweighted down output lands in
+// row pair_out[p] of v.  The row programs and layouts are those of the
+// single-token launch, so every v row is bit-identical to the value the fused
+// single-token combine multiplies by its routing weight.
+
+__device__ __forceinline__ int checked_index(const int32_t* idx, int p, int n, unsigned* err) {
+  int v = idx[p];
+  if (v < 0 || v >= n) {
+    if (err) atomicOr(err, 8u);  // out-of-range token / row index: clamped to 0, flagged
+    v = 0;
+  }
+  return v;
+}
+
+// gate/up: rows [c * R, (c + 1) * R) of the P * I rows of all pairs.
+struct GateUpPairsProg {
+  ExpertTables t;
+  const int32_t* pair_expert;
+  const int32_t* pair_token;
+  const uint4* ximg;  // T token images, img_stride quads apart
+  size_t img_stride;
+  float* act;  // [P][I]
+  int P, I, T;
+  int rows_per_cta;
+  float swiglu_limit;
+  unsigned* err;
+
+  __device__ __forceinline__ int first_p(int cta) const { return (cta * rows_per_cta) / I; }
+  __device__ __forceinline__ int njobs(int cta) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(P * I, a + rows_per_cta);
+    if (a >= b) return 0;
+    return (b - 1) / I - a / I + 1;
+  }
+  __device__ __forceinline__ Job job(int cta, int j) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(P * I, a + rows_per_cta);
+    const int p = a / I + j;
+    Job J;
+    const int e = checked_expert(pair_expert, p, t.num_experts, err);
+    const int tok = checked_index(pair_token, p, T, err);
+    J.src.wa = t.gate[e];
+    J.src.wb = t.up[e];
+    J.src.sa = t.gate_scale ? t.gate_scale[e] : nullptr;
+    J.src.sb = t.up_scale ? t.up_scale[e] : nullptr;
+    J.ximg = ximg + static_cast<size_t>(tok) * img_stride;
+    J.row_begin = max(a, p * I) - p * I;
+    J.row_end = min(b, (p + 1) * I) - p * I;
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int cta, int j, int row, float va, float vb) const {
+    const int p = first_p(cta) + j;
+    act[static_cast<size_t>(p) * I + row] = swiglu(va, vb, swiglu_limit);
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
+// down: rows [c * R, (c + 1) * R) of the P * O rows of all pairs; no combine.
+struct DownPairsProg {
+  ExpertTables t;
+  const int32_t* pair_expert;
+  const int32_t* pair_out;  // nullptr: row p
+  const uint4* ximg;        // P activation images, img_stride quads apart
+  size_t img_stride;
+  float* v;                 // [v_rows][O]
+  int P, O, v_rows;
+  int rows_per_cta;
+  unsigned* err;
+
+  __device__ __forceinline__ int first_p(int cta) const { return (cta * rows_per_cta) / O; }
+  __device__ __forceinline__ int njobs(int cta) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(P * O, a + rows_per_cta);
+    if (a >= b) return 0;
+    return (b - 1) / O - a / O + 1;
+  }
+  __device__ __forceinline__ Job job(int cta, int j) const {
+    const int a = cta * rows_per_cta;
+    const int b = min(P * O, a + rows_per_cta);
+    const int p = a / O + j;
+    Job J;
+    const int e = checked_expert(pair_expert, p, t.num_experts, err);
+    J.src.wa = t.down[e];
+    J.src.sa = t.down_scale ? t.down_scale[e] : nullptr;
+    J.src.wb = nullptr;
+    J.src.sb = nullptr;
+    J.ximg = ximg + static_cast<size_t>(p) * img_stride;
+    J.row_begin = max(a, p * O) - p * O;
+    J.row_end = min(b, (p + 1) * O) - p * O;
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int cta, int j, int row, float va, float) const {
+    const int p = first_p(cta) + j;
+    const int r = pair_out ? checked_index(pair_out, p, v_rows, err) : p;
+    v[static_cast<size_t>(r) * O + row] = va;
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
+// Weighted top-k combine of pair outputs, per token in slot order, with the
+// arithmetic of the fused single-token combine (out = 0; out += w * down):
+// out[t][i] = (((w0 * v[r0][i]) + w1 * v[r1][i]) + ...).  grid (ceil(O/256), T).
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ v, const int32_t* __restrict__ slot_row,
+                                                      const float* __restrict__ w, int K, int O, int v_rows,
+                                                      float* __restrict__ out, unsigned* err) {
+  const int t = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= O) return;
+  float acc = 0.0f;
+  for (int j = 0; j < K; ++j) {
+    const int r = checked_index(slot_row + static_cast<size_t>(t) * K, j, v_rows, err);
+    const float p = __fmul_rn(w[static_cast<size_t>(t) * K + j], v[static_cast<size_t>(r) * O + i]);
+    acc = __fadd_rn(j == 0 ? 0.0f : acc, p);
+  }
+  out[static_cast<size_t>(t) * O + i] = acc;
+}
+
 // Router (crates/objeta-cuda/src/bin/deepseek_single_layer_moe.rs:720-740):
 // max-subtracted softmax, then the first top_k of a stable descending sort
 // (ties keep the lower expert index); optional renormalisation of the kept
@@ -132,6 +250,10 @@ struct DownProg {
 __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int n, int top_k,
                                                            int renorm, int32_t* __restrict__ ids,
                                                            float* __restrict__ weights) {
+  // CTA b routes token b (logits row b, ids / weights row b).
+  logits += static_cast<size_t>(blockIdx.x) * n;
+  ids += static_cast<size_t>(blockIdx.x) * top_k;
+  weights += static_cast<size_t>(blockIdx.x) * top_k;
   extern __shared__ float sp[];  // [n] exp values, then probs
   __shared__ float s_max, s_sum;
   if (threadIdx.x == 0) {

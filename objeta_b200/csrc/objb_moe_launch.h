@@ -21,6 +21,17 @@ int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weigh
                  const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
                  size_t scratch_bytes, cudaEvent_t mid = nullptr, unsigned* err_word = nullptr);
 
+// Multi-token MoE over (expert, token) pairs: v[pair_out[p]] = down(SwiGLU(
+// gate x[pair_token[p]], up x[pair_token[p]])) of expert pair_expert[p].
+int moe_pairs_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out);
+int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_expert, const int32_t* pair_token,
+              const int32_t* pair_out, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
+              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word = nullptr);
+int moe_combine(const float* v, size_t v_rows, const int32_t* slot_row, const float* weights, size_t num_tokens,
+                size_t top_k, size_t out_dim, float* out, cudaStream_t stream, unsigned* err_word = nullptr);
+int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t top_k, int renorm, int32_t* ids,
+                        float* weights, cudaStream_t stream);
+
 int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream);
 

@@ -1,0 +1,260 @@
+"""Multi-token and expert-parallel selected-expert MoE.
+
+The reference runs one token at a time through
+``MoeExecutor::execute_selected_moe_cuda`` (crates/objeta-cuda/src/moe.rs:
+352-751) and has no expert parallelism; this module is the multi-token,
+multi-GPU form of the same layer:
+
+* ``router_topk_batched``: the reference router (deepseek_single_layer_moe.rs:
+  720-740) for T tokens, one CTA per token;
+* ``moe_pairs``: the layer over a list of (expert, token) pairs, each pair's
+  unweighted down-projection output in its own row;
+* ``moe_combine``: the weighted top-k combine per token, in slot order, with
+  the reference's arithmetic (out = 0; out += w * down; moe.rs:1319-1321);
+* ``DispatchPlan`` / ``ExpertParallelMoe``: experts of a layer block-
+  partitioned over the ranks of a process group (expert e on rank
+  e // (E / G)); every rank routes its own tokens, the routing table is
+  all-gathered, token rows go to the experts' ranks with one all-to-all, the
+  pair outputs come back with a second, and each token's owner combines
+  them in slot order.  Every pair output is computed by the same row
+  programs whichever rank runs it, so the result does not depend on the
+  number of ranks.
+
+Collectives are ``torch.distributed`` calls (NCCL on GPUs, gloo on CPU); the
+compute is the CUDA library unless a test supplies another ``compute``.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from .quant import _dev_ptr
+
+c_size = ctypes.c_size_t
+c_int = ctypes.c_int
+c_void_p = ctypes.c_void_p
+
+_lib.register_signatures({
+    "objb_moe_pairs_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
+    "objb_moe_pairs_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_size, c_void_p,
+                                      c_void_p, c_size, ctypes.c_float, c_void_p]),
+    "objb_moe_combine_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p,
+                                        c_void_p]),
+    "objb_router_topk_batched_device": (c_int, [c_void_p, c_size, c_size, c_size, c_int, c_void_p, c_void_p,
+                                                c_void_p]),
+})
+
+
+def router_topk_batched(d_logits, top_k: int, renormalize: bool = False, stream=None):
+    """Router of T tokens: d_logits [T, E] f32 -> (ids [T, k] int32,
+    weights [T, k] f32), each row as ``router_topk`` computes it."""
+    import torch
+    T, E = d_logits.shape
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=d_logits.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=d_logits.device)
+    _lib.call("objb_router_topk_batched_device", _dev_ptr(d_logits), T, E, top_k, int(bool(renormalize)),
+              _dev_ptr(ids), _dev_ptr(w), _lib.stream_handle(stream))
+    return ids, w
+
+
+def moe_pairs(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 0.0, stream=None):
+    """v[pair_out[p]] = down_e(SwiGLU(gate_e x_t, up_e x_t)) with
+    e = pair_expert[p], t = pair_token[p] (device int32 tensors); d_x [T, H],
+    d_v [V, O] f32.  ``pair_out`` None writes row p."""
+    P = pair_expert.numel()
+    T = d_x.shape[0]
+    _lib.call("objb_moe_pairs_device", ctypes.byref(layer._c), P, _dev_ptr(pair_expert), _dev_ptr(pair_token),
+              _dev_ptr(pair_out) if pair_out is not None else None, T, _dev_ptr(d_x), _dev_ptr(d_v),
+              d_v.shape[0], float(swiglu_limit), _lib.stream_handle(stream))
+    return d_v
+
+
+def moe_pairs_scratch_bytes(layer, num_pairs: int, num_tokens: int) -> int:
+    n = c_size()
+    _lib.call("objb_moe_pairs_scratch_bytes", ctypes.byref(layer._c), num_pairs, num_tokens, ctypes.byref(n))
+    return int(n.value)
+
+
+def moe_combine(d_v, slot_row, d_w, d_out, stream=None):
+    """d_out[t] = sum_j d_w[t, j] * d_v[slot_row[t, j]] in slot order."""
+    T, K = slot_row.shape
+    _lib.call("objb_moe_combine_device", _dev_ptr(d_v), d_v.shape[0], _dev_ptr(slot_row), _dev_ptr(d_w), T, K,
+              d_v.shape[1], _dev_ptr(d_out), _lib.stream_handle(stream))
+    return d_out
+
+
+@dataclass
+class DispatchPlan:
+    """Where every (token, slot) of every rank goes, computed identically on
+    all ranks from the all-gathered routing table ``ids_all`` [G, T, k].
+
+    Buffers, all grouped by peer rank in ascending order:
+
+    * x send: this rank's tokens that need rank r (ascending token index);
+    * x recv: rank s's tokens that need this rank (ascending);
+    * v send: one row per pair computed here, ordered (source rank, token,
+      slot); pairs are *computed* in expert order (``pair_*`` arrays) and
+      written to ``pair_out``;
+    * v recv: this rank's (token, slot) outputs, ordered (owner rank, token,
+      slot); ``slot_row[t, j]`` is the row holding token t's slot j.
+    """
+    world: int
+    rank: int
+    experts_per_rank: int
+    send_idx: np.ndarray          # [sum send_counts] token indices
+    send_counts: list
+    recv_counts: list
+    pair_expert: np.ndarray       # [P] local expert index
+    pair_token: np.ndarray        # [P] row of the x recv buffer
+    pair_out: np.ndarray          # [P] row of the v send buffer
+    v_send_counts: list
+    v_recv_counts: list
+    slot_row: np.ndarray          # [T, k] row of the v recv buffer
+
+    @staticmethod
+    def build(ids_all: np.ndarray, rank: int, world: int, num_experts: int) -> "DispatchPlan":
+        ids_all = np.asarray(ids_all, dtype=np.int64)
+        G, T, K = ids_all.shape
+        if G != world:
+            raise ValueError(f"routing table has {G} ranks, world is {world}")
+        if num_experts % world:
+            raise ValueError(f"num_experts {num_experts} is not divisible by world {world}")
+        if ids_all.size and (ids_all.min() < 0 or ids_all.max() >= num_experts):
+            raise ValueError("expert id out of range in routing table")
+        epr = num_experts // world
+        owner = ids_all // epr                                   # [G, T, K]
+        # needs[s, t, r]: token t of rank s has a slot on rank r
+        needs = np.zeros((G, T, G), dtype=bool)
+        gi, ti, _ = np.indices(owner.shape)
+        needs[gi.ravel(), ti.ravel(), owner.ravel()] = True
+        # x send (mine) and x recv (others' tokens that need me)
+        send_lists = [np.nonzero(needs[rank, :, r])[0] for r in range(G)]
+        send_idx = np.concatenate(send_lists) if send_lists else np.zeros(0, np.int64)
+        send_counts = [int(len(v)) for v in send_lists]
+        recv_lists = [np.nonzero(needs[s, :, rank])[0] for s in range(G)]
+        recv_counts = [int(len(v)) for v in recv_lists]
+        # pairs computed here, in v-send order (source rank, token, slot)
+        pe, pt = [], []
+        v_send_counts = []
+        row0 = 0
+        for s in range(G):
+            pos = {int(t): row0 + i for i, t in enumerate(recv_lists[s])}
+            row0 += len(recv_lists[s])
+            mask = owner[s] == rank                               # [T, K]
+            tt, jj = np.nonzero(mask)                             # row-major: token, then slot
+            pe.append(ids_all[s, tt, jj] - rank * epr)
+            pt.append(np.array([pos[int(t)] for t in tt], dtype=np.int64))
+            v_send_counts.append(int(len(tt)))
+        pe = np.concatenate(pe) if pe else np.zeros(0, np.int64)
+        pt = np.concatenate(pt) if pt else np.zeros(0, np.int64)
+        out_rows = np.arange(len(pe), dtype=np.int64)
+        order = np.argsort(pe, kind="stable")                     # compute grouped by expert
+        # v recv: my (token, slot) outputs grouped by owner rank
+        mine = owner[rank]                                        # [T, K]
+        slot_row = np.zeros((T, K), dtype=np.int64)
+        v_recv_counts = []
+        row = 0
+        for r in range(G):
+            tt, jj = np.nonzero(mine == r)
+            slot_row[tt, jj] = row + np.arange(len(tt))
+            row += len(tt)
+            v_recv_counts.append(int(len(tt)))
+        return DispatchPlan(world=G, rank=rank, experts_per_rank=epr, send_idx=send_idx.astype(np.int64),
+                            send_counts=send_counts, recv_counts=recv_counts,
+                            pair_expert=pe[order].astype(np.int32), pair_token=pt[order].astype(np.int32),
+                            pair_out=out_rows[order].astype(np.int32), v_send_counts=v_send_counts,
+                            v_recv_counts=v_recv_counts, slot_row=slot_row.astype(np.int32))
+
+    @property
+    def num_pairs(self) -> int:
+        return int(self.pair_expert.size)
+
+    def exchange_bytes(self, hidden: int, out_dim: int) -> dict:
+        """Bytes this rank sends to other ranks (dispatch, combine)."""
+        me = self.rank
+        disp = sum(c for r, c in enumerate(self.send_counts) if r != me) * hidden * 4
+        comb = sum(c for s, c in enumerate(self.v_send_counts) if s != me) * out_dim * 4
+        return {"dispatch": disp, "combine": comb}
+
+
+class ExpertParallelMoe:
+    """One MoE layer whose experts are split over the ranks of ``group``.
+
+    ``layer``: this rank's shard, a ``MoeLayer`` holding experts
+    [rank * E / G, (rank + 1) * E / G) in local order.  ``forward(x, ids, w)``
+    takes this rank's T tokens (x [T, H], ids / w [T, k] from the router) and
+    returns their outputs [T, O].  T must be the same on every rank.
+
+    ``compute(plan, x_recv, n_rows) -> v_send`` and ``combine(v_recv, plan,
+    w) -> out`` default to the CUDA library; tests on CPU pass their own."""
+
+    def __init__(self, layer, num_experts: int, top_k: int, rank: int = 0, world: int = 1, group=None,
+                 out_dim: int | None = None, compute=None, combine=None, swiglu_limit: float = 0.0):
+        self.layer = layer
+        self.num_experts = int(num_experts)
+        self.top_k = int(top_k)
+        self.rank, self.world, self.group = int(rank), int(world), group
+        self.out_dim = int(out_dim if out_dim is not None else layer.out_dim)
+        self.swiglu_limit = float(swiglu_limit)
+        self._compute = compute or self._cuda_compute
+        self._combine = combine or self._cuda_combine
+        self.last_plan = None
+
+    # ---- default (CUDA) compute and combine
+    def _cuda_compute(self, plan: DispatchPlan, x_recv, n_rows: int):
+        import torch
+        dev = x_recv.device
+        v = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=dev)
+        if plan.num_pairs == 0:
+            return v
+        meta = torch.from_numpy(np.concatenate([plan.pair_expert, plan.pair_token, plan.pair_out])).pin_memory()
+        meta = meta.to(dev, non_blocking=True)
+        P = plan.num_pairs
+        moe_pairs(self.layer, meta[:P], meta[P:2 * P], x_recv, v, pair_out=meta[2 * P:],
+                  swiglu_limit=self.swiglu_limit, stream=torch.cuda.current_stream(dev))
+        return v
+
+    def _cuda_combine(self, v_recv, plan: DispatchPlan, w):
+        import torch
+        T, K = plan.slot_row.shape
+        out = torch.empty(T, self.out_dim, dtype=torch.float32, device=w.device)
+        slot = torch.from_numpy(plan.slot_row).pin_memory().to(w.device, non_blocking=True)
+        return moe_combine(v_recv, slot, w.contiguous(), out, stream=torch.cuda.current_stream(w.device))
+
+    # ---- the layer
+    def plan(self, ids) -> DispatchPlan:
+        import torch
+        import torch.distributed as dist
+        ids = ids.to(torch.int32).contiguous()
+        if self.world > 1:
+            parts = [torch.empty_like(ids) for _ in range(self.world)]
+            dist.all_gather(parts, ids, group=self.group)
+            ids_all = torch.stack(parts).cpu().numpy()
+        else:
+            ids_all = ids.cpu().numpy()[None]
+        return DispatchPlan.build(ids_all, self.rank, self.world, self.num_experts)
+
+    def forward(self, x, ids, w):
+        import torch
+        import torch.distributed as dist
+        plan = self.plan(ids)
+        self.last_plan = plan
+        H = x.shape[1]
+        if self.world > 1:
+            idx = torch.from_numpy(plan.send_idx).to(x.device)
+            x_send = x.index_select(0, idx)
+            x_recv = torch.empty(sum(plan.recv_counts), H, dtype=x.dtype, device=x.device)
+            dist.all_to_all_single(x_recv, x_send, plan.recv_counts, plan.send_counts, group=self.group)
+        else:
+            # one rank: every token needs rank 0 and arrives in token order
+            x_recv = x
+        v_send = self._compute(plan, x_recv, sum(plan.v_send_counts))
+        if self.world > 1:
+            v_recv = torch.empty(sum(plan.v_recv_counts), self.out_dim, dtype=v_send.dtype, device=v_send.device)
+            dist.all_to_all_single(v_recv, v_send, plan.v_recv_counts, plan.v_send_counts, group=self.group)
+        else:
+            v_recv = v_send
+        return self._combine(v_recv, plan, w)
