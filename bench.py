@@ -273,6 +273,17 @@ def run_ours(args, world, rank, local):
     # ---- e2e through the public host-slice API (QuantBackend.gemv)
     e2e = run_e2e(qb, cases, headline, args, world, rank, dev)
 
+    # ---- MoE configs (reported beside the headline)
+    moe = {}
+    if not args.no_moe:
+        for c in cases:
+            c["copies"] = c["copies"][:1]
+        torch.cuda.empty_cache()
+        msteps = max(3, min(args.steps, 20))
+        moe["c3_q4_stack"] = bench_c3(qb, dev, gen, msteps, args.warmup, peak)
+        moe["c4_fp4_routed"] = bench_c4(dev, gen, msteps, args.warmup, peak)
+        moe["c5_ep_resident"] = bench_c5_resident(qb, dev, gen, world, rank, None, msteps, args.warmup, peak)
+
     result = None
     if rank == 0:
         result = {
@@ -286,7 +297,7 @@ def run_ours(args, world, rank, local):
                        "parallelism": f"replicas x{world} (no exchange)",
                        "l2_defeat": "weights rotated over >= 4x L2 per case",
                        "bytes_per_step": step_bytes, "cuda_graph": True},
-            "roofline": roofline, "cases": case_out, "e2e": e2e,
+            "roofline": roofline, "cases": case_out, "e2e": e2e, "moe": moe,
             "gpu_launches": args.steps * len(headline) * 2,  # x-image prep + GEMV per case
             "clocks": sampler.summary(),
         }
@@ -365,6 +376,217 @@ def cpu_baseline(cases, headline, args):
     return {"value": round(nbytes / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"one pass of the 12 configs[1] GEMVs (full size), row-parallel over {threads} threads, "
                       f"{el:.2f} s", "seconds": round(el, 2)}
+
+
+# ------------------------------------------------------------ MoE configs
+C3 = dict(layers=4, experts=8, top_k=2, hidden=4096, inter=14336)
+C4 = dict(experts=256, top_k=8, hidden=4096, inter=2048)
+C5 = dict(experts=256, top_k=8, hidden=2048, inter=512, tokens=(1, 16, 256), zipf=1.1)
+Q4_EXPERT_BYTES = lambda H, I: 3 * I * (H // 32) * 18                           # gate + up + down
+FP4_EXPERT_BYTES = lambda H, I: 3 * (I * H // 2 + I * H // 32)                   # split weight + E8M0
+
+
+def _graph_time(stream, phases, steps, warmup):
+    """Captures one CUDA graph per phase (each phase enqueues one step on
+    `stream`), replays `warmup` then `steps` steps round-robin; returns the
+    device time of the timed steps (ms, CUDA events on `stream`)."""
+    import torch
+    graphs = []
+    for fn in phases:
+        with torch.cuda.stream(stream):
+            fn()  # outside capture first: workspaces, kernel attributes
+    torch.cuda.synchronize()
+    for fn in phases:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+        graphs.append(g)
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        with torch.cuda.stream(stream):
+            graphs[(warmup + i) % len(graphs)].replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    del graphs
+    return ms
+
+
+def _q4_experts(qb, n, H, I, O, gen, dev):
+    import torch
+    from objeta_b200 import QGemvShape, QuantFormat
+    mats = {"gate": [], "up": [], "down": []}
+    for _ in range(n):
+        for name, (r, c) in (("gate", (I, H)), ("up", (I, H)), ("down", (O, I))):
+            m = torch.randn(r, c, device=dev, generator=gen) * 0.02
+            mats[name].append(qb.quantize_matrix_device(QuantFormat.Q4_0, m, QGemvShape.new(QuantFormat.Q4_0, r, c)))
+            del m
+    return mats
+
+
+def bench_c3(qb, dev, gen, steps, warmup, peak):
+    """4 Q4_0 layers, 8 experts, top-2 (renormalised), H 4096,
+    I 14336, one token; each layer's output is the next layer's input."""
+    import torch
+    from objeta_b200.moe import MoeLayer
+    c = C3
+    H, I, L, E, K = c["hidden"], c["inter"], c["layers"], c["experts"], c["top_k"]
+    layers = []
+    for _ in range(L):
+        m = _q4_experts(qb, E, H, I, H, gen, dev)
+        layers.append(MoeLayer(0, H, I, H, m["gate"], m["up"], m["down"]))
+    S = 8
+    logits = torch.randn(S, L, E, device=dev, generator=gen)
+    x0 = torch.randn(S, H, device=dev, generator=gen)
+    bufs = [torch.empty(H, device=dev) for _ in range(2)]
+    ids = [torch.empty(K, dtype=torch.int32, device=dev) for _ in range(L)]
+    ws = [torch.empty(K, device=dev) for _ in range(L)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def phase(sidx):
+        def fn():
+            x = x0[sidx]
+            for li, layer in enumerate(layers):
+                layer.forward(logits[sidx, li], K, x, renormalize=True, d_out=bufs[li % 2], stream=stream,
+                              ids=ids[li], weights=ws[li])
+                x = bufs[li % 2]
+        return fn
+    ms = _graph_time(stream, [phase(i) for i in range(S)], steps, warmup)
+    per_tok = ms / steps
+    nbytes = L * K * Q4_EXPERT_BYTES(H, I)
+    gbs = nbytes / (per_tok / 1e3) / 1e9
+    del layers
+    torch.cuda.empty_cache()
+    return {"config": "configs[2] Q4_0 MoE stack: 4 layers x top-2 of 8, H 4096, I 14336, 1 token",
+            "tokens_per_s": round(1e3 / per_tok, 1), "us_per_token": round(per_tok * 1e3, 2),
+            "weight_bytes_per_token": nbytes, "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4),
+            "launches_per_token": L * 5, "l2_defeat": "198 MB of experts per layer, 8 routing phases",
+            "steps": steps}
+
+
+def bench_c4(dev, gen, steps, warmup, peak):
+    """configs[3] routed part: 256 split-FP4 experts (codes uniform, E8M0
+    scales 2^-8..2^-4), H 4096, I 2048, router top-8 (renormalised), one
+    token."""
+    import torch
+    from objeta_b200.moe import MoeLayer
+    c = C4
+    H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
+    t = {n: [] for n in ("gw", "gs", "uw", "us", "dw", "ds")}
+    for _ in range(E):
+        for wn, sn, r, cc in (("gw", "gs", I, H), ("uw", "us", I, H), ("dw", "ds", H, I)):
+            t[wn].append(torch.randint(0, 256, (r * cc // 2,), device=dev, dtype=torch.uint8, generator=gen))
+            t[sn].append(torch.randint(119, 124, (r * cc // 32,), device=dev, dtype=torch.uint8, generator=gen))
+    layer = MoeLayer(3, H, I, H, t["gw"], t["uw"], t["dw"], t["gs"], t["us"], t["ds"])
+    S = 8
+    logits = torch.randn(S, E, device=dev, generator=gen)
+    x0 = torch.randn(S, H, device=dev, generator=gen)
+    out = torch.empty(H, device=dev)
+    ids = torch.empty(K, dtype=torch.int32, device=dev)
+    ws = torch.empty(K, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def phase(sidx):
+        return lambda: layer.forward(logits[sidx], K, x0[sidx], renormalize=True, d_out=out, stream=stream,
+                                     ids=ids, weights=ws)
+    ms = _graph_time(stream, [phase(i) for i in range(S)], steps, warmup)
+    per_tok = ms / steps
+    nbytes = K * FP4_EXPERT_BYTES(H, I)
+    gbs = nbytes / (per_tok / 1e3) / 1e9
+    del layer, t
+    torch.cuda.empty_cache()
+    return {"config": "configs[3] routed experts: split FP4 E2M1 + E8M0, 256 experts top-8, H 4096, I 2048, "
+                      "1 token (shared bf16 expert not included)",
+            "tokens_per_s": round(1e3 / per_tok, 1), "us_per_token": round(per_tok * 1e3, 2),
+            "weight_bytes_per_token": nbytes, "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4),
+            "launches_per_token": 5, "l2_defeat": "8 routing phases x 107 MB", "steps": steps}
+
+
+def zipf_routes(T, E, K, s, perm, rng):
+    """Top-k expert ids per token drawn from Zipf(s) over the permutation
+    `perm` (rank i -> expert perm[i]), distinct within a token; weights are
+    a softmax of N(0,1) over the k picks."""
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p /= p.sum()
+    ids = np.stack([perm[rng.choice(E, K, replace=False, p=p)] for _ in range(T)]).astype(np.int32)
+    lg = rng.standard_normal((T, K))
+    w = np.exp(lg - lg.max(1, keepdims=True))
+    w = (w / w.sum(1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
+def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
+    """configs[4] expert-parallel layer, all of this rank's experts resident:
+    256 Q4_0 experts block-partitioned over the ranks, H 2048, I 512, top-8
+    Zipf(1.1) routing, T tokens per rank, NCCL all-to-all dispatch/combine."""
+    import torch
+    import torch.distributed as dist
+    from objeta_b200.ep import ExpertParallelMoe
+    from objeta_b200.moe import MoeLayer
+    c = C5
+    H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
+    epr = E // world
+    # every rank builds the same experts from the same seed, keeps its block
+    g = torch.Generator(device=dev).manual_seed(4242)
+    m = _q4_experts(qb, E, H, I, H, g, dev)
+    sl = slice(rank * epr, (rank + 1) * epr)
+    layer = MoeLayer(0, H, I, H, m["gate"][sl], m["up"][sl], m["down"][sl])
+    del m
+    torch.cuda.empty_cache()
+    perm = np.random.default_rng(7).permutation(E)
+    ep = ExpertParallelMoe(layer, E, K, rank=rank, world=world, group=group)
+    res = {}
+    for T in c["tokens"]:
+        rng = np.random.default_rng(1000 * T + rank)
+        S = 4
+        xs = [torch.randn(T, H, device=dev, generator=gen) for _ in range(S)]
+        routes = [zipf_routes(T, E, K, c["zipf"], perm, rng) for _ in range(S)]
+        ids = [torch.from_numpy(r[0]).to(dev) for r in routes]
+        ws = [torch.from_numpy(r[1]).to(dev) for r in routes]
+        n = max(3, min(steps, 10))
+        # bytes each step must move: this rank's distinct experts, and rows
+        # sent to other ranks (from the dispatch plans, outside the timing)
+        plans = [ep.plan(ids[i]) for i in range(S)]
+        uniq = sum(len(np.unique(plans[i % S].pair_expert)) for i in range(n))
+        nvb = sum(sum(plans[i % S].exchange_bytes(H, H).values()) for i in range(n))
+        for i in range(warmup):
+            ep.forward(xs[i % S], ids[i % S], ws[i % S])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(group=group)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(n):
+            ep.forward(xs[i % S], ids[i % S], ws[i % S])
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
+        stats = torch.tensor([ms, uniq * Q4_EXPERT_BYTES(H, I), nvb], dtype=torch.float64, device=dev)
+        if world > 1:
+            mx = stats.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+            dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=group)
+            ms = float(mx[0])
+        per_step = ms / n
+        wbytes = float(stats[1]) / n
+        nv = float(stats[2]) / n
+        gbs = wbytes / (per_step / 1e3) / 1e9
+        res[f"T{T}"] = {"tokens_per_s": round(T * world * 1e3 / per_step, 1), "us_per_step": round(per_step * 1e3, 1),
+                        "unique_expert_bytes_per_step_all_ranks": int(wbytes), "GB/s_all_ranks": round(gbs, 1),
+                        "frac_of_aggregate_hbm": round(gbs / (peak * world), 4),
+                        "nvlink_bytes_per_step_all_ranks": int(nv), "steps": n}
+    del ep, layer
+    torch.cuda.empty_cache()
+    return {"config": f"configs[4] EP layer, experts resident: 256 Q4_0 experts / {world} rank(s), H 2048, I 512, "
+                      "top-8 Zipf(1.1), T tokens per rank",
+            "scaling": "weak (T tokens per rank)", "timer": "CUDA events around whole steps, max over ranks; one rank: "
+            "device-only (sort + pairs + combine); several: host dispatch plan + 2 all-to-alls per step", **res}
 
 
 # --------------------------------------------------------- reference arm
@@ -454,6 +676,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="fmt:RxC, e.g. q4_0:151936x2048 (one GEMV alone)")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE configs reported beside the headline")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")

@@ -126,16 +126,17 @@ int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s,
   OBJB_TRY(workspace_get(device, stream, ximage_quads<RD>(L) * 16, &ws));
   uint4* img = static_cast<uint4*>(ws);
   OBJB_TRY(launch_ximage<RD>(L, x, 0, 1, img, 0, stream));
-  const int nst = (L.rows + L.tstage - 1) / L.tstage;
-  int grid = std::min(nst, props.sm_count);
-  const int st_per_cta = (nst + grid - 1) / grid;
-  grid = (nst + st_per_cta - 1) / st_per_cta;
+  // Rows split evenly over the SMs in whole 4-row batches (a CTA's last
+  // stage may be short), so every SM streams the same number of bytes.
+  int per_cta = (L.rows + props.sm_count - 1) / props.sm_count;
+  per_cta = (per_cta + 3) / 4 * 4;
+  const int grid = (L.rows + per_cta - 1) / per_cta;
   dev::GemvProg prog;
   prog.src = dev::StageSource{w, s, nullptr, nullptr};
   prog.ximg = img;
   prog.y = y;
   prog.rows = L.rows;
-  prog.rows_per_cta = st_per_cta * L.tstage;
+  prog.rows_per_cta = per_cta;
   prog.err = err;
   const size_t smem = pipe_smem_bytes(L);
   auto kernel = dev::pipe_kernel<RD, dev::GemvProg, false>;

@@ -216,7 +216,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     const int total = s.K * s.I;
     const int T = p.lg.tstage;
     int R = (total + props.sm_count - 1) / props.sm_count;
-    R = (R + T - 1) / T * T;
+    R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
     const int grid = (total + R - 1) / R;
     dev::GateUpProg prog;
     prog.t = t;
@@ -241,7 +241,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
   {
     const int T = p.ld.tstage;
     int R = (s.O + props.sm_count - 1) / props.sm_count;
-    R = (R + T - 1) / T * T;
+    R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
     const int grid = (s.O + R - 1) / R;
     dev::DownProg prog;
     prog.t = t;
@@ -306,7 +306,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     const int total = P * s.I;
     const int TS = p.lg.tstage;
     int R = (total + props.sm_count - 1) / props.sm_count;
-    R = (R + TS - 1) / TS * TS;
+    R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
     const int grid = (total + R - 1) / R;
     dev::GateUpPairsProg prog;
     prog.t = t;
@@ -333,7 +333,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     const int total = P * s.O;
     const int TS = p.ld.tstage;
     int R = (total + props.sm_count - 1) / props.sm_count;
-    R = (R + TS - 1) / TS * TS;
+    R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
     const int grid = (total + R - 1) / R;
     dev::DownPairsProg prog;
     prog.t = t;

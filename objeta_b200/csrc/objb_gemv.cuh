@@ -131,6 +131,8 @@ __global__ void __launch_bounds__(256) ximage_f32_kernel(const RowLayout L, cons
                                                          size_t x_stride, int nvec, uint4* __restrict__ img,
                                                          size_t img_stride_quads) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // x may be the output of the kernel this one was launched behind.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int NQ = RD::XRegs::kQuads;
   const int ntp = L.nseg * 32;
   const int total = nvec * ntp * NQ;
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
                                                             size_t x_stride, int nvec, uint4* __restrict__ img,
                                                             size_t img_stride_quads) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // x may be the output of the kernel this one was launched behind.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   using T = Tile<FMT>;
   const int ntp = L.nseg * 32;
   const int nb_img = ntp * T::P;  // blocks covered by the image (incl. idle lanes)
@@ -295,6 +299,10 @@ constexpr int kPipeThreads = (kMaxConsumerWarps + 1) * 32;
 // DUAL streams a second matrix of the same shape through the same stages.
 template <class RD, class Prog, bool DUAL>
 __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L, const Prog prog) {
+  // Let the next launch of the stream (when it was launched with programmatic
+  // serialization: an x-image prep, which waits for this grid before reading
+  // anything) be scheduled now, so its launch and this grid's tail overlap.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const SmemPlan sp = carve_smem(smem_raw, L, 2);
   const int ncw = L.nseg * L.ngrp;

@@ -22,32 +22,9 @@ int ensure_smem_attr(K kernel, int device, size_t bytes) {
 
 // Launches the x-image prep kernel for `nvec` vectors into `img`, then lets
 // the caller launch the consumer kernel with programmatic serialization.
-template <class RD>
-int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int nvec, uint4* img,
-                  size_t img_stride_quads, cudaStream_t stream) {
-  dev::RowLayout dl;
-  std::memcpy(&dl, &L, sizeof(dl));
-  if constexpr (dev::IsDigitRD<RD>::value) {
-    const int warps = L.nseg * 32 * 2 * nvec;
-    const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
-    dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img,
-                                                                                 img_stride_quads);
-  } else {
-    const int n = L.nseg * 32 * RD::XRegs::kQuads * nvec;
-    const int grid = std::max(1, std::min((n + 255) / 256, 2048));
-    dev::ximage_f32_kernel<RD><<<grid, 256, 0, stream>>>(dl, x, x_stride, nvec, img, img_stride_quads);
-  }
-  OBJB_CUDA(cudaGetLastError(), "launch x-image kernel");
-  return OBJB_OK;
-}
-
-template <class RD>
-size_t ximage_quads(const RowLayoutHost& L) {
-  return static_cast<size_t>(RD::XRegs::kQuads) * L.nseg * 32;
-}
-
-// Launches `kernel` with programmatic stream serialization (it may start while
-// the previous kernel in the stream, the x-image prep, is still running).
+// Launches `kernel` with programmatic stream serialization: it may start while
+// the previous kernel in the stream is still running, and must wait
+// (griddepcontrol.wait) before touching anything that kernel produces.
 template <class... KArgs, class... Args>
 int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cudaStream_t stream,
                Args... args) {
@@ -64,6 +41,33 @@ int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cud
   OBJB_CUDA(cudaLaunchKernelEx(&cfg, kernel, args...), "launch pipelined kernel");
   return OBJB_OK;
 }
+
+template <class RD>
+int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int nvec, uint4* img,
+                  size_t img_stride_quads, cudaStream_t stream) {
+  dev::RowLayout dl;
+  std::memcpy(&dl, &L, sizeof(dl));
+  // Launched with programmatic serialization: the kernel waits
+  // (griddepcontrol.wait) for the preceding grid before reading x, so its
+  // launch overlaps that grid's tail.
+  if constexpr (dev::IsDigitRD<RD>::value) {
+    const int warps = L.nseg * 32 * 2 * nvec;
+    const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
+    return launch_pdl(dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt>, grid, 256, 0, stream, dl, x, x_stride,
+                      nvec, img, img_stride_quads);
+  } else {
+    const int n = L.nseg * 32 * RD::XRegs::kQuads * nvec;
+    const int grid = std::max(1, std::min((n + 255) / 256, 2048));
+    return launch_pdl(dev::ximage_f32_kernel<RD>, grid, 256, 0, stream, dl, x, x_stride, nvec, img,
+                      img_stride_quads);
+  }
+}
+
+template <class RD>
+size_t ximage_quads(const RowLayoutHost& L) {
+  return static_cast<size_t>(RD::XRegs::kQuads) * L.nseg * 32;
+}
+
 
 
 }  // namespace objb

@@ -189,10 +189,13 @@ class ExpertParallelMoe:
     returns their outputs [T, O].  T must be the same on every rank.
 
     ``compute(plan, x_recv, n_rows) -> v_send`` and ``combine(v_recv, plan,
-    w) -> out`` default to the CUDA library; tests on CPU pass their own."""
+    w) -> out`` default to the CUDA library; tests on CPU pass their own.
+    With one rank the default path stays on the device (no host round trip);
+    ``plan_on_host=True`` makes it take the multi-rank path instead."""
 
     def __init__(self, layer, num_experts: int, top_k: int, rank: int = 0, world: int = 1, group=None,
-                 out_dim: int | None = None, compute=None, combine=None, swiglu_limit: float = 0.0):
+                 out_dim: int | None = None, compute=None, combine=None, swiglu_limit: float = 0.0,
+                 plan_on_host: bool = False):
         self.layer = layer
         self.num_experts = int(num_experts)
         self.top_k = int(top_k)
@@ -201,7 +204,33 @@ class ExpertParallelMoe:
         self.swiglu_limit = float(swiglu_limit)
         self._compute = compute or self._cuda_compute
         self._combine = combine or self._cuda_combine
+        self._device_only = compute is None and combine is None and not plan_on_host
         self.last_plan = None
+        self._pin = None     # pinned int32 staging for plan arrays (grow-only)
+        self._dmeta = None   # device copy (grow-only)
+        self._slot_cache = {}
+
+    def _stage(self, arrays, dev):
+        """One H2D copy of the int32 plan arrays; returns device views.  The
+        staging buffer is reused: the host sync of the next step's routing
+        table orders the copy before any rewrite."""
+        import torch
+        n = sum(int(a.size) for a in arrays)
+        if self._pin is None or self._pin.numel() < n:
+            cap = max(1024, 1 << (n - 1).bit_length())
+            self._pin = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+            self._dmeta = torch.empty(cap, dtype=torch.int32, device=dev)
+        host = self._pin.numpy()
+        off = 0
+        for a in arrays:
+            host[off:off + a.size] = a.ravel()
+            off += a.size
+        self._dmeta[:n].copy_(self._pin[:n], non_blocking=True)
+        views, off = [], 0
+        for a in arrays:
+            views.append(self._dmeta[off:off + a.size].view(a.shape))
+            off += a.size
+        return views
 
     # ---- default (CUDA) compute and combine
     def _cuda_compute(self, plan: DispatchPlan, x_recv, n_rows: int):
@@ -210,19 +239,44 @@ class ExpertParallelMoe:
         v = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=dev)
         if plan.num_pairs == 0:
             return v
-        meta = torch.from_numpy(np.concatenate([plan.pair_expert, plan.pair_token, plan.pair_out])).pin_memory()
-        meta = meta.to(dev, non_blocking=True)
-        P = plan.num_pairs
-        moe_pairs(self.layer, meta[:P], meta[P:2 * P], x_recv, v, pair_out=meta[2 * P:],
-                  swiglu_limit=self.swiglu_limit, stream=torch.cuda.current_stream(dev))
+        pe, pt, po, slot = self._stage([plan.pair_expert, plan.pair_token, plan.pair_out, plan.slot_row], dev)
+        self._staged_slot = slot
+        moe_pairs(self.layer, pe, pt, x_recv, v, pair_out=po, swiglu_limit=self.swiglu_limit,
+                  stream=torch.cuda.current_stream(dev))
         return v
 
     def _cuda_combine(self, v_recv, plan: DispatchPlan, w):
         import torch
         T, K = plan.slot_row.shape
         out = torch.empty(T, self.out_dim, dtype=torch.float32, device=w.device)
-        slot = torch.from_numpy(plan.slot_row).pin_memory().to(w.device, non_blocking=True)
+        slot = getattr(self, "_staged_slot", None)
+        if slot is None or plan.num_pairs == 0:
+            (slot,) = self._stage([plan.slot_row], w.device)
+        self._staged_slot = None
         return moe_combine(v_recv, slot, w.contiguous(), out, stream=torch.cuda.current_stream(w.device))
+
+    def _forward_one_rank(self, x, ids, w):
+        """World size 1: no host round trip.  Pairs are the (token, slot)
+        entries sorted by expert on the device (stable, so ties keep token
+        order); pair p's output goes to row t * k + j, which the combine
+        reads in slot order."""
+        import torch
+        T, K = ids.shape
+        flat = ids.reshape(-1).to(torch.int32)
+        key = (T, K, x.device)
+        if key not in self._slot_cache:
+            self._slot_cache[key] = torch.arange(T * K, dtype=torch.int32, device=x.device).view(T, K)
+        slot = self._slot_cache[key]
+        _, perm = torch.sort(flat, stable=True)
+        perm = perm.to(torch.int32)
+        pair_expert = flat.index_select(0, perm)
+        pair_token = torch.div(perm, K, rounding_mode="floor").to(torch.int32)
+        stream = torch.cuda.current_stream(x.device)
+        v = torch.empty(T * K, self.out_dim, dtype=torch.float32, device=x.device)
+        moe_pairs(self.layer, pair_expert, pair_token, x.contiguous(), v, pair_out=perm,
+                  swiglu_limit=self.swiglu_limit, stream=stream)
+        out = torch.empty(T, self.out_dim, dtype=torch.float32, device=x.device)
+        return moe_combine(v, slot, w.contiguous(), out, stream=stream)
 
     # ---- the layer
     def plan(self, ids) -> DispatchPlan:
@@ -240,6 +294,9 @@ class ExpertParallelMoe:
     def forward(self, x, ids, w):
         import torch
         import torch.distributed as dist
+        if self.world == 1 and self._device_only:
+            self.last_plan = None
+            return self._forward_one_rank(x, ids, w)
         plan = self.plan(ids)
         self.last_plan = plan
         H = x.shape[1]

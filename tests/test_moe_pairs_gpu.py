@@ -188,10 +188,13 @@ def test_ep_single_rank_matches_fused(cuda_device):
     ids, ws = _routes(T, E, K, seed=6)
     x = torch.randn(T, H, device="cuda")
     di, dw = torch.from_numpy(ids).cuda(), torch.from_numpy(ws).cuda()
-    ep = ExpertParallelMoe(layer, E, K)
-    got = ep.forward(x, di, dw)
-    torch.cuda.synchronize()
-    assert _bits_equal(got, _fused_per_token(layer, x, di, dw))
+    ref = _fused_per_token(layer, x, di, dw)
+    for host in (False, True):  # device-only one-rank path, and the multi-rank (host plan) path
+        ep = ExpertParallelMoe(layer, E, K, plan_on_host=host)
+        for _ in range(2):
+            got = ep.forward(x, di, dw)
+            torch.cuda.synchronize()
+            assert _bits_equal(got, ref)
 
 
 # ------------------------------------------------------------ two ranks
