@@ -190,12 +190,13 @@ def run_ours(args, world, rank, local):
         launch_step(0, cases)
     torch.cuda.synchronize()
 
-    def build_graphs(clist):
+    def build_graphs(clist, events=True):
         period = max(len(c["copies"]) for c in clist)
         gs, es = [], []
         for p in range(period):
             g = torch.cuda.CUDAGraph()
-            evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2 * len(clist))]
+            evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(2 * len(clist))] \
+                if events else None
             with torch.cuda.graph(g, stream=stream):
                 launch_step(p, clist, evs)
             gs.append(g)
@@ -228,17 +229,25 @@ def run_ours(args, world, rank, local):
         # each phase's events hold its last replay; average over phases used
         used = sorted({(warmup + s) % period for s in range(steps)})
         for p in used:
+            if es[p] is None:
+                continue
             for i in range(len(clist)):
                 per[i] += es[p][2 * i].elapsed_time(es[p][2 * i + 1]) / len(used)
         if world > 1:
             dist.barrier()
         return t0.elapsed_time(t1), per
 
+    # The headline times the sweep as a caller runs it: back to back, no
+    # instrumentation between the GEMVs.  Per-case times (and the roofline of
+    # the dominant case) come from a second set of graphs with an event pair
+    # around every GEMV.
+    plain, _ = build_graphs(headline, events=False)
     graphs, graph_events = build_graphs(headline)
     xgraphs, xevents = build_graphs(extra)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
-    elapsed, per_head = timed(graphs, graph_events, headline, args.steps, args.warmup, sampler)
+    elapsed, _ = timed(plain, [None] * len(plain), headline, args.steps, args.warmup, sampler)
+    _, per_head = timed(graphs, graph_events, headline, max(3, min(args.steps, 10)), 3)
     _, per_extra = timed(xgraphs, xevents, extra, max(3, min(args.steps, 10)), 3)
     if world > 1:
         t = torch.tensor([elapsed], device=dev)
@@ -281,7 +290,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
         msteps = max(3, min(args.steps, 20))
         moe["c3_q4_stack"] = bench_c3(qb, dev, gen, msteps, args.warmup, peak)
-        moe["c4_fp4_routed"] = bench_c4(dev, gen, msteps, args.warmup, peak)
+        moe["c4_fp4_shared"] = bench_c4(dev, gen, msteps, args.warmup, peak)
         moe["c5_ep_resident"] = bench_c5_resident(qb, dev, gen, world, rank, None, msteps, args.warmup, peak)
 
     result = None
@@ -296,7 +305,8 @@ def run_ours(args, world, rank, local):
                        "shapes": [f"{r}x{c}" for r, c in SHAPES], "global_batch": 1 * world,
                        "parallelism": f"replicas x{world} (no exchange)",
                        "l2_defeat": "weights rotated over >= 4x L2 per case",
-                       "bytes_per_step": step_bytes, "cuda_graph": True},
+                       "bytes_per_step": step_bytes, "cuda_graph": True,
+                       "timing": "headline: graph replays of the 12 GEMVs back to back; per case: event pairs"},
             "roofline": roofline, "cases": case_out, "e2e": e2e, "moe": moe,
             "gpu_launches": args.steps * len(headline) * 2,  # x-image prep + GEMV per case
             "clocks": sampler.summary(),
@@ -305,7 +315,7 @@ def run_ours(args, world, rank, local):
         result["cpu_baseline"] = cb
     if world > 1:
         dist.barrier()
-        del graphs, xgraphs
+        del graphs, xgraphs, plain
         dist.destroy_process_group()
     return result
 
@@ -470,11 +480,11 @@ def bench_c3(qb, dev, gen, steps, warmup, peak):
 
 
 def bench_c4(dev, gen, steps, warmup, peak):
-    """configs[3] routed part: 256 split-FP4 experts (codes uniform, E8M0
-    scales 2^-8..2^-4), H 4096, I 2048, router top-8 (renormalised), one
-    token."""
+    """256 split-FP4 experts (codes uniform, E8M0 scales
+    2^-8..2^-4), H 4096, I 2048, router top-8 (renormalised), plus one bf16
+    shared expert added onto the routed output; one token."""
     import torch
-    from objeta_b200.moe import MoeLayer
+    from objeta_b200.moe import MoeLayer, ffn_bf16_device
     c = C4
     H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
     t = {n: [] for n in ("gw", "gs", "uw", "us", "dw", "ds")}
@@ -483,6 +493,9 @@ def bench_c4(dev, gen, steps, warmup, peak):
             t[wn].append(torch.randint(0, 256, (r * cc // 2,), device=dev, dtype=torch.uint8, generator=gen))
             t[sn].append(torch.randint(119, 124, (r * cc // 32,), device=dev, dtype=torch.uint8, generator=gen))
     layer = MoeLayer(3, H, I, H, t["gw"], t["uw"], t["dw"], t["gs"], t["us"], t["ds"])
+    # the shared expert: bf16 ~ N(0, 0.02^2), added onto the routed output
+    sh = [(torch.randn(r, cc, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+          for r, cc in ((I, H), (I, H), (H, I))]
     S = 8
     logits = torch.randn(S, E, device=dev, generator=gen)
     x0 = torch.randn(S, H, device=dev, generator=gen)
@@ -492,19 +505,22 @@ def bench_c4(dev, gen, steps, warmup, peak):
     stream = torch.cuda.Stream(device=dev)
 
     def phase(sidx):
-        return lambda: layer.forward(logits[sidx], K, x0[sidx], renormalize=True, d_out=out, stream=stream,
-                                     ids=ids, weights=ws)
+        def fn():
+            layer.forward(logits[sidx], K, x0[sidx], renormalize=True, d_out=out, stream=stream, ids=ids,
+                          weights=ws)
+            ffn_bf16_device(sh[0], sh[1], sh[2], H, I, H, x0[sidx], out, accumulate=True, stream=stream)
+        return fn
     ms = _graph_time(stream, [phase(i) for i in range(S)], steps, warmup)
     per_tok = ms / steps
-    nbytes = K * FP4_EXPERT_BYTES(H, I)
+    nbytes = K * FP4_EXPERT_BYTES(H, I) + 3 * I * H * 2
     gbs = nbytes / (per_tok / 1e3) / 1e9
     del layer, t
     torch.cuda.empty_cache()
-    return {"config": "configs[3] routed experts: split FP4 E2M1 + E8M0, 256 experts top-8, H 4096, I 2048, "
-                      "1 token (shared bf16 expert not included)",
+    return {"config": "configs[3]: 256 split FP4 E2M1 + E8M0 experts top-8 plus 1 bf16 shared expert, H 4096, "
+                      "I 2048, 1 token (out = routed combine + shared)",
             "tokens_per_s": round(1e3 / per_tok, 1), "us_per_token": round(per_tok * 1e3, 2),
             "weight_bytes_per_token": nbytes, "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4),
-            "launches_per_token": 5, "l2_defeat": "8 routing phases x 107 MB", "steps": steps}
+            "launches_per_token": 9, "l2_defeat": "8 routing phases x 107 MB routed + 50 MB shared", "steps": steps}
 
 
 def zipf_routes(T, E, K, s, perm, rng):
@@ -554,19 +570,23 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
         plans = [ep.plan(ids[i]) for i in range(S)]
         uniq = sum(len(np.unique(plans[i % S].pair_expert)) for i in range(n))
         nvb = sum(sum(plans[i % S].exchange_bytes(H, H).values()) for i in range(n))
-        for i in range(warmup):
-            ep.forward(xs[i % S], ids[i % S], ws[i % S])
-        torch.cuda.synchronize()
-        if world > 1:
+        if world == 1:
+            # one rank: the step has no host round trip, so it is captured
+            stream = torch.cuda.Stream(device=dev)
+            ms = _graph_time(stream, [(lambda i=i: ep.forward(xs[i], ids[i], ws[i])) for i in range(S)], n, warmup)
+        else:
+            for i in range(warmup):
+                ep.forward(xs[i % S], ids[i % S], ws[i % S])
+            torch.cuda.synchronize()
             dist.barrier(group=group)
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for i in range(n):
-            ep.forward(xs[i % S], ids[i % S], ws[i % S])
-        t1.record()
-        torch.cuda.synchronize()
-        ms = t0.elapsed_time(t1)
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for i in range(n):
+                ep.forward(xs[i % S], ids[i % S], ws[i % S])
+            t1.record()
+            torch.cuda.synchronize()
+            ms = t0.elapsed_time(t1)
         stats = torch.tensor([ms, uniq * Q4_EXPERT_BYTES(H, I), nvb], dtype=torch.float64, device=dev)
         if world > 1:
             mx = stats.clone()
@@ -586,7 +606,8 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
     return {"config": f"configs[4] EP layer, experts resident: 256 Q4_0 experts / {world} rank(s), H 2048, I 512, "
                       "top-8 Zipf(1.1), T tokens per rank",
             "scaling": "weak (T tokens per rank)", "timer": "CUDA events around whole steps, max over ranks; one rank: "
-            "device-only (sort + pairs + combine); several: host dispatch plan + 2 all-to-alls per step", **res}
+            "device-only step (sort + pairs + combine) replayed as CUDA graphs; several: host dispatch plan + "
+            "2 NCCL all-to-alls per step", **res}
 
 
 # --------------------------------------------------------- reference arm

@@ -159,6 +159,22 @@ int objb_gemv_fp4_split_device(const void *d_weight, const void *d_scale,
                                const float *d_x, float *d_y, size_t rows,
                                size_t cols, objb_stream_t stream);
 
+/* Dense bf16 GEMV (no QuantFormat in the reference; the shared expert of a
+ * DeepSeek-style layer): y[rows] = W x with W bf16 [rows, cols] row-major,
+ * widened to f32 as the reference's bf16 conversion does (objeta-parser
+ * lib.rs:334-337), f32 accumulation.  cols must be a multiple of 32. */
+int objb_gemv_bf16_device(const void *d_w, const float *d_x, float *d_y, size_t rows,
+                          size_t cols, objb_stream_t stream);
+
+/* One dense SwiGLU FFN in bf16 (the shared expert): act = SwiGLU(gate x,
+ * up x) as silu_mul computes it (moe.cu:2-22), v = down act; d_out = v, or
+ * d_out += v when accumulate is nonzero (routed output + shared output).
+ * gate / up are [intermediate, hidden], down [out_dim, intermediate]. */
+int objb_ffn_bf16_device(const void *d_gate, const void *d_up, const void *d_down,
+                         size_t hidden, size_t intermediate, size_t out_dim,
+                         const float *d_x, float *d_out, int accumulate, float swiglu_limit,
+                         objb_stream_t stream);
+
 /* quantize_matrix_cpu (quant.rs:506-581) on the device: packs a dense f32
  * [rows, cols] matrix into the format's blocks, byte-identical to the
  * reference CPU packers (q4/q5/iq3/fp4_quantize_block, quant.rs:814-926). */

@@ -87,6 +87,9 @@ _SIGS = {
     "objb_gemv_device": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_size, c_size, c_void_p]),
     "objb_gemv_fp4_split_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size, c_size,
                                            c_void_p]),
+    "objb_gemv_bf16_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_void_p]),
+    "objb_ffn_bf16_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p, c_void_p,
+                                     c_int, ctypes.c_float, c_void_p]),
     "objb_quantize_matrix_device": (c_int, [c_int, c_void_p, c_size, c_size, c_void_p, c_void_p]),
     "objb_fp4_decode_split_device": (c_int, [c_void_p, c_void_p, c_size, c_size, c_void_p, c_void_p]),
 }

@@ -112,6 +112,42 @@ struct RowDotSplitFp4 {
   }
 };
 
+// Dense bf16 rows (the shared expert of a DeepSeek-style layer; not a
+// reference QuantFormat).  A lane reads 16-byte chunks (8 columns) c0 + 32 i,
+// i < 8, so consecutive lanes read consecutive chunks (conflict-free 128-bit
+// shared loads); its 64 x values are the matching columns, as float pairs.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+struct RowDotBf16 {
+  using XRegs = Words<16>;
+  int c0, nchunks;
+  __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
+    c0 = seg * 256 + lane;
+    nchunks = L.cols / 8;
+  }
+  __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
+    const int c = (lt / 32) * 256 + (q / 2) * 32 + lt % 32;
+    return c < L.cols / 8 ? c * 8 + 4 * (q % 2) : -1;
+  }
+  __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t*, const XRegs& xr) const {
+    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = c0 + 32 * i;
+      if (c < nchunks) {
+        const uint4 v = *reinterpret_cast<const uint4*>(wrow + 16 * c);
+        a0 = __ffma2_rn(bf16x2_to_float2(v.x), xr.f2(4 * i + 0), a0);
+        a1 = __ffma2_rn(bf16x2_to_float2(v.y), xr.f2(4 * i + 1), a1);
+        a0 = __ffma2_rn(bf16x2_to_float2(v.z), xr.f2(4 * i + 2), a0);
+        a1 = __ffma2_rn(bf16x2_to_float2(v.w), xr.f2(4 * i + 3), a1);
+      }
+    }
+    return (a0.x + a0.y) + (a1.x + a1.y);
+  }
+};
+
 template <class XR>
 __device__ __forceinline__ void load_ximage(const uint4* __restrict__ img, int ntp, int lt, XR& xr) {
 #pragma unroll

@@ -226,7 +226,7 @@ struct DownPairsProg {
 // Weighted top-k combine of pair outputs, per token in slot order, with the
 // arithmetic of the fused single-token combine (out = 0; out += w * down):
 // out[t][i] = (((w0 * v[r0][i]) + w1 * v[r1][i]) + ...).  grid (ceil(O/256), T).
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ v, const int32_t* __restrict__ slot_row,
+static __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ v, const int32_t* __restrict__ slot_row,
                                                       const float* __restrict__ w, int K, int O, int v_rows,
                                                       float* __restrict__ out, unsigned* err) {
   const int t = blockIdx.y;
@@ -241,13 +241,61 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   out[static_cast<size_t>(t) * O + i] = acc;
 }
 
+// ---- one dense SwiGLU FFN (the shared expert): gate/up rows with SwiGLU in
+// the epilogue, then down rows, optionally added onto out (routed + shared).
+struct FfnGateUpProg {
+  StageSource src;  // wa = gate, wb = up
+  const uint4* ximg;
+  float* act;
+  int I;
+  int rows_per_cta;
+  float swiglu_limit;
+  unsigned* err;
+  __device__ __forceinline__ int njobs(int cta) const { return cta * rows_per_cta < I ? 1 : 0; }
+  __device__ __forceinline__ Job job(int cta, int) const {
+    Job J;
+    J.src = src;
+    J.ximg = ximg;
+    J.row_begin = cta * rows_per_cta;
+    J.row_end = min(I, J.row_begin + rows_per_cta);
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int, int, int row, float va, float vb) const {
+    act[row] = swiglu(va, vb, swiglu_limit);
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
+struct FfnDownProg {
+  StageSource src;  // wa = down
+  const uint4* ximg;
+  float* out;
+  int O;
+  int rows_per_cta;
+  int accumulate;
+  unsigned* err;
+  __device__ __forceinline__ int njobs(int cta) const { return cta * rows_per_cta < O ? 1 : 0; }
+  __device__ __forceinline__ Job job(int cta, int) const {
+    Job J;
+    J.src = src;
+    J.ximg = ximg;
+    J.row_begin = cta * rows_per_cta;
+    J.row_end = min(O, J.row_begin + rows_per_cta);
+    return J;
+  }
+  __device__ __forceinline__ void epilogue(int, int, int row, float va, float) const {
+    out[row] = accumulate ? __fadd_rn(out[row], va) : va;
+  }
+  __device__ __forceinline__ void finalize(int, int, int) const {}
+};
+
 // Router (crates/objeta-cuda/src/bin/deepseek_single_layer_moe.rs:720-740):
 // max-subtracted softmax, then the first top_k of a stable descending sort
 // (ties keep the lower expert index); optional renormalisation of the kept
 // weights by their sequential sum.  One CTA; the sequential f32 sum of the
 // reference is kept (thread 0 sums in expert order).  exp is evaluated in
 // double precision and rounded to f32.
-__global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int n, int top_k,
+static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int n, int top_k,
                                                            int renorm, int32_t* __restrict__ ids,
                                                            float* __restrict__ weights) {
   // CTA b routes token b (logits row b, ids / weights row b).
@@ -298,13 +346,13 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restri
 
 // Elementwise kernels of the generic (unaligned-shape) MoE path, same
 // arithmetic as silu_mul / weighted_accum (moe.cu:2-34).
-__global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+static __global__ void silu_mul_kernel(const float* __restrict__ gate, const float* __restrict__ up,
                                 float* __restrict__ act, int n, float limit) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) act[i] = swiglu(gate[i], up[i], limit);
 }
 
-__global__ void weighted_accum_kernel(const float* __restrict__ down, float* __restrict__ out,
+static __global__ void weighted_accum_kernel(const float* __restrict__ down, float* __restrict__ out,
                                       const float* __restrict__ weights, int k, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = __fadd_rn(k == 0 ? 0.0f : out[i], __fmul_rn(weights[k], down[i]));

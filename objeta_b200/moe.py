@@ -440,6 +440,16 @@ def router_topk(d_logits, top_k: int, renormalize: bool = False, stream=None, id
     return ids, weights
 
 
+def ffn_bf16_device(d_gate, d_up, d_down, hidden: int, intermediate: int, out_dim: int, d_x, d_out,
+                    accumulate: bool = False, swiglu_limit: float = 0.0, stream=None):
+    """The dense bf16 SwiGLU FFN (a DeepSeek-style shared expert):
+    d_out = down(SwiGLU(gate x, up x)), or d_out += it with ``accumulate``."""
+    _lib.call("objb_ffn_bf16_device", _dev_ptr(d_gate), _dev_ptr(d_up), _dev_ptr(d_down), hidden, intermediate,
+              out_dim, _dev_ptr(d_x), _dev_ptr(d_out), int(bool(accumulate)), float(swiglu_limit),
+              _lib.stream_handle(stream))
+    return d_out
+
+
 class MoeLayer:
     """A MoE layer resident on the device (objb_moe_layer).
 

@@ -241,6 +241,13 @@ def gemv_device(fmt, d_qweights, d_x, d_y, rows, cols, stream=None):
               _dev_ptr(d_y), rows, cols, _lib.stream_handle(stream))
 
 
+def gemv_bf16_device(d_w, d_x, d_y, rows, cols, stream=None):
+    """objb_gemv_bf16_device: dense bf16 weights (any 16-bit tensor holding
+    bf16 bits) times f32 x."""
+    _lib.call("objb_gemv_bf16_device", _dev_ptr(d_w), _dev_ptr(d_x), _dev_ptr(d_y), rows, cols,
+              _lib.stream_handle(stream))
+
+
 def gemv_fp4_split_device(d_weight, d_scale, d_x, d_y, rows, cols, stream=None):
     _lib.call("objb_gemv_fp4_split_device", _dev_ptr(d_weight), _dev_ptr(d_scale), _dev_ptr(d_x),
               _dev_ptr(d_y), rows, cols, _lib.stream_handle(stream))
