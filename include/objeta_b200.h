@@ -466,6 +466,23 @@ int objb_moe_execute_selected_native_fp4(objb_moe_executor *ex, objb_stream_t st
                                          size_t layer_id, objb_expert_cache *cache, float *out,
                                          objb_moe_telemetry *telemetry);
 
+/* Multi-token form of objb_moe_execute_selected (no reference counterpart:
+ * the reference runs one token per call) on device activations: num_pairs
+ * (expert, token) pairs given as host int32 arrays (pair_out may be NULL:
+ * row p), d_x [num_tokens][hidden] and d_v [v_rows][out_dim] on the device.
+ * Each distinct expert among the pairs is resolved once, in order of first
+ * appearance, with the reference executor's admission rules (moe.rs:483-583:
+ * oversized-expert bypass or self-eviction risk, then get / insert per
+ * tensor); then all pairs run as one objb_moe_pairs_device launch sequence.
+ * Telemetry counts each distinct expert once.  Synchronises `stream`. */
+int objb_moe_execute_pairs(objb_moe_executor *ex, objb_stream_t stream, int fmt,
+                           const objb_expert_weights *experts, size_t num_experts,
+                           const int32_t *pair_expert, const int32_t *pair_token,
+                           const int32_t *pair_out, size_t num_pairs, const float *d_x,
+                           size_t num_tokens, size_t hidden, size_t intermediate,
+                           size_t out_dim, size_t layer_id, objb_expert_cache *cache,
+                           float *d_v, size_t v_rows, objb_moe_telemetry *tel);
+
 #ifdef __cplusplus
 }
 #endif

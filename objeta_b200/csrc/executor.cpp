@@ -97,6 +97,79 @@ int fail_len(const char* what, size_t got, size_t want) {
                    std::string(what) + " len " + std::to_string(got) + " != expected " + std::to_string(want));
 }
 
+// Byte accounting and per-call uploads of one executor call.
+struct Resolved {
+  size_t weight_loaded = 0, weight_reused = 0, scale_loaded = 0, scale_reused = 0;
+  size_t bytes_gate = 0, bytes_up = 0, bytes_down = 0;
+  std::vector<void*> transients;  // bypassed tensors, freed after the call
+};
+
+// Resolves the 3 (or 6) tensors of expert `expert_id` to device pointers the
+// way the reference executor does (moe.rs:483-583): an expert larger than the
+// whole cache is either bypassed (uploaded for this call only) or counted as
+// a self-eviction risk; each tensor is then looked up (hit: reused bytes) or
+// inserted (miss: loaded bytes).  Without a cache every tensor is uploaded.
+int resolve_expert(objb_expert_cache* cache, cudaStream_t stream, int fmt, bool split, size_t layer_id,
+                   size_t expert_id, const TensorRef* t, const void** ptrs, Resolved* r) {
+  const int ntens = split ? 6 : 3;
+  size_t expert_bytes = 0;
+  for (int i = 0; i < ntens; ++i) expert_bytes += t[i].len;
+  // bytes_by_tensor_kind: gate / up / down (weight + scale for FP4)
+  if (split) {
+    r->bytes_gate += t[0].len + t[1].len;
+    r->bytes_up += t[2].len + t[3].len;
+    r->bytes_down += t[4].len + t[5].len;
+  } else {
+    r->bytes_gate += t[0].len;
+    r->bytes_up += t[1].len;
+    r->bytes_down += t[2].len;
+  }
+  bool bypass = false;
+  if (cache) {
+    std::lock_guard<std::mutex> lk(cache->mu);
+    if (expert_bytes > cache->st.capacity_bytes) {  // moe.rs:483-494
+      if (cache->st.bypass_oversized_experts) {
+        bypass = true;
+        cache->st.oversized_expert_bypass_count += 1;
+      } else {
+        cache->st.self_eviction_risk_count += 1;
+      }
+    }
+  }
+  int rc = OBJB_OK;
+  for (int i = 0; i < ntens && rc == OBJB_OK; ++i) {
+    size_t& loaded = t[i].is_scale ? r->scale_loaded : r->weight_loaded;
+    size_t& reused = t[i].is_scale ? r->scale_reused : r->weight_reused;
+    const void* dp = nullptr;
+    if (cache && !bypass) {
+      std::lock_guard<std::mutex> lk(cache->mu);
+      objb_expert_cache_key key{layer_id, expert_id, t[i].kind, fmt};
+      rc = cache_get(cache, &key, &dp);
+      if (rc == OBJB_OK && dp) {
+        reused += t[i].len;
+      } else if (rc == OBJB_OK) {
+        loaded += t[i].len;
+        rc = cache_insert(cache, &key, t[i].host, t[i].len, stream, &dp, nullptr);
+      }
+    } else {
+      if (cache) {  // bypassed expert: counted as a bypassed insert per tensor
+        std::lock_guard<std::mutex> lk(cache->mu);
+        cache->st.cache_insert_attempt_count += 1;
+        cache->st.cache_insert_bypass_count += 1;
+      }
+      void* p = nullptr;
+      cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(t[i].len, 16), stream);
+      if (e == cudaSuccess && t[i].len) e = cudaMemcpyAsync(p, t[i].host, t[i].len, cudaMemcpyHostToDevice, stream);
+      if (e != cudaSuccess) rc = cuda_status(e, "upload expert tensor", __FILE__, __LINE__);
+      if (p) r->transients.push_back(p);
+      loaded += t[i].len;
+      dp = p;
+    }
+    ptrs[i] = dp;
+  }
+  return rc;
+}
+
 // The shared body of execute_selected_moe_cuda / _native_fp4_cuda.
 // tensors_of(k) fills the 3 (or 6) TensorRefs of selected expert k; the
 // device tables get one entry per selected slot.
@@ -116,72 +189,25 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
   OBJB_TRY(grow_dev(&ex->d_out, &ex->d_out_cap, out_dim * 4, "allocate device out"));
   OBJB_CUDA(cudaMemcpyAsync(ex->d_x, x, hidden * 4, cudaMemcpyHostToDevice, stream), "copy x to device");
 
-  size_t weight_loaded = 0, weight_reused = 0, scale_loaded = 0, scale_reused = 0;
-  size_t bytes_gate = 0, bytes_up = 0, bytes_down = 0;
+  Resolved res;
   std::vector<const void*> ptrs(K * ntens, nullptr);
-  std::vector<void*> transients;
   std::set<int64_t> unique;
   int rc = OBJB_OK;
   for (size_t k = 0; k < K && rc == OBJB_OK; ++k) {
     TensorRef t[6];
     tensors_of(k, t);
     unique.insert(sel_ids[k]);
-    size_t expert_bytes = 0;
-    for (int i = 0; i < ntens; ++i) expert_bytes += t[i].len;
-    // bytes_by_tensor_kind: gate / up / down (weight + scale for FP4)
-    if (split) {
-      bytes_gate += t[0].len + t[1].len;
-      bytes_up += t[2].len + t[3].len;
-      bytes_down += t[4].len + t[5].len;
-    } else {
-      bytes_gate += t[0].len;
-      bytes_up += t[1].len;
-      bytes_down += t[2].len;
-    }
-    bool bypass = false;
-    if (cache) {
-      std::lock_guard<std::mutex> lk(cache->mu);
-      if (expert_bytes > cache->st.capacity_bytes) {  // moe.rs:483-494
-        if (cache->st.bypass_oversized_experts) {
-          bypass = true;
-          cache->st.oversized_expert_bypass_count += 1;
-        } else {
-          cache->st.self_eviction_risk_count += 1;
-        }
-      }
-    }
-    for (int i = 0; i < ntens && rc == OBJB_OK; ++i) {
-      size_t& loaded = t[i].is_scale ? scale_loaded : weight_loaded;
-      size_t& reused = t[i].is_scale ? scale_reused : weight_reused;
-      const void* dp = nullptr;
-      if (cache && !bypass) {
-        std::lock_guard<std::mutex> lk(cache->mu);
-        objb_expert_cache_key key{layer_id, static_cast<size_t>(sel_ids[k]), t[i].kind, fmt};
-        rc = cache_get(cache, &key, &dp);
-        if (rc == OBJB_OK && dp) {
-          reused += t[i].len;
-        } else if (rc == OBJB_OK) {
-          loaded += t[i].len;
-          rc = cache_insert(cache, &key, t[i].host, t[i].len, stream, &dp, nullptr);
-        }
-      } else {
-        if (cache) {  // bypassed expert: counted as a bypassed insert per tensor
-          std::lock_guard<std::mutex> lk(cache->mu);
-          cache->st.cache_insert_attempt_count += 1;
-          cache->st.cache_insert_bypass_count += 1;
-        }
-        void* p = nullptr;
-        cudaError_t e = cudaMallocAsync(&p, std::max<size_t>(t[i].len, 16), stream);
-        if (e == cudaSuccess && t[i].len)
-          e = cudaMemcpyAsync(p, t[i].host, t[i].len, cudaMemcpyHostToDevice, stream);
-        if (e != cudaSuccess) rc = cuda_status(e, "upload expert tensor", __FILE__, __LINE__);
-        if (p) transients.push_back(p);
-        loaded += t[i].len;
-        dp = p;
-      }
-      ptrs[k * ntens + i] = dp;
-    }
+    rc = resolve_expert(cache, stream, fmt, split, layer_id, static_cast<size_t>(sel_ids[k]), t, &ptrs[k * ntens],
+                        &res);
   }
+  size_t& weight_loaded = res.weight_loaded;
+  size_t& weight_reused = res.weight_reused;
+  size_t& scale_loaded = res.scale_loaded;
+  size_t& scale_reused = res.scale_reused;
+  size_t& bytes_gate = res.bytes_gate;
+  size_t& bytes_up = res.bytes_up;
+  size_t& bytes_down = res.bytes_down;
+  std::vector<void*>& transients = res.transients;
   if (rc == OBJB_OK) rc = cudaEventRecord(ev[2], stream) == cudaSuccess ? OBJB_OK : OBJB_FAIL(OBJB_ERR_RUNTIME, "record h2d stop", "cudaEventRecord failed");
 
   // Device tables: one entry per selected slot; ids are the slots themselves.
@@ -321,6 +347,149 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
   return OBJB_OK;
 }
 
+// Multi-token form: the distinct experts of a pair list are resolved once
+// each (first-appearance order), then every pair runs in one pair launch
+// sequence; x and v stay on the device.  Ends with a stream synchronize like
+// the single-token call (the pinned staging block is reused by the next call).
+int execute_pairs(objb_moe_executor* ex, cudaStream_t stream, int fmt, const objb_expert_weights* experts,
+                  size_t num_experts, const int32_t* pair_expert, const int32_t* pair_token, const int32_t* pair_out,
+                  size_t P, const float* d_x, size_t T, size_t hidden, size_t intermediate, size_t out_dim,
+                  size_t layer_id, objb_expert_cache* cache, float* d_v, size_t v_rows, objb_moe_telemetry* tel) {
+  DeviceGuard g;
+  OBJB_TRY(g.enter(ex->device));
+  cudaEvent_t* ev = ex->ev;
+  OBJB_CUDA(cudaEventRecord(ev[0], stream), "record total start");
+  // distinct experts, first appearance order -> table slot
+  std::vector<int32_t> slot_of(num_experts, -1);
+  std::vector<int32_t> uniq;
+  for (size_t p = 0; p < P; ++p) {
+    const int32_t e = pair_expert[p];
+    if (slot_of[e] < 0) {
+      slot_of[e] = static_cast<int32_t>(uniq.size());
+      uniq.push_back(e);
+    }
+  }
+  const size_t U = uniq.size();
+  Resolved res;
+  std::vector<const void*> ptrs(U * 3, nullptr);
+  int rc = OBJB_OK;
+  for (size_t u = 0; u < U && rc == OBJB_OK; ++u) {
+    const objb_expert_weights& e = experts[uniq[u]];
+    TensorRef t[3] = {TensorRef{e.w_gate, e.w_gate_len, OBJB_KIND_GATE, false},
+                      TensorRef{e.w_up, e.w_up_len, OBJB_KIND_UP, false},
+                      TensorRef{e.w_down, e.w_down_len, OBJB_KIND_DOWN, false}};
+    rc = resolve_expert(cache, stream, fmt, false, layer_id, static_cast<size_t>(uniq[u]), t, &ptrs[u * 3], &res);
+  }
+  if (rc == OBJB_OK) cudaEventRecord(ev[2], stream);
+  uint32_t flags = 0;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15u) flags |= OBJB_MOE_UNALIGNED;
+  const size_t meta = U * 3 * sizeof(void*) + 3 * P * sizeof(int32_t) + 64;
+  if (rc == OBJB_OK) rc = grow_host(&ex->h_meta, &ex->h_meta_cap, meta);
+  if (rc == OBJB_OK) rc = grow_dev(&ex->d_meta, &ex->d_meta_cap, meta, "allocate MoE tables");
+  objb_moe_layer layer = {};
+  const int32_t *d_pe = nullptr, *d_pt = nullptr, *d_po = nullptr;
+  if (rc == OBJB_OK) {
+    uint8_t* h = static_cast<uint8_t*>(ex->h_meta);
+    const void** tab = reinterpret_cast<const void**>(h);
+    for (int i = 0; i < 3; ++i)
+      for (size_t u = 0; u < U; ++u) tab[i * U + u] = ptrs[u * 3 + i];
+    int32_t* pe = reinterpret_cast<int32_t*>(h + U * 3 * sizeof(void*));
+    int32_t* pt = pe + P;
+    int32_t* po = pt + P;
+    for (size_t p = 0; p < P; ++p) {
+      pe[p] = slot_of[pair_expert[p]];
+      pt[p] = pair_token[p];
+      po[p] = pair_out ? pair_out[p] : static_cast<int32_t>(p);
+    }
+    OBJB_CUDA(cudaMemcpyAsync(ex->d_meta, ex->h_meta, meta, cudaMemcpyHostToDevice, stream), "copy MoE tables");
+    const void* const* dtab = static_cast<const void* const*>(ex->d_meta);
+    d_pe = reinterpret_cast<const int32_t*>(static_cast<uint8_t*>(ex->d_meta) + U * 3 * sizeof(void*));
+    d_pt = d_pe + P;
+    d_po = d_pt + P;
+    layer.fmt = fmt;
+    layer.flags = flags;
+    layer.hidden = hidden;
+    layer.intermediate = intermediate;
+    layer.out_dim = out_dim;
+    layer.num_experts = U;
+    layer.d_gate = dtab;
+    layer.d_up = dtab + U;
+    layer.d_down = dtab + 2 * U;
+  }
+  if (rc == OBJB_OK) {
+    size_t need = 0;
+    rc = moe_pairs_scratch_bytes(&layer, P, T, &need);
+    if (rc == OBJB_OK) rc = grow_dev(&ex->d_scratch, &ex->d_scratch_cap, need, "allocate MoE scratch");
+    if (rc == OBJB_OK) cudaEventRecord(ev[3], stream);
+    if (rc == OBJB_OK)
+      rc = moe_pairs(&layer, P, d_pe, d_pt, d_po, T, d_x, d_v, v_rows, 0.0f, stream, ex->d_scratch,
+                     ex->d_scratch_cap);
+    if (rc == OBJB_OK) cudaEventRecord(ev[5], stream);
+  }
+  if (cache) {  // release point: everything handed to the kernels is enqueued
+    std::lock_guard<std::mutex> lk(cache->mu);
+    int r2 = cache_release(cache, stream);
+    if (rc == OBJB_OK) rc = r2;
+  }
+  for (void* p : res.transients) cudaFreeAsync(p, stream);
+  cudaError_t se = cudaStreamSynchronize(stream);
+  if (rc != OBJB_OK) return rc;
+  if (se != cudaSuccess) return cuda_status(se, "synchronize MoE stream", __FILE__, __LINE__);
+  {
+    unsigned* w = nullptr;
+    OBJB_TRY(device_error_word(ex->device, &w));
+    unsigned v = 0;
+    OBJB_CUDA(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost), "read device error word");
+    if (v) {
+      cudaMemset(w, 0, sizeof(unsigned));
+      return OBJB_FAIL(OBJB_ERR_INTERNAL, "run multi-token MoE", "device error word " + std::to_string(v));
+    }
+  }
+  const size_t logical = res.bytes_gate + res.bytes_up + res.bytes_down;
+  const size_t loaded = res.weight_loaded + res.scale_loaded, reused = res.weight_reused + res.scale_reused;
+  if (logical != loaded + reused)
+    return OBJB_FAIL(OBJB_ERR_INTERNAL, "account MoE bytes", "MoE Byte invariant violated!");
+  if (tel) {
+    std::memset(tel, 0, sizeof(*tel));
+    float h2d = 0, comp = 0, tot = 0;
+    cudaEventElapsedTime(&h2d, ev[0], ev[2]);
+    cudaEventElapsedTime(&comp, ev[3], ev[5]);
+    cudaEventElapsedTime(&tot, ev[0], ev[5]);
+    tel->selected_expert_count = U;
+    tel->logical_expert_bytes_requested = logical;
+    tel->actual_expert_bytes_loaded = loaded;
+    tel->resident_cache_bytes_reused = reused;
+    tel->weight_bytes_loaded = res.weight_loaded;
+    tel->weight_bytes_reused = res.weight_reused;
+    if (cache) {
+      std::lock_guard<std::mutex> lk(cache->mu);
+      const objb_expert_cache_stats& s = cache->st;
+      tel->resident_cache_resident_bytes = s.resident_bytes;
+      tel->resident_cache_capacity_bytes = s.capacity_bytes;
+      tel->resident_cache_hit_count = s.hit_count;
+      tel->resident_cache_miss_count = s.miss_count;
+      tel->resident_cache_eviction_count = s.eviction_count;
+      tel->resident_cache_insert_attempt_count = s.cache_insert_attempt_count;
+      tel->resident_cache_insert_accept_count = s.cache_insert_accept_count;
+      tel->resident_cache_insert_bypass_count = s.cache_insert_bypass_count;
+      tel->resident_cache_oversized_tensor_bypass_count = s.oversized_tensor_bypass_count;
+      tel->resident_cache_oversized_expert_bypass_count = s.oversized_expert_bypass_count;
+      tel->resident_cache_self_eviction_risk_count = s.self_eviction_risk_count;
+    }
+    tel->h2d_ms = h2d;
+    tel->gate_up_qgemv_ms = comp;  // gate/up + SwiGLU + down of all pairs
+    tel->total_ms = tot;
+    tel->unaccounted_ms = std::max(0.0f, tot - h2d - comp);
+    tel->bytes_gate = res.bytes_gate;
+    tel->bytes_up = res.bytes_up;
+    tel->bytes_down = res.bytes_down;
+    tel->bytes_per_expert = U ? logical / U : 0;
+    tel->selected_working_set_bytes = logical;
+  }
+  return OBJB_OK;
+}
+
 int validate_common(size_t x_len, size_t hidden, size_t intermediate, const char* which) {
   if (x_len != hidden)
     return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, (std::string("validate ") + which + " input x size").c_str(),
@@ -451,6 +620,44 @@ int objb_moe_execute_selected_native_fp4(objb_moe_executor* ex, objb_stream_t st
   };
   return execute(ex, static_cast<cudaStream_t>(stream), OBJB_FP4_E2M1, true, num_selected, sel_ids, sel_weights, x,
                  hidden, intermediate, out_dim, layer_id, cache, out, tel, 2 * (guw + gus) + dnw + dns, tensors_of);
+}
+
+int objb_moe_execute_pairs(objb_moe_executor* ex, objb_stream_t stream, int fmt, const objb_expert_weights* experts,
+                           size_t num_experts, const int32_t* pair_expert, const int32_t* pair_token,
+                           const int32_t* pair_out, size_t num_pairs, const float* d_x, size_t num_tokens,
+                           size_t hidden, size_t intermediate, size_t out_dim, size_t layer_id,
+                           objb_expert_cache* cache, float* d_v, size_t v_rows, objb_moe_telemetry* tel) {
+  clear_error();
+  if (!ex || !experts || !pair_expert || !pair_token || !d_x || !d_v)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_execute_pairs", "null argument");
+  if (fmt != OBJB_Q4_0 && fmt != OBJB_Q5_0 && fmt != OBJB_IQ3_0)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "objb_moe_execute_pairs",
+                     "the multi-token executor supports Q4_0, Q5_0 and IQ3_0 experts");
+  if (num_pairs == 0 || num_tokens == 0 || num_experts == 0 || num_experts > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_execute_pairs", "empty pair list, tokens or experts");
+  std::lock_guard<std::mutex> lk(ex->mu);
+  OBJB_TRY(validate_common(hidden, hidden, intermediate, "execute_pairs"));
+  const size_t bb = static_cast<size_t>(block_bytes(fmt));
+  const size_t gu = intermediate * (hidden / 32) * bb;
+  const size_t dn = out_dim * (intermediate / 32) * bb;
+  for (size_t p = 0; p < num_pairs; ++p) {
+    OBJB_TRY(check_index(pair_expert[p], num_experts));
+    if (pair_token[p] < 0 || static_cast<size_t>(pair_token[p]) >= num_tokens)
+      return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate pair token",
+                       "token index " + std::to_string(pair_token[p]) + " out of bounds (len=" +
+                           std::to_string(num_tokens) + ")");
+    const size_t row = pair_out ? static_cast<size_t>(pair_out[p]) : p;
+    if ((pair_out && pair_out[p] < 0) || row >= v_rows)
+      return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate pair output row",
+                       "output row " + std::to_string(row) + " out of bounds (v_rows=" + std::to_string(v_rows) + ")");
+    const objb_expert_weights& e = experts[pair_expert[p]];
+    if (e.w_gate_len != gu) return fail_len("w_gate", e.w_gate_len, gu);
+    if (e.w_up_len != gu) return fail_len("w_up", e.w_up_len, gu);
+    if (e.w_down_len != dn) return fail_len("w_down", e.w_down_len, dn);
+  }
+  return execute_pairs(ex, static_cast<cudaStream_t>(stream), fmt, experts, num_experts, pair_expert, pair_token,
+                       pair_out, num_pairs, d_x, num_tokens, hidden, intermediate, out_dim, layer_id, cache, d_v,
+                       v_rows, tel);
 }
 
 }  // extern "C"

@@ -315,3 +315,31 @@ class ExpertParallelMoe:
         else:
             v_recv = v_send
         return self._combine(v_recv, plan, w)
+
+
+class CachedExpertCompute:
+    """Per-rank compute for ``ExpertParallelMoe`` when this rank's experts
+    live in host memory and reach the GPU through a ``CudaExpertCache``
+    (device LRU + admission, uploads on the cache's side stream): the pairs
+    of a step go to ``MoeExecutor.execute_pairs``, which resolves each
+    distinct expert once.  ``experts`` are this rank's ``ExpertWeights`` in
+    local order."""
+
+    def __init__(self, executor, cache, experts, hidden: int, intermediate: int, out_dim: int, layer_id: int = 0,
+                 fmt=0):
+        self.executor, self.cache = executor, cache
+        self.table = executor.expert_table(experts)
+        self.hidden, self.intermediate, self.out_dim = int(hidden), int(intermediate), int(out_dim)
+        self.layer_id, self.fmt = int(layer_id), fmt
+        self.last_telemetry = None
+
+    def __call__(self, plan: DispatchPlan, x_recv, n_rows: int):
+        import torch
+        v = torch.empty(n_rows, self.out_dim, dtype=torch.float32, device=x_recv.device)
+        if plan.num_pairs == 0:
+            return v
+        self.last_telemetry = self.executor.execute_pairs(
+            self.table, plan.pair_expert, plan.pair_token, x_recv.contiguous(), v, self.hidden, self.intermediate,
+            self.out_dim, self.layer_id, cache=self.cache, pair_out=plan.pair_out, fmt=self.fmt,
+            stream=torch.cuda.current_stream(x_recv.device))
+        return v

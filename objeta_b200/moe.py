@@ -146,6 +146,9 @@ _lib.register_signatures({
                                                      c_void_p, c_void_p, c_size, c_void_p, c_size, c_size,
                                                      c_size, c_size, c_size, c_void_p, c_void_p,
                                                      ctypes.POINTER(_TelC)]),
+    "objb_moe_execute_pairs": (c_int, [c_void_p, c_void_p, c_int, ctypes.POINTER(_ExpertC), c_size, c_void_p,
+                                       c_void_p, c_void_p, c_size, c_void_p, c_size, c_size, c_size, c_size,
+                                       c_size, c_void_p, c_void_p, c_size, ctypes.POINTER(_TelC)]),
     "objb_moe_scratch_bytes": (c_int, [ctypes.POINTER(_LayerC), c_size, ctypes.POINTER(c_size)]),
     "objb_router_topk_device": (c_int, [c_void_p, c_size, c_size, c_int, c_void_p, c_void_p, c_void_p]),
     "objb_moe_selected_device": (c_int, [ctypes.POINTER(_LayerC), c_void_p, c_void_p, c_size, c_void_p,
@@ -404,6 +407,33 @@ class MoeExecutor:
                   intermediate, out_dim, layer_id, cache._h if cache is not None else None, out.ctypes.data,
                   ctypes.byref(tel))
         return out, MoeTelemetry._from_c(tel)
+
+    def expert_table(self, experts):
+        """A C table of host expert weights for ``execute_pairs``; keep it
+        (and the arrays it points into) alive while it is used."""
+        keep = [(_host_u8(e.w_gate), _host_u8(e.w_up), _host_u8(e.w_down)) for e in experts]
+        arr = (_ExpertC * max(1, len(keep)))()
+        for i, (g, u, d) in enumerate(keep):
+            arr[i] = _ExpertC(g.ctypes.data_as(c_u8p), g.size, u.ctypes.data_as(c_u8p), u.size,
+                              d.ctypes.data_as(c_u8p), d.size)
+        return (arr, len(keep), keep)
+
+    def execute_pairs(self, table, pair_expert, pair_token, d_x, d_v, hidden, intermediate, out_dim, layer_id,
+                      cache=None, pair_out=None, fmt=QuantFormat.Q4_0, stream=None):
+        """Multi-token form of ``execute_selected_moe_cuda`` on device
+        activations (objb_moe_execute_pairs): host int32 pair arrays, d_x
+        [T, hidden] and d_v [V, out_dim] device tensors; each distinct expert
+        is resolved through ``cache`` once per call.  Returns MoeTelemetry."""
+        arr, n, _ = table
+        pe = np.ascontiguousarray(pair_expert, dtype=np.int32)
+        pt = np.ascontiguousarray(pair_token, dtype=np.int32)
+        po = None if pair_out is None else np.ascontiguousarray(pair_out, dtype=np.int32)
+        tel = _TelC()
+        _lib.call("objb_moe_execute_pairs", self._h, _lib.stream_handle(stream), int(QuantFormat(fmt)), arr, n,
+                  pe.ctypes.data, pt.ctypes.data, po.ctypes.data if po is not None else None, pe.size,
+                  _dev_ptr(d_x), d_x.shape[0], hidden, intermediate, out_dim, layer_id,
+                  cache._h if cache is not None else None, _dev_ptr(d_v), d_v.shape[0], ctypes.byref(tel))
+        return MoeTelemetry._from_c(tel)
 
     def execute_selected_moe_native_fp4_cuda(self, quant, stream, experts, selected_experts, x, hidden,
                                              intermediate, out_dim, layer_id, cache=None):
