@@ -292,6 +292,7 @@ def run_ours(args, world, rank, local):
         moe["c3_q4_stack"] = bench_c3(qb, dev, gen, msteps, args.warmup, peak)
         moe["c4_fp4_shared"] = bench_c4(dev, gen, msteps, args.warmup, peak)
         moe["c5_ep_resident"] = bench_c5_resident(qb, dev, gen, world, rank, None, msteps, args.warmup, peak)
+        moe["c5_ep_cache"] = bench_c5_cache(qb, dev, gen, world, rank, None, msteps, args.warmup, peak)
 
     result = None
     if rank == 0:
@@ -610,6 +611,91 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
             "2 NCCL all-to-alls per step", **res}
 
 
+def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
+    """configs[4] as specified: this rank's 256 / G Q4_0 experts live in
+    pinned host memory and reach the GPU through a CudaExpertCache holding
+    25% of them (LRU + admission); T tokens per rank, Zipf(1.1) routing,
+    NCCL all-to-all dispatch / combine.  Misses are PCIe uploads."""
+    import torch
+    import torch.distributed as dist
+    from objeta_b200._lib import call
+    from objeta_b200.ep import CachedExpertCompute, ExpertParallelMoe
+    from objeta_b200.moe import CudaExpertCache, ExpertWeights, MoeExecutor
+    c = C5
+    H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
+    epr = E // world
+    g = torch.Generator(device=dev).manual_seed(4242)
+    m = _q4_experts(qb, E, H, I, H, g, dev)
+    sl = range(rank * epr, (rank + 1) * epr)
+    host = []
+    for e in sl:
+        ts = [m[n][e].cpu().numpy() for n in ("gate", "up", "down")]
+        for t in ts:
+            call("objb_host_register", t.ctypes.data, t.nbytes)
+        host.append(ExpertWeights(*ts))
+    del m
+    torch.cuda.empty_cache()
+    ebytes = Q4_EXPERT_BYTES(H, I)
+    cap_experts = max(1, epr // 4)
+    cache = CudaExpertCache(cap_experts * ebytes, rank if world > 1 else torch.cuda.current_device())
+    ex = MoeExecutor(torch.cuda.current_device())
+    comp = CachedExpertCompute(ex, cache, host, H, I, H)
+    ep = ExpertParallelMoe(None, E, K, rank=rank, world=world, group=group, out_dim=H, compute=comp)
+    perm = np.random.default_rng(7).permutation(E)
+    res = {}
+    for T in c["tokens"]:
+        rng = np.random.default_rng(2000 * T + rank)
+        S = 4
+        xs = [torch.randn(T, H, device=dev, generator=gen) for _ in range(S)]
+        routes = [zipf_routes(T, E, K, c["zipf"], perm, rng) for _ in range(S)]
+        ids = [torch.from_numpy(r[0]).to(dev) for r in routes]
+        ws = [torch.from_numpy(r[1]).to(dev) for r in routes]
+        n = max(3, min(steps, 10))
+        for i in range(warmup):
+            ep.forward(xs[i % S], ids[i % S], ws[i % S])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(group=group)
+        st0 = cache.stats()
+        loaded = reused = 0
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(n):
+            ep.forward(xs[i % S], ids[i % S], ws[i % S])
+            tel = comp.last_telemetry
+            if tel is not None:
+                loaded += tel.actual_expert_bytes_loaded
+                reused += tel.resident_cache_bytes_reused
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1)
+        st1 = cache.stats()
+        stats = torch.tensor([ms, loaded, reused], dtype=torch.float64, device=dev)
+        if world > 1:
+            mx = stats.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+            dist.all_reduce(stats, op=dist.ReduceOp.SUM, group=group)
+            ms = float(mx[0])
+        per_step = ms / n
+        hits = st1["hit_count"] - st0["hit_count"]
+        misses = st1["miss_count"] - st0["miss_count"]
+        res[f"T{T}"] = {"tokens_per_s": round(T * world * 1e3 / per_step, 1), "us_per_step": round(per_step * 1e3, 1),
+                        "pcie_bytes_per_step_all_ranks": int(float(stats[1]) / n),
+                        "cache_reused_bytes_per_step_all_ranks": int(float(stats[2]) / n),
+                        "pcie_GB/s_all_ranks": round(float(stats[1]) / n / (per_step / 1e3) / 1e9, 1),
+                        "rank0_tensor_hit_rate": round(hits / max(1, hits + misses), 3), "steps": n}
+    for e in host:
+        for t in (e.w_gate, e.w_up, e.w_down):
+            call("objb_host_unregister", t.ctypes.data)
+    del ep, comp, cache, ex
+    torch.cuda.empty_cache()
+    return {"config": f"configs[4] EP layer with expert cache: 256 Q4_0 experts / {world} rank(s) in pinned host "
+                      f"memory, cache = {cap_experts} experts per GPU (25%), H 2048, I 512, top-8 Zipf(1.1), "
+                      "T tokens per rank",
+            "bound": "PCIe (cache misses) + HBM", "scaling": "weak (T tokens per rank)", **res}
+
+
 # --------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
     if rank != 0:
@@ -691,6 +777,9 @@ def run_case(args, local):
 
 
 def main():
+    # NCCL's own log lines (e.g. its version banner when NCCL_DEBUG is set)
+    # go to stderr, so stdout carries only the result line.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

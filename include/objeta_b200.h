@@ -109,6 +109,18 @@ typedef struct {
 } objb_device_info;
 int objb_device_info_get(int device, objb_device_info *out);
 
+/* QGemvNumerics (quant.rs:156-161) and compare_outputs (quant.rs:676-723):
+ * cosine similarity and relative L2 error from f64 sums in element order,
+ * max |actual - reference| in f32; InvalidInput "reference len .. != actual
+ * len .." on a length mismatch.  Host arrays. */
+typedef struct {
+  float cosine_similarity;
+  float relative_l2_error;
+  float max_abs_error;
+} objb_qgemv_numerics;
+int objb_compare_outputs(const float *reference, size_t reference_len, const float *actual,
+                         size_t actual_len, objb_qgemv_numerics *out);
+
 /* Reads and clears the device's error word.  Kernels with bounded waits
  * (bulk-copy pipelines, peer flags) record a nonzero code there instead of
  * hanging when a wait expires; 0 means no wait has expired.  Replaces no

@@ -1,6 +1,8 @@
 // capi.cpp -- error recording, metadata and device plumbing of the C ABI.
 #include <cuda_runtime.h>
 
+#include <cmath>
+
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
@@ -243,6 +245,34 @@ int objb_host_register(void* ptr, size_t bytes) {
 int objb_host_unregister(void* ptr) {
   clear_error();
   OBJB_CUDA(cudaHostUnregister(ptr), "unpin host range");
+  return OBJB_OK;
+}
+
+int objb_compare_outputs(const float* reference, size_t reference_len, const float* actual, size_t actual_len,
+                         objb_qgemv_numerics* out) {
+  clear_error();
+  if (!out || (reference_len && !reference) || (actual_len && !actual))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "compare quantized GEMV outputs", "null argument");
+  if (reference_len != actual_len)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "compare quantized GEMV outputs",
+                     "reference len " + std::to_string(reference_len) + " != actual len " +
+                         std::to_string(actual_len));
+  // f64 sums in element order; the difference and its magnitude in f32.
+  double dot = 0.0, ref_norm = 0.0, act_norm = 0.0, sq_err = 0.0;
+  float max_abs = 0.0f;
+  for (size_t i = 0; i < reference_len; ++i) {
+    const double r = reference[i], a = actual[i];
+    dot += r * a;
+    ref_norm += r * r;
+    act_norm += a * a;
+    const float diff = actual[i] - reference[i];
+    sq_err += static_cast<double>(diff) * static_cast<double>(diff);
+    max_abs = std::fmax(max_abs, std::fabs(diff));
+  }
+  out->cosine_similarity =
+      ref_norm > 0.0 && act_norm > 0.0 ? static_cast<float>(dot / (std::sqrt(ref_norm) * std::sqrt(act_norm))) : 1.0f;
+  out->relative_l2_error = ref_norm > 0.0 ? static_cast<float>(std::sqrt(sq_err) / std::sqrt(ref_norm)) : 0.0f;
+  out->max_abs_error = max_abs;
   return OBJB_OK;
 }
 

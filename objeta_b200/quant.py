@@ -263,3 +263,29 @@ def device_error_take(device: int = 0) -> int:
     w = ctypes.c_uint(0)
     _lib.call("objb_device_error_take", device, ctypes.byref(w))
     return int(w.value)
+
+
+@dataclass
+class QGemvNumerics:
+    """quant.rs:156-161."""
+    cosine_similarity: float
+    relative_l2_error: float
+    max_abs_error: float
+
+
+class _NumericsC(ctypes.Structure):
+    _fields_ = [("cosine_similarity", ctypes.c_float), ("relative_l2_error", ctypes.c_float),
+                ("max_abs_error", ctypes.c_float)]
+
+
+def compare_outputs(reference, actual) -> QGemvNumerics:
+    """compare_outputs (quant.rs:676-723) through objb_compare_outputs: cosine
+    and relative L2 from f64 sums in element order, f32 max-abs error."""
+    r = np.ascontiguousarray(reference, dtype=np.float32).reshape(-1)
+    a = np.ascontiguousarray(actual, dtype=np.float32).reshape(-1)
+    out = _NumericsC()
+    _lib.call("objb_compare_outputs", r.ctypes.data, r.size, a.ctypes.data, a.size, ctypes.byref(out))
+    return QGemvNumerics(float(out.cosine_similarity), float(out.relative_l2_error), float(out.max_abs_error))
+
+
+q4_compare = q5_compare = fp4_compare = compare_outputs

@@ -83,3 +83,27 @@ def test_compute_fails_loudly_without_gpu():
     with pytest.raises(objeta_b200.CudaError) as ei:
         objeta_b200.QuantBackend(0)
     assert ei.value.kind in ("Runtime", "Unsupported")
+
+
+def test_compare_outputs_matches_reference_definition():
+    """quant.rs:676-723 through the C ABI (host code, no GPU): against the
+    oracle restatement, a mismatch error, and the empty / zero-norm cases."""
+    import numpy as np
+    from objeta_b200._lib import CudaError
+    from objeta_b200.quant import compare_outputs
+    from oracle import oracle as O
+    rng = np.random.default_rng(1)
+    r = rng.standard_normal(1000).astype(np.float32)
+    a = (r + rng.standard_normal(1000).astype(np.float32) * 1e-3).astype(np.float32)
+    got = compare_outputs(r, a)
+    ref = O.compare_outputs(r, a)
+    assert abs(got.cosine_similarity - ref["cosine_similarity"]) <= 1e-6
+    assert abs(got.relative_l2_error - ref["relative_l2_error"]) <= 1e-6 * max(1.0, ref["relative_l2_error"])
+    assert got.max_abs_error == np.float32(ref["max_abs_error"])
+    z = compare_outputs(np.zeros(4, np.float32), np.zeros(4, np.float32))
+    assert (z.cosine_similarity, z.relative_l2_error, z.max_abs_error) == (1.0, 0.0, 0.0)
+    try:
+        compare_outputs(r, a[:-1])
+        raise AssertionError("length mismatch accepted")
+    except CudaError as e:
+        assert e.kind == "InvalidInput" and "reference len 1000 != actual len 999" in e.source_message
