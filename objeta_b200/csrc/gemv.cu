@@ -59,8 +59,18 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
   const int ngrp = std::max(1, max_consumer_warps / nseg);
   int per_row = row_bytes + srow_bytes;
   if (dual) per_row *= 2;
-  constexpr int kStageTarget = 48 * 1024;
-  constexpr int kSmemBudget = 200 * 1024;
+#ifndef OBJB_STAGE_TARGET
+#define OBJB_STAGE_TARGET (48 * 1024)
+#endif
+#ifndef OBJB_SMEM_BUDGET
+#define OBJB_SMEM_BUDGET (200 * 1024)
+#endif
+#ifndef OBJB_STAGE_MAX
+#define OBJB_STAGE_MAX (OBJB_SMEM_BUDGET / 2 - 4096)
+#endif
+  constexpr int kStageTarget = OBJB_STAGE_TARGET;
+  constexpr int kSmemBudget = OBJB_SMEM_BUDGET;
+  constexpr int kStageMax = OBJB_STAGE_MAX;
   // One stage gives every row group one 4-row batch when that fits; small rows
   // get several batches per stage.
   const int quantum = ngrp * 4;
@@ -69,7 +79,8 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
     T = quantum;
     while (T + quantum <= dev::kMaxRowsPerStage && (T + quantum) * per_row <= kStageTarget) T += quantum;
   } else {
-    T = std::max(1, std::min(quantum, (kSmemBudget / 2 - 4096) / per_row));
+    T = std::max(1, std::min(quantum, kStageMax / per_row));
+    if (T > 4) T = T / 4 * 4;
   }
   T = std::min(T, dev::kMaxRowsPerStage);
   const int stage_bytes = ((T * per_row) + 127) / 128 * 128;
