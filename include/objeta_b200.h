@@ -286,13 +286,19 @@ int objb_moe_selected_device_noalloc(const objb_moe_layer *layer, const int32_t 
  * expert's weights are streamed once while they sit in L2.  Every output row
  * is bit-identical to the value the single-token launch computes for the same
  * expert and x.  Out-of-range ids or rows are clamped to 0 and flagged in the
- * device error word (bit 8).  Scratch comes from the per-stream workspace. */
+ * device error word (bit 8).  Scratch comes from the per-stream workspace,
+ * sized for num_pairs.  d_num_pairs (may be NULL): a device int32 holding the
+ * number of pairs to run (at most num_pairs), written by an earlier kernel on
+ * the stream -- the work is then split over the SMs inside the kernels, so a
+ * pair list built on the device needs no host round trip (aligned layers
+ * only). */
 int objb_moe_pairs_scratch_bytes(const objb_moe_layer *layer, size_t num_pairs,
                                  size_t num_tokens, size_t *bytes);
 int objb_moe_pairs_device(const objb_moe_layer *layer, size_t num_pairs,
-                          const int32_t *d_pair_expert, const int32_t *d_pair_token,
-                          const int32_t *d_pair_out, size_t num_tokens, const float *d_x,
-                          float *d_v, size_t v_rows, float swiglu_limit, objb_stream_t stream);
+                          const int32_t *d_num_pairs, const int32_t *d_pair_expert,
+                          const int32_t *d_pair_token, const int32_t *d_pair_out,
+                          size_t num_tokens, const float *d_x, float *d_v, size_t v_rows,
+                          float swiglu_limit, objb_stream_t stream);
 
 /* The weighted top-k combine (moe.rs:1319-1321) for num_tokens tokens:
  * d_out[t][i] = sum over j = 0..top_k-1, in slot order, of
@@ -494,6 +500,30 @@ int objb_moe_execute_pairs(objb_moe_executor *ex, objb_stream_t stream, int fmt,
                            size_t num_tokens, size_t hidden, size_t intermediate,
                            size_t out_dim, size_t layer_id, objb_expert_cache *cache,
                            float *d_v, size_t v_rows, objb_moe_telemetry *tel);
+
+/* ---- expert parallelism, device side (no counterpart in the reference).
+ * A rank holds experts [rank*E/G, (rank+1)*E/G).  After the host framework
+ * all-gathers the routing table d_ids_all [G][T][top_k] (and the routing
+ * weights and token rows [G*T][hidden]):
+ *  - objb_ep_build_pairs_device writes this rank's pairs (local expert id,
+ *    token row s*T + t, output row (s*T + t)*top_k + j) grouped by expert into
+ *    arrays of G*T*top_k entries and their number into *d_num_pairs, for
+ *    objb_moe_pairs_device with d_num_pairs (v has G*T*top_k rows);
+ *  - objb_ep_partial_combine_device folds, per routing row (s, t), w * v over
+ *    the slots whose expert is local, in slot order: d_partial [G][T][out_dim];
+ *  - after an all-to-all of the partials, objb_ep_sum_partials_device adds
+ *    d_parts [G][T][out_dim] over ranks in rank order into d_out [T][out_dim].
+ * Expert ids out of range are dropped and flagged (device error word bit 8). */
+int objb_ep_build_pairs_device(const int32_t *d_ids_all, size_t world, size_t tokens,
+                               size_t top_k, size_t num_experts, size_t rank,
+                               int32_t *d_pair_expert, int32_t *d_pair_token,
+                               int32_t *d_pair_out, int32_t *d_num_pairs, objb_stream_t stream);
+int objb_ep_partial_combine_device(const int32_t *d_ids_all, const float *d_w_all,
+                                   const float *d_v, size_t world, size_t tokens, size_t top_k,
+                                   size_t num_experts, size_t rank, size_t out_dim,
+                                   float *d_partial, objb_stream_t stream);
+int objb_ep_sum_partials_device(const float *d_parts, size_t world, size_t tokens,
+                                size_t out_dim, float *d_out, objb_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -272,8 +272,8 @@ size_t pairs_need(const MoePlan<RD>& p, const MoeShape& s, int T) {
 
 template <class RD, int FMT, bool SPLIT>
 int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* pair_expert,
-              const int32_t* pair_token, const int32_t* pair_out, const float* x, float* v, int v_rows,
-              float limit, cudaStream_t stream, void* scratch, size_t scratch_bytes, bool aligned,
+              const int32_t* pair_token, const int32_t* pair_out, const int32_t* d_count, const float* x, float* v,
+              int v_rows, float limit, cudaStream_t stream, void* scratch, size_t scratch_bytes, bool aligned,
               unsigned* err_word) {
   int device = 0;
   OBJB_TRY(current_device(&device));
@@ -291,6 +291,9 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
   const dev::ExpertTables t = tables_of(l);
   const int P = s.K;
   if (!p.fast) {
+    if (d_count)
+      return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "run multi-token MoE pairs",
+                       "a device-side pair count needs 16-byte aligned experts and aligned shapes");
     dev::moe_generic_pairs_gateup_kernel<FMT, SPLIT><<<(P * s.I + 7) / 8, 256, 0, stream>>>(
         t, pair_expert, pair_token, P, s.I, s.H, T, x, act, limit, err);
     OBJB_CUDA(cudaGetLastError(), "launch generic pair gate/up kernel");
@@ -304,10 +307,10 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
   OBJB_TRY(launch_ximage<RD>(p.lg, x, static_cast<size_t>(s.H), T, imgx, p.imgx_quads, stream));
   {
     const int total = P * s.I;
-    const int TS = p.lg.tstage;
     int R = (total + props.sm_count - 1) / props.sm_count;
     R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
-    const int grid = (total + R - 1) / R;
+    // with a device-side count the split is made in the kernel over all SMs
+    const int grid = d_count ? props.sm_count : (total + R - 1) / R;
     dev::GateUpPairsProg prog;
     prog.t = t;
     prog.pair_expert = pair_expert;
@@ -318,7 +321,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.P = P;
     prog.I = s.I;
     prog.T = T;
-    prog.rows_per_cta = R;
+    prog.rows_per_cta = d_count ? 0 : R;
+    prog.count = d_count;
     prog.swiglu_limit = limit;
     prog.err = err;
     const size_t smem = pipe_smem_bytes(p.lg);
@@ -328,13 +332,12 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     std::memcpy(&dl, &p.lg, sizeof(dl));
     OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
   }
-  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream));
+  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream, d_count));
   {
     const int total = P * s.O;
-    const int TS = p.ld.tstage;
     int R = (total + props.sm_count - 1) / props.sm_count;
     R = (R + 3) / 4 * 4;  // whole 4-row batches; stages may end short
-    const int grid = (total + R - 1) / R;
+    const int grid = d_count ? props.sm_count : (total + R - 1) / R;
     dev::DownPairsProg prog;
     prog.t = t;
     prog.pair_expert = pair_expert;
@@ -345,7 +348,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.P = P;
     prog.O = s.O;
     prog.v_rows = v_rows;
-    prog.rows_per_cta = R;
+    prog.rows_per_cta = d_count ? 0 : R;
+    prog.count = d_count;
     prog.err = err;
     const size_t smem = pipe_smem_bytes(p.ld);
     auto kernel = dev::pipe_kernel<RD, dev::DownPairsProg, false>;
@@ -473,7 +477,8 @@ int moe_pairs_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t nu
 
 int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_expert, const int32_t* pair_token,
               const int32_t* pair_out, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
-              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word) {
+              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word,
+              const int32_t* d_num_pairs) {
   MoeShape s;
   bool split = false;
   OBJB_TRY(validate_pairs(l, num_pairs, num_tokens, &s, &split));
@@ -486,8 +491,8 @@ int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_exp
   const int T = static_cast<int>(num_tokens);
   const int VR = static_cast<int>(v_rows);
 #define OBJB_PAIRS(RDT, F, SP)                                                                                   \
-  return run_pairs<RDT, F, SP>(*l, s, T, pair_expert, pair_token, pair_out, x, v, VR, limit, stream, scratch, \
-                               scratch_bytes, aligned, err_word)
+  return run_pairs<RDT, F, SP>(*l, s, T, pair_expert, pair_token, pair_out, d_num_pairs, x, v, VR, limit, stream, \
+                               scratch, scratch_bytes, aligned, err_word)
   if (split) OBJB_PAIRS(dev::RowDotSplitFp4, OBJB_FP4_E2M1, true);
   switch (l->fmt) {
     case OBJB_Q4_0: OBJB_PAIRS(dev::RowDot<OBJB_Q4_0>, OBJB_Q4_0, false);
@@ -596,9 +601,10 @@ int objb_moe_pairs_scratch_bytes(const objb_moe_layer* layer, size_t num_pairs, 
   return objb::moe_pairs_scratch_bytes(layer, num_pairs, num_tokens, bytes);
 }
 
-int objb_moe_pairs_device(const objb_moe_layer* layer, size_t num_pairs, const int32_t* d_pair_expert,
-                          const int32_t* d_pair_token, const int32_t* d_pair_out, size_t num_tokens,
-                          const float* d_x, float* d_v, size_t v_rows, float swiglu_limit, objb_stream_t stream_) {
+int objb_moe_pairs_device(const objb_moe_layer* layer, size_t num_pairs, const int32_t* d_num_pairs,
+                          const int32_t* d_pair_expert, const int32_t* d_pair_token, const int32_t* d_pair_out,
+                          size_t num_tokens, const float* d_x, float* d_v, size_t v_rows, float swiglu_limit,
+                          objb_stream_t stream_) {
   objb::clear_error();
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   size_t need = 0;
@@ -608,7 +614,7 @@ int objb_moe_pairs_device(const objb_moe_layer* layer, size_t num_pairs, const i
   void* ws = nullptr;
   OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
   return objb::moe_pairs(layer, num_pairs, d_pair_expert, d_pair_token, d_pair_out, num_tokens, d_x, d_v, v_rows,
-                         swiglu_limit, stream, ws, need, nullptr);
+                         swiglu_limit, stream, ws, need, nullptr, d_num_pairs);
 }
 
 int objb_moe_combine_device(const float* d_v, size_t v_rows, const int32_t* d_slot_row, const float* d_weights,

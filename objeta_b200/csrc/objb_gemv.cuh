@@ -165,10 +165,11 @@ __device__ __forceinline__ void load_ximage(const uint4* __restrict__ img, int n
 template <class RD>
 __global__ void __launch_bounds__(256) ximage_f32_kernel(const RowLayout L, const float* __restrict__ x,
                                                          size_t x_stride, int nvec, uint4* __restrict__ img,
-                                                         size_t img_stride_quads) {
+                                                         size_t img_stride_quads, const int32_t* count) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // x may be the output of the kernel this one was launched behind.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) nvec = min(max(*count, 0), nvec);  // vectors to build (device), at most nvec
   constexpr int NQ = RD::XRegs::kQuads;
   const int ntp = L.nseg * 32;
   const int total = nvec * ntp * NQ;
@@ -196,10 +197,11 @@ __global__ void __launch_bounds__(256) ximage_f32_kernel(const RowLayout L, cons
 template <int FMT>
 __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, const float* __restrict__ x,
                                                             size_t x_stride, int nvec, uint4* __restrict__ img,
-                                                            size_t img_stride_quads) {
+                                                            size_t img_stride_quads, const int32_t* count) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // x may be the output of the kernel this one was launched behind.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) nvec = min(max(*count, 0), nvec);  // vectors to build (device), at most nvec
   using T = Tile<FMT>;
   const int ntp = L.nseg * 32;
   const int nb_img = ntp * T::P;  // blocks covered by the image (incl. idle lanes)

@@ -44,7 +44,7 @@ int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, size_t smem, cud
 
 template <class RD>
 int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int nvec, uint4* img,
-                  size_t img_stride_quads, cudaStream_t stream) {
+                  size_t img_stride_quads, cudaStream_t stream, const int32_t* count = nullptr) {
   dev::RowLayout dl;
   std::memcpy(&dl, &L, sizeof(dl));
   // Launched with programmatic serialization: the kernel waits
@@ -54,12 +54,12 @@ int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int n
     const int warps = L.nseg * 32 * 2 * nvec;
     const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
     return launch_pdl(dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt>, grid, 256, 0, stream, dl, x, x_stride,
-                      nvec, img, img_stride_quads);
+                      nvec, img, img_stride_quads, count);
   } else {
     const int n = L.nseg * 32 * RD::XRegs::kQuads * nvec;
     const int grid = std::max(1, std::min((n + 255) / 256, 2048));
     return launch_pdl(dev::ximage_f32_kernel<RD>, grid, 256, 0, stream, dl, x, x_stride, nvec, img,
-                      img_stride_quads);
+                      img_stride_quads, count);
   }
 }
 

@@ -138,6 +138,12 @@ __device__ __forceinline__ int checked_index(const int32_t* idx, int p, int n, u
   return v;
 }
 
+// Rows per CTA for `total` rows over the grid: even, in whole 4-row batches.
+__device__ __forceinline__ int split_rows(int total) {
+  const int g = static_cast<int>(gridDim.x);
+  return ((total + g - 1) / g + 3) / 4 * 4;
+}
+
 // gate/up: rows [c * R, (c + 1) * R) of the P * I rows of all pairs.
 struct GateUpPairsProg {
   ExpertTables t;
@@ -147,20 +153,23 @@ struct GateUpPairsProg {
   size_t img_stride;
   float* act;  // [P][I]
   int P, I, T;
-  int rows_per_cta;
+  int rows_per_cta;  // 0: derived in the kernel from *count
+  const int32_t* count;  // pairs to run (device), nullptr: all P
   float swiglu_limit;
   unsigned* err;
 
-  __device__ __forceinline__ int first_p(int cta) const { return (cta * rows_per_cta) / I; }
+  __device__ __forceinline__ int np() const { return count ? min(max(__ldg(count), 0), P) : P; }
+  __device__ __forceinline__ int R() const { return rows_per_cta ? rows_per_cta : split_rows(np() * I); }
+  __device__ __forceinline__ int first_p(int cta) const { return (cta * R()) / I; }
   __device__ __forceinline__ int njobs(int cta) const {
-    const int a = cta * rows_per_cta;
-    const int b = min(P * I, a + rows_per_cta);
+    const int a = cta * R();
+    const int b = min(np() * I, a + R());
     if (a >= b) return 0;
     return (b - 1) / I - a / I + 1;
   }
   __device__ __forceinline__ Job job(int cta, int j) const {
-    const int a = cta * rows_per_cta;
-    const int b = min(P * I, a + rows_per_cta);
+    const int a = cta * R();
+    const int b = min(np() * I, a + R());
     const int p = a / I + j;
     Job J;
     const int e = checked_expert(pair_expert, p, t.num_experts, err);
@@ -190,19 +199,22 @@ struct DownPairsProg {
   size_t img_stride;
   float* v;                 // [v_rows][O]
   int P, O, v_rows;
-  int rows_per_cta;
+  int rows_per_cta;         // 0: derived in the kernel from *count
+  const int32_t* count;     // pairs to run (device), nullptr: all P
   unsigned* err;
 
-  __device__ __forceinline__ int first_p(int cta) const { return (cta * rows_per_cta) / O; }
+  __device__ __forceinline__ int np() const { return count ? min(max(__ldg(count), 0), P) : P; }
+  __device__ __forceinline__ int R() const { return rows_per_cta ? rows_per_cta : split_rows(np() * O); }
+  __device__ __forceinline__ int first_p(int cta) const { return (cta * R()) / O; }
   __device__ __forceinline__ int njobs(int cta) const {
-    const int a = cta * rows_per_cta;
-    const int b = min(P * O, a + rows_per_cta);
+    const int a = cta * R();
+    const int b = min(np() * O, a + R());
     if (a >= b) return 0;
     return (b - 1) / O - a / O + 1;
   }
   __device__ __forceinline__ Job job(int cta, int j) const {
-    const int a = cta * rows_per_cta;
-    const int b = min(P * O, a + rows_per_cta);
+    const int a = cta * R();
+    const int b = min(np() * O, a + R());
     const int p = a / O + j;
     Job J;
     const int e = checked_expert(pair_expert, p, t.num_experts, err);

@@ -26,7 +26,8 @@ int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weigh
 int moe_pairs_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out);
 int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_expert, const int32_t* pair_token,
               const int32_t* pair_out, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
-              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word = nullptr);
+              cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word = nullptr,
+              const int32_t* d_num_pairs = nullptr);
 int moe_combine(const float* v, size_t v_rows, const int32_t* slot_row, const float* weights, size_t num_tokens,
                 size_t top_k, size_t out_dim, float* out, cudaStream_t stream, unsigned* err_word = nullptr);
 int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t top_k, int renorm, int32_t* ids,

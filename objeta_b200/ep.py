@@ -39,13 +39,54 @@ c_void_p = ctypes.c_void_p
 
 _lib.register_signatures({
     "objb_moe_pairs_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
-    "objb_moe_pairs_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_size, c_void_p,
-                                      c_void_p, c_size, ctypes.c_float, c_void_p]),
+    "objb_moe_pairs_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_size,
+                                      c_void_p, c_void_p, c_size, ctypes.c_float, c_void_p]),
     "objb_moe_combine_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p,
                                         c_void_p]),
     "objb_router_topk_batched_device": (c_int, [c_void_p, c_size, c_size, c_size, c_int, c_void_p, c_void_p,
                                                 c_void_p]),
+    "objb_ep_build_pairs_device": (c_int, [c_void_p, c_size, c_size, c_size, c_size, c_size, c_void_p, c_void_p,
+                                           c_void_p, c_void_p, c_void_p]),
+    "objb_ep_partial_combine_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_size,
+                                               c_size, c_size, c_void_p, c_void_p]),
+    "objb_ep_sum_partials_device": (c_int, [c_void_p, c_size, c_size, c_size, c_void_p, c_void_p]),
 })
+
+
+def ep_build_pairs(ids_all, rank: int, num_experts: int, stream=None):
+    """This rank's pairs from the routing table ids_all [G, T, k] (device
+    int32), built on the device: returns (pair_expert, pair_token, pair_out,
+    count) device int32 tensors; the arrays have G*T*k entries of which the
+    first ``count`` are used.  pair_token indexes the all-gathered token rows
+    [G*T, H]; pair_out is the routing entry's flat index (s*T + t)*k + j."""
+    import torch
+    G, T, K = ids_all.shape
+    n = G * T * K
+    buf = torch.empty(3 * n + 1, dtype=torch.int32, device=ids_all.device)
+    pe, pt, po, cnt = buf[:n], buf[n:2 * n], buf[2 * n:3 * n], buf[3 * n:]
+    _lib.call("objb_ep_build_pairs_device", _dev_ptr(ids_all), G, T, K, num_experts, rank, _dev_ptr(pe),
+              _dev_ptr(pt), _dev_ptr(po), _dev_ptr(cnt), _lib.stream_handle(stream))
+    return pe, pt, po, cnt
+
+
+def ep_partial_combine(ids_all, w_all, v, rank: int, num_experts: int, out_dim: int, stream=None):
+    """Per routing row (s, t): the slot-order fold of w * v over the slots
+    whose expert lives on this rank -> partial [G, T, out_dim]."""
+    import torch
+    G, T, K = ids_all.shape
+    part = torch.empty(G, T, out_dim, dtype=torch.float32, device=v.device)
+    _lib.call("objb_ep_partial_combine_device", _dev_ptr(ids_all), _dev_ptr(w_all), _dev_ptr(v), G, T, K,
+              num_experts, rank, out_dim, _dev_ptr(part), _lib.stream_handle(stream))
+    return part
+
+
+def ep_sum_partials(parts, stream=None):
+    """out[t] = sum over ranks r (in rank order) of parts[r, t]."""
+    import torch
+    G, T, O_ = parts.shape
+    out = torch.empty(T, O_, dtype=torch.float32, device=parts.device)
+    _lib.call("objb_ep_sum_partials_device", _dev_ptr(parts), G, T, O_, _dev_ptr(out), _lib.stream_handle(stream))
+    return out
 
 
 def router_topk_batched(d_logits, top_k: int, renormalize: bool = False, stream=None):
@@ -60,15 +101,17 @@ def router_topk_batched(d_logits, top_k: int, renormalize: bool = False, stream=
     return ids, w
 
 
-def moe_pairs(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 0.0, stream=None):
+def moe_pairs(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 0.0, stream=None,
+              d_count=None):
     """v[pair_out[p]] = down_e(SwiGLU(gate_e x_t, up_e x_t)) with
     e = pair_expert[p], t = pair_token[p] (device int32 tensors); d_x [T, H],
-    d_v [V, O] f32.  ``pair_out`` None writes row p."""
+    d_v [V, O] f32.  ``pair_out`` None writes row p.  ``d_count``: a device
+    int32 with the number of pairs to run (the arrays' length is the cap)."""
     P = pair_expert.numel()
     T = d_x.shape[0]
-    _lib.call("objb_moe_pairs_device", ctypes.byref(layer._c), P, _dev_ptr(pair_expert), _dev_ptr(pair_token),
-              _dev_ptr(pair_out) if pair_out is not None else None, T, _dev_ptr(d_x), _dev_ptr(d_v),
-              d_v.shape[0], float(swiglu_limit), _lib.stream_handle(stream))
+    _lib.call("objb_moe_pairs_device", ctypes.byref(layer._c), P, _dev_ptr(d_count) if d_count is not None else None,
+              _dev_ptr(pair_expert), _dev_ptr(pair_token), _dev_ptr(pair_out) if pair_out is not None else None, T,
+              _dev_ptr(d_x), _dev_ptr(d_v), d_v.shape[0], float(swiglu_limit), _lib.stream_handle(stream))
     return d_v
 
 
@@ -190,12 +233,25 @@ class ExpertParallelMoe:
 
     ``compute(plan, x_recv, n_rows) -> v_send`` and ``combine(v_recv, plan,
     w) -> out`` default to the CUDA library; tests on CPU pass their own.
-    With one rank the default path stays on the device (no host round trip);
-    ``plan_on_host=True`` makes it take the multi-rank path instead."""
+    Paths:
+
+    * one rank (default compute): on the device, bit-identical to the
+      single-token launch;
+    * several ranks, ``exchange="device"`` (default compute): no host round
+      trip -- all-gathers of the routing table, weights and token rows, the
+      pair list built on the device, pair launches with a device-side count,
+      a per-rank partial combine (slot order) and one all-to-all of the
+      partials, summed on the token owner in rank order.  Deterministic, and
+      within the reference tolerance of the one-rank result, but the
+      association of the combine depends on the rank count;
+    * ``exchange="host"`` or ``plan_on_host=True`` (and any injected compute):
+      the routing table goes to the host, a ``DispatchPlan`` sends only the
+      needed token rows and pair outputs, and the owner combines in slot
+      order -- bit-identical for any rank count."""
 
     def __init__(self, layer, num_experts: int, top_k: int, rank: int = 0, world: int = 1, group=None,
                  out_dim: int | None = None, compute=None, combine=None, swiglu_limit: float = 0.0,
-                 plan_on_host: bool = False):
+                 plan_on_host: bool = False, exchange: str = "device"):
         self.layer = layer
         self.num_experts = int(num_experts)
         self.top_k = int(top_k)
@@ -205,6 +261,9 @@ class ExpertParallelMoe:
         self._compute = compute or self._cuda_compute
         self._combine = combine or self._cuda_combine
         self._device_only = compute is None and combine is None and not plan_on_host
+        if exchange not in ("device", "host"):
+            raise ValueError(f"exchange must be 'device' or 'host', not {exchange!r}")
+        self._device_exchange = self._device_only and exchange == "device"
         self.last_plan = None
         self._pin = None     # pinned int32 staging for plan arrays (grow-only)
         self._dmeta = None   # device copy (grow-only)
@@ -278,6 +337,28 @@ class ExpertParallelMoe:
         out = torch.empty(T, self.out_dim, dtype=torch.float32, device=x.device)
         return moe_combine(v, slot, w.contiguous(), out, stream=stream)
 
+    def _forward_device_exchange(self, x, ids, w):
+        import torch
+        import torch.distributed as dist
+        G, (T, K) = self.world, ids.shape
+        dev = x.device
+        stream = torch.cuda.current_stream(dev)
+        ids = ids.to(torch.int32).contiguous()
+        ids_all = torch.empty(G, T, K, dtype=torch.int32, device=dev)
+        w_all = torch.empty(G, T, K, dtype=torch.float32, device=dev)
+        x_all = torch.empty(G * T, x.shape[1], dtype=x.dtype, device=dev)
+        dist.all_gather_into_tensor(ids_all, ids, group=self.group)
+        dist.all_gather_into_tensor(w_all, w.contiguous(), group=self.group)
+        dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
+        pe, pt, po, cnt = ep_build_pairs(ids_all, self.rank, self.num_experts, stream=stream)
+        v = torch.empty(G * T * K, self.out_dim, dtype=torch.float32, device=dev)
+        moe_pairs(self.layer, pe, pt, x_all, v, pair_out=po, swiglu_limit=self.swiglu_limit, stream=stream,
+                  d_count=cnt)
+        part = ep_partial_combine(ids_all, w_all, v, self.rank, self.num_experts, self.out_dim, stream=stream)
+        recv = torch.empty_like(part)
+        dist.all_to_all_single(recv, part, group=self.group)
+        return ep_sum_partials(recv, stream=stream)
+
     # ---- the layer
     def plan(self, ids) -> DispatchPlan:
         import torch
@@ -297,6 +378,9 @@ class ExpertParallelMoe:
         if self.world == 1 and self._device_only:
             self.last_plan = None
             return self._forward_one_rank(x, ids, w)
+        if self._device_exchange:
+            self.last_plan = None
+            return self._forward_device_exchange(x, ids, w)
         plan = self.plan(ids)
         self.last_plan = plan
         H = x.shape[1]
