@@ -525,6 +525,62 @@ int objb_ep_partial_combine_device(const int32_t *d_ids_all, const float *d_w_al
 int objb_ep_sum_partials_device(const float *d_parts, size_t world, size_t tokens,
                                 size_t out_dim, float *d_out, objb_stream_t stream);
 
+/* ---- official DeepSeek arithmetic: activations quantized to F8_E4M3 with one
+ * E8M0 scale per 128 values (deepseek.rs:1444-1525 for the codecs). */
+
+/* cuda_act_quant_device (quant.rs:1229-1282): rows x cols f32 -> E4M3 codes
+ * [rows][cols] + E8M0 scales [rows][cols/128], bit-identical to the reference
+ * CPU act_quant (cpu_act_quant, deepseek.rs:1484).  InvalidInput "cols ..
+ * not divisible by 128". */
+int objb_act_quant_device(const float *d_x, size_t rows, size_t cols, uint8_t *d_values,
+                          uint8_t *d_scales, objb_stream_t stream);
+
+/* cuda_fp8_act_fp4_weight_gemv_device (quant.rs:1284-1326): y[rows] = W a with
+ * a = act_quant output (E4M3 [cols] + E8M0 [cols/128]) and W the split FP4
+ * layout (weight [rows, cols/2], E8M0 [rows, cols/32]).  Block sums are exact
+ * integers (act * 2^9 in three 7-bit digits, 2 * FP4 in int8, dp4a). */
+int objb_gemv_fp8_fp4_device(const uint8_t *d_act, const uint8_t *d_act_scales,
+                             const void *d_weight, const void *d_weight_scales, float *d_y,
+                             size_t rows, size_t cols, objb_stream_t stream);
+
+/* cuda_fp8_act_fp8_weight_gemv_device (quant.rs:1328-1363): weight E4M3
+ * [rows, cols] with E8M0 scales on a 128 x 128 tile grid. */
+int objb_gemv_fp8_fp8_device(const uint8_t *d_act, const uint8_t *d_act_scales,
+                             const void *d_weight, const void *d_weight_scales, float *d_y,
+                             size_t rows, size_t cols, objb_stream_t stream);
+
+/* The routed experts of execute_selected_moe_official_routed_fp4_cuda
+ * (moe.rs:1393-1548) on a device-resident split-FP4 layer: act_quant(x) ->
+ * FP8 x FP4 gate/up with SwiGLU -> act_quant(act) -> FP8 x FP4 down with the
+ * weighted combine in selection order.  The SwiGLU is the official CPU
+ * path's (deepseek.rs:1707-1711): only the up value is clamped to
+ * +-swiglu_limit (the reference executor passes 10).  hidden and
+ * intermediate must be multiples of 512. */
+int objb_moe_official_scratch_bytes(const objb_moe_layer *layer, size_t top_k, size_t *bytes);
+int objb_moe_official_selected_device(const objb_moe_layer *layer, const int32_t *d_ids,
+                                      const float *d_weights, size_t top_k, const float *d_x,
+                                      float *d_out, float swiglu_limit, objb_stream_t stream);
+
+/* DeepSeekFp8SharedExpertWeightsDevice (moe.rs:1372-1379): device pointers. */
+typedef struct {
+  const void *gate_weight, *gate_scale;
+  const void *up_weight, *up_scale;
+  const void *down_weight, *down_scale;
+} objb_fp8_shared_expert;
+
+/* MoeExecutor::execute_selected_moe_official_routed_fp4_cuda (moe.rs:1393):
+ * host split-FP4 experts through the cache (as the native FP4 call), the
+ * official routed arithmetic, and, when `shared` is not NULL, the FP8 shared
+ * expert (act_quant -> FP8 x FP8 gate/up -> SwiGLU (up clamped to +-10) -> act_quant ->
+ * down) added with weight 1.  Telemetry as the reference (routed FP4 bytes,
+ * shared FP8 bytes, shared_expert_ms). */
+int objb_moe_execute_selected_official_fp4(
+    objb_moe_executor *ex, objb_stream_t stream, const objb_fp4_expert_weights *experts,
+    size_t num_experts, const int64_t *selected_ids, const float *selected_weights,
+    size_t num_selected, const float *x, size_t x_len, size_t hidden, size_t intermediate,
+    size_t out_dim, size_t layer_id, objb_expert_cache *cache,
+    const objb_fp8_shared_expert *shared, float *out, objb_moe_telemetry *telemetry);
+
 #ifdef __cplusplus
 }
 #endif

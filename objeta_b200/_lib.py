@@ -89,6 +89,11 @@ _SIGS = {
                                            c_void_p]),
     "objb_gemv_bf16_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_void_p]),
     "objb_compare_outputs": (c_int, [c_void_p, c_size, c_void_p, c_size, c_void_p]),
+    "objb_act_quant_device": (c_int, [c_void_p, c_size, c_size, c_void_p, c_void_p, c_void_p]),
+    "objb_gemv_fp8_fp4_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size, c_size,
+                                         c_void_p]),
+    "objb_gemv_fp8_fp8_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size, c_size,
+                                         c_void_p]),
     "objb_ffn_bf16_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p, c_void_p,
                                      c_int, ctypes.c_float, c_void_p]),
     "objb_quantize_matrix_device": (c_int, [c_int, c_void_p, c_size, c_size, c_void_p, c_void_p]),

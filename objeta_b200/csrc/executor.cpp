@@ -17,6 +17,7 @@
 #include "objb_common.h"
 #include "objb_launch.h"
 #include "objb_moe_launch.h"
+#include "objb_official_launch.h"
 
 namespace objb {
 int cache_get(objb_expert_cache* c, const objb_expert_cache_key* k, const void** out);
@@ -173,11 +174,18 @@ int resolve_expert(objb_expert_cache* cache, cudaStream_t stream, int fmt, bool 
 // The shared body of execute_selected_moe_cuda / _native_fp4_cuda.
 // tensors_of(k) fills the 3 (or 6) TensorRefs of selected expert k; the
 // device tables get one entry per selected slot.
+// The official DeepSeek variant of a call (execute_selected_moe_official_routed_fp4_cuda).
+struct Official {
+  float swiglu_limit = 10.0f;  // the reference executor's silu_mul limit (moe.rs:1525)
+  const objb_fp8_shared_expert* shared = nullptr;
+};
+
 template <class TensorsOf>
 int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, size_t num_selected,
             const int64_t* sel_ids, const float* sel_weights, const float* x, size_t hidden,
             size_t intermediate, size_t out_dim, size_t layer_id, objb_expert_cache* cache, float* out,
-            objb_moe_telemetry* tel, size_t single_expert_bytes, TensorsOf tensors_of) {
+            objb_moe_telemetry* tel, size_t single_expert_bytes, TensorsOf tensors_of,
+            const Official* official = nullptr) {
   DeviceGuard g;
   OBJB_TRY(g.enter(ex->device));
   const size_t K = num_selected;
@@ -258,18 +266,33 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
   }
   if (rc == OBJB_OK && K > 0) {
     size_t need = 0;
-    rc = moe_scratch_bytes(&layer, K, &need);
+    rc = official ? moe_official_scratch_bytes(&layer, K, &need) : moe_scratch_bytes(&layer, K, &need);
+    if (official && official->shared)
+      need = std::max(need, shared_expert_fp8_scratch(static_cast<int>(hidden), static_cast<int>(intermediate),
+                                                      static_cast<int>(out_dim)));
     if (rc == OBJB_OK) rc = grow_dev(&ex->d_scratch, &ex->d_scratch_cap, need, "allocate MoE scratch");
     if (rc == OBJB_OK) rc = cudaEventRecord(ev[3], stream) == cudaSuccess ? OBJB_OK : OBJB_ERR_RUNTIME;
     if (rc == OBJB_OK)
-      rc = moe_selected(&layer, d_ids, d_w, K, static_cast<const float*>(ex->d_x), static_cast<float*>(ex->d_out),
-                        0.0f, stream, ex->d_scratch, ex->d_scratch_cap, ev[4]);
+      rc = official ? moe_official_selected(&layer, d_ids, d_w, K, static_cast<const float*>(ex->d_x),
+                                            static_cast<float*>(ex->d_out), official->swiglu_limit, stream,
+                                            ex->d_scratch, ex->d_scratch_cap, ev[4])
+                    : moe_selected(&layer, d_ids, d_w, K, static_cast<const float*>(ex->d_x),
+                                   static_cast<float*>(ex->d_out), 0.0f, stream, ex->d_scratch, ex->d_scratch_cap,
+                                   ev[4]);
   } else if (rc == OBJB_OK) {
     cudaEventRecord(ev[3], stream);
     OBJB_CUDA(cudaMemsetAsync(ex->d_out, 0, out_dim * 4, stream), "zero output");
     cudaEventRecord(ev[4], stream);
   }
   if (rc == OBJB_OK) rc = cudaEventRecord(ev[5], stream) == cudaSuccess ? OBJB_OK : OBJB_ERR_RUNTIME;
+  const bool shared = official && official->shared;
+  if (rc == OBJB_OK && shared) {
+    // the shared expert reads the device x and adds onto the routed output
+    rc = shared_expert_fp8(official->shared, static_cast<const float*>(ex->d_x), static_cast<int>(hidden),
+                           static_cast<int>(intermediate), static_cast<int>(out_dim), official->swiglu_limit,
+                           static_cast<float*>(ex->d_out), stream, ex->d_scratch, ex->d_scratch_cap);
+    if (rc == OBJB_OK) rc = cudaEventRecord(ev[7], stream) == cudaSuccess ? OBJB_OK : OBJB_ERR_RUNTIME;
+  }
   if (rc == OBJB_OK) {
     cudaError_t e = cudaMemcpyAsync(out, ex->d_out, out_dim * 4, cudaMemcpyDeviceToHost, stream);
     if (e != cudaSuccess) rc = cuda_status(e, "copy output to host", __FILE__, __LINE__);
@@ -305,7 +328,13 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
     cudaEventElapsedTime(&h2d, ev[1], ev[2]);
     cudaEventElapsedTime(&gu, ev[3], ev[4]);
     cudaEventElapsedTime(&dn, ev[4], ev[5]);
-    cudaEventElapsedTime(&d2h, ev[5], ev[6]);
+    float sh_ms = 0;
+    if (shared) {
+      cudaEventElapsedTime(&sh_ms, ev[5], ev[7]);
+      cudaEventElapsedTime(&d2h, ev[7], ev[6]);
+    } else {
+      cudaEventElapsedTime(&d2h, ev[5], ev[6]);
+    }
     cudaEventElapsedTime(&tot, ev[0], ev[6]);
     tel->selected_expert_count = K;
     tel->logical_expert_bytes_requested = logical;
@@ -337,7 +366,21 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
     tel->down_qgemv_ms = dn;     // the weighted accumulate is fused into the down launch
     tel->accum_ms = 0.0f;
     tel->total_ms = tot;
-    tel->unaccounted_ms = std::max(0.0f, tot - h2d - gu - dn - d2h);
+    tel->unaccounted_ms = std::max(0.0f, tot - h2d - gu - dn - d2h - sh_ms);
+    if (official) {  // moe.rs:1612-1650
+      const size_t shared_bytes =
+          shared ? 2 * (intermediate * hidden) + out_dim * intermediate +
+                       2 * (intermediate * hidden / 128) + out_dim * intermediate / 128
+                 : 0;
+      tel->shared_expert_ms = sh_ms;
+      tel->routed_fp4_bytes_loaded = loaded;
+      tel->routed_fp4_bytes_reused = reused;
+      tel->shared_fp8_bytes_loaded = shared_bytes;
+      tel->shared_fp8_bytes_reused = 0;
+      tel->total_logical_bytes = unique.size() * single_expert_bytes + shared_bytes;
+      tel->total_loaded_bytes = loaded + shared_bytes;
+      tel->total_reused_bytes = reused;
+    }
     tel->bytes_gate = bytes_gate;
     tel->bytes_up = bytes_up;
     tel->bytes_down = bytes_down;
@@ -658,6 +701,49 @@ int objb_moe_execute_pairs(objb_moe_executor* ex, objb_stream_t stream, int fmt,
   return execute_pairs(ex, static_cast<cudaStream_t>(stream), fmt, experts, num_experts, pair_expert, pair_token,
                        pair_out, num_pairs, d_x, num_tokens, hidden, intermediate, out_dim, layer_id, cache, d_v,
                        v_rows, tel);
+}
+
+int objb_moe_execute_selected_official_fp4(objb_moe_executor* ex, objb_stream_t stream,
+                                           const objb_fp4_expert_weights* experts, size_t num_experts,
+                                           const int64_t* sel_ids, const float* sel_weights, size_t num_selected,
+                                           const float* x, size_t x_len, size_t hidden, size_t intermediate,
+                                           size_t out_dim, size_t layer_id, objb_expert_cache* cache,
+                                           const objb_fp8_shared_expert* shared, float* out,
+                                           objb_moe_telemetry* tel) {
+  clear_error();
+  if (!ex || !out || !x)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_execute_selected_official_fp4", "null argument");
+  std::lock_guard<std::mutex> lk(ex->mu);
+  OBJB_TRY(validate_common(x_len, hidden, intermediate, "execute_selected_moe_official_routed_fp4_cuda"));
+  if (hidden % 128 || intermediate % 128)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "validate official MoE shape",
+                     "hidden and intermediate must be multiples of 128 (act_quant blocks)");
+  const size_t guw = intermediate * (hidden / 2), gus = intermediate * (hidden / 32);
+  const size_t dnw = out_dim * (intermediate / 2), dns = out_dim * (intermediate / 32);
+  for (size_t k = 0; k < num_selected; ++k) {
+    OBJB_TRY(check_index(sel_ids[k], num_experts));
+    const objb_fp4_expert_weights& e = experts[sel_ids[k]];
+    if (e.gate_weight_len != guw) return fail_len("gate_weight", e.gate_weight_len, guw);
+    if (e.gate_scale_len != gus) return fail_len("gate_scale", e.gate_scale_len, gus);
+    if (e.up_weight_len != guw) return fail_len("up_weight", e.up_weight_len, guw);
+    if (e.up_scale_len != gus) return fail_len("up_scale", e.up_scale_len, gus);
+    if (e.down_weight_len != dnw) return fail_len("down_weight", e.down_weight_len, dnw);
+    if (e.down_scale_len != dns) return fail_len("down_scale", e.down_scale_len, dns);
+  }
+  auto tensors_of = [&](size_t k, TensorRef* t) {
+    const objb_fp4_expert_weights& e = experts[sel_ids[k]];
+    t[0] = TensorRef{e.gate_weight, e.gate_weight_len, OBJB_KIND_GATE_WEIGHT, false};
+    t[1] = TensorRef{e.gate_scale, e.gate_scale_len, OBJB_KIND_GATE_SCALE, true};
+    t[2] = TensorRef{e.up_weight, e.up_weight_len, OBJB_KIND_UP_WEIGHT, false};
+    t[3] = TensorRef{e.up_scale, e.up_scale_len, OBJB_KIND_UP_SCALE, true};
+    t[4] = TensorRef{e.down_weight, e.down_weight_len, OBJB_KIND_DOWN_WEIGHT, false};
+    t[5] = TensorRef{e.down_scale, e.down_scale_len, OBJB_KIND_DOWN_SCALE, true};
+  };
+  Official off;
+  off.shared = shared;
+  return execute(ex, static_cast<cudaStream_t>(stream), OBJB_FP4_E2M1, true, num_selected, sel_ids, sel_weights, x,
+                 hidden, intermediate, out_dim, layer_id, cache, out, tel, 2 * (guw + gus) + dnw + dns, tensors_of,
+                 &off);
 }
 
 }  // extern "C"

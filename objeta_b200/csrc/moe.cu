@@ -10,6 +10,8 @@
 #include "objb_host_launch.cuh"
 #include "objb_moe.cuh"
 #include "objb_moe_launch.h"
+#include "objb_official.cuh"
+#include "objb_official_launch.h"
 
 namespace objb {
 namespace dev {
@@ -539,6 +541,128 @@ int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t
   return OBJB_OK;
 }
 
+// ---- official DeepSeek routed experts (execute_selected_moe_official_routed_fp4_cuda,
+// moe.rs:1393-1548): act_quant(x) -> FP8 x FP4 gate/up with SwiGLU -> act_quant(act)
+// -> FP8 x FP4 down with the weighted combine.  Split-FP4 layers only.
+namespace {
+
+struct OfficialPlan {
+  RowLayoutHost lg, ld;
+  size_t codes_x = 0, scales_x = 0, act = 0, codes_a = 0, scales_a = 0, imgx = 0, imga = 0, total = 0;
+};
+
+int plan_official(const MoeShape& s, OfficialPlan* p) {
+  if (s.H % 512 || s.I % 512)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "plan official MoE", "hidden and intermediate must be multiples of 512");
+  if (!plan_fp8_fp4(s.I, s.H, true, &p->lg) || !plan_fp8_fp4(s.O, s.I, false, &p->ld))
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "plan official MoE", "shape does not fit the row pipeline");
+  auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  p->codes_x = r256(s.H);
+  p->scales_x = r256(s.H / 128);
+  p->act = r256(static_cast<size_t>(s.K) * s.I * 4);
+  p->codes_a = r256(static_cast<size_t>(s.K) * s.I);
+  p->scales_a = r256(static_cast<size_t>(s.K) * s.I / 128);
+  p->imgx = fp8_image_quads(p->lg) * 16;
+  p->imga = fp8_image_quads(p->ld) * 16 * s.K;
+  p->total = p->codes_x + p->scales_x + p->act + p->codes_a + p->scales_a + p->imgx + p->imga + 256;
+  return OBJB_OK;
+}
+
+}  // namespace
+
+int moe_official_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_layer(l, top_k, &s, &split));
+  if (!split) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "plan official MoE", "needs a split FP4 layer (scale tables)");
+  OfficialPlan p;
+  OBJB_TRY(plan_official(s, &p));
+  *out = p.total;
+  return OBJB_OK;
+}
+
+int moe_official_selected(const objb_moe_layer* l, const int32_t* ids, const float* weights, size_t top_k,
+                          const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
+                          size_t scratch_bytes, cudaEvent_t mid, unsigned* err_word) {
+  MoeShape s;
+  bool split = false;
+  OBJB_TRY(validate_layer(l, top_k, &s, &split));
+  if (!split) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run official MoE", "needs a split FP4 layer (scale tables)");
+  if (!ids || !weights || !x || !out) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run official MoE", "null device pointer");
+  if (l->flags & OBJB_MOE_UNALIGNED)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "run official MoE", "expert tensors must be 16-byte aligned");
+  OfficialPlan p;
+  OBJB_TRY(plan_official(s, &p));
+  if (scratch_bytes < p.total)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run official MoE",
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(p.total));
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  unsigned* err = err_word;
+  if (!err) OBJB_TRY(device_error_word(device, &err));
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  uint8_t* codes_x = sc;
+  uint8_t* scales_x = codes_x + p.codes_x;
+  float* act = reinterpret_cast<float*>(scales_x + p.scales_x);
+  uint8_t* codes_a = reinterpret_cast<uint8_t*>(act) + p.act;
+  uint8_t* scales_a = codes_a + p.codes_a;
+  uint4* imgx = reinterpret_cast<uint4*>(scales_a + p.scales_a);
+  uint4* imga = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(imgx) + p.imgx);
+  const dev::ExpertTables t = tables_of(*l);
+  OBJB_TRY(act_quant(x, 1, s.H, codes_x, scales_x, stream, "act_quant hidden"));
+  OBJB_TRY(launch_ximage_fp8(p.lg, codes_x, scales_x, 1, imgx, 0, stream));
+  {
+    const int total = s.K * s.I;
+    int R = (total + props.sm_count - 1) / props.sm_count;
+    R = (R + 3) / 4 * 4;
+    dev::GateUpProg prog;
+    prog.t = t;
+    prog.ids = ids;
+    prog.ximg = imgx;
+    prog.act = act;
+    prog.K = s.K;
+    prog.I = s.I;
+    prog.rows_per_cta = R;
+    prog.swiglu_limit = limit;
+    prog.err = err;
+    prog.clamp_gate = false;
+    const size_t smem = pipe_smem_bytes(p.lg);
+    auto kernel = dev::pipe_kernel<dev::RowDotFp8Fp4, dev::GateUpProg, true>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.lg, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, (total + R - 1) / R, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  if (mid) OBJB_CUDA(cudaEventRecord(mid, stream), "record gate/up end");
+  OBJB_TRY(act_quant(act, s.K, s.I, codes_a, scales_a, stream, "act_quant intermediate"));
+  const size_t qa = fp8_image_quads(p.ld);
+  OBJB_TRY(launch_ximage_fp8(p.ld, codes_a, scales_a, s.K, imga, qa, stream));
+  {
+    int R = (s.O + props.sm_count - 1) / props.sm_count;
+    R = (R + 3) / 4 * 4;
+    dev::DownProg prog;
+    prog.t = t;
+    prog.ids = ids;
+    prog.weights = weights;
+    prog.ximg = imga;
+    prog.img_stride = qa;
+    prog.out = out;
+    prog.K = s.K;
+    prog.O = s.O;
+    prog.rows_per_cta = R;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(p.ld);
+    auto kernel = dev::pipe_kernel<dev::RowDotFp8Fp4, dev::DownProg, false>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &p.ld, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, (s.O + R - 1) / R, (p.ld.nseg * p.ld.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  return OBJB_OK;
+}
+
 int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream) {
   if (!logits || !ids || !weights)
@@ -629,6 +753,27 @@ int objb_router_topk_batched_device(const float* d_logits, size_t num_tokens, si
   objb::clear_error();
   return objb::router_topk_batched(d_logits, num_tokens, num_experts, top_k, renormalize, d_ids, d_weights,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int objb_moe_official_scratch_bytes(const objb_moe_layer* layer, size_t top_k, size_t* bytes) {
+  objb::clear_error();
+  if (!bytes) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_official_scratch_bytes", "null output pointer");
+  return objb::moe_official_scratch_bytes(layer, top_k, bytes);
+}
+
+int objb_moe_official_selected_device(const objb_moe_layer* layer, const int32_t* d_ids, const float* d_weights,
+                                      size_t top_k, const float* d_x, float* d_out, float swiglu_limit,
+                                      objb_stream_t stream_) {
+  objb::clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  OBJB_TRY(objb::moe_official_scratch_bytes(layer, top_k, &need));
+  int device = 0;
+  OBJB_TRY(objb::current_device(&device));
+  void* ws = nullptr;
+  OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
+  return objb::moe_official_selected(layer, d_ids, d_weights, top_k, d_x, d_out, swiglu_limit, stream, ws, need,
+                                     nullptr, nullptr);
 }
 
 }  // extern "C"

@@ -18,10 +18,12 @@ namespace dev {
 // silu_mul (crates/objeta-cuda/kernels/moe.cu:2-22): with limit > 0 the up
 // value is clamped to [-limit, limit] and the gate to <= limit; then
 // act = g / (1 + exp(-g)) * u.
-__device__ __forceinline__ float swiglu(float g, float u, float limit) {
+// The official DeepSeek experts (deepseek.rs:1675-1680, 1707-1711) clamp only
+// the up value: clamp_gate = false.
+__device__ __forceinline__ float swiglu(float g, float u, float limit, bool clamp_gate = true) {
   if (limit > 0.0f) {
     u = fminf(limit, fmaxf(-limit, u));
-    g = fminf(limit, g);
+    if (clamp_gate) g = fminf(limit, g);
   }
   const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
   return __fmul_rn(silu, u);
@@ -58,6 +60,7 @@ struct GateUpProg {
   int rows_per_cta;
   float swiglu_limit;
   unsigned* err;
+  bool clamp_gate = true;  // false: the official experts' SwiGLU (up clamped only)
 
   __device__ __forceinline__ int first_k(int cta) const { return (cta * rows_per_cta) / I; }
   __device__ __forceinline__ int njobs(int cta) const {
@@ -83,7 +86,7 @@ struct GateUpProg {
   }
   __device__ __forceinline__ void epilogue(int cta, int j, int row, float va, float vb) const {
     const int k = first_k(cta) + j;
-    act[static_cast<size_t>(k) * I + row] = swiglu(va, vb, swiglu_limit);
+    act[static_cast<size_t>(k) * I + row] = swiglu(va, vb, swiglu_limit, clamp_gate);
   }
   __device__ __forceinline__ void finalize(int, int, int) const {}
 };

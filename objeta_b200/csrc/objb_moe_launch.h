@@ -33,6 +33,12 @@ int moe_combine(const float* v, size_t v_rows, const int32_t* slot_row, const fl
 int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t top_k, int renorm, int32_t* ids,
                         float* weights, cudaStream_t stream);
 
+// Official DeepSeek routed experts (FP8 activations, split FP4 weights).
+int moe_official_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out);
+int moe_official_selected(const objb_moe_layer* l, const int32_t* ids, const float* weights, size_t top_k,
+                          const float* x, float* out, float limit, cudaStream_t stream, void* scratch,
+                          size_t scratch_bytes, cudaEvent_t mid = nullptr, unsigned* err_word = nullptr);
+
 int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t* ids, float* weights,
                 cudaStream_t stream);
 

@@ -108,6 +108,24 @@ class _TelC(ctypes.Structure):
                 + [(n, c_size) for n in _TEL_TAIL_FIELDS])
 
 
+class _SharedFp8C(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("gate_weight", "gate_scale", "up_weight", "up_scale", "down_weight",
+                                        "down_scale")]
+
+
+@dataclass
+class DeepSeekFp8SharedExpertWeightsDevice:
+    """moe.rs:1372-1379: the FP8 shared expert, device tensors (uint8):
+    E4M3 weights gate / up [inter, hidden], down [hidden, inter] and E8M0
+    scales on a 128 x 128 tile grid."""
+    gate_weight: object
+    gate_scale: object
+    up_weight: object
+    up_scale: object
+    down_weight: object
+    down_scale: object
+
+
 class _LayerC(ctypes.Structure):
     _fields_ = [("fmt", c_int), ("flags", ctypes.c_uint32), ("hidden", c_size), ("intermediate", c_size),
                 ("out_dim", c_size), ("num_experts", c_size), ("d_gate", c_void_p), ("d_up", c_void_p),
@@ -150,6 +168,13 @@ _lib.register_signatures({
                                        c_void_p, c_void_p, c_size, c_void_p, c_size, c_size, c_size, c_size,
                                        c_size, c_void_p, c_void_p, c_size, ctypes.POINTER(_TelC)]),
     "objb_moe_scratch_bytes": (c_int, [ctypes.POINTER(_LayerC), c_size, ctypes.POINTER(c_size)]),
+    "objb_moe_official_selected_device": (c_int, [ctypes.POINTER(_LayerC), c_void_p, c_void_p, c_size, c_void_p,
+                                                  c_void_p, ctypes.c_float, c_void_p]),
+    "objb_moe_execute_selected_official_fp4": (c_int, [c_void_p, c_void_p, ctypes.POINTER(_Fp4ExpertC), c_size,
+                                                       c_void_p, c_void_p, c_size, c_void_p, c_size, c_size,
+                                                       c_size, c_size, c_size, c_void_p,
+                                                       ctypes.POINTER(_SharedFp8C), c_void_p,
+                                                       ctypes.POINTER(_TelC)]),
     "objb_router_topk_device": (c_int, [c_void_p, c_size, c_size, c_int, c_void_p, c_void_p, c_void_p]),
     "objb_moe_selected_device": (c_int, [ctypes.POINTER(_LayerC), c_void_p, c_void_p, c_size, c_void_p,
                                          c_void_p, ctypes.c_float, c_void_p]),
@@ -435,6 +460,32 @@ class MoeExecutor:
                   cache._h if cache is not None else None, _dev_ptr(d_v), d_v.shape[0], ctypes.byref(tel))
         return MoeTelemetry._from_c(tel)
 
+    def execute_selected_moe_official_routed_fp4_cuda(self, quant, stream, experts, selected_experts, x, hidden,
+                                                      intermediate, out_dim, layer_id, cache=None,
+                                                      shared_expert=None):
+        """moe.rs:1393-1660: the official DeepSeek arithmetic (act_quant +
+        FP8 x FP4 routed experts, optional FP8 shared expert on the device)."""
+        names = ("gate_weight", "gate_scale", "up_weight", "up_scale", "down_weight", "down_scale")
+        keep = [[_host_u8(getattr(e, n)) for n in names] for e in experts]
+        arr = (_Fp4ExpertC * max(1, len(keep)))()
+        for i, ts in enumerate(keep):
+            vals = []
+            for t in ts:
+                vals += [t.ctypes.data_as(c_u8p), t.size]
+            arr[i] = _Fp4ExpertC(*vals)
+        ids, ws = _selection(selected_experts)
+        xv = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        out = np.zeros(out_dim, dtype=np.float32)
+        tel = _TelC()
+        sh = None
+        if shared_expert is not None:
+            sh = _SharedFp8C(*[_dev_ptr(getattr(shared_expert, n)) for n in names])
+        _lib.call("objb_moe_execute_selected_official_fp4", self._h, _lib.stream_handle(stream), arr, len(keep),
+                  ids.ctypes.data, ws.ctypes.data, ids.size, xv.ctypes.data, xv.size, hidden, intermediate,
+                  out_dim, layer_id, cache._h if cache is not None else None,
+                  ctypes.byref(sh) if sh is not None else None, out.ctypes.data, ctypes.byref(tel))
+        return out, MoeTelemetry._from_c(tel)
+
     def execute_selected_moe_native_fp4_cuda(self, quant, stream, experts, selected_experts, x, hidden,
                                              intermediate, out_dim, layer_id, cache=None):
         """moe.rs:816-1280."""
@@ -529,6 +580,17 @@ class MoeLayer:
         (objb_moe_selected_device_noalloc); ``d_out`` must be given.  Calls
         that overlap on the GPU share that array and race."""
         _lib.call("objb_moe_selected_device_noalloc", ctypes.byref(self._c), _dev_ptr(d_ids), _dev_ptr(d_weights),
+                  d_ids.numel(), _dev_ptr(d_x), _dev_ptr(d_out), float(swiglu_limit), _lib.stream_handle(stream))
+        return d_out
+
+    def forward_official_selected(self, d_ids, d_weights, d_x, d_out=None, swiglu_limit: float = 10.0,
+                                  stream=None):
+        """The official DeepSeek routed arithmetic on this split-FP4 layer
+        (objb_moe_official_selected_device)."""
+        import torch
+        if d_out is None:
+            d_out = torch.empty(self.out_dim, dtype=torch.float32, device=self.device)
+        _lib.call("objb_moe_official_selected_device", ctypes.byref(self._c), _dev_ptr(d_ids), _dev_ptr(d_weights),
                   d_ids.numel(), _dev_ptr(d_x), _dev_ptr(d_out), float(swiglu_limit), _lib.stream_handle(stream))
         return d_out
 

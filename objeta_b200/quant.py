@@ -289,3 +289,47 @@ def compare_outputs(reference, actual) -> QGemvNumerics:
 
 
 q4_compare = q5_compare = fp4_compare = compare_outputs
+
+
+# ---------------------------------------------------- official DeepSeek activation path
+def act_quant_device(d_x, rows: int, cols: int, stream=None):
+    """cuda_act_quant_device (quant.rs:1229-1282): rows x cols f32 on the
+    device -> (E4M3 codes uint8 [rows*cols], E8M0 scales uint8 [rows*cols/128]),
+    bit-identical to the reference CPU act_quant."""
+    import torch
+    vals = torch.empty(rows * cols, dtype=torch.uint8, device=d_x.device)
+    scales = torch.empty(max(1, rows * cols // 128), dtype=torch.uint8, device=d_x.device)
+    _lib.call("objb_act_quant_device", _dev_ptr(d_x), rows, cols, _dev_ptr(vals), _dev_ptr(scales),
+              _lib.stream_handle(stream))
+    return vals, scales[: rows * cols // 128]
+
+
+def cuda_act_quant(backend, stream, x, rows: int, cols: int):
+    """cuda_act_quant (quant.rs:1119-1227), host slice in and out: returns
+    (codes, scales) numpy arrays."""
+    import torch
+    xv = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    if cols % 128:
+        raise _lib.CudaError(5, f"InvalidInput error during cuda_act_quant at objeta_b200::quant.py (quant.py): "
+                                f"cols {cols} not divisible by 128")
+    if xv.size != rows * cols:
+        raise _lib.CudaError(5, f"InvalidInput error during cuda_act_quant at objeta_b200::quant.py (quant.py): "
+                                f"input len {xv.size} != rows {rows} * cols {cols}")
+    dev = getattr(backend, "device", 0)
+    with torch.cuda.device(dev):
+        v, s = act_quant_device(torch.from_numpy(xv).to(f"cuda:{dev}"), rows, cols, stream)
+        return v.cpu().numpy(), s.cpu().numpy()
+
+
+def gemv_fp8_fp4_device(d_act, d_act_scales, d_weight, d_weight_scales, d_y, rows: int, cols: int, stream=None):
+    """cuda_fp8_act_fp4_weight_gemv_device (quant.rs:1284-1326)."""
+    _lib.call("objb_gemv_fp8_fp4_device", _dev_ptr(d_act), _dev_ptr(d_act_scales), _dev_ptr(d_weight),
+              _dev_ptr(d_weight_scales), _dev_ptr(d_y), rows, cols, _lib.stream_handle(stream))
+    return d_y
+
+
+def gemv_fp8_fp8_device(d_act, d_act_scales, d_weight, d_weight_scales, d_y, rows: int, cols: int, stream=None):
+    """cuda_fp8_act_fp8_weight_gemv_device (quant.rs:1328-1363)."""
+    _lib.call("objb_gemv_fp8_fp8_device", _dev_ptr(d_act), _dev_ptr(d_act_scales), _dev_ptr(d_weight),
+              _dev_ptr(d_weight_scales), _dev_ptr(d_y), rows, cols, _lib.stream_handle(stream))
+    return d_y

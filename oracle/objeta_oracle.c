@@ -696,3 +696,163 @@ void oro_seeded_f32s(size_t len, uint64_t seed, float *out) {
     out[i] = unit * 2.0f - 1.0f;
   }
 }
+
+/* ---------------------------------------------------------------------------
+ * Official DeepSeek arithmetic (activations quantized to FP8), restated from
+ * crates/objeta-parser/src/deepseek.rs:1444-1715.
+ * ------------------------------------------------------------------------- */
+
+/* deepseek.rs:1444-1481 (f32_to_f8e4m3_exact).  Below 2^-7 the subnormal
+ * branch rounds |v| * 16 (always 0 there); [2^-7, 2^-6) encodes with exponent
+ * field 0; >= 448 saturates to 0x7E / 0xFE. */
+uint8_t oro_f32_to_f8e4m3_exact(float v) {
+  const float a = fabsf(v);
+  if (a < 1.0f / 128.0f) {
+    const uint8_t sign = v < 0.0f ? 0x80 : 0;
+    uint8_t q = rs_as_u8(roundf(a * 16.0f));
+    if (q > 7) q = 7;
+    return (uint8_t)(sign | q);
+  }
+  if (a >= 448.0f) return v < 0.0f ? 0xFE : 0x7E;
+  const uint8_t sign = v < 0.0f ? 0x80 : 0;
+  const uint32_t bits = f32_to_bits(a);
+  const int32_t exp32 = (int32_t)((bits >> 23) & 0xFF) - 127;
+  int32_t exp_f8 = exp32 + 7;
+  if (exp_f8 < 0) exp_f8 = 0;
+  const uint32_t mant_bits = bits & 0x7FFFFF;
+  uint8_t mant3 = (uint8_t)((mant_bits + (1u << 19)) >> 20);
+  uint8_t exp_final = (uint8_t)exp_f8;
+  if (mant3 >= 8) {
+    mant3 = 0;
+    exp_final = exp_final == 255 ? 255 : (uint8_t)(exp_final + 1);
+  }
+  if (exp_final > 14) {
+    exp_final = 14;
+    mant3 = 7;
+  }
+  return (uint8_t)(sign | (uint8_t)(exp_final << 3) | (mant3 & 7));
+}
+
+/* deepseek.rs:1484-1525 (cpu_act_quant): per block, amax = max(|x|, 1e-4),
+ * scale = 2^ceil(log2(amax * (1/448))), y = e4m3(clamp(x / scale, +-448)),
+ * s = clamp(log2 scale + 127, 0, 255).  n % block == 0. */
+int oro_act_quant(const float *x, size_t n, size_t block, uint8_t *y, uint8_t *s) {
+  if (block == 0 || n % block) return -1;
+  const float inv = 1.0f / 448.0f;
+  for (size_t b = 0; b < n / block; ++b) {
+    float amax = 0.0f;
+    for (size_t i = b * block; i < (b + 1) * block; ++i) {
+      const float a = fabsf(x[i]);
+      if (a > amax) amax = a;
+    }
+    amax = rs_max(amax, 1e-4f);
+    const float raw = amax * inv;
+    int32_t lc = -127;
+    if (raw > 0.0f) {
+      const float c = ceilf(log2f(raw));
+      if (c != c) lc = 0;
+      else if (c >= 2147483647.0f) lc = 2147483647;
+      else if (c <= -2147483648.0f) lc = (int32_t)-2147483647 - 1;
+      else lc = (int32_t)c;
+    }
+    const float scale = ldexpf(1.0f, lc);
+    const int64_t e = (int64_t)lc + 127;
+    s[b] = (uint8_t)(e < 0 ? 0 : (e > 255 ? 255 : e));
+    for (size_t i = b * block; i < (b + 1) * block; ++i)
+      y[i] = oro_f32_to_f8e4m3_exact(rs_clamp(x[i] / scale, -448.0f, 448.0f));
+  }
+  return 0;
+}
+
+/* deepseek.rs:1528-1570 (cpu_fp8_act_fp4_weight_gemv_f32): sequential f32
+ * sum over the packed bytes, low nibble then high, each term
+ * ((act * act_scale) * fp4) * weight_scale; act blocks of 128, weight
+ * blocks of 32, parser FP4 table (code 8 = +0.0). */
+void oro_fp8_act_fp4_weight_gemv_f32(const uint8_t *act, const uint8_t *act_s, const uint8_t *w,
+                                     const uint8_t *ws, size_t rows, size_t cols, float *y) {
+  const size_t phys = cols / 2, scols = cols / 32;
+  for (size_t r = 0; r < rows; ++r) {
+    float sum = 0.0f;
+    for (size_t cg = 0; cg < phys; ++cg) {
+      const uint8_t b = w[r * phys + cg];
+      const size_t lo = cg * 2, hi = lo + 1;
+      const float t_lo = oro_f8e4m3_to_f32(act[lo]) * oro_f8e8m0_to_f32(act_s[lo / 128]) *
+                         FP4_E2M1FN_TABLE[b & 0x0F] * oro_f8e8m0_to_f32(ws[r * scols + lo / 32]);
+      const float t_hi = oro_f8e4m3_to_f32(act[hi]) * oro_f8e8m0_to_f32(act_s[hi / 128]) *
+                         FP4_E2M1FN_TABLE[(b >> 4) & 0x0F] * oro_f8e8m0_to_f32(ws[r * scols + hi / 32]);
+      sum += t_lo;
+      sum += t_hi;
+    }
+    y[r] = sum;
+  }
+}
+
+/* deepseek.rs:1630-1660 (cpu_fp8_act_fp8_weight_gemv): f64 sum of
+ * act * act_scale * w * w_scale; weight scales on a 128 x 128 tile grid. */
+void oro_fp8_act_fp8_weight_gemv(const uint8_t *act, const uint8_t *act_s, const uint8_t *w,
+                                 const uint8_t *ws, size_t rows, size_t cols, float *y) {
+  const size_t wsc = (cols + 127) / 128;
+  for (size_t r = 0; r < rows; ++r) {
+    double sum = 0.0;
+    for (size_t c = 0; c < cols; ++c) {
+      sum += (double)oro_f8e4m3_to_f32(act[c]) * (double)oro_f8e8m0_to_f32(act_s[c / 128]) *
+             (double)oro_f8e4m3_to_f32(w[r * cols + c]) * (double)oro_f8e8m0_to_f32(ws[(r / 128) * wsc + c / 128]);
+    }
+    y[r] = (float)sum;
+  }
+}
+
+/* SwiGLU of the official experts (deepseek.rs:1675-1680, 1707-1711): only
+ * the up value is clamped; act = g / (1 + exp(-g)) * clamp(u). */
+static void official_swiglu(const float *g, const float *u, size_t n, float limit, float *act) {
+  for (size_t i = 0; i < n; ++i) {
+    const float uu = rs_clamp(u[i], -limit, limit);
+    act[i] = g[i] / (1.0f + expf(-g[i])) * uu;
+  }
+}
+
+/* deepseek.rs:1690-1715 (cpu_routed_expert_fp4_official_f32): act_quant(x),
+ * gate / up fp8 x fp4 GEMVs, SwiGLU, act_quant(act), down GEMV. */
+int oro_routed_expert_fp4_official_f32(const uint8_t *gw, const uint8_t *gs, const uint8_t *uw, const uint8_t *us,
+                                       const uint8_t *dw, const uint8_t *ds, const float *x, size_t dim,
+                                       size_t inter, size_t out_dim, float swiglu_limit, float *out) {
+  if (dim % 128 || inter % 128) return -1;
+  uint8_t *a = (uint8_t *)malloc(dim), *as = (uint8_t *)malloc(dim / 128);
+  uint8_t *a2 = (uint8_t *)malloc(inter), *as2 = (uint8_t *)malloc(inter / 128);
+  float *g = (float *)malloc(inter * 4), *u = (float *)malloc(inter * 4), *act = (float *)malloc(inter * 4);
+  int rc = -2;
+  if (a && as && a2 && as2 && g && u && act) {
+    oro_act_quant(x, dim, 128, a, as);
+    oro_fp8_act_fp4_weight_gemv_f32(a, as, gw, gs, inter, dim, g);
+    oro_fp8_act_fp4_weight_gemv_f32(a, as, uw, us, inter, dim, u);
+    official_swiglu(g, u, inter, swiglu_limit, act);
+    oro_act_quant(act, inter, 128, a2, as2);
+    oro_fp8_act_fp4_weight_gemv_f32(a2, as2, dw, ds, out_dim, inter, out);
+    rc = 0;
+  }
+  free(a); free(as); free(a2); free(as2); free(g); free(u); free(act);
+  return rc;
+}
+
+/* deepseek.rs:1662-1688 (cpu_shared_expert_fp8_official): the same with fp8
+ * x fp8 GEMVs (f64 sums). */
+int oro_shared_expert_fp8_official(const uint8_t *w1, const uint8_t *s1, const uint8_t *w3, const uint8_t *s3,
+                                   const uint8_t *w2, const uint8_t *s2, const float *x, size_t dim, size_t inter,
+                                   float swiglu_limit, float *out) {
+  if (dim % 128 || inter % 128) return -1;
+  uint8_t *a = (uint8_t *)malloc(dim), *as = (uint8_t *)malloc(dim / 128);
+  uint8_t *a2 = (uint8_t *)malloc(inter), *as2 = (uint8_t *)malloc(inter / 128);
+  float *g = (float *)malloc(inter * 4), *u = (float *)malloc(inter * 4), *act = (float *)malloc(inter * 4);
+  int rc = -2;
+  if (a && as && a2 && as2 && g && u && act) {
+    oro_act_quant(x, dim, 128, a, as);
+    oro_fp8_act_fp8_weight_gemv(a, as, w1, s1, inter, dim, g);
+    oro_fp8_act_fp8_weight_gemv(a, as, w3, s3, inter, dim, u);
+    official_swiglu(g, u, inter, swiglu_limit, act);
+    oro_act_quant(act, inter, 128, a2, as2);
+    oro_fp8_act_fp8_weight_gemv(a2, as2, w2, s2, dim, inter, out);
+    rc = 0;
+  }
+  free(a); free(as); free(a2); free(as2); free(g); free(u); free(act);
+  return rc;
+}

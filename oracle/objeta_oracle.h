@@ -87,6 +87,22 @@ int oro_router(const float *router_weights, const float *hidden,
 
 void oro_seeded_f32s(size_t len, uint64_t seed, float *out);
 
+/* Official DeepSeek arithmetic (deepseek.rs:1444-1715). */
+uint8_t oro_f32_to_f8e4m3_exact(float v);
+int oro_act_quant(const float *x, size_t n, size_t block, uint8_t *y, uint8_t *s);
+void oro_fp8_act_fp4_weight_gemv_f32(const uint8_t *act, const uint8_t *act_s, const uint8_t *w,
+                                     const uint8_t *ws, size_t rows, size_t cols, float *y);
+void oro_fp8_act_fp8_weight_gemv(const uint8_t *act, const uint8_t *act_s, const uint8_t *w,
+                                 const uint8_t *ws, size_t rows, size_t cols, float *y);
+int oro_routed_expert_fp4_official_f32(const uint8_t *gw, const uint8_t *gs, const uint8_t *uw,
+                                       const uint8_t *us, const uint8_t *dw, const uint8_t *ds,
+                                       const float *x, size_t dim, size_t inter, size_t out_dim,
+                                       float swiglu_limit, float *out);
+int oro_shared_expert_fp8_official(const uint8_t *w1, const uint8_t *s1, const uint8_t *w3,
+                                   const uint8_t *s3, const uint8_t *w2, const uint8_t *s2,
+                                   const float *x, size_t dim, size_t inter, float swiglu_limit,
+                                   float *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -90,6 +90,21 @@ def lib():
                                      ctypes.c_size_t, _c_i64p, _c_f32p]
             L.oro_seeded_f32s.restype = None
             L.oro_seeded_f32s.argtypes = [ctypes.c_size_t, ctypes.c_uint64, _c_f32p]
+            L.oro_f32_to_f8e4m3_exact.restype = ctypes.c_uint8
+            L.oro_f32_to_f8e4m3_exact.argtypes = [ctypes.c_float]
+            L.oro_act_quant.restype = ctypes.c_int
+            L.oro_act_quant.argtypes = [_c_f32p, ctypes.c_size_t, ctypes.c_size_t, _c_u8p, _c_u8p]
+            for n in ("oro_fp8_act_fp4_weight_gemv_f32", "oro_fp8_act_fp8_weight_gemv"):
+                getattr(L, n).restype = None
+                getattr(L, n).argtypes = [_c_u8p, _c_u8p, _c_u8p, _c_u8p, ctypes.c_size_t, ctypes.c_size_t,
+                                          _c_f32p]
+            L.oro_routed_expert_fp4_official_f32.restype = ctypes.c_int
+            L.oro_routed_expert_fp4_official_f32.argtypes = [_c_u8p] * 6 + [_c_f32p, ctypes.c_size_t,
+                                                                            ctypes.c_size_t, ctypes.c_size_t,
+                                                                            ctypes.c_float, _c_f32p]
+            L.oro_shared_expert_fp8_official.restype = ctypes.c_int
+            L.oro_shared_expert_fp8_official.argtypes = [_c_u8p] * 6 + [_c_f32p, ctypes.c_size_t, ctypes.c_size_t,
+                                                                        ctypes.c_float, _c_f32p]
             _lib = L
     return _lib
 
@@ -283,3 +298,64 @@ def compare_outputs(reference, actual):
     rel = np.sqrt(sq) / np.sqrt(rn) if rn > 0 else 0.0
     return {"cosine_similarity": float(cos), "relative_l2_error": float(rel),
             "max_abs_error": max_abs}
+
+
+# ---------------------------------------------------------------- official DeepSeek path
+def f32_to_f8e4m3_exact(v: float) -> int:
+    """deepseek.rs:1444-1481."""
+    return int(lib().oro_f32_to_f8e4m3_exact(ctypes.c_float(v)))
+
+
+def act_quant(x, block: int = 128):
+    """deepseek.rs:1484-1525 (cpu_act_quant) -> (E4M3 codes, E8M0 scales)."""
+    xv = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    y = np.zeros(xv.size, np.uint8)
+    s = np.zeros(xv.size // block if block else 0, np.uint8)
+    if lib().oro_act_quant(_f32(xv), xv.size, block, _u8(y), _u8(s)) != 0:
+        raise ValueError("input length must be multiple of block_size")
+    return y, s
+
+
+def _u8c(a):
+    return np.ascontiguousarray(a, dtype=np.uint8).reshape(-1)
+
+
+def fp8_act_fp4_weight_gemv_f32(act, act_s, w, ws, rows: int, cols: int) -> np.ndarray:
+    """deepseek.rs:1528-1570 (sequential f32 sum)."""
+    a, as_, wv, wsv = _u8c(act), _u8c(act_s), _u8c(w), _u8c(ws)
+    y = np.zeros(rows, np.float32)
+    lib().oro_fp8_act_fp4_weight_gemv_f32(_u8(a), _u8(as_), _u8(wv), _u8(wsv), rows, cols, _f32(y))
+    return y
+
+
+def fp8_act_fp8_weight_gemv(act, act_s, w, ws, rows: int, cols: int) -> np.ndarray:
+    """deepseek.rs:1630-1660 (f64 sum)."""
+    a, as_, wv, wsv = _u8c(act), _u8c(act_s), _u8c(w), _u8c(ws)
+    y = np.zeros(rows, np.float32)
+    lib().oro_fp8_act_fp8_weight_gemv(_u8(a), _u8(as_), _u8(wv), _u8(wsv), rows, cols, _f32(y))
+    return y
+
+
+def routed_expert_fp4_official_f32(gw, gs, uw, us, dw, ds, x, dim: int, inter: int, out_dim: int,
+                                   swiglu_limit: float) -> np.ndarray:
+    """deepseek.rs:1690-1715 (cpu_routed_expert_fp4_official_f32)."""
+    ts = [_u8c(t) for t in (gw, gs, uw, us, dw, ds)]
+    xv = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.zeros(out_dim, np.float32)
+    rc = lib().oro_routed_expert_fp4_official_f32(*[_u8(t) for t in ts], _f32(xv), dim, inter, out_dim,
+                                                  ctypes.c_float(swiglu_limit), _f32(out))
+    if rc != 0:
+        raise ValueError(f"oro_routed_expert_fp4_official_f32 rc={rc}")
+    return out
+
+
+def shared_expert_fp8_official(w1, s1, w3, s3, w2, s2, x, dim: int, inter: int, swiglu_limit: float) -> np.ndarray:
+    """deepseek.rs:1662-1688 (cpu_shared_expert_fp8_official)."""
+    ts = [_u8c(t) for t in (w1, s1, w3, s3, w2, s2)]
+    xv = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.zeros(dim, np.float32)
+    rc = lib().oro_shared_expert_fp8_official(*[_u8(t) for t in ts], _f32(xv), dim, inter,
+                                              ctypes.c_float(swiglu_limit), _f32(out))
+    if rc != 0:
+        raise ValueError(f"oro_shared_expert_fp8_official rc={rc}")
+    return out

@@ -178,3 +178,40 @@ def test_native_fp4_expert_bytes():
     # moe.rs:2474-2478: 6 tensors of a 256/512/256 expert = 208896 bytes
     h, i, o = 256, 512, 256
     assert (i * h // 2) * 2 + (i * h // 32) * 2 + (o * i // 2) + (o * i // 32) == 208896
+
+
+# ---------------------------------------------- official DeepSeek path (deepseek.rs)
+def test_act_quant_fixture():
+    """deepseek.rs:1382-1394 (test_act_quant_fixture): block 8, scales 127 and 120."""
+    x = np.array([1.0, 448.0, -448.0, 0.0, 100.0, 200.0, -100.0, -200.0,
+                  1.0, 2.0, 0.5, -0.5, 0.0, 0.0, 0.0, 0.0], np.float32)
+    y, s = O.act_quant(x, 8)
+    assert y.size == 16 and s.size == 2
+    assert s.tolist() == [127, 120]
+
+
+def test_f32_to_f8e4m3_exact_codes():
+    """deepseek.rs:1444-1481: the encoder's branches, and decode(encode(v)) == v
+    for every normal E4M3 value (exponent fields 1..14)."""
+    enc = O.f32_to_f8e4m3_exact
+    assert enc(1.0) == 0x38 and enc(2.0) == 0x40 and enc(3.0) == 0x44 and enc(4.0) == 0x48
+    assert enc(448.0) == 0x7E and enc(-1000.0) == 0xFE
+    assert enc(0.001) == 0 and enc(-0.001) == 0x80         # below 2^-7: flushed (signed)
+    assert enc(1.5 / 128) == 0x04                           # [2^-7, 2^-6): exponent field 0
+    for c in range(256):
+        e = (c >> 3) & 15
+        if 1 <= e <= 14:
+            v = O.f8e4m3_to_f32(c)
+            assert enc(v) == c, hex(c)
+
+
+def test_fp8_fp4_gemv_oracle_small_case():
+    """Hand-checked: act = [1, 2] * 2^0 (codes 0x38, 0x40), weights +1 / -0.5."""
+    act = np.zeros(128, np.uint8)
+    act[0], act[1] = 0x38, 0x40
+    act_s = np.array([127], np.uint8)
+    w = np.zeros(64, np.uint8)
+    w[0] = 0x2 | (0x9 << 4)               # codes 2 (+1.0) and 9 (-0.5)
+    ws = np.full(4, 127, np.uint8)
+    y = O.fp8_act_fp4_weight_gemv_f32(act, act_s, w, ws, 1, 128)
+    assert y[0] == np.float32(1.0 * 1.0 + 2.0 * -0.5)
