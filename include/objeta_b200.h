@@ -525,6 +525,21 @@ int objb_ep_partial_combine_device(const int32_t *d_ids_all, const float *d_w_al
 int objb_ep_sum_partials_device(const float *d_parts, size_t world, size_t tokens,
                                 size_t out_dim, float *d_out, objb_stream_t stream);
 
+/* cpu_gate_ref (dsl_moe.rs:768-881), the DeepSeek V4 gate, for num_tokens
+ * tokens (one CTA each): logits = W h with W f32 [num_experts][hidden_size]
+ * (sequential f32 sums, bit-identical to the reference); scores by
+ * score_func (0 softmax, 1 sigmoid, 2 sqrt-softplus); ids = top_k of
+ * scores + bias (d_gate_bias may be NULL; stable: ties keep the lower index)
+ * or, for a hash layer (d_tid2eid != NULL, d_input_ids required),
+ * tid2eid[input_id * top_k + k]; weights = scores[ids], normalised by their
+ * sum unless softmax, times route_scale.  An input id out of range gives ids
+ * -1, NaN weights and device error word bit 8. */
+int objb_deepseek_gate_device(const float *d_gate_weight, const float *d_gate_bias,
+                              const int64_t *d_tid2eid, size_t tid2eid_len, const float *d_hidden,
+                              const int64_t *d_input_ids, size_t num_tokens, size_t num_experts,
+                              size_t hidden_size, size_t top_k, int score_func, float route_scale,
+                              int32_t *d_ids, float *d_weights, objb_stream_t stream);
+
 /* ---- official DeepSeek arithmetic: activations quantized to F8_E4M3 with one
  * E8M0 scale per 128 values (deepseek.rs:1444-1525 for the codecs). */
 

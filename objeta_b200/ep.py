@@ -50,7 +50,31 @@ _lib.register_signatures({
     "objb_ep_partial_combine_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_size,
                                                c_size, c_size, c_void_p, c_void_p]),
     "objb_ep_sum_partials_device": (c_int, [c_void_p, c_size, c_size, c_size, c_void_p, c_void_p]),
+    "objb_deepseek_gate_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_void_p, c_void_p, c_size, c_size,
+                                          c_size, c_size, c_int, ctypes.c_float, c_void_p, c_void_p, c_void_p]),
 })
+
+SOFTMAX, SIGMOID, SQRT_SOFTPLUS = 0, 1, 2
+
+
+def deepseek_gate(d_gate_weight, d_hidden, top_k: int, score_func: int = SQRT_SOFTPLUS, route_scale: float = 1.5,
+                  d_gate_bias=None, d_tid2eid=None, d_input_ids=None, stream=None):
+    """The DeepSeek V4 gate (cpu_gate_ref, dsl_moe.rs:768-881) on the device
+    for T tokens: d_gate_weight f32 [E, H], d_hidden f32 [T, H]; returns
+    (ids int32 [T, k], weights f32 [T, k])."""
+    import torch
+    E, H = d_gate_weight.shape
+    hid = d_hidden.reshape(-1, H)
+    T = hid.shape[0]
+    ids = torch.empty(T, top_k, dtype=torch.int32, device=hid.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=hid.device)
+    _lib.call("objb_deepseek_gate_device", _dev_ptr(d_gate_weight),
+              _dev_ptr(d_gate_bias) if d_gate_bias is not None else None,
+              _dev_ptr(d_tid2eid) if d_tid2eid is not None else None,
+              0 if d_tid2eid is None else d_tid2eid.numel(), _dev_ptr(hid),
+              _dev_ptr(d_input_ids) if d_input_ids is not None else None, T, E, H, top_k, int(score_func),
+              float(route_scale), _dev_ptr(ids), _dev_ptr(w), _lib.stream_handle(stream))
+    return ids, w
 
 
 def ep_build_pairs(ids_all, rank: int, num_experts: int, stream=None):

@@ -856,3 +856,91 @@ int oro_shared_expert_fp8_official(const uint8_t *w1, const uint8_t *s1, const u
   free(a); free(as); free(a2); free(as2); free(g); free(u); free(act);
   return rc;
 }
+
+/* dsl_moe.rs:768-881 (cpu_gate_ref): DeepSeek gate.  logits = W.h (sequential
+ * f32, separate multiply and add); scores by score_func (0 softmax, 1 sigmoid,
+ * 2 sqrt-softplus with the reference's branches, including ln_1p(exp(-v))
+ * below -20); selection = top_k of scores + bias by a stable descending sort,
+ * or tid2eid[input_id * top_k + k] for hash layers; weights = scores of the
+ * selection, divided by their sequential sum unless softmax, times
+ * route_scale.  Returns ORO_INVALID_INPUT when a hash layer's input_id is out
+ * of range. */
+int oro_deepseek_gate(const float *gate_weight, const float *gate_bias, const int64_t *tid2eid,
+                      size_t tid2eid_len, const float *hidden, int64_t input_id, size_t num_experts,
+                      size_t hidden_size, size_t top_k, int score_func, float route_scale, int64_t *ids,
+                      float *weights) {
+  if (num_experts == 0 || top_k > num_experts) return ORO_INVALID_INPUT;
+  float *logits = malloc(num_experts * sizeof(float));
+  float *scores = malloc(num_experts * sizeof(float));
+  float *sel = malloc(num_experts * sizeof(float));
+  size_t *idx = malloc(num_experts * sizeof(size_t));
+  size_t *tmp = malloc(num_experts * sizeof(size_t));
+  int rc = ORO_OK;
+  if (!logits || !scores || !sel || !idx || !tmp) {
+    rc = ORO_INVALID_INPUT;
+    goto done;
+  }
+  for (size_t e = 0; e < num_experts; ++e) {
+    float sum = 0.0f;
+    for (size_t h = 0; h < hidden_size; ++h) sum += gate_weight[e * hidden_size + h] * hidden[h];
+    logits[e] = sum;
+  }
+  if (score_func == 0) {
+    float m = -INFINITY, s = 0.0f;
+    for (size_t e = 0; e < num_experts; ++e) m = rs_max(m, logits[e]);
+    for (size_t e = 0; e < num_experts; ++e) {
+      scores[e] = expf(logits[e] - m);
+      s += scores[e];
+    }
+    for (size_t e = 0; e < num_experts; ++e) scores[e] /= s;
+  } else if (score_func == 1) {
+    for (size_t e = 0; e < num_experts; ++e) scores[e] = 1.0f / (1.0f + expf(-logits[e]));
+  } else {
+    for (size_t e = 0; e < num_experts; ++e) {
+      const float v = logits[e];
+      const float sp = v > 20.0f ? v : (v < -20.0f ? log1pf(expf(-v)) : log1pf(expf(v)));
+      scores[e] = sqrtf(sp);
+    }
+  }
+  if (tid2eid) {
+    if (input_id < 0 || (size_t)input_id >= tid2eid_len / top_k) {
+      rc = ORO_INVALID_INPUT;
+      goto done;
+    }
+    for (size_t k = 0; k < top_k; ++k) ids[k] = tid2eid[(size_t)input_id * top_k + k];
+  } else {
+    for (size_t e = 0; e < num_experts; ++e) sel[e] = scores[e] + (gate_bias ? gate_bias[e] : 0.0f);
+    if (!gate_bias)
+      for (size_t e = 0; e < num_experts; ++e) sel[e] = scores[e];
+    for (size_t e = 0; e < num_experts; ++e) idx[e] = e;
+    for (size_t width = 1; width < num_experts; width *= 2) {
+      for (size_t lo = 0; lo < num_experts; lo += 2 * width) {
+        size_t mid = lo + width < num_experts ? lo + width : num_experts;
+        size_t hi = lo + 2 * width < num_experts ? lo + 2 * width : num_experts;
+        size_t i = lo, j = mid, o = lo;
+        while (i < mid && j < hi) {
+          if (sel[idx[j]] > sel[idx[i]]) tmp[o++] = idx[j++];
+          else tmp[o++] = idx[i++];
+        }
+        while (i < mid) tmp[o++] = idx[i++];
+        while (j < hi) tmp[o++] = idx[j++];
+      }
+      memcpy(idx, tmp, num_experts * sizeof(size_t));
+    }
+    for (size_t k = 0; k < top_k; ++k) ids[k] = (int64_t)idx[k];
+  }
+  for (size_t k = 0; k < top_k; ++k) {
+    const int64_t e = ids[k];
+    weights[k] = (e >= 0 && (size_t)e < num_experts) ? scores[e] : NAN;
+  }
+  if (score_func != 0) {
+    float s = 0.0f;
+    for (size_t k = 0; k < top_k; ++k) s += weights[k];
+    if (s > 0.0f)
+      for (size_t k = 0; k < top_k; ++k) weights[k] /= s;
+  }
+  for (size_t k = 0; k < top_k; ++k) weights[k] *= route_scale;
+done:
+  free(logits); free(scores); free(sel); free(idx); free(tmp);
+  return rc;
+}

@@ -87,6 +87,13 @@ int oro_router(const float *router_weights, const float *hidden,
 
 void oro_seeded_f32s(size_t len, uint64_t seed, float *out);
 
+/* DeepSeek gate (dsl_moe.rs:768-881); score_func 0 softmax, 1 sigmoid,
+ * 2 sqrt-softplus; tid2eid may be NULL (non-hash layer). */
+int oro_deepseek_gate(const float *gate_weight, const float *gate_bias, const int64_t *tid2eid,
+                      size_t tid2eid_len, const float *hidden, int64_t input_id, size_t num_experts,
+                      size_t hidden_size, size_t top_k, int score_func, float route_scale, int64_t *ids,
+                      float *weights);
+
 /* Official DeepSeek arithmetic (deepseek.rs:1444-1715). */
 uint8_t oro_f32_to_f8e4m3_exact(float v);
 int oro_act_quant(const float *x, size_t n, size_t block, uint8_t *y, uint8_t *s);

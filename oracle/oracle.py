@@ -105,6 +105,10 @@ def lib():
             L.oro_shared_expert_fp8_official.restype = ctypes.c_int
             L.oro_shared_expert_fp8_official.argtypes = [_c_u8p] * 6 + [_c_f32p, ctypes.c_size_t, ctypes.c_size_t,
                                                                         ctypes.c_float, _c_f32p]
+            L.oro_deepseek_gate.restype = ctypes.c_int
+            L.oro_deepseek_gate.argtypes = [_c_f32p, _c_f32p, _c_i64p, ctypes.c_size_t, _c_f32p, ctypes.c_int64,
+                                             ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int,
+                                             ctypes.c_float, _c_i64p, _c_f32p]
             _lib = L
     return _lib
 
@@ -359,3 +363,24 @@ def shared_expert_fp8_official(w1, s1, w3, s3, w2, s2, x, dim: int, inter: int, 
     if rc != 0:
         raise ValueError(f"oro_shared_expert_fp8_official rc={rc}")
     return out
+
+
+SOFTMAX, SIGMOID, SQRT_SOFTPLUS = 0, 1, 2
+
+
+def deepseek_gate(gate_weight, hidden, num_experts: int, hidden_size: int, top_k: int, score_func: int,
+                  route_scale: float, gate_bias=None, tid2eid=None, input_id=None):
+    """dsl_moe.rs:768-881 (cpu_gate_ref) -> (ids int64 [top_k], weights f32)."""
+    gw = np.ascontiguousarray(gate_weight, dtype=np.float32).reshape(-1)
+    hv = np.ascontiguousarray(hidden, dtype=np.float32).reshape(-1)
+    b = None if gate_bias is None else np.ascontiguousarray(gate_bias, dtype=np.float32).reshape(-1)
+    t = None if tid2eid is None else np.ascontiguousarray(tid2eid, dtype=np.int64).reshape(-1)
+    ids = np.zeros(top_k, np.int64)
+    w = np.zeros(top_k, np.float32)
+    rc = lib().oro_deepseek_gate(_f32(gw), _f32(b) if b is not None else None, _i64(t) if t is not None else None,
+                                 0 if t is None else t.size, _f32(hv), -1 if input_id is None else int(input_id),
+                                 num_experts, hidden_size, top_k, score_func, ctypes.c_float(route_scale),
+                                 _i64(ids), _f32(w))
+    if rc != 0:
+        raise ValueError("input_id is required for hash layers and must be in range")
+    return ids, w

@@ -215,3 +215,52 @@ def test_fp8_fp4_gemv_oracle_small_case():
     ws = np.full(4, 127, np.uint8)
     y = O.fp8_act_fp4_weight_gemv_f32(act, act_s, w, ws, 1, 128)
     assert y[0] == np.float32(1.0 * 1.0 + 2.0 * -0.5)
+
+
+# ------------------------------------------------------ DeepSeek gate (dsl_moe.rs:883-1000)
+def test_gate_sqrtsoftplus_scores():
+    ids, w = O.deepseek_gate(np.zeros(256 * 4096), np.full(4096, 0.1), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5)
+    assert ids.size == 6 and abs(float(w.sum()) - 1.5) < 1e-4
+    assert ids.tolist() == [0, 1, 2, 3, 4, 5]            # equal scores: the stable sort keeps index order
+
+
+def test_gate_bias_affects_selection_not_weights():
+    gate = np.zeros(256 * 4096, np.float32)
+    gate[0] = 1.0
+    ids, _ = O.deepseek_gate(gate, np.ones(4096), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5, gate_bias=np.zeros(256))
+    assert 0 in ids.tolist()
+    bias = np.zeros(256, np.float32)
+    bias[7] = 100.0
+    ids2, w2 = O.deepseek_gate(gate, np.ones(4096), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5, gate_bias=bias)
+    assert ids2[0] == 7 and abs(float(w2.sum()) - 1.5) < 1e-4
+
+
+def test_gate_hash_layer_tid2eid():
+    tid2eid = np.arange(129280 * 6) % 256
+    ids, w = O.deepseek_gate(np.zeros(256 * 4096), np.full(4096, 0.1), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5,
+                             tid2eid=tid2eid, input_id=42)
+    assert ids.tolist() == tid2eid[42 * 6:43 * 6].tolist() and abs(float(w.sum()) - 1.5) < 1e-4
+    import pytest
+    with pytest.raises(ValueError):
+        O.deepseek_gate(np.zeros(256 * 4096), np.full(4096, 0.1), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5,
+                        tid2eid=tid2eid, input_id=129280)
+
+
+def test_gate_hash_layer_weights_from_hidden():
+    gate = np.zeros((256, 4096), np.float32)
+    gate[0] = 0.5
+    gate[100] = 2.0
+    tid2eid = np.arange(129280 * 6) % 256
+    ia, wa = O.deepseek_gate(gate, np.ones(4096), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5, tid2eid=tid2eid, input_id=0)
+    ib, wb = O.deepseek_gate(gate, -np.ones(4096), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5, tid2eid=tid2eid, input_id=0)
+    assert ia.tolist() == [0, 1, 2, 3, 4, 5] and ib.tolist() == ia.tolist()
+    assert not np.array_equal(wa, wb)
+
+
+def test_gate_route_scale_and_top_k():
+    _, w = O.deepseek_gate(np.zeros(256 * 4096), np.full(4096, 0.42), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5)
+    assert abs(float(w.sum()) - 1.5) < 1e-4
+    gate = np.zeros((256, 4096), np.float32)
+    gate[10], gate[20], gate[30] = 3.0, 2.0, 1.0
+    ids, _ = O.deepseek_gate(gate, np.ones(4096), 256, 4096, 6, O.SQRT_SOFTPLUS, 1.5)
+    assert ids[:3].tolist() == [10, 20, 30]
