@@ -596,6 +596,52 @@ int objb_moe_execute_selected_official_fp4(
     size_t out_dim, size_t layer_id, objb_expert_cache *cache,
     const objb_fp8_shared_expert *shared, float *out, objb_moe_telemetry *telemetry);
 
+/* ---- safetensors weights (ModelWeights, objeta-parser lib.rs:97-330): an
+ * mmap of one file or of every *.safetensors file of a directory (file-name
+ * order), indexed by tensor name; "__metadata__" is skipped. */
+enum {
+  OBJB_DTYPE_F32 = 0,
+  OBJB_DTYPE_F16 = 1,
+  OBJB_DTYPE_BF16 = 2,
+  OBJB_DTYPE_I64 = 3,
+  OBJB_DTYPE_I32 = 4,
+  OBJB_DTYPE_I8 = 5,
+  OBJB_DTYPE_U8 = 6,
+  OBJB_DTYPE_F8_E8M0 = 7,
+  OBJB_DTYPE_F8_E4M3 = 8,
+  OBJB_DTYPE_BOOL = 9
+};
+
+/* TensorInfo (lib.rs:21-28); offset is absolute in its file. */
+typedef struct {
+  int dtype;
+  int ndim;
+  size_t shape[8];
+  size_t offset, nbytes, nelem;
+} objb_tensor_info;
+
+typedef struct objb_weights objb_weights;
+
+/* ModelWeights::open: Io for unreadable paths, InvalidInput for malformed
+ * headers ("header length exceeds file size", "invalid tensor entry ..",
+ * "Unknown dtype: .."). */
+int objb_weights_open(const char *path, objb_weights **out);
+void objb_weights_close(objb_weights *w);
+int objb_weights_count(objb_weights *w, size_t *n);                       /* len() */
+int objb_weights_name_at(objb_weights *w, size_t i, const char **name);   /* keys(), sorted */
+int objb_weights_info(objb_weights *w, const char *name, objb_tensor_info *info);
+/* get_raw: a pointer into the mapping, valid until objb_weights_close. */
+int objb_weights_raw(objb_weights *w, const char *name, const void **data, size_t *nbytes);
+/* get_f32: F32 as is, F16 / BF16 widened as the reference (lib.rs:285-337). */
+int objb_weights_get_f32(objb_weights *w, const char *name, float *out, size_t out_len);
+/* Pins the weights for asynchronous DMA into the expert cache or the device:
+ * the mapping itself (read-only host registration) where the platform
+ * allows it, else a pinned host slab holding a copy of each file.  Pointers
+ * from objb_weights_raw taken after this call point into pinned memory. */
+int objb_weights_pin(objb_weights *w);
+int objb_weights_to_device(objb_weights *w, const char *name, void *d_dst, size_t dst_bytes,
+                           objb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
