@@ -300,6 +300,26 @@ int objb_moe_pairs_device(const objb_moe_layer *layer, size_t num_pairs,
                           size_t num_tokens, const float *d_x, float *d_v, size_t v_rows,
                           float swiglu_limit, objb_stream_t stream);
 
+/* objb_moe_pairs_device for Q4_0 layers on the tensor cores (tcgen05 kind::i8
+ * MMAs into tensor memory): the same arguments and outputs, with each run of
+ * equal experts in the pair list taken 32 pairs at a time against one
+ * 128-row tile of the expert's matrix, so a weight tile is decoded once per
+ * 32 pairs instead of once per pair.  Block sums are the same exact integers
+ * as the CUDA-core path; the f32 block terms are added in another order, so
+ * rows agree with objb_moe_pairs_device within the f32 tolerance, not
+ * bit for bit (each row is still a function of (expert, x) alone, whatever
+ * else is in the pair list).  Pairs must be grouped by expert; an expert
+ * that appears in several separate runs is streamed once per run.  Q4_0
+ * layers with 16-byte aligned experts and hidden, intermediate multiples of
+ * 256 only (OBJB_ERR_UNSUPPORTED otherwise). */
+int objb_moe_pairs_tc_scratch_bytes(const objb_moe_layer *layer, size_t num_pairs,
+                                    size_t num_tokens, size_t *bytes);
+int objb_moe_pairs_tc_device(const objb_moe_layer *layer, size_t num_pairs,
+                             const int32_t *d_num_pairs, const int32_t *d_pair_expert,
+                             const int32_t *d_pair_token, const int32_t *d_pair_out,
+                             size_t num_tokens, const float *d_x, float *d_v, size_t v_rows,
+                             float swiglu_limit, objb_stream_t stream);
+
 /* The weighted top-k combine (moe.rs:1319-1321) for num_tokens tokens:
  * d_out[t][i] = sum over j = 0..top_k-1, in slot order, of
  * d_weights[t][j] * d_v[d_slot_row[t][j]][i], starting from 0 -- the exact

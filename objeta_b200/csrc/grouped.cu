@@ -1,0 +1,677 @@
+// grouped.cu -- the multi-token ("grouped expert") MoE contraction on the
+// tensor cores: for Q4_0 experts, each 128-row tile of an expert's matrix is
+// multiplied with the digit planes of up to 32 vectors routed to that expert
+// by tcgen05 kind::i8 MMAs (unsigned 4-bit codes x signed 7-bit digits, S32
+// in tensor memory), one MMA per 32-column block; the epilogue combines the
+// three digit products into the exact integer block sum and applies the
+// block's f16 row scale and the vector's block scale in f32:
+//   y[v][r] = sum_b d[r][b] * 2^(E[v][b]-20) * (sum_i q[r][b][i] X[v][b][i] - 8 sum_i X[v][b][i])
+// -- the arithmetic of the CUDA-core row programs, summed in another order.
+//
+// A launch works on pairs sorted by expert: "slices" (pieces of at most 32
+// pairs of one expert) are found on the device (no host round trip), and
+// each (slice, 128-row tile) is one work item of a persistent grid.  A work
+// item walks its K in steps of 8 blocks (256 columns):
+//   * all threads stage the step's raw Q4_0 bytes (128 rows x 144 bytes) and
+//     the live vectors' digit planes with 16-byte cp.async, two steps ahead
+//     in a three-deep shared-memory ring;
+//   * the raw rows are unpacked to one code byte per column in the
+//     core-matrix order the MMA reads (K-major, no swizzle);
+//   * one thread issues the MMAs two blocks at a time into one of two
+//     tensor-memory slots, so the epilogue of one pair of blocks overlaps
+//     the MMAs of the next;
+//   * warps 0-3 fold the even blocks, warps 4-7 the odd ones (tensor-memory
+//     lanes = tile rows); the two partial sums are added at the item's end.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "objb_common.h"
+#include "objb_decode.cuh"
+#include "objb_host_launch.cuh"
+#include "objb_launch.h"
+#include "objb_moe.cuh"
+#include "objb_tc.cuh"
+
+namespace objb {
+namespace dev {
+
+constexpr int kTcRows = 128;               // M of the MMA: rows per tile
+constexpr int kTcNvp = 32;                 // pairs per slice
+constexpr int kTcNp = 3 * kTcNvp;          // MMA N: three digit planes of kTcNvp vectors
+constexpr int kTcKB = 8;                   // 32-column blocks per step
+constexpr int kTcStages = 3;               // ring depth: two steps in flight ahead
+constexpr int kTcThreads = 256;
+constexpr int kTcRawRow = kTcKB * 18;      // raw Q4_0 bytes of one row per step
+constexpr int kTcKch = 2 * kTcKB;          // 16-byte K columns of a staged operand
+constexpr int kTcBlockCols = 128;          // tensor-memory columns of one block's accumulators (>= kTcNp)
+constexpr int kTcSlotCols = 2 * kTcBlockCols;  // one MMA group (two blocks)
+constexpr uint32_t kTcTmemCols = 512;      // two slots
+
+struct TcSmem {
+  alignas(1024) uint8_t a[kTcRows * kTcKB * 32];            // unpacked codes (also the partial-sum exchange)
+  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // digit planes
+  alignas(16) uint8_t raw[kTcStages][kTcRows * kTcRawRow];  // raw Q4_0 bytes
+  alignas(16) float xs[kTcStages][kTcNvp][kTcKB];
+  alignas(16) int32_t noff[kTcStages][kTcNvp][kTcKB];
+  float d[kTcKB][kTcRows];
+  int32_t out_row[kTcNvp];
+  alignas(8) uint64_t bar[2];
+  uint32_t tmem_base;
+};
+static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
+static_assert(kTcNp <= kTcBlockCols && 2 * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Digit planes of one 32-value block of vector v (one warp, one value per
+// lane): X = rint(x * 2^(20-E)), E the block's frexp exponent, split in three
+// signed 7-bit digits; plane k at planes[(v * 3 + k) * C + col]; per block
+// 2^(E-20) (NaN when the block is not finite) and -off * sum X.
+__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int off, int8_t* planes, float* xsc,
+                                                int32_t* noff) {
+  const int lane = threadIdx.x & 31, nb = C / 32;
+  float m = fabsf(xe);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  int E = 0;
+  frexpf(m, &E);
+  const int X = __float2int_rn(ldexpf(xe, 20 - E));
+  const int d0 = ((X + 64) & 127) - 64;
+  const int X1 = (X - d0) / 128;
+  const int d1 = ((X1 + 64) & 127) - 64;
+  const int d2 = (X1 - d1) / 128;
+  const int sx = __reduce_add_sync(0xFFFFFFFFu, X);
+  int8_t* p = planes + static_cast<size_t>(v) * 3 * C + b * 32 + lane;
+  p[0] = static_cast<int8_t>(d0);
+  p[C] = static_cast<int8_t>(d1);
+  p[2 * C] = static_cast<int8_t>(d2);
+  if (lane == 0) {
+    xsc[static_cast<size_t>(v) * nb + b] = isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000);
+    noff[static_cast<size_t>(v) * nb + b] = -off * sx;
+  }
+}
+
+// Digit planes of `nvec` vectors (rows of x, x_stride apart); one warp per
+// (vector, block).
+__global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict__ x, size_t x_stride, int nvec,
+                                                        const int32_t* count, int C, int off,
+                                                        int8_t* __restrict__ planes, float* __restrict__ xsc,
+                                                        int32_t* __restrict__ noff) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) nvec = min(max(*count, 0), nvec);
+  const int nb = C / 32, lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb; wi += warps) {
+    const int v = wi / nb, b = wi % nb;
+    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, off, planes, xsc, noff);
+  }
+}
+
+// act = SwiGLU(g, u) of every pair (rows of I floats) straight into digit
+// planes; one warp per (pair, block).
+__global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(const float* __restrict__ g,
+                                                               const float* __restrict__ u, int P,
+                                                               const int32_t* count, int I, float limit, int off,
+                                                               int8_t* __restrict__ planes, float* __restrict__ xsc,
+                                                               int32_t* __restrict__ noff) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) P = min(max(*count, 0), P);
+  const int nb = I / 32, lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < P * nb; wi += warps) {
+    const int p = wi / nb, b = wi % nb;
+    const size_t i = static_cast<size_t>(p) * I + b * 32 + lane;
+    tc_block_digits(swiglu(g[i], u[i], limit), p, b, I, off, planes, xsc, noff);
+  }
+}
+
+// Work slices of the expert-sorted pair list: runs of equal experts cut into
+// pieces of at most `nvp` pairs -> slice_start / slice_len [0..n), n in
+// *nslices.  One CTA; each thread scans a contiguous slice of the pairs.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp_tot) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nt = blockDim.x;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) warp_tot[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = (nt + 31) >> 5;
+    int w = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) warp_tot[lane] = w;
+  }
+  __syncthreads();
+  *total = warp_tot[((nt + 31) >> 5) - 1];
+  return incl - v + (wid ? warp_tot[wid - 1] : 0);
+}
+
+__global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restrict__ pe, int P, const int32_t* count,
+                                                         int nvp, int32_t* __restrict__ run_start,
+                                                         int32_t* __restrict__ slice_start,
+                                                         int32_t* __restrict__ slice_len,
+                                                         int32_t* __restrict__ nslices) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ int warp_tot[32];
+  if (count) P = min(max(*count, 0), P);
+  const int nt = blockDim.x, tid = threadIdx.x;
+  // 1. run starts
+  int per = (P + nt - 1) / nt;
+  int a = min(P, tid * per), b = min(P, a + per);
+  int local = 0;
+  for (int p = a; p < b; ++p) local += (p == 0 || pe[p] != pe[p - 1]);
+  int nruns = 0;
+  int pos = block_exclusive_scan(local, &nruns, warp_tot);
+  for (int p = a; p < b; ++p)
+    if (p == 0 || pe[p] != pe[p - 1]) run_start[pos++] = p;
+  __syncthreads();
+  // 2. slices of each run
+  per = (nruns + nt - 1) / nt;
+  a = min(nruns, tid * per);
+  b = min(nruns, a + per);
+  local = 0;
+  for (int r = a; r < b; ++r) {
+    const int len = (r + 1 < nruns ? run_start[r + 1] : P) - run_start[r];
+    local += (len + nvp - 1) / nvp;
+  }
+  int total = 0;
+  pos = block_exclusive_scan(local, &total, warp_tot);
+  for (int r = a; r < b; ++r) {
+    const int s0 = run_start[r], s1 = r + 1 < nruns ? run_start[r + 1] : P;
+    for (int q = s0; q < s1; q += nvp) {
+      slice_start[pos] = q;
+      slice_len[pos] = min(nvp, s1 - q);
+      ++pos;
+    }
+  }
+  if (tid == 0) *nslices = total;
+}
+
+// Operands of one launch of the grouped kernel.
+struct TcArgs {
+  const uint8_t* const* W;   // expert matrices [R][C/32 blocks of 18 bytes]
+  const uint8_t* const* W2;  // second matrix of the same experts (gate + up in one launch), or null
+  int num_experts, R, C;
+  const int32_t* pe;         // expert of each pair (sorted)
+  const int32_t* slot_vec;   // vector of each pair (null: the pair index)
+  const int32_t* slot_out;   // output row of each pair (null: the pair index)
+  const int32_t* slice_start;
+  const int32_t* slice_len;
+  const int32_t* nslices;
+  const int8_t* planes;      // digit planes [nvec][3][C]
+  const float* xsc;          // [nvec][C/32]
+  const int32_t* noff;       // [nvec][C/32]
+  int nvec;
+  float* out;                // [out_rows][R]
+  float* out2;               // for W2
+  int out_rows;
+  unsigned* err;
+};
+
+struct TcItem {
+  const uint8_t* w;
+  float* dst;
+  int tile, s0, ns;
+};
+
+__device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int mats) {
+  TcItem it;
+  const int mat = w % mats, rest = w / mats;
+  const int sl = rest / tiles;
+  it.tile = rest % tiles;
+  it.s0 = A.slice_start[sl];
+  it.ns = min(max(A.slice_len[sl], 1), kTcNvp);
+  int e = A.pe[it.s0];
+  if (e < 0 || e >= A.num_experts) e = 0;  // flagged at the item's start
+  it.w = mat ? A.W2[e] : A.W[e];
+  it.dst = mat ? A.out2 : A.out;
+  return it;
+}
+
+__device__ __forceinline__ int tc_vec(const TcArgs& A, int p) {
+  const int v = A.slot_vec ? A.slot_vec[p] : p;
+  return (v < 0 || v >= A.nvec) ? 0 : v;
+}
+
+// Stages step `chunk` of item `it` into ring slot `st`: raw rows, the live
+// vectors' digit planes (rows k * kTcNvp + i of the B operand) and their
+// block scales.
+__device__ __forceinline__ void tc_prefetch(TcSmem& sm, int st, const TcArgs& A, const TcItem& it, int chunk,
+                                            size_t row_bytes) {
+  const int tid = threadIdx.x, nb = A.C / 32;
+  constexpr int kPieces = kTcRawRow / 16;
+  const uint8_t* base = it.w + static_cast<size_t>(chunk) * kTcRawRow;
+  for (int t = tid; t < kTcRows * kPieces; t += kTcThreads) {
+    const int r = t / kPieces, p = t % kPieces;
+    const int row = it.tile * kTcRows + r;
+    if (row < A.R) cp_async16(sm.raw[st] + r * kTcRawRow + p * 16, base + static_cast<size_t>(row) * row_bytes + p * 16);
+  }
+  for (int t = tid; t < 3 * it.ns * kTcKch; t += kTcThreads) {
+    const int rr = t / kTcKch, p = t % kTcKch;
+    const int k = rr / it.ns, i = rr % it.ns;
+    const int v = tc_vec(A, it.s0 + i);
+    const int brow = k * kTcNvp + i;
+    cp_async16(sm.b[st] + ((brow >> 3) * kTcKch + p) * 128 + (brow & 7) * 16,
+               A.planes + (static_cast<size_t>(v) * 3 + k) * A.C + chunk * (kTcKB * 32) + p * 16);
+  }
+  for (int t = tid; t < it.ns * 4; t += kTcThreads) {
+    const int i = t >> 2, q = t & 3;
+    const size_t off = static_cast<size_t>(tc_vec(A, it.s0 + i)) * nb + chunk * kTcKB + (q & 1) * 4;
+    if (q < 2) cp_async16(&sm.xs[st][i][(q & 1) * 4], A.xsc + off);
+    else cp_async16(&sm.noff[st][i][(q & 1) * 4], A.noff + off);
+  }
+}
+
+// Raw rows of ring slot `st` -> code bytes in core-matrix order and the row
+// scales; two threads per row, four blocks each.
+__device__ __forceinline__ void tc_unpack(TcSmem& sm, int st) {
+  const int tid = threadIdx.x;
+  const int r = tid & (kTcRows - 1), h = tid >> 7;
+  const uint8_t* seg = sm.raw[st] + r * kTcRawRow + h * 72;
+  uint32_t w[18];
+  if (h == 0) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 x = *reinterpret_cast<const uint4*>(seg + 16 * q);
+      w[4 * q] = x.x, w[4 * q + 1] = x.y, w[4 * q + 2] = x.z, w[4 * q + 3] = x.w;
+    }
+    const uint2 y = *reinterpret_cast<const uint2*>(seg + 64);
+    w[16] = y.x, w[17] = y.y;
+  } else {
+    const uint2 y = *reinterpret_cast<const uint2*>(seg);
+    w[0] = y.x, w[1] = y.y;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 x = *reinterpret_cast<const uint4*>(seg + 8 + 16 * q);
+      w[2 + 4 * q] = x.x, w[3 + 4 * q] = x.y, w[4 + 4 * q] = x.z, w[5 + 4 * q] = x.w;
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    // block b occupies bytes [18 b, 18 b + 18) of the 72: f16 scale, 16 code bytes
+    uint32_t d16, qs[4];
+    if (b % 2 == 0) {
+      const int wb = 18 * b / 4;
+      d16 = w[wb] & 0xFFFFu;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) qs[m] = __funnelshift_r(w[wb + m], w[wb + m + 1], 16);
+    } else {
+      const int wb = (18 * b + 2) / 4;
+      d16 = w[wb - 1] >> 16;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) qs[m] = w[wb + m];
+    }
+    uint32_t c[8];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t lo = qs[m] & 0x0F0F0F0Fu, hi = (qs[m] >> 4) & 0x0F0F0F0Fu;
+      c[2 * m] = __byte_perm(lo, hi, 0x5140);      // codes 8m .. 8m+3
+      c[2 * m + 1] = __byte_perm(lo, hi, 0x7362);  // codes 8m+4 .. 8m+7
+    }
+    const int j = 4 * h + b;
+    uint8_t* dst = sm.a + ((r >> 3) * kTcKch + 2 * j) * 128 + (r & 7) * 16;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(c[0], c[1], c[2], c[3]);
+    *reinterpret_cast<uint4*>(dst + 128) = make_uint4(c[4], c[5], c[6], c[7]);
+    sm.d[j][r] = f16_bits_to_f32(d16);
+  }
+}
+
+// MMAs of blocks 2g, 2g+1 of the staged step into tensor-memory slot g & 1.
+__device__ __forceinline__ void tc_issue_group(TcSmem& sm, int st, int g, uint32_t tmem, uint32_t idesc) {
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const int j = 2 * g + jj;
+    const uint64_t da = umma_desc_kmajor(smem_addr(sm.a + 2 * j * 128), 128, kTcKch * 128);
+    const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
+    umma_i8(tmem + (g & 1) * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
+  }
+  umma_commit(&sm.bar[g & 1]);
+}
+
+// The grouped contraction of Q4_0 matrices: out[slot_out[p]][r] = y[vector
+// slot_vec[p]][r] of expert pe[p]'s matrix for every pair p.  Needs C a
+// multiple of 256 (rows of whole 16-byte pieces per step).
+__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  TcSmem& sm = *reinterpret_cast<TcSmem*>(tc_smem_raw);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.bar[0])));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.bar[1])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(&sm.tmem_base, kTcTmemCols);
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  const int nb = A.C / 32, nchunks = nb / kTcKB;
+  const size_t row_bytes = static_cast<size_t>(nb) * 18;
+  const int tiles = (A.R + kTcRows - 1) / kTcRows;
+  const int mats = A.W2 ? 2 : 1;
+  const int total = *A.nslices * tiles * mats;
+  const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nsteps = my_items * nchunks;
+  const uint32_t idesc = umma_idesc_u8s8(kTcRows, kTcNp);
+  const int quarter = warp & 3, half = warp >> 2;   // tensor-memory lanes 32*quarter..; blocks of parity `half`
+  const int trow = 32 * quarter + lane;             // this thread's tile row in the epilogue
+  const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
+
+  auto item_at = [&](int s) { return tc_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
+#pragma unroll 1
+  for (int s = 0; s < kTcStages - 1; ++s) {
+    if (s < nsteps) tc_prefetch(sm, s, A, item_at(s), s % nchunks, row_bytes);
+    cp_async_commit();
+  }
+  float acc[kTcNvp];
+#pragma unroll
+  for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+  TcItem cur{};
+  uint32_t phase[2] = {0u, 0u};
+  bool ok = true;
+#pragma unroll 1
+  for (int s = 0; s < nsteps; ++s) {
+    const int chunk = s % nchunks, st = s % kTcStages;
+    if (s + kTcStages - 1 < nsteps) {
+      const int s2 = s + kTcStages - 1;
+      tc_prefetch(sm, s2 % kTcStages, A, item_at(s2), s2 % nchunks, row_bytes);
+    }
+    cp_async_commit();
+    if (chunk == 0) {
+      cur = item_at(s);
+      if (tid < kTcNvp) {
+        int o = -1;
+        if (tid < cur.ns) {
+          const int p = cur.s0 + tid;
+          o = A.slot_out ? A.slot_out[p] : p;
+          const int v = A.slot_vec ? A.slot_vec[p] : p;
+          const int e = A.pe[p];
+          if (o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) {
+            if (A.err) atomicOr(A.err, 8u);
+            if (o >= A.out_rows) o = -1;
+          }
+        }
+        sm.out_row[tid] = o;
+      }
+    }
+    cp_async_wait<kTcStages - 1>();
+    __syncthreads();
+    tc_unpack(sm, st);
+    fence_async_shared();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after_sync();
+      tc_issue_group(sm, st, 0, tmem, idesc);
+    }
+    const int nvg = (cur.ns + 7) >> 3;
+#pragma unroll
+    for (int g = 0; g < kTcKB / 2; ++g) {
+      const bool done = mbar_wait_bounded(&sm.bar[g & 1], phase[g & 1], A.err, kErrFullWaitTimeout);
+      phase[g & 1] ^= 1u;
+      if (!__syncthreads_and(done)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      if (tid == 0 && g + 1 < kTcKB / 2) tc_issue_group(sm, st, g + 1, tmem, idesc);
+      // epilogue of block j = 2g + half: exact block sums -> f32
+      const int j = 2 * g + half;
+      const uint32_t taddr = tmem + lane_addr + (g & 1) * kTcSlotCols + half * kTcBlockCols;
+      uint32_t rv[3][4][8];
+#pragma unroll
+      for (int vg = 0; vg < 4; ++vg)
+        if (vg < nvg) {
+#pragma unroll
+          for (int k = 0; k < 3; ++k) tmem_ld8(taddr + k * kTcNvp + 8 * vg, rv[k][vg]);
+        }
+      tmem_wait_ld();
+      const float dr = sm.d[j][trow];
+#pragma unroll
+      for (int vg = 0; vg < 4; ++vg)
+        if (vg < nvg) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int i = 8 * vg + u;
+            const int S = static_cast<int>(rv[0][vg][u]) + static_cast<int>(rv[1][vg][u]) * 128 +
+                          static_cast<int>(rv[2][vg][u]) * 16384 + sm.noff[st][i][j];
+            acc[i] = fmaf(__int2float_rn(S), dr * sm.xs[st][i][j], acc[i]);
+          }
+        }
+      tc_fence_before_sync();
+    }
+    if (!ok) break;
+    __syncthreads();
+    if (chunk == nchunks - 1) {
+      // odd-block partial sums through shared memory, then one store per live pair
+      float* xchg = reinterpret_cast<float*>(sm.a);  // [kTcNvp][kTcRows]
+      if (half == 1) {
+#pragma unroll
+        for (int i = 0; i < kTcNvp; ++i) xchg[i * kTcRows + trow] = acc[i];
+      }
+      __syncthreads();
+      const int grow = cur.tile * kTcRows + trow;
+      if (half == 0 && grow < A.R) {
+#pragma unroll
+        for (int i = 0; i < kTcNvp; ++i) {
+          const int o = sm.out_row[i];
+          if (i < cur.ns && o >= 0)
+            cur.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + xchg[i * kTcRows + trow];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+      __syncthreads();
+    }
+  }
+  cp_async_wait<0>();
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kTcTmemCols);
+}
+
+}  // namespace dev
+
+namespace {
+
+struct TcLayout {
+  size_t planes_x, xsc_x, noff_x, g, u, planes_a, xsc_a, noff_a, run_start, slice_start, slice_len, nslices, total;
+};
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I) {
+  TcLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  L.planes_x = take(T * 3 * H);
+  L.xsc_x = take(T * (H / 32) * 4);
+  L.noff_x = take(T * (H / 32) * 4);
+  L.g = take(P * I * 4);
+  L.u = take(P * I * 4);
+  L.planes_a = take(P * 3 * I);
+  L.xsc_a = take(P * (I / 32) * 4);
+  L.noff_a = take(P * (I / 32) * 4);
+  L.run_start = take(P * 4);
+  L.slice_start = take(P * 4);
+  L.slice_len = take(P * 4);
+  L.nslices = take(4);
+  L.total = off;
+  return L;
+}
+
+int validate_tc(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens) {
+  if (!l) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "null layer");
+  if (l->fmt != OBJB_Q4_0 || l->d_gate_scale || l->d_up_scale || l->d_down_scale)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "grouped Q4_0 MoE pairs", "the tensor-core pair path takes Q4_0 experts");
+  if ((l->flags & OBJB_MOE_UNALIGNED) != 0)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "grouped Q4_0 MoE pairs", "expert tensors must be 16-byte aligned");
+  if (!l->d_gate || !l->d_up || !l->d_down || l->num_experts == 0 || l->num_experts > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "missing expert tables");
+  if (l->hidden == 0 || l->intermediate == 0 || l->out_dim == 0 || l->hidden > (1u << 20) ||
+      l->intermediate > (1u << 20) || l->out_dim > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "shape out of range");
+  if (l->hidden % 256 || l->intermediate % 256)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "grouped Q4_0 MoE pairs",
+                     "hidden and intermediate must be multiples of 256 (rows staged in 16-byte pieces)");
+  if (num_pairs == 0 || num_pairs > (1u << 20) || num_tokens == 0 || num_tokens > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "need 1 <= num_pairs, num_tokens <= 2^20");
+  if (num_pairs * std::max(l->intermediate, l->out_dim) > (1u << 30) || num_tokens * l->hidden > (1ull << 34))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "num_pairs * rows too large");
+  return OBJB_OK;
+}
+
+}  // namespace
+
+bool moe_pairs_tc_supported(const objb_moe_layer* l) {
+  return l && l->fmt == OBJB_Q4_0 && !l->d_gate_scale && (l->flags & OBJB_MOE_UNALIGNED) == 0 &&
+         l->hidden % 256 == 0 && l->intermediate % 256 == 0;
+}
+
+int moe_pairs_tc_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out) {
+  OBJB_TRY(validate_tc(l, num_pairs, num_tokens));
+  *out = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate).total;
+  return OBJB_OK;
+}
+
+// The multi-token pairs of moe_pairs for Q4_0 layers on the tensor cores:
+// digit planes of the T token vectors, the slices of the expert-sorted pair
+// list, gate and up of every pair in one grouped launch, SwiGLU straight
+// into the digit planes of the P activations, and down into v[pair_out[p]]
+// (or v[p]).
+int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, const int32_t* pt, const int32_t* po,
+                 size_t num_tokens, const float* x, float* v, size_t v_rows, float limit, cudaStream_t stream,
+                 void* scratch, size_t scratch_bytes, unsigned* err_word, const int32_t* d_count) {
+  OBJB_TRY(validate_tc(l, num_pairs, num_tokens));
+  if (!pe || !pt || !x || !v || !scratch)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "null device pointer");
+  if (v_rows < (po ? 1 : num_pairs) || v_rows > (1u << 30))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "v_rows cannot hold the pair outputs");
+  const TcLayout L = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate);
+  if (scratch_bytes < L.total)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs",
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(L.total));
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  unsigned* err = err_word;
+  if (!err) OBJB_TRY(device_error_word(device, &err));
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  int8_t* planes_x = reinterpret_cast<int8_t*>(sc + L.planes_x);
+  float* xsc_x = reinterpret_cast<float*>(sc + L.xsc_x);
+  int32_t* noff_x = reinterpret_cast<int32_t*>(sc + L.noff_x);
+  float* g = reinterpret_cast<float*>(sc + L.g);
+  float* u = reinterpret_cast<float*>(sc + L.u);
+  int8_t* planes_a = reinterpret_cast<int8_t*>(sc + L.planes_a);
+  float* xsc_a = reinterpret_cast<float*>(sc + L.xsc_a);
+  int32_t* noff_a = reinterpret_cast<int32_t*>(sc + L.noff_a);
+  int32_t* run_start = reinterpret_cast<int32_t*>(sc + L.run_start);
+  int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
+  int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
+  int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
+  const int P = static_cast<int>(num_pairs), T = static_cast<int>(num_tokens);
+  const int H = static_cast<int>(l->hidden), I = static_cast<int>(l->intermediate), O = static_cast<int>(l->out_dim);
+  auto warp_grid = [&](int nvec, int C) {
+    const long long warps = static_cast<long long>(nvec) * (C / 32);
+    return static_cast<int>(std::max(1LL, std::min((warps * 32 + 255) / 256, 16LL * props.sm_count)));
+  };
+  const size_t smem = sizeof(dev::TcSmem);
+  OBJB_TRY(ensure_smem_attr(dev::tc_q4_grouped_kernel, device, smem));
+
+  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, run_start,
+                      slice_start, slice_len, nslices));
+  OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
+                      static_cast<const int32_t*>(nullptr), H, 8, planes_x, xsc_x, noff_x));
+  dev::TcArgs a{};
+  a.W = reinterpret_cast<const uint8_t* const*>(l->d_gate);
+  a.W2 = reinterpret_cast<const uint8_t* const*>(l->d_up);
+  a.num_experts = static_cast<int>(l->num_experts);
+  a.R = I;
+  a.C = H;
+  a.pe = pe;
+  a.slot_vec = pt;
+  a.slot_out = nullptr;
+  a.slice_start = slice_start;
+  a.slice_len = slice_len;
+  a.nslices = nslices;
+  a.planes = planes_x;
+  a.xsc = xsc_x;
+  a.noff = noff_x;
+  a.nvec = T;
+  a.out = g;
+  a.out2 = u;
+  a.out_rows = P;
+  a.err = err;
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, static_cast<const float*>(g),
+                      static_cast<const float*>(u), P, d_count, I, limit, 8, planes_a, xsc_a, noff_a));
+  a.W = reinterpret_cast<const uint8_t* const*>(l->d_down);
+  a.W2 = nullptr;
+  a.R = O;
+  a.C = I;
+  a.slot_vec = nullptr;
+  a.slot_out = po;
+  a.planes = planes_a;
+  a.xsc = xsc_a;
+  a.noff = noff_a;
+  a.nvec = P;
+  a.out = v;
+  a.out2 = nullptr;
+  a.out_rows = static_cast<int>(v_rows);
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  return OBJB_OK;
+}
+
+}  // namespace objb
+
+extern "C" {
+
+int objb_moe_pairs_tc_scratch_bytes(const objb_moe_layer* layer, size_t num_pairs, size_t num_tokens,
+                                    size_t* bytes) {
+  objb::clear_error();
+  if (!bytes) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_pairs_tc_scratch_bytes", "null output pointer");
+  return objb::moe_pairs_tc_scratch_bytes(layer, num_pairs, num_tokens, bytes);
+}
+
+int objb_moe_pairs_tc_device(const objb_moe_layer* layer, size_t num_pairs, const int32_t* d_num_pairs,
+                             const int32_t* d_pair_expert, const int32_t* d_pair_token, const int32_t* d_pair_out,
+                             size_t num_tokens, const float* d_x, float* d_v, size_t v_rows, float swiglu_limit,
+                             objb_stream_t stream_) {
+  objb::clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  OBJB_TRY(objb::moe_pairs_tc_scratch_bytes(layer, num_pairs, num_tokens, &need));
+  int device = 0;
+  OBJB_TRY(objb::current_device(&device));
+  void* ws = nullptr;
+  OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
+  return objb::moe_pairs_tc(layer, num_pairs, d_pair_expert, d_pair_token, d_pair_out, num_tokens, d_x, d_v, v_rows,
+                            swiglu_limit, stream, ws, need, nullptr, d_num_pairs);
+}
+
+}  // extern "C"

@@ -41,6 +41,9 @@ _lib.register_signatures({
     "objb_moe_pairs_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
     "objb_moe_pairs_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_size,
                                       c_void_p, c_void_p, c_size, ctypes.c_float, c_void_p]),
+    "objb_moe_pairs_tc_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
+    "objb_moe_pairs_tc_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_size,
+                                         c_void_p, c_void_p, c_size, ctypes.c_float, c_void_p]),
     "objb_moe_combine_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p,
                                         c_void_p]),
     "objb_router_topk_batched_device": (c_int, [c_void_p, c_size, c_size, c_size, c_int, c_void_p, c_void_p,
@@ -136,6 +139,20 @@ def moe_pairs(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_li
     _lib.call("objb_moe_pairs_device", ctypes.byref(layer._c), P, _dev_ptr(d_count) if d_count is not None else None,
               _dev_ptr(pair_expert), _dev_ptr(pair_token), _dev_ptr(pair_out) if pair_out is not None else None, T,
               _dev_ptr(d_x), _dev_ptr(d_v), d_v.shape[0], float(swiglu_limit), _lib.stream_handle(stream))
+    return d_v
+
+
+def moe_pairs_tc(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 0.0, stream=None,
+                 d_count=None):
+    """moe_pairs for Q4_0 layers on the tensor cores (tcgen05 kind::i8):
+    runs of equal experts are taken 32 pairs at a time per 128-row weight
+    tile.  Same arguments; pairs must be grouped by expert."""
+    P = pair_expert.numel()
+    T = d_x.shape[0]
+    _lib.call("objb_moe_pairs_tc_device", ctypes.byref(layer._c), P,
+              _dev_ptr(d_count) if d_count is not None else None, _dev_ptr(pair_expert), _dev_ptr(pair_token),
+              _dev_ptr(pair_out) if pair_out is not None else None, T, _dev_ptr(d_x), _dev_ptr(d_v), d_v.shape[0],
+              float(swiglu_limit), _lib.stream_handle(stream))
     return d_v
 
 
