@@ -37,47 +37,83 @@
 namespace objb {
 namespace dev {
 
-constexpr int kTcRows = 128;               // M of the MMA: rows per tile
-constexpr int kTcNvp = 32;                 // pairs per slice
-constexpr int kTcNp = 3 * kTcNvp;          // MMA N: three digit planes of kTcNvp vectors
-constexpr int kTcKB = 8;                   // 32-column blocks per step
-constexpr int kTcStages = 3;               // ring depth: two steps in flight ahead
-constexpr int kTcThreads = 256;
-constexpr int kTcRawRow = kTcKB * 18;      // raw Q4_0 bytes of one row per step
-constexpr int kTcKch = 2 * kTcKB;          // 16-byte K columns of a staged operand
-constexpr int kTcBlockCols = 128;          // tensor-memory columns of one block's accumulators (>= kTcNp)
+constexpr int kTcRows = 128;                   // M of the MMA: rows per tile
+constexpr int kTcNvp = 32;                     // pairs per slice
+constexpr int kTcNp = 3 * kTcNvp;              // MMA N: three digit planes of kTcNvp vectors
+constexpr int kTcKB = 8;                       // 32-column blocks per step
+constexpr int kTcStages = 3;                   // ring of raw rows + digit planes + block scales
+constexpr int kTcAbuf = 2;                     // unpacked code buffers
+constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
+constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
+constexpr int kTcBlockCols = 128;              // tensor-memory columns of one block's accumulators (>= kTcNp)
 constexpr int kTcSlotCols = 2 * kTcBlockCols;  // one MMA group (two blocks)
-constexpr uint32_t kTcTmemCols = 512;      // two slots
+constexpr uint32_t kTcTmemCols = 512;          // two slots
+// warp roles
+constexpr int kTcProducerWarps = 4;  // warps 0-3
+constexpr int kTcMmaWarp = 4;
+constexpr int kTcUnpackWarp0 = 5, kTcUnpackWarps = 4;
+constexpr int kTcEpiWarp0 = 9, kTcEpiWarps = 8;
+constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 
 struct TcSmem {
-  alignas(1024) uint8_t a[kTcRows * kTcKB * 32];            // unpacked codes (also the partial-sum exchange)
-  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // digit planes
+  alignas(1024) uint8_t a[kTcAbuf][kTcRows * kTcKB * 32];   // signed codes q - 8, core-matrix order
+  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // digit planes, core-matrix order
   alignas(16) uint8_t raw[kTcStages][kTcRows * kTcRawRow];  // raw Q4_0 bytes
-  alignas(16) float xs[kTcStages][kTcNvp][kTcKB];
-  alignas(16) int32_t noff[kTcStages][kTcNvp][kTcKB];
-  float d[kTcKB][kTcRows];
-  int32_t out_row[kTcNvp];
-  alignas(8) uint64_t bar[2];
+  alignas(16) float xs[kTcStages][kTcKB][kTcNvp];           // vector block scales 2^(E-20)
+  alignas(16) float d[kTcAbuf][kTcKB][kTcRows];             // row block scales
+  alignas(16) float xchg[kTcNvp][kTcRows];                  // odd-block partial sums
+  alignas(8) uint64_t full[kTcStages], empty[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
+  uint64_t t_full[2], t_empty[2], x_full, x_empty;
   uint32_t tmem_base;
 };
 static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
 static_assert(kTcNp <= kTcBlockCols && 2 * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
+static_assert(kTcUnpackWarps * 32 == kTcRows && kTcEpiWarps == 8, "warp roles");
+
+// Arrival counts of the pipeline barriers.
+constexpr uint32_t kTcFullCount = 32 * kTcProducerWarps;             // producer threads (cp.async arrivals)
+constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps + kTcEpiWarps;  // MMA commit, unpack, epilogue
+constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;              // every unpack thread
+constexpr uint32_t kTcAEmptyCount = 1 + kTcEpiWarps;                  // MMA commit, epilogue (row scales)
+constexpr uint32_t kTcTEmptyCount = kTcEpiWarps;
+constexpr uint32_t kTcXFullCount = 32 * kTcEpiWarps / 2;           // every odd-block thread
+constexpr uint32_t kTcXEmptyCount = kTcEpiWarps / 2;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+// One arrival on `bar` once every cp.async this thread issued has landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Bounded wait that gives up early only when another wait of the launch
+// already timed out (other error bits, e.g. a flagged index, do not stop it).
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+  for (uint32_t i = 0; i < kMaxSpins; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (err && (i & 1023u) == 1023u &&
+        (*reinterpret_cast<volatile unsigned*>(err) & (kErrFullWaitTimeout | kErrEmptyWaitTimeout)) != 0u)
+      return false;
+  }
+  if (err) atomicOr(err, kErrFullWaitTimeout);
+  return false;
+}
+
+// Instruction descriptor of kind::i8 with both operands signed.
+__host__ __device__ constexpr uint32_t umma_idesc_s8s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((static_cast<uint32_t>(n) >> 3) << 17) |
+         ((static_cast<uint32_t>(m) >> 4) << 24);
 }
 
 // Digit planes of one 32-value block of vector v (one warp, one value per
 // lane): X = rint(x * 2^(20-E)), E the block's frexp exponent, split in three
 // signed 7-bit digits; plane k at planes[(v * 3 + k) * C + col]; per block
-// 2^(E-20) (NaN when the block is not finite) and -off * sum X.
-__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int off, int8_t* planes, float* xsc,
-                                                int32_t* noff) {
+// 2^(E-20) (NaN when the block is not finite).
+__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc) {
   const int lane = threadIdx.x & 31, nb = C / 32;
   float m = fabsf(xe);
 #pragma unroll
@@ -89,23 +125,19 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   const int X1 = (X - d0) / 128;
   const int d1 = ((X1 + 64) & 127) - 64;
   const int d2 = (X1 - d1) / 128;
-  const int sx = __reduce_add_sync(0xFFFFFFFFu, X);
   int8_t* p = planes + static_cast<size_t>(v) * 3 * C + b * 32 + lane;
   p[0] = static_cast<int8_t>(d0);
   p[C] = static_cast<int8_t>(d1);
   p[2 * C] = static_cast<int8_t>(d2);
-  if (lane == 0) {
+  if (lane == 0)
     xsc[static_cast<size_t>(v) * nb + b] = isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000);
-    noff[static_cast<size_t>(v) * nb + b] = -off * sx;
-  }
 }
 
 // Digit planes of `nvec` vectors (rows of x, x_stride apart); one warp per
 // (vector, block).
 __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict__ x, size_t x_stride, int nvec,
-                                                        const int32_t* count, int C, int off,
-                                                        int8_t* __restrict__ planes, float* __restrict__ xsc,
-                                                        int32_t* __restrict__ noff) {
+                                                        const int32_t* count, int C, int8_t* __restrict__ planes,
+                                                        float* __restrict__ xsc) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count) nvec = min(max(*count, 0), nvec);
@@ -113,7 +145,7 @@ __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict_
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb; wi += warps) {
     const int v = wi / nb, b = wi % nb;
-    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, off, planes, xsc, noff);
+    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, planes, xsc);
   }
 }
 
@@ -121,9 +153,8 @@ __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict_
 // planes; one warp per (pair, block).
 __global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(const float* __restrict__ g,
                                                                const float* __restrict__ u, int P,
-                                                               const int32_t* count, int I, float limit, int off,
-                                                               int8_t* __restrict__ planes, float* __restrict__ xsc,
-                                                               int32_t* __restrict__ noff) {
+                                                               const int32_t* count, int I, float limit,
+                                                               int8_t* __restrict__ planes, float* __restrict__ xsc) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count) P = min(max(*count, 0), P);
@@ -132,7 +163,7 @@ __global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(const float* __re
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < P * nb; wi += warps) {
     const int p = wi / nb, b = wi % nb;
     const size_t i = static_cast<size_t>(p) * I + b * 32 + lane;
-    tc_block_digits(swiglu(g[i], u[i], limit), p, b, I, off, planes, xsc, noff);
+    tc_block_digits(swiglu(g[i], u[i], limit), p, b, I, planes, xsc);
   }
 }
 
@@ -219,7 +250,6 @@ struct TcArgs {
   const int32_t* nslices;
   const int8_t* planes;      // digit planes [nvec][3][C]
   const float* xsc;          // [nvec][C/32]
-  const int32_t* noff;       // [nvec][C/32]
   int nvec;
   float* out;                // [out_rows][R]
   float* out2;               // for W2
@@ -241,7 +271,7 @@ __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int
   it.s0 = A.slice_start[sl];
   it.ns = min(max(A.slice_len[sl], 1), kTcNvp);
   int e = A.pe[it.s0];
-  if (e < 0 || e >= A.num_experts) e = 0;  // flagged at the item's start
+  if (e < 0 || e >= A.num_experts) e = 0;  // flagged at the item's end
   it.w = mat ? A.W2[e] : A.W[e];
   it.dst = mat ? A.out2 : A.out;
   return it;
@@ -252,115 +282,116 @@ __device__ __forceinline__ int tc_vec(const TcArgs& A, int p) {
   return (v < 0 || v >= A.nvec) ? 0 : v;
 }
 
-// Stages step `chunk` of item `it` into ring slot `st`: raw rows, the live
-// vectors' digit planes (rows k * kTcNvp + i of the B operand) and their
-// block scales.
-__device__ __forceinline__ void tc_prefetch(TcSmem& sm, int st, const TcArgs& A, const TcItem& it, int chunk,
-                                            size_t row_bytes) {
-  const int tid = threadIdx.x, nb = A.C / 32;
+// Producer (kTcProducerWarps warps, pt = thread index among them): stages
+// step `chunk` of item `it` in ring slot `st` by 16-byte cp.async -- the
+// tile's raw rows (nine pieces per row), the live vectors' digit-plane pieces
+// (rows k * kTcNvp + i of the B operand) and block scales -- and every
+// producer thread reports the completion of its copies on full[st].  Lane i
+// < ns of each producer warp holds vector i's plane row base (vrow) and block
+// scales (vxs) for this item; the other lanes fetch them by shuffle.
+__device__ __forceinline__ void tc_produce(TcSmem& sm, int st, const TcArgs& A, const TcItem& it, int chunk,
+                                          size_t row_bytes, const int8_t* vrow, const float* vxs, int pt) {
   constexpr int kPieces = kTcRawRow / 16;
-  const uint8_t* base = it.w + static_cast<size_t>(chunk) * kTcRawRow;
-  for (int t = tid; t < kTcRows * kPieces; t += kTcThreads) {
+  constexpr int kPT = 32 * kTcProducerWarps;
+  const int lane = pt & 31, pw = pt >> 5;
+  const int rows = min(kTcRows, A.R - it.tile * kTcRows);
+  const uint8_t* base = it.w + static_cast<size_t>(it.tile) * kTcRows * row_bytes + static_cast<size_t>(chunk) * kTcRawRow;
+  for (int t = pt; t < rows * kPieces; t += kPT) {
     const int r = t / kPieces, p = t % kPieces;
-    const int row = it.tile * kTcRows + r;
-    if (row < A.R) cp_async16(sm.raw[st] + r * kTcRawRow + p * 16, base + static_cast<size_t>(row) * row_bytes + p * 16);
+    cp_async16(sm.raw[st] + r * kTcRawRow + p * 16, base + static_cast<size_t>(r) * row_bytes + p * 16);
   }
-  for (int t = tid; t < 3 * it.ns * kTcKch; t += kTcThreads) {
-    const int rr = t / kTcKch, p = t % kTcKch;
-    const int k = rr / it.ns, i = rr % it.ns;
-    const int v = tc_vec(A, it.s0 + i);
-    const int brow = k * kTcNvp + i;
-    cp_async16(sm.b[st] + ((brow >> 3) * kTcKch + p) * 128 + (brow & 7) * 16,
-               A.planes + (static_cast<size_t>(v) * 3 + k) * A.C + chunk * (kTcKB * 32) + p * 16);
+  // plane pieces: warp pw takes pieces [pw * 32 + 32 * kTcProducerWarps * n) of ns * 48
+  const int nb_copies = it.ns * 3 * kTcKch;
+  for (int t0 = pw * 32; t0 < nb_copies; t0 += kPT) {
+    const int t = t0 + lane;
+    const int i = min(t / (3 * kTcKch), it.ns - 1), rem = t % (3 * kTcKch);
+    const int8_t* src = reinterpret_cast<const int8_t*>(
+        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(vrow), i));
+    if (t < nb_copies) {
+      const int k = rem / kTcKch, p = rem % kTcKch;
+      const int brow = k * kTcNvp + i;
+      cp_async16(sm.b[st] + ((brow >> 3) * kTcKch + p) * 128 + (brow & 7) * 16,
+                 src + static_cast<size_t>(k) * A.C + chunk * (kTcKB * 32) + p * 16);
+    }
   }
-  for (int t = tid; t < it.ns * 4; t += kTcThreads) {
-    const int i = t >> 2, q = t & 3;
-    const size_t off = static_cast<size_t>(tc_vec(A, it.s0 + i)) * nb + chunk * kTcKB + (q & 1) * 4;
-    if (q < 2) cp_async16(&sm.xs[st][i][(q & 1) * 4], A.xsc + off);
-    else cp_async16(&sm.noff[st][i][(q & 1) * 4], A.noff + off);
+  const int nx = it.ns * kTcKB;
+  for (int t0 = pw * 32; t0 < nx; t0 += kPT) {
+    const int t = t0 + lane;
+    const int i = min(t / kTcKB, it.ns - 1), j = t % kTcKB;
+    const float* src = reinterpret_cast<const float*>(
+        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(vxs), i));
+    if (t < nx) cp_async4(&sm.xs[st][j][i], src + chunk * kTcKB + j);
   }
+  cp_async_mbar_arrive(&sm.full[st]);
 }
 
-// Raw rows of ring slot `st` -> code bytes in core-matrix order and the row
-// scales; two threads per row, four blocks each.
-__device__ __forceinline__ void tc_unpack(TcSmem& sm, int st) {
-  const int tid = threadIdx.x;
-  const int r = tid & (kTcRows - 1), h = tid >> 7;
-  const uint8_t* seg = sm.raw[st] + r * kTcRawRow + h * 72;
-  uint32_t w[18];
-  if (h == 0) {
+// Unpack (four warps, thread = tile row): raw row of ring slot `st` -> signed
+// codes q - 8 in core-matrix order (A buffer `ab`) and the row's block scales.
+__device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
+  uint32_t w[kTcRawRow / 4];
+  const uint8_t* src = sm.raw[st] + r * kTcRawRow;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 x = *reinterpret_cast<const uint4*>(seg + 16 * q);
-      w[4 * q] = x.x, w[4 * q + 1] = x.y, w[4 * q + 2] = x.z, w[4 * q + 3] = x.w;
-    }
-    const uint2 y = *reinterpret_cast<const uint2*>(seg + 64);
-    w[16] = y.x, w[17] = y.y;
-  } else {
-    const uint2 y = *reinterpret_cast<const uint2*>(seg);
-    w[0] = y.x, w[1] = y.y;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 x = *reinterpret_cast<const uint4*>(seg + 8 + 16 * q);
-      w[2 + 4 * q] = x.x, w[3 + 4 * q] = x.y, w[4 + 4 * q] = x.z, w[5 + 4 * q] = x.w;
-    }
+  for (int q = 0; q < kTcRawRow / 16; ++q) {
+    const uint4 x = *reinterpret_cast<const uint4*>(src + 16 * q);
+    w[4 * q] = x.x, w[4 * q + 1] = x.y, w[4 * q + 2] = x.z, w[4 * q + 3] = x.w;
   }
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    // block b occupies bytes [18 b, 18 b + 18) of the 72: f16 scale, 16 code bytes
+  for (int b = 0; b < kTcKB; ++b) {
+    // block b occupies bytes [18 b, 18 b + 18): f16 scale, 16 code bytes
+    const int wi = 18 * b / 4;
     uint32_t d16, qs[4];
-    if (b % 2 == 0) {
-      const int wb = 18 * b / 4;
-      d16 = w[wb] & 0xFFFFu;
+    if ((18 * b) % 4 == 0) {
+      d16 = w[wi] & 0xFFFFu;
 #pragma unroll
-      for (int m = 0; m < 4; ++m) qs[m] = __funnelshift_r(w[wb + m], w[wb + m + 1], 16);
+      for (int m = 0; m < 4; ++m) qs[m] = __funnelshift_r(w[wi + m], w[wi + m + 1], 16);
     } else {
-      const int wb = (18 * b + 2) / 4;
-      d16 = w[wb - 1] >> 16;
+      d16 = w[wi] >> 16;
 #pragma unroll
-      for (int m = 0; m < 4; ++m) qs[m] = w[wb + m];
+      for (int m = 0; m < 4; ++m) qs[m] = w[wi + 1 + m];
     }
     uint32_t c[8];
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      const uint32_t lo = qs[m] & 0x0F0F0F0Fu, hi = (qs[m] >> 4) & 0x0F0F0F0Fu;
-      c[2 * m] = __byte_perm(lo, hi, 0x5140);      // codes 8m .. 8m+3
-      c[2 * m + 1] = __byte_perm(lo, hi, 0x7362);  // codes 8m+4 .. 8m+7
+      // bytes q in [0, 15] -> q - 8 as int8: (q + 0x78) ^ 0x80, no carry between bytes
+      const uint32_t lo = (qs[m] & 0x0F0F0F0Fu) + 0x78787878u, hi = ((qs[m] >> 4) & 0x0F0F0F0Fu) + 0x78787878u;
+      c[2 * m] = __byte_perm(lo, hi, 0x5140) ^ 0x80808080u;      // codes 8m .. 8m+3
+      c[2 * m + 1] = __byte_perm(lo, hi, 0x7362) ^ 0x80808080u;  // codes 8m+4 .. 8m+7
     }
-    const int j = 4 * h + b;
-    uint8_t* dst = sm.a + ((r >> 3) * kTcKch + 2 * j) * 128 + (r & 7) * 16;
+    uint8_t* dst = sm.a[ab] + ((r >> 3) * kTcKch + 2 * b) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(c[0], c[1], c[2], c[3]);
     *reinterpret_cast<uint4*>(dst + 128) = make_uint4(c[4], c[5], c[6], c[7]);
-    sm.d[j][r] = f16_bits_to_f32(d16);
+    sm.d[ab][b][r] = f16_bits_to_f32(d16);
   }
-}
-
-// MMAs of blocks 2g, 2g+1 of the staged step into tensor-memory slot g & 1.
-__device__ __forceinline__ void tc_issue_group(TcSmem& sm, int st, int g, uint32_t tmem, uint32_t idesc) {
-#pragma unroll
-  for (int jj = 0; jj < 2; ++jj) {
-    const int j = 2 * g + jj;
-    const uint64_t da = umma_desc_kmajor(smem_addr(sm.a + 2 * j * 128), 128, kTcKch * 128);
-    const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
-    umma_i8(tmem + (g & 1) * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
-  }
-  umma_commit(&sm.bar[g & 1]);
 }
 
 // The grouped contraction of Q4_0 matrices: out[slot_out[p]][r] = y[vector
 // slot_vec[p]][r] of expert pe[p]'s matrix for every pair p.  Needs C a
-// multiple of 256 (rows of whole 16-byte pieces per step).
+// multiple of 256 (rows of whole 16-byte pieces per step).  Warp roles:
+// producer (0), MMA issuer (1), unpack (2-5), epilogue (6-13); every hand-off
+// is an mbarrier with a bounded wait.
 __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>(tc_smem_raw);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.bar[0])));
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.bar[1])));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&sm.full[i], kTcFullCount);
+      mbar_init(&sm.empty[i], kTcEmptyCount);
+    }
+    for (int i = 0; i < kTcAbuf; ++i) {
+      mbar_init(&sm.a_full[i], kTcAFullCount);
+      mbar_init(&sm.a_empty[i], kTcAEmptyCount);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.t_full[i], 1);
+      mbar_init(&sm.t_empty[i], kTcTEmptyCount);
+    }
+    mbar_init(&sm.x_full, kTcXFullCount);
+    mbar_init(&sm.x_empty, kTcXEmptyCount);
+    fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(&sm.tmem_base, kTcTmemCols);
+  if (warp == kTcMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
@@ -373,121 +404,170 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
   const int total = *A.nslices * tiles * mats;
   const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int nsteps = my_items * nchunks;
-  const uint32_t idesc = umma_idesc_u8s8(kTcRows, kTcNp);
-  const int quarter = warp & 3, half = warp >> 2;   // tensor-memory lanes 32*quarter..; blocks of parity `half`
-  const int trow = 32 * quarter + lane;             // this thread's tile row in the epilogue
-  const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
-
   auto item_at = [&](int s) { return tc_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
+
+  if (warp < kTcProducerWarps) {
+    TcItem it{};
+    const int8_t* vrow = A.planes;
+    const float* vxs = A.xsc;
 #pragma unroll 1
-  for (int s = 0; s < kTcStages - 1; ++s) {
-    if (s < nsteps) tc_prefetch(sm, s, A, item_at(s), s % nchunks, row_bytes);
-    cp_async_commit();
-  }
-  float acc[kTcNvp];
-#pragma unroll
-  for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
-  TcItem cur{};
-  uint32_t phase[2] = {0u, 0u};
-  bool ok = true;
-#pragma unroll 1
-  for (int s = 0; s < nsteps; ++s) {
-    const int chunk = s % nchunks, st = s % kTcStages;
-    if (s + kTcStages - 1 < nsteps) {
-      const int s2 = s + kTcStages - 1;
-      tc_prefetch(sm, s2 % kTcStages, A, item_at(s2), s2 % nchunks, row_bytes);
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kTcStages, chunk = s % nchunks;
+      if (chunk == 0) {
+        it = item_at(s);
+        const int v = lane < it.ns ? tc_vec(A, it.s0 + lane) : 0;
+        vrow = A.planes + static_cast<size_t>(v) * 3 * A.C;
+        vxs = A.xsc + static_cast<size_t>(v) * nb;
+      }
+      if (s >= kTcStages && !tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err)) break;
+      tc_produce(sm, st, A, it, chunk, row_bytes, vrow, vxs, tid);
     }
-    cp_async_commit();
-    if (chunk == 0) {
-      cur = item_at(s);
-      if (tid < kTcNvp) {
-        int o = -1;
-        if (tid < cur.ns) {
-          const int p = cur.s0 + tid;
-          o = A.slot_out ? A.slot_out[p] : p;
-          const int v = A.slot_vec ? A.slot_vec[p] : p;
-          const int e = A.pe[p];
-          if (o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) {
-            if (A.err) atomicOr(A.err, 8u);
-            if (o >= A.out_rows) o = -1;
+    cp_async_wait_all();
+  } else if (warp == kTcMmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_s8s8(kTcRows, kTcNp);
+#pragma unroll 1
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kTcStages, ab = s % kTcAbuf;
+        if (!tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
+            !tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err))
+          break;
+        fence_async_shared();  // digit planes written by cp.async, read by the MMAs
+        tc_fence_after_sync();
+        bool ok = true;
+#pragma unroll 1
+        for (int g = 0; g < kTcKB / 2; ++g) {
+          const int G = (kTcKB / 2) * s + g, slot = G & 1;
+          if (G >= 2 && !tc_wait(&sm.t_empty[slot], ((G >> 1) - 1) & 1, A.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * g + jj;
+            const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
+            const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
+            umma_i8(tmem + slot * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
+          }
+          umma_commit(&sm.t_full[slot]);
+        }
+        if (!ok) break;
+        umma_commit(&sm.a_empty[ab]);
+        umma_commit(&sm.empty[st]);
+      }
+    }
+  } else if (warp < kTcEpiWarp0) {
+    const int r = tid - 32 * kTcUnpackWarp0;
+#pragma unroll 1
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kTcStages, ab = s % kTcAbuf;
+      if (!tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err)) break;
+      if (s >= kTcAbuf && !tc_wait(&sm.a_empty[ab], ((s / kTcAbuf) - 1) & 1, A.err)) break;
+      tc_unpack(sm, st, ab, r);
+      fence_async_shared();  // codes written here, read by the MMAs
+      mbar_arrive(&sm.a_full[ab]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[st]);
+    }
+  } else {
+    const int ew = warp - kTcEpiWarp0;
+    const int quarter = warp & 3, half = ew >> 2;  // tensor-memory lanes 32*quarter..; blocks of parity `half`
+    const int trow = 32 * quarter + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
+    float acc[kTcNvp];
+#pragma unroll
+    for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+    int items_done = 0;
+    TcItem it{};
+#pragma unroll 1
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kTcStages, ab = s % kTcAbuf, chunk = s % nchunks;
+      if (chunk == 0) it = item_at(s);
+      const int nvg = (it.ns + 7) >> 3;
+      // block scales (cp.async) and row scales (unpack) of this step are read below
+      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err) && tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err);
+#pragma unroll 1
+      for (int g = 0; g < kTcKB / 2 && ok; ++g) {
+        const int G = (kTcKB / 2) * s + g, slot = G & 1;
+        if (!tc_wait(&sm.t_full[slot], (G >> 1) & 1, A.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const int j = 2 * g + half;
+        const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + half * kTcBlockCols;
+        const float dr = sm.d[ab][j][trow];
+#pragma unroll
+        for (int vg = 0; vg < kTcNvp / 8; ++vg) {
+          if (vg < nvg) {
+            uint32_t r0[8], r1[8], r2[8];
+            tmem_ld8(taddr + 8 * vg, r0);
+            tmem_ld8(taddr + kTcNvp + 8 * vg, r1);
+            tmem_ld8(taddr + 2 * kTcNvp + 8 * vg, r2);
+            tmem_wait_ld();
+            const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[st][j][8 * vg]);
+            const float4 xb = *reinterpret_cast<const float4*>(&sm.xs[st][j][8 * vg + 4]);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int S = static_cast<int>(r0[u]) + static_cast<int>(r1[u]) * 128 + static_cast<int>(r2[u]) * 16384;
+              acc[8 * vg + u] = fmaf(__int2float_rn(S), dr * xv[u], acc[8 * vg + u]);
+            }
           }
         }
-        sm.out_row[tid] = o;
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.t_empty[slot]);
       }
-    }
-    cp_async_wait<kTcStages - 1>();
-    __syncthreads();
-    tc_unpack(sm, st);
-    fence_async_shared();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after_sync();
-      tc_issue_group(sm, st, 0, tmem, idesc);
-    }
-    const int nvg = (cur.ns + 7) >> 3;
-#pragma unroll
-    for (int g = 0; g < kTcKB / 2; ++g) {
-      const bool done = mbar_wait_bounded(&sm.bar[g & 1], phase[g & 1], A.err, kErrFullWaitTimeout);
-      phase[g & 1] ^= 1u;
-      if (!__syncthreads_and(done)) {
-        ok = false;
-        break;
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.a_empty[ab]);
+        mbar_arrive(&sm.empty[st]);
       }
-      tc_fence_after_sync();
-      if (tid == 0 && g + 1 < kTcKB / 2) tc_issue_group(sm, st, g + 1, tmem, idesc);
-      // epilogue of block j = 2g + half: exact block sums -> f32
-      const int j = 2 * g + half;
-      const uint32_t taddr = tmem + lane_addr + (g & 1) * kTcSlotCols + half * kTcBlockCols;
-      uint32_t rv[3][4][8];
+      if (chunk == nchunks - 1) {
+        // odd-block partial sums through shared memory, then one store per live pair
+        if (half == 1) {
+          if (items_done > 0 && !tc_wait(&sm.x_empty, (items_done - 1) & 1, A.err)) break;
 #pragma unroll
-      for (int vg = 0; vg < 4; ++vg)
-        if (vg < nvg) {
+          for (int i = 0; i < kTcNvp; ++i) sm.xchg[i][trow] = acc[i];
+          mbar_arrive(&sm.x_full);
+        } else {
+          if (!tc_wait(&sm.x_full, items_done & 1, A.err)) break;
+          const int grow = it.tile * kTcRows + trow;
 #pragma unroll
-          for (int k = 0; k < 3; ++k) tmem_ld8(taddr + k * kTcNvp + 8 * vg, rv[k][vg]);
-        }
-      tmem_wait_ld();
-      const float dr = sm.d[j][trow];
-#pragma unroll
-      for (int vg = 0; vg < 4; ++vg)
-        if (vg < nvg) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = 8 * vg + u;
-            const int S = static_cast<int>(rv[0][vg][u]) + static_cast<int>(rv[1][vg][u]) * 128 +
-                          static_cast<int>(rv[2][vg][u]) * 16384 + sm.noff[st][i][j];
-            acc[i] = fmaf(__int2float_rn(S), dr * sm.xs[st][i][j], acc[i]);
+          for (int i = 0; i < kTcNvp; ++i) {
+            if (i < it.ns) {
+              const int p = it.s0 + i;
+              const int o = A.slot_out ? A.slot_out[p] : p;
+              if (o >= 0 && o < A.out_rows && grow < A.R)
+                it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + sm.xchg[i][trow];
+            }
           }
+          if (ew == 0 && lane < it.ns) {
+            const int p = it.s0 + lane;
+            const int o = A.slot_out ? A.slot_out[p] : p;
+            const int v = A.slot_vec ? A.slot_vec[p] : p;
+            const int e = A.pe[p];
+            if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) && A.err)
+              atomicOr(A.err, kErrBadExpertId);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.x_empty);
         }
-      tc_fence_before_sync();
-    }
-    if (!ok) break;
-    __syncthreads();
-    if (chunk == nchunks - 1) {
-      // odd-block partial sums through shared memory, then one store per live pair
-      float* xchg = reinterpret_cast<float*>(sm.a);  // [kTcNvp][kTcRows]
-      if (half == 1) {
 #pragma unroll
-        for (int i = 0; i < kTcNvp; ++i) xchg[i * kTcRows + trow] = acc[i];
+        for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+        ++items_done;
       }
-      __syncthreads();
-      const int grow = cur.tile * kTcRows + trow;
-      if (half == 0 && grow < A.R) {
-#pragma unroll
-        for (int i = 0; i < kTcNvp; ++i) {
-          const int o = sm.out_row[i];
-          if (i < cur.ns && o >= 0)
-            cur.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + xchg[i * kTcRows + trow];
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
-      __syncthreads();
     }
   }
-  cp_async_wait<0>();
   tc_fence_before_sync();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, kTcTmemCols);
+  if (warp == kTcMmaWarp) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
 }
 
 }  // namespace dev
@@ -495,7 +575,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
 namespace {
 
 struct TcLayout {
-  size_t planes_x, xsc_x, noff_x, g, u, planes_a, xsc_a, noff_a, run_start, slice_start, slice_len, nslices, total;
+  size_t planes_x, xsc_x, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, nslices, total;
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -510,12 +590,10 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I) {
   };
   L.planes_x = take(T * 3 * H);
   L.xsc_x = take(T * (H / 32) * 4);
-  L.noff_x = take(T * (H / 32) * 4);
   L.g = take(P * I * 4);
   L.u = take(P * I * 4);
   L.planes_a = take(P * 3 * I);
   L.xsc_a = take(P * (I / 32) * 4);
-  L.noff_a = take(P * (I / 32) * 4);
   L.run_start = take(P * 4);
   L.slice_start = take(P * 4);
   L.slice_len = take(P * 4);
@@ -584,12 +662,10 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   uint8_t* sc = static_cast<uint8_t*>(scratch);
   int8_t* planes_x = reinterpret_cast<int8_t*>(sc + L.planes_x);
   float* xsc_x = reinterpret_cast<float*>(sc + L.xsc_x);
-  int32_t* noff_x = reinterpret_cast<int32_t*>(sc + L.noff_x);
   float* g = reinterpret_cast<float*>(sc + L.g);
   float* u = reinterpret_cast<float*>(sc + L.u);
   int8_t* planes_a = reinterpret_cast<int8_t*>(sc + L.planes_a);
   float* xsc_a = reinterpret_cast<float*>(sc + L.xsc_a);
-  int32_t* noff_a = reinterpret_cast<int32_t*>(sc + L.noff_a);
   int32_t* run_start = reinterpret_cast<int32_t*>(sc + L.run_start);
   int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
   int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
@@ -606,7 +682,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, run_start,
                       slice_start, slice_len, nslices));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
-                      static_cast<const int32_t*>(nullptr), H, 8, planes_x, xsc_x, noff_x));
+                      static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x));
   dev::TcArgs a{};
   a.W = reinterpret_cast<const uint8_t* const*>(l->d_gate);
   a.W2 = reinterpret_cast<const uint8_t* const*>(l->d_up);
@@ -621,7 +697,6 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.nslices = nslices;
   a.planes = planes_x;
   a.xsc = xsc_x;
-  a.noff = noff_x;
   a.nvec = T;
   a.out = g;
   a.out2 = u;
@@ -629,7 +704,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.err = err;
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, static_cast<const float*>(g),
-                      static_cast<const float*>(u), P, d_count, I, limit, 8, planes_a, xsc_a, noff_a));
+                      static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a));
   a.W = reinterpret_cast<const uint8_t* const*>(l->d_down);
   a.W2 = nullptr;
   a.R = O;
@@ -638,7 +713,6 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.slot_out = po;
   a.planes = planes_a;
   a.xsc = xsc_a;
-  a.noff = noff_a;
   a.nvec = P;
   a.out = v;
   a.out2 = nullptr;
