@@ -10,22 +10,33 @@
 //
 // A launch works on pairs sorted by expert: "slices" (pieces of at most 32
 // pairs of one expert) are found on the device (no host round trip), and
-// each (slice, 128-row tile) is one work item of a persistent grid.  A work
-// item walks its K in steps of 8 blocks (256 columns):
-//   * all threads stage the step's raw Q4_0 bytes (128 rows x 144 bytes) and
-//     the live vectors' digit planes with 16-byte cp.async, two steps ahead
-//     in a three-deep shared-memory ring;
-//   * the raw rows are unpacked to one code byte per column in the
-//     core-matrix order the MMA reads (K-major, no swizzle);
+// each (slice, 128-row tile) is one work item of a persistent grid.  Before
+// the contraction, the digit planes and block scales of every slice are
+// gathered into a slice image laid out exactly as the MMA reads its B
+// operand (16 or 32 vectors wide).  A work item walks its K in steps of 8
+// blocks (256 columns):
+//   * one producer thread stages a step with one 2-D TMA copy of the raw
+//     Q4_0 tile (128 rows x 144 bytes; a per-stage tensor map whose global
+//     address is rewritten on the device for each expert, rows past the
+//     matrix end zero-filled) and two bulk copies of the slice image;
+//   * four unpack warps turn the raw rows into signed code bytes q - 8 in
+//     core-matrix order (K-major, no swizzle) and the row block scales;
 //   * one thread issues the MMAs two blocks at a time into one of two
-//     tensor-memory slots, so the epilogue of one pair of blocks overlaps
-//     the MMAs of the next;
-//   * warps 0-3 fold the even blocks, warps 4-7 the odd ones (tensor-memory
-//     lanes = tile rows); the two partial sums are added at the item's end.
+//     tensor-memory slots (an MMA of this shape costs about 100 cycles to
+//     issue whatever its N, so the group, not the slot count, sets the pace);
+//   * sixteen epilogue warps (tensor-memory lanes = tile rows; blocks of one
+//     parity and half of the vectors each) fold the exact block sums into
+//     f32 row sums; the two parity halves are added at the item's end.
+// Every hand-off is an mbarrier with a bounded wait.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "objb_common.h"
 #include "objb_decode.cuh"
@@ -38,64 +49,112 @@ namespace objb {
 namespace dev {
 
 constexpr int kTcRows = 128;                   // M of the MMA: rows per tile
-constexpr int kTcNvp = 32;                     // pairs per slice
-constexpr int kTcNp = 3 * kTcNvp;              // MMA N: three digit planes of kTcNvp vectors
+constexpr int kTcNvp = 32;                     // pairs per slice (at most)
+constexpr int kTcUnit = 16;                    // vectors per slice-image unit; a slice is 1 or 2 units wide
+constexpr int kTcNp = 3 * kTcNvp;              // widest MMA N: three digit planes of kTcNvp vectors
 constexpr int kTcKB = 8;                       // 32-column blocks per step
-constexpr int kTcStages = 3;                   // ring of raw rows + digit planes + block scales
+constexpr int kTcStages = 3;                   // ring of raw tiles + slice-image steps
 constexpr int kTcAbuf = 2;                     // unpacked code buffers
 constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
 constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
 constexpr int kTcBlockCols = 128;              // tensor-memory columns of one block's accumulators (>= kTcNp)
 constexpr int kTcSlotCols = 2 * kTcBlockCols;  // one MMA group (two blocks)
-constexpr uint32_t kTcTmemCols = 512;          // two slots
+constexpr int kTcSlots = 2;                    // tensor-memory slots
+constexpr uint32_t kTcTmemCols = 512;
+constexpr int kTcUnitBBytes = 3 * kTcUnit * kTcKB * 32;  // digit planes of one unit, one step
+constexpr int kTcUnitXFloats = kTcKB * kTcUnit;          // block scales of one unit, one step
 // warp roles
-constexpr int kTcProducerWarps = 4;  // warps 0-3
-constexpr int kTcMmaWarp = 4;
-constexpr int kTcUnpackWarp0 = 5, kTcUnpackWarps = 4;
-constexpr int kTcEpiWarp0 = 9, kTcEpiWarps = 8;
+constexpr int kTcProducerWarp = 0;
+constexpr int kTcMmaWarp = 1;
+constexpr int kTcUnpackWarp0 = 2, kTcUnpackWarps = 4;
+constexpr int kTcEpiWarp0 = 6, kTcEpiWarps = 16;
 constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 
 struct TcSmem {
   alignas(1024) uint8_t a[kTcAbuf][kTcRows * kTcKB * 32];   // signed codes q - 8, core-matrix order
-  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // digit planes, core-matrix order
-  alignas(16) uint8_t raw[kTcStages][kTcRows * kTcRawRow];  // raw Q4_0 bytes
-  alignas(16) float xs[kTcStages][kTcKB][kTcNvp];           // vector block scales 2^(E-20)
+  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // slice image step (digit planes)
+  alignas(128) uint8_t raw[kTcStages][kTcRows * kTcRawRow]; // raw Q4_0 tile step (TMA box)
+  alignas(16) float xs[kTcStages][kTcKB * kTcNvp];          // vector block scales [block][vector]
   alignas(16) float d[kTcAbuf][kTcKB][kTcRows];             // row block scales
   alignas(16) float xchg[kTcNvp][kTcRows];                  // odd-block partial sums
+  alignas(128) CUtensorMap tmap[kTcStages];                 // per-stage tensor maps being rewritten
   alignas(8) uint64_t full[kTcStages], empty[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
-  uint64_t t_full[2], t_empty[2], x_full, x_empty;
+  uint64_t t_full[kTcSlots], t_empty[kTcSlots], x_full, x_empty;
   uint32_t tmem_base;
 };
 static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
-static_assert(kTcNp <= kTcBlockCols && 2 * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
-static_assert(kTcUnpackWarps * 32 == kTcRows && kTcEpiWarps == 8, "warp roles");
+static_assert(kTcNp <= kTcBlockCols && kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
+static_assert(kTcUnpackWarps * 32 == kTcRows && kTcEpiWarps == 16 && kTcNvp == 2 * kTcUnit, "warp roles");
 
 // Arrival counts of the pipeline barriers.
-constexpr uint32_t kTcFullCount = 32 * kTcProducerWarps;             // producer threads (cp.async arrivals)
+constexpr uint32_t kTcFullCount = 1;                                  // producer (arrive + transaction bytes)
 constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps + kTcEpiWarps;  // MMA commit, unpack, epilogue
-constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;              // every unpack thread
+constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;               // every unpack thread
 constexpr uint32_t kTcAEmptyCount = 1 + kTcEpiWarps;                  // MMA commit, epilogue (row scales)
 constexpr uint32_t kTcTEmptyCount = kTcEpiWarps;
-constexpr uint32_t kTcXFullCount = 32 * kTcEpiWarps / 2;           // every odd-block thread
+constexpr uint32_t kTcXFullCount = 32 * kTcEpiWarps / 2;              // every odd-block thread
 constexpr uint32_t kTcXEmptyCount = kTcEpiWarps / 2;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+// 1-D bulk copy (both addresses 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void tc_bulk(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
 }
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+// 2-D tiled TMA load of the box at (x, y) of the tensor map (no multicast).
+__device__ __forceinline__ void tc_tma_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
 }
-// One arrival on `bar` once every cp.async this thread issued has landed.
-__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+// Tensor map in shared memory: new global address.
+__device__ __forceinline__ void tc_tmap_set_addr(CUtensorMap* smem_map, const void* addr) {
+  asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(smem_addr(smem_map)),
+               "l"(reinterpret_cast<uint64_t>(addr))
+               : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Copies a tensor map from shared to global memory with a release fence of
+// the tensor-map proxy (whole warp).
+__device__ __forceinline__ void tc_tmap_publish(CUtensorMap* gmem_map, const CUtensorMap* smem_map) {
+  asm volatile(
+      "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::"l"(
+          reinterpret_cast<uint64_t>(gmem_map)),
+      "r"(smem_addr(smem_map))
+      : "memory");
+}
+__device__ __forceinline__ void tc_tmap_acquire(const CUtensorMap* gmem_map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(gmem_map))
+               : "memory");
+}
+
 // Bounded wait that gives up early only when another wait of the launch
 // already timed out (other error bits, e.g. a flagged index, do not stop it).
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
   for (uint32_t i = 0; i < kMaxSpins; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (err && (i & 1023u) == 1023u &&
+        (*reinterpret_cast<volatile unsigned*>(err) & (kErrFullWaitTimeout | kErrEmptyWaitTimeout)) != 0u)
+      return false;
+  }
+  if (err) atomicOr(err, kErrFullWaitTimeout);
+  return false;
+}
+
+// Bounded wait without suspending the thread between polls (lowest wake-up
+// latency; for the single MMA-issuing thread).
+__device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned* err) {
+  for (uint32_t i = 0; i < 64u * kMaxSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (err && (i & 4095u) == 4095u &&
         (*reinterpret_cast<volatile unsigned*>(err) & (kErrFullWaitTimeout | kErrEmptyWaitTimeout)) != 0u)
       return false;
   }
@@ -197,10 +256,12 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp
 }
 
 __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restrict__ pe, int P, const int32_t* count,
-                                                         int nvp, int32_t* __restrict__ run_start,
+                                                         int32_t* __restrict__ run_start,
                                                          int32_t* __restrict__ slice_start,
                                                          int32_t* __restrict__ slice_len,
-                                                         int32_t* __restrict__ nslices) {
+                                                         int32_t* __restrict__ slice_unit,
+                                                         int32_t* __restrict__ nslices, int unit_cap,
+                                                         unsigned* err) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ int warp_tot[32];
   if (count) P = min(max(*count, 0), P);
@@ -215,26 +276,87 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
   for (int p = a; p < b; ++p)
     if (p == 0 || pe[p] != pe[p - 1]) run_start[pos++] = p;
   __syncthreads();
-  // 2. slices of each run
+  // 2. slices of each run, and their offsets in slice-image units
   per = (nruns + nt - 1) / nt;
   a = min(nruns, tid * per);
   b = min(nruns, a + per);
   local = 0;
-  for (int r = a; r < b; ++r) {
-    const int len = (r + 1 < nruns ? run_start[r + 1] : P) - run_start[r];
-    local += (len + nvp - 1) / nvp;
-  }
-  int total = 0;
-  pos = block_exclusive_scan(local, &total, warp_tot);
+  int lunits = 0;
   for (int r = a; r < b; ++r) {
     const int s0 = run_start[r], s1 = r + 1 < nruns ? run_start[r + 1] : P;
-    for (int q = s0; q < s1; q += nvp) {
+    for (int q = s0; q < s1; q += kTcNvp) {
+      ++local;
+      lunits += (min(kTcNvp, s1 - q) + kTcUnit - 1) / kTcUnit;
+    }
+  }
+  int total = 0, total_units = 0;
+  pos = block_exclusive_scan(local, &total, warp_tot);
+  int upos = block_exclusive_scan(lunits, &total_units, warp_tot);
+  for (int r = a; r < b; ++r) {
+    const int s0 = run_start[r], s1 = r + 1 < nruns ? run_start[r + 1] : P;
+    for (int q = s0; q < s1; q += kTcNvp) {
+      const int len = min(kTcNvp, s1 - q);
       slice_start[pos] = q;
-      slice_len[pos] = min(nvp, s1 - q);
+      slice_len[pos] = len;
+      slice_unit[pos] = upos;
+      upos += (len + kTcUnit - 1) / kTcUnit;
       ++pos;
     }
   }
-  if (tid == 0) *nslices = total;
+  // a pair list not grouped by expert can need more image space than sized
+  // for: run nothing and flag it
+  if (tid == 0) {
+    *nslices = total_units <= unit_cap ? total : 0;
+    if (total_units > unit_cap && err) atomicOr(err, kErrBadExpertId);
+  }
+}
+
+// The slice images of one contraction: for slice sl, step c, the B operand
+// rows k * nv + i (plane k of the slice's vector i, nv = 16 or 32; zero rows
+// past the slice's length) in core-matrix order, then the block scales
+// [block][vector]; unit offsets from tc_slices_kernel.
+__global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict__ slice_start,
+                                                       const int32_t* __restrict__ slice_len,
+                                                       const int32_t* __restrict__ slice_unit,
+                                                       const int32_t* __restrict__ nslices,
+                                                       const int8_t* __restrict__ planes,
+                                                       const float* __restrict__ xsc,
+                                                       const int32_t* __restrict__ slot_vec, int nvec, int C,
+                                                       uint8_t* __restrict__ bimg, float* __restrict__ ximg) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int nchunks = C / (kTcKB * 32), nb = C / 32;
+  const int total = *nslices * nchunks;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int sl = w / nchunks, c = w % nchunks;
+    const int s0 = slice_start[sl], ns = slice_len[sl];
+    const int nv = ns > kTcUnit ? 2 * kTcUnit : kTcUnit, units = nv / kTcUnit;
+    const size_t uoff = static_cast<size_t>(slice_unit[sl]) * nchunks + static_cast<size_t>(c) * units;
+    uint8_t* bdst = bimg + uoff * kTcUnitBBytes;
+    for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
+      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
+      const int brow = 8 * (cm / kTcKch) + r, p = cm % kTcKch;
+      const int k = brow / nv, i = brow % nv;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (i < ns) {
+        int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
+        v = (v < 0 || v >= nvec) ? 0 : v;
+        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + p * 16);
+      }
+      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) = val;
+    }
+    float* xdst = ximg + uoff * kTcUnitXFloats;
+    for (int q = threadIdx.x; q < kTcKB * nv; q += blockDim.x) {
+      const int j = q / nv, i = q % nv;
+      float val = 0.0f;
+      if (i < ns) {
+        int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
+        v = (v < 0 || v >= nvec) ? 0 : v;
+        val = xsc[static_cast<size_t>(v) * nb + c * kTcKB + j];
+      }
+      xdst[q] = val;
+    }
+  }
 }
 
 // Operands of one launch of the grouped kernel.
@@ -247,9 +369,12 @@ struct TcArgs {
   const int32_t* slot_out;   // output row of each pair (null: the pair index)
   const int32_t* slice_start;
   const int32_t* slice_len;
+  const int32_t* slice_unit;
   const int32_t* nslices;
-  const int8_t* planes;      // digit planes [nvec][3][C]
-  const float* xsc;          // [nvec][C/32]
+  const uint8_t* bimg;       // slice images (tc_image_kernel)
+  const float* ximg;
+  CUtensorMap* gmaps;        // kTcStages global tensor-map slots per CTA
+  int box_rows;              // rows of the tensor map's box (min(128, R))
   int nvec;
   float* out;                // [out_rows][R]
   float* out2;               // for W2
@@ -260,7 +385,7 @@ struct TcArgs {
 struct TcItem {
   const uint8_t* w;
   float* dst;
-  int tile, s0, ns;
+  int tile, s0, ns, nv, unit;
 };
 
 __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int mats) {
@@ -270,59 +395,13 @@ __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int
   it.tile = rest % tiles;
   it.s0 = A.slice_start[sl];
   it.ns = min(max(A.slice_len[sl], 1), kTcNvp);
+  it.nv = it.ns > kTcUnit ? 2 * kTcUnit : kTcUnit;
+  it.unit = A.slice_unit[sl];
   int e = A.pe[it.s0];
   if (e < 0 || e >= A.num_experts) e = 0;  // flagged at the item's end
   it.w = mat ? A.W2[e] : A.W[e];
   it.dst = mat ? A.out2 : A.out;
   return it;
-}
-
-__device__ __forceinline__ int tc_vec(const TcArgs& A, int p) {
-  const int v = A.slot_vec ? A.slot_vec[p] : p;
-  return (v < 0 || v >= A.nvec) ? 0 : v;
-}
-
-// Producer (kTcProducerWarps warps, pt = thread index among them): stages
-// step `chunk` of item `it` in ring slot `st` by 16-byte cp.async -- the
-// tile's raw rows (nine pieces per row), the live vectors' digit-plane pieces
-// (rows k * kTcNvp + i of the B operand) and block scales -- and every
-// producer thread reports the completion of its copies on full[st].  Lane i
-// < ns of each producer warp holds vector i's plane row base (vrow) and block
-// scales (vxs) for this item; the other lanes fetch them by shuffle.
-__device__ __forceinline__ void tc_produce(TcSmem& sm, int st, const TcArgs& A, const TcItem& it, int chunk,
-                                          size_t row_bytes, const int8_t* vrow, const float* vxs, int pt) {
-  constexpr int kPieces = kTcRawRow / 16;
-  constexpr int kPT = 32 * kTcProducerWarps;
-  const int lane = pt & 31, pw = pt >> 5;
-  const int rows = min(kTcRows, A.R - it.tile * kTcRows);
-  const uint8_t* base = it.w + static_cast<size_t>(it.tile) * kTcRows * row_bytes + static_cast<size_t>(chunk) * kTcRawRow;
-  for (int t = pt; t < rows * kPieces; t += kPT) {
-    const int r = t / kPieces, p = t % kPieces;
-    cp_async16(sm.raw[st] + r * kTcRawRow + p * 16, base + static_cast<size_t>(r) * row_bytes + p * 16);
-  }
-  // plane pieces: warp pw takes pieces [pw * 32 + 32 * kTcProducerWarps * n) of ns * 48
-  const int nb_copies = it.ns * 3 * kTcKch;
-  for (int t0 = pw * 32; t0 < nb_copies; t0 += kPT) {
-    const int t = t0 + lane;
-    const int i = min(t / (3 * kTcKch), it.ns - 1), rem = t % (3 * kTcKch);
-    const int8_t* src = reinterpret_cast<const int8_t*>(
-        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(vrow), i));
-    if (t < nb_copies) {
-      const int k = rem / kTcKch, p = rem % kTcKch;
-      const int brow = k * kTcNvp + i;
-      cp_async16(sm.b[st] + ((brow >> 3) * kTcKch + p) * 128 + (brow & 7) * 16,
-                 src + static_cast<size_t>(k) * A.C + chunk * (kTcKB * 32) + p * 16);
-    }
-  }
-  const int nx = it.ns * kTcKB;
-  for (int t0 = pw * 32; t0 < nx; t0 += kPT) {
-    const int t = t0 + lane;
-    const int i = min(t / kTcKB, it.ns - 1), j = t % kTcKB;
-    const float* src = reinterpret_cast<const float*>(
-        __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(vxs), i));
-    if (t < nx) cp_async4(&sm.xs[st][j][i], src + chunk * kTcKB + j);
-  }
-  cp_async_mbar_arrive(&sm.full[st]);
 }
 
 // Unpack (four warps, thread = tile row): raw row of ring slot `st` -> signed
@@ -366,10 +445,11 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
 
 // The grouped contraction of Q4_0 matrices: out[slot_out[p]][r] = y[vector
 // slot_vec[p]][r] of expert pe[p]'s matrix for every pair p.  Needs C a
-// multiple of 256 (rows of whole 16-byte pieces per step).  Warp roles:
-// producer (0), MMA issuer (1), unpack (2-5), epilogue (6-13); every hand-off
-// is an mbarrier with a bounded wait.
-__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
+// multiple of 256 and the slice images of this launch.  `tmpl`: a 2-D tensor
+// map over one matrix (inner dimension C/32*18 bytes, R rows, box 144 x 128)
+// whose global address is replaced per expert.
+__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A,
+                                                                      const __grid_constant__ CUtensorMap tmpl) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>(tc_smem_raw);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -383,13 +463,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       mbar_init(&sm.a_full[i], kTcAFullCount);
       mbar_init(&sm.a_empty[i], kTcAEmptyCount);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTcSlots; ++i) {
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kTcTEmptyCount);
     }
     mbar_init(&sm.x_full, kTcXFullCount);
     mbar_init(&sm.x_empty, kTcXEmptyCount);
     fence_mbar_init();
+  }
+  if (tid < kTcStages * 8) {  // the tensor-map template into each stage's shared copy
+    const uint4* src = reinterpret_cast<const uint4*>(&tmpl);
+    reinterpret_cast<uint4*>(&sm.tmap[tid / 8])[tid % 8] = src[tid % 8];
   }
   if (warp == kTcMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
   __syncthreads();
@@ -398,7 +482,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int nb = A.C / 32, nchunks = nb / kTcKB;
-  const size_t row_bytes = static_cast<size_t>(nb) * 18;
   const int tiles = (A.R + kTcRows - 1) / kTcRows;
   const int mats = A.W2 ? 2 : 1;
   const int total = *A.nslices * tiles * mats;
@@ -406,39 +489,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
   const int nsteps = my_items * nchunks;
   auto item_at = [&](int s) { return tc_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
 
-  if (warp < kTcProducerWarps) {
+  if (warp == kTcProducerWarp) {
+    CUtensorMap* gmaps = A.gmaps + static_cast<size_t>(blockIdx.x) * kTcStages;
+    const uint8_t* map_addr[kTcStages] = {nullptr, nullptr, nullptr};
     TcItem it{};
-    const int8_t* vrow = A.planes;
-    const float* vxs = A.xsc;
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kTcStages, chunk = s % nchunks;
-      if (chunk == 0) {
-        it = item_at(s);
-        const int v = lane < it.ns ? tc_vec(A, it.s0 + lane) : 0;
-        vrow = A.planes + static_cast<size_t>(v) * 3 * A.C;
-        vxs = A.xsc + static_cast<size_t>(v) * nb;
+      if (chunk == 0) it = item_at(s);
+      bool ok = s < kTcStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err);
+      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+      // the stage's tensor map follows the item's matrix (its last copy has landed: the stage is empty)
+      const uint8_t* cur = st == 0 ? map_addr[0] : (st == 1 ? map_addr[1] : map_addr[2]);
+      if (cur != it.w) {
+        if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
+        __syncwarp();
+        tc_tmap_publish(&gmaps[st], &sm.tmap[st]);
+        if (lane == 0) tc_tmap_acquire(&gmaps[st]);
+        if (st == 0) map_addr[0] = it.w;
+        else if (st == 1) map_addr[1] = it.w;
+        else map_addr[2] = it.w;
       }
-      if (s >= kTcStages && !tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err)) break;
-      tc_produce(sm, st, A, it, chunk, row_bytes, vrow, vxs, tid);
+      if (lane == 0) {
+        const int units = it.nv / kTcUnit;
+        const uint32_t bbytes = units * kTcUnitBBytes, xbytes = units * kTcUnitXFloats * 4;
+        const size_t uoff = static_cast<size_t>(it.unit) * nchunks + static_cast<size_t>(chunk) * units;
+        mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kTcRawRow + bbytes + xbytes);
+        tc_tma_2d(sm.raw[st], &gmaps[st], chunk * kTcRawRow, it.tile * kTcRows, &sm.full[st]);
+        tc_bulk(sm.b[st], A.bimg + uoff * kTcUnitBBytes, bbytes, &sm.full[st]);
+        tc_bulk(sm.xs[st], A.ximg + uoff * kTcUnitXFloats, xbytes, &sm.full[st]);
+      }
+      __syncwarp();
     }
-    cp_async_wait_all();
   } else if (warp == kTcMmaWarp) {
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_s8s8(kTcRows, kTcNp);
+      uint32_t idesc = 0;
 #pragma unroll 1
       for (int s = 0; s < nsteps; ++s) {
         const int st = s % kTcStages, ab = s % kTcAbuf;
-        if (!tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
-            !tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err))
+        if (s % nchunks == 0) idesc = umma_idesc_s8s8(kTcRows, 3 * item_at(s).nv);
+        if (!tc_spin(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
+            !tc_spin(&sm.full[st], (s / kTcStages) & 1, A.err))
           break;
-        fence_async_shared();  // digit planes written by cp.async, read by the MMAs
+        fence_async_shared();  // codes written by the unpack threads, read by the MMAs
         tc_fence_after_sync();
         bool ok = true;
 #pragma unroll 1
         for (int g = 0; g < kTcKB / 2; ++g) {
-          const int G = (kTcKB / 2) * s + g, slot = G & 1;
-          if (G >= 2 && !tc_wait(&sm.t_empty[slot], ((G >> 1) - 1) & 1, A.err)) {
+          const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
+          if (G >= kTcSlots && !tc_spin(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err)) {
             ok = false;
             break;
           }
@@ -472,12 +571,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     }
   } else {
     const int ew = warp - kTcEpiWarp0;
-    const int quarter = warp & 3, half = ew >> 2;  // tensor-memory lanes 32*quarter..; blocks of parity `half`
+    const int quarter = warp & 3;            // tensor-memory lanes 32*quarter ..
+    const int half = (ew >> 2) & 1;          // blocks of this parity
+    const int vh = ew >> 3;                  // vectors 16*vh .. 16*vh+15
     const int trow = 32 * quarter + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
-    float acc[kTcNvp];
+    float acc[kTcUnit];
 #pragma unroll
-    for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kTcUnit; ++i) acc[i] = 0.0f;
     int items_done = 0;
     TcItem it{};
 #pragma unroll 1
@@ -485,12 +586,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       const int st = s % kTcStages, ab = s % kTcAbuf, chunk = s % nchunks;
       if (chunk == 0) it = item_at(s);
       const int nvg = (it.ns + 7) >> 3;
-      // block scales (cp.async) and row scales (unpack) of this step are read below
+      // block scales (bulk copy) and row scales (unpack) of this step are read below
       bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err) && tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err);
 #pragma unroll 1
       for (int g = 0; g < kTcKB / 2 && ok; ++g) {
-        const int G = (kTcKB / 2) * s + g, slot = G & 1;
-        if (!tc_wait(&sm.t_full[slot], (G >> 1) & 1, A.err)) {
+        const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
+        if (!tc_wait(&sm.t_full[slot], (G / kTcSlots) & 1, A.err)) {
           ok = false;
           break;
         }
@@ -498,21 +599,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
         const int j = 2 * g + half;
         const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + half * kTcBlockCols;
         const float dr = sm.d[ab][j][trow];
+        const float* xsj = &sm.xs[st][j * it.nv];
 #pragma unroll
-        for (int vg = 0; vg < kTcNvp / 8; ++vg) {
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int vg = 2 * vh + h2;
           if (vg < nvg) {
             uint32_t r0[8], r1[8], r2[8];
             tmem_ld8(taddr + 8 * vg, r0);
-            tmem_ld8(taddr + kTcNvp + 8 * vg, r1);
-            tmem_ld8(taddr + 2 * kTcNvp + 8 * vg, r2);
+            tmem_ld8(taddr + it.nv + 8 * vg, r1);
+            tmem_ld8(taddr + 2 * it.nv + 8 * vg, r2);
             tmem_wait_ld();
-            const float4 xa = *reinterpret_cast<const float4*>(&sm.xs[st][j][8 * vg]);
-            const float4 xb = *reinterpret_cast<const float4*>(&sm.xs[st][j][8 * vg + 4]);
+            const float4 xa = *reinterpret_cast<const float4*>(xsj + 8 * vg);
+            const float4 xb = *reinterpret_cast<const float4*>(xsj + 8 * vg + 4);
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
               const int S = static_cast<int>(r0[u]) + static_cast<int>(r1[u]) * 128 + static_cast<int>(r2[u]) * 16384;
-              acc[8 * vg + u] = fmaf(__int2float_rn(S), dr * xv[u], acc[8 * vg + u]);
+              acc[8 * h2 + u] = fmaf(__int2float_rn(S), dr * xv[u], acc[8 * h2 + u]);
             }
           }
         }
@@ -531,18 +634,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
         if (half == 1) {
           if (items_done > 0 && !tc_wait(&sm.x_empty, (items_done - 1) & 1, A.err)) break;
 #pragma unroll
-          for (int i = 0; i < kTcNvp; ++i) sm.xchg[i][trow] = acc[i];
+          for (int i = 0; i < kTcUnit; ++i) sm.xchg[kTcUnit * vh + i][trow] = acc[i];
           mbar_arrive(&sm.x_full);
         } else {
           if (!tc_wait(&sm.x_full, items_done & 1, A.err)) break;
           const int grow = it.tile * kTcRows + trow;
 #pragma unroll
-          for (int i = 0; i < kTcNvp; ++i) {
-            if (i < it.ns) {
-              const int p = it.s0 + i;
+          for (int i = 0; i < kTcUnit; ++i) {
+            const int vi = kTcUnit * vh + i;
+            if (vi < it.ns) {
+              const int p = it.s0 + vi;
               const int o = A.slot_out ? A.slot_out[p] : p;
               if (o >= 0 && o < A.out_rows && grow < A.R)
-                it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + sm.xchg[i][trow];
+                it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + sm.xchg[vi][trow];
             }
           }
           if (ew == 0 && lane < it.ns) {
@@ -557,7 +661,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
           if (lane == 0) mbar_arrive(&sm.x_empty);
         }
 #pragma unroll
-        for (int i = 0; i < kTcNvp; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < kTcUnit; ++i) acc[i] = 0.0f;
         ++items_done;
       }
     }
@@ -575,12 +679,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
 namespace {
 
 struct TcLayout {
-  size_t planes_x, xsc_x, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, nslices, total;
+  size_t planes_x, xsc_x, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit, nslices, bimg, ximg,
+      gmaps, total;
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
-TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I) {
+// Slice-image units (16 vectors) a pair list grouped by expert can need:
+// slices are runs cut at 32 pairs, so sum ceil(len / 16) <= P / 16 + slices
+// and slices <= P / 32 + runs, runs <= distinct experts.  (A list that is not
+// grouped may need more; the slices kernel then runs nothing and flags it.)
+size_t tc_max_units(size_t P, size_t E) { return 3 * P / 32 + std::min(P, E) + 2; }
+
+TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_count) {
   TcLayout L;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -588,6 +699,7 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I) {
     off += align256(bytes);
     return at;
   };
+  const size_t units = tc_max_units(P, E), nchunks = std::max(H, I) / (dev::kTcKB * 32);
   L.planes_x = take(T * 3 * H);
   L.xsc_x = take(T * (H / 32) * 4);
   L.g = take(P * I * 4);
@@ -597,7 +709,11 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I) {
   L.run_start = take(P * 4);
   L.slice_start = take(P * 4);
   L.slice_len = take(P * 4);
+  L.slice_unit = take(P * 4);
   L.nslices = take(4);
+  L.bimg = take(units * nchunks * dev::kTcUnitBBytes);
+  L.ximg = take(units * nchunks * dev::kTcUnitXFloats * 4);
+  L.gmaps = take(2 * static_cast<size_t>(sm_count) * dev::kTcStages * sizeof(CUtensorMap));
   L.total = off;
   return L;
 }
@@ -623,6 +739,31 @@ int validate_tc(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens) {
   return OBJB_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+int tc_encode_tiled(CUtensorMap* map, void* base, size_t row_bytes, size_t rows, int box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) return OBJB_FAIL(OBJB_ERR_DRIVER, "grouped Q4_0 MoE pairs", "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(dev::kTcRawRow), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return OBJB_FAIL(OBJB_ERR_DRIVER, "grouped Q4_0 MoE pairs", "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return OBJB_OK;
+}
+
 }  // namespace
 
 bool moe_pairs_tc_supported(const objb_moe_layer* l) {
@@ -632,15 +773,19 @@ bool moe_pairs_tc_supported(const objb_moe_layer* l) {
 
 int moe_pairs_tc_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out) {
   OBJB_TRY(validate_tc(l, num_pairs, num_tokens));
-  *out = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate).total;
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  *out = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate, l->num_experts, props.sm_count).total;
   return OBJB_OK;
 }
 
 // The multi-token pairs of moe_pairs for Q4_0 layers on the tensor cores:
-// digit planes of the T token vectors, the slices of the expert-sorted pair
-// list, gate and up of every pair in one grouped launch, SwiGLU straight
-// into the digit planes of the P activations, and down into v[pair_out[p]]
-// (or v[p]).
+// slices of the expert-sorted pair list, digit planes of the T token vectors
+// and their slice images, gate and up of every pair in one grouped launch,
+// SwiGLU straight into the digit planes of the P activations, their slice
+// images, and down into v[pair_out[p]] (or v[p]).
 int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, const int32_t* pt, const int32_t* po,
                  size_t num_tokens, const float* x, float* v, size_t v_rows, float limit, cudaStream_t stream,
                  void* scratch, size_t scratch_bytes, unsigned* err_word, const int32_t* d_count) {
@@ -649,14 +794,14 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
     return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "null device pointer");
   if (v_rows < (po ? 1 : num_pairs) || v_rows > (1u << 30))
     return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs", "v_rows cannot hold the pair outputs");
-  const TcLayout L = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate);
-  if (scratch_bytes < L.total)
-    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs",
-                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(L.total));
   int device = 0;
   OBJB_TRY(current_device(&device));
   DeviceProps props;
   OBJB_TRY(device_props(device, &props));
+  const TcLayout L = tc_layout(num_pairs, num_tokens, l->hidden, l->intermediate, l->num_experts, props.sm_count);
+  if (scratch_bytes < L.total)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "grouped Q4_0 MoE pairs",
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(L.total));
   unsigned* err = err_word;
   if (!err) OBJB_TRY(device_error_word(device, &err));
   uint8_t* sc = static_cast<uint8_t*>(scratch);
@@ -669,55 +814,75 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   int32_t* run_start = reinterpret_cast<int32_t*>(sc + L.run_start);
   int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
   int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
+  int32_t* slice_unit = reinterpret_cast<int32_t*>(sc + L.slice_unit);
   int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
+  uint8_t* bimg = sc + L.bimg;
+  float* ximg = reinterpret_cast<float*>(sc + L.ximg);
+  CUtensorMap* gmaps = reinterpret_cast<CUtensorMap*>(sc + L.gmaps);
   const int P = static_cast<int>(num_pairs), T = static_cast<int>(num_tokens);
   const int H = static_cast<int>(l->hidden), I = static_cast<int>(l->intermediate), O = static_cast<int>(l->out_dim);
   auto warp_grid = [&](int nvec, int C) {
     const long long warps = static_cast<long long>(nvec) * (C / 32);
     return static_cast<int>(std::max(1LL, std::min((warps * 32 + 255) / 256, 16LL * props.sm_count)));
   };
+  const size_t row_gu = static_cast<size_t>(H / 32) * 18, row_dn = static_cast<size_t>(I / 32) * 18;
+  CUtensorMap tm_gu, tm_dn;
+  OBJB_TRY(tc_encode_tiled(&tm_gu, scratch, row_gu, static_cast<size_t>(I), std::min(dev::kTcRows, I)));
+  OBJB_TRY(tc_encode_tiled(&tm_dn, scratch, row_dn, static_cast<size_t>(O), std::min(dev::kTcRows, O)));
   const size_t smem = sizeof(dev::TcSmem);
   OBJB_TRY(ensure_smem_attr(dev::tc_q4_grouped_kernel, device, smem));
+  const int img_grid = 2 * props.sm_count;
 
-  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, run_start,
-                      slice_start, slice_len, nslices));
+  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, run_start, slice_start, slice_len,
+                      slice_unit, nslices, static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
                       static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x));
+  OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
+                      static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
+                      static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_x),
+                      static_cast<const float*>(xsc_x), pt, T, H, bimg, ximg));
   dev::TcArgs a{};
   a.W = reinterpret_cast<const uint8_t* const*>(l->d_gate);
   a.W2 = reinterpret_cast<const uint8_t* const*>(l->d_up);
   a.num_experts = static_cast<int>(l->num_experts);
   a.R = I;
   a.C = H;
+  a.box_rows = std::min(dev::kTcRows, I);
   a.pe = pe;
   a.slot_vec = pt;
   a.slot_out = nullptr;
   a.slice_start = slice_start;
   a.slice_len = slice_len;
+  a.slice_unit = slice_unit;
   a.nslices = nslices;
-  a.planes = planes_x;
-  a.xsc = xsc_x;
+  a.bimg = bimg;
+  a.ximg = ximg;
+  a.gmaps = gmaps;
   a.nvec = T;
   a.out = g;
   a.out2 = u;
   a.out_rows = P;
   a.err = err;
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_gu));
   OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, static_cast<const float*>(g),
                       static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a));
+  OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
+                      static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
+                      static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_a),
+                      static_cast<const float*>(xsc_a), static_cast<const int32_t*>(nullptr), P, I, bimg, ximg));
   a.W = reinterpret_cast<const uint8_t* const*>(l->d_down);
   a.W2 = nullptr;
   a.R = O;
   a.C = I;
+  a.box_rows = std::min(dev::kTcRows, O);
   a.slot_vec = nullptr;
   a.slot_out = po;
-  a.planes = planes_a;
-  a.xsc = xsc_a;
   a.nvec = P;
   a.out = v;
   a.out2 = nullptr;
   a.out_rows = static_cast<int>(v_rows);
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  a.gmaps = gmaps + static_cast<size_t>(props.sm_count) * dev::kTcStages;
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_dn));
   return OBJB_OK;
 }
 

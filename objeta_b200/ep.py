@@ -156,6 +156,20 @@ def moe_pairs_tc(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu
     return d_v
 
 
+# Token slots (tokens x top_k per rank) from which ExpertParallelMoe's
+# "auto" mode takes the grouped tensor-core path: below this the CUDA-core
+# pair programs, which stream each pair's experts straight from HBM, are
+# faster (measured on B200 at hidden 2048 / intermediate 512, top-8).
+GROUPED_MIN_SLOTS = 256
+
+
+def grouped_supported(layer) -> bool:
+    """The grouped tensor-core pairs path takes Q4_0 layers (16-byte aligned
+    experts) whose hidden and intermediate sizes are multiples of 256."""
+    return (int(layer.fmt) == 0 and layer._tensors[3] is None and (layer._c.flags & 1) == 0
+            and layer.hidden % 256 == 0 and layer.intermediate % 256 == 0)
+
+
 def moe_pairs_scratch_bytes(layer, num_pairs: int, num_tokens: int) -> int:
     n = c_size()
     _lib.call("objb_moe_pairs_scratch_bytes", ctypes.byref(layer._c), num_pairs, num_tokens, ctypes.byref(n))
@@ -277,7 +291,7 @@ class ExpertParallelMoe:
     Paths:
 
     * one rank (default compute): on the device, bit-identical to the
-      single-token launch;
+      single-token launch on the CUDA-core pair programs;
     * several ranks, ``exchange="device"`` (default compute): no host round
       trip -- all-gathers of the routing table, weights and token rows, the
       pair list built on the device, pair launches with a device-side count,
@@ -288,11 +302,19 @@ class ExpertParallelMoe:
     * ``exchange="host"`` or ``plan_on_host=True`` (and any injected compute):
       the routing table goes to the host, a ``DispatchPlan`` sends only the
       needed token rows and pair outputs, and the owner combines in slot
-      order -- bit-identical for any rank count."""
+      order -- bit-identical for any rank count.
+
+    ``grouped``: "auto" (default) runs the pairs on the grouped tensor-core
+    path (``moe_pairs_tc``) when the layer supports it and this rank's token
+    slots T * k reach ``GROUPED_MIN_SLOTS``; "on" always (the layer must
+    support it), "off" never.  Its rows are within the reference tolerance of
+    the CUDA-core ones and, like them, depend only on (expert, token row), so
+    the choice -- made from T * k, not from the rank count -- keeps results
+    independent of the number of ranks."""
 
     def __init__(self, layer, num_experts: int, top_k: int, rank: int = 0, world: int = 1, group=None,
                  out_dim: int | None = None, compute=None, combine=None, swiglu_limit: float = 0.0,
-                 plan_on_host: bool = False, exchange: str = "device"):
+                 plan_on_host: bool = False, exchange: str = "device", grouped: str = "auto"):
         self.layer = layer
         self.num_experts = int(num_experts)
         self.top_k = int(top_k)
@@ -305,6 +327,11 @@ class ExpertParallelMoe:
         if exchange not in ("device", "host"):
             raise ValueError(f"exchange must be 'device' or 'host', not {exchange!r}")
         self._device_exchange = self._device_only and exchange == "device"
+        if grouped not in ("auto", "on", "off"):
+            raise ValueError(f"grouped must be 'auto', 'on' or 'off', not {grouped!r}")
+        if grouped == "on" and (layer is None or not grouped_supported(layer)):
+            raise ValueError("grouped='on' needs a Q4_0 layer with hidden, intermediate multiples of 256")
+        self.grouped = grouped
         self.last_plan = None
         self._pin = None     # pinned int32 staging for plan arrays (grow-only)
         self._dmeta = None   # device copy (grow-only)
@@ -332,6 +359,14 @@ class ExpertParallelMoe:
             off += a.size
         return views
 
+    def _pairs_fn(self, slots: int):
+        """moe_pairs or moe_pairs_tc for a step with `slots` = T * k token slots."""
+        if self.grouped == "on":
+            return moe_pairs_tc
+        if self.grouped == "auto" and slots >= GROUPED_MIN_SLOTS and grouped_supported(self.layer):
+            return moe_pairs_tc
+        return moe_pairs
+
     # ---- default (CUDA) compute and combine
     def _cuda_compute(self, plan: DispatchPlan, x_recv, n_rows: int):
         import torch
@@ -341,8 +376,8 @@ class ExpertParallelMoe:
             return v
         pe, pt, po, slot = self._stage([plan.pair_expert, plan.pair_token, plan.pair_out, plan.slot_row], dev)
         self._staged_slot = slot
-        moe_pairs(self.layer, pe, pt, x_recv, v, pair_out=po, swiglu_limit=self.swiglu_limit,
-                  stream=torch.cuda.current_stream(dev))
+        self._pairs_fn(plan.slot_row.size)(self.layer, pe, pt, x_recv, v, pair_out=po,
+                                           swiglu_limit=self.swiglu_limit, stream=torch.cuda.current_stream(dev))
         return v
 
     def _cuda_combine(self, v_recv, plan: DispatchPlan, w):
@@ -373,8 +408,8 @@ class ExpertParallelMoe:
         pair_token = torch.div(perm, K, rounding_mode="floor").to(torch.int32)
         stream = torch.cuda.current_stream(x.device)
         v = torch.empty(T * K, self.out_dim, dtype=torch.float32, device=x.device)
-        moe_pairs(self.layer, pair_expert, pair_token, x.contiguous(), v, pair_out=perm,
-                  swiglu_limit=self.swiglu_limit, stream=stream)
+        self._pairs_fn(T * K)(self.layer, pair_expert, pair_token, x.contiguous(), v, pair_out=perm,
+                              swiglu_limit=self.swiglu_limit, stream=stream)
         out = torch.empty(T, self.out_dim, dtype=torch.float32, device=x.device)
         return moe_combine(v, slot, w.contiguous(), out, stream=stream)
 
@@ -393,8 +428,8 @@ class ExpertParallelMoe:
         dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
         pe, pt, po, cnt = ep_build_pairs(ids_all, self.rank, self.num_experts, stream=stream)
         v = torch.empty(G * T * K, self.out_dim, dtype=torch.float32, device=dev)
-        moe_pairs(self.layer, pe, pt, x_all, v, pair_out=po, swiglu_limit=self.swiglu_limit, stream=stream,
-                  d_count=cnt)
+        self._pairs_fn(T * K)(self.layer, pe, pt, x_all, v, pair_out=po, swiglu_limit=self.swiglu_limit,
+                              stream=stream, d_count=cnt)
         part = ep_partial_combine(ids_all, w_all, v, self.rank, self.num_experts, self.out_dim, stream=stream)
         recv = torch.empty_like(part)
         dist.all_to_all_single(recv, part, group=self.group)

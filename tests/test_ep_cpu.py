@@ -205,3 +205,31 @@ def test_two_gloo_ranks_match_single_rank_and_reference():
             ref = O.selected_moe_q4(experts, list(zip(ids[t].tolist(), ws[t].tolist())), x[t], H, I, OUT)
             assert np.array_equal(out[t].view(np.uint32), ref.view(np.uint32)), f"rank {r} token {t}"
         assert xb["dispatch"] > 0 or xb["combine"] >= 0
+
+
+def test_grouped_path_selection():
+    """"auto" takes the tensor-core pairs path from GROUPED_MIN_SLOTS token
+    slots on supported layers only; "on" insists on support; the choice
+    depends on T * k, not on the rank count."""
+    from types import SimpleNamespace
+    from objeta_b200 import ep as E
+
+    def layer(fmt=0, H=2048, I=512, flags=0, split=False):
+        return SimpleNamespace(fmt=fmt, hidden=H, intermediate=I, out_dim=H, _c=SimpleNamespace(flags=flags),
+                               _tensors=[None, None, None, object() if split else None, None, None])
+
+    ok = layer()
+    m = E.ExpertParallelMoe(ok, 256, 8)
+    assert m._pairs_fn(E.GROUPED_MIN_SLOTS - 1) is E.moe_pairs
+    assert m._pairs_fn(E.GROUPED_MIN_SLOTS) is E.moe_pairs_tc
+    m2 = E.ExpertParallelMoe(ok, 256, 8, rank=1, world=2)
+    assert m2._pairs_fn(E.GROUPED_MIN_SLOTS) is E.moe_pairs_tc
+    assert E.ExpertParallelMoe(ok, 256, 8, grouped="off")._pairs_fn(10 ** 6) is E.moe_pairs
+    assert E.ExpertParallelMoe(ok, 256, 8, grouped="on")._pairs_fn(1) is E.moe_pairs_tc
+    for bad in (layer(fmt=1), layer(I=800), layer(flags=1), layer(fmt=3, split=True)):
+        assert not E.grouped_supported(bad)
+        assert E.ExpertParallelMoe(bad, 256, 8)._pairs_fn(10 ** 6) is E.moe_pairs
+        with pytest.raises(ValueError):
+            E.ExpertParallelMoe(bad, 256, 8, grouped="on")
+    with pytest.raises(ValueError):
+        E.ExpertParallelMoe(ok, 256, 8, grouped="yes")

@@ -173,3 +173,51 @@ def test_tc_pairs_rejects_unstaged_widths(cuda_device):
     with pytest.raises(CudaError):
         moe_pairs_tc(layer, torch.zeros(1, dtype=torch.int32, device="cuda"),
                      torch.zeros(1, dtype=torch.int32, device="cuda"), x, v)
+
+
+def test_tc_pairs_ungrouped_list_is_flagged(cuda_device):
+    """A pair list that is not grouped by expert can need more slice-image
+    space than the launch reserves: nothing runs, the device error word is
+    flagged, and the output rows are left as they were."""
+    import torch
+    from objeta_b200.ep import moe_pairs_tc
+    from objeta_b200.quant import device_error_take
+    E, H, I, OUT, P = 2, 256, 256, 256, 96
+    layer, _ = _q4_layer(O.Q4_0, E, H, I, OUT, seed=6)
+    device_error_take(cuda_device)
+    x = torch.randn(P, H, device="cuda")
+    v = torch.full((P, OUT), 3.0, device="cuda")
+    pe = (torch.arange(P, dtype=torch.int32, device="cuda") % 2).contiguous()
+    pt = torch.arange(P, dtype=torch.int32, device="cuda")
+    moe_pairs_tc(layer, pe, pt, x, v)
+    torch.cuda.synchronize()
+    assert device_error_take(cuda_device) & 8
+    assert bool((v == 3.0).all())
+
+
+def test_ep_grouped_matches_fused_and_plans(cuda_device):
+    """ExpertParallelMoe at T * k >= GROUPED_MIN_SLOTS runs the grouped path:
+    within the MoE bound of the fused single-token path (both against the
+    oracle), and bit-identical between the device-sorted pair list and the
+    host dispatch plan (rows depend only on (expert, token))."""
+    import torch
+    from objeta_b200.ep import GROUPED_MIN_SLOTS, ExpertParallelMoe
+    E, H, I, OUT, K, T = 16, 1024, 512, 1024, 8, 40
+    assert T * K >= GROUPED_MIN_SLOTS
+    layer, mats = _q4_layer(O.Q4_0, E, H, I, OUT, seed=77)
+    ids, ws = _zipf_routes(T, E, K, seed=21)
+    xs = np.random.default_rng(4).standard_normal((T, H)).astype(np.float32)
+    x, di, dw = torch.from_numpy(xs).cuda(), torch.from_numpy(ids).cuda(), torch.from_numpy(ws).cuda()
+    a = ExpertParallelMoe(layer, E, K).forward(x, di, dw)
+    b = ExpertParallelMoe(layer, E, K, plan_on_host=True).forward(x, di, dw)
+    c = ExpertParallelMoe(layer, E, K, grouped="off").forward(x, di, dw)
+    torch.cuda.synchronize()
+    assert _bits_equal(a, b)
+    assert not _bits_equal(a, c)  # the grouped path really ran
+    host = [(mats["gate"][e].cpu().numpy(), mats["up"][e].cpu().numpy(), mats["down"][e].cpu().numpy())
+            for e in range(E)]
+    got, ref_c = a.cpu().numpy(), c.cpu().numpy()
+    for t in range(0, T, 8):
+        sel = list(zip(ids[t].tolist(), ws[t].tolist()))
+        bound = moe_bound(q4_matrices(host, H, I, OUT), sel, xs[t], H, I, OUT)
+        assert np.all(np.abs(got[t].astype(np.float64) - ref_c[t]) <= 2 * bound)
