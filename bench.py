@@ -3,10 +3,15 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --case q4_0:151936x2048 [--steps K] [--warmup W]
+    python bench.py --grouped 256 [--steps K] [--warmup W]
 
 `--case` runs one GEMV of the sweep alone (W + K plain launches, rotating
 over its weight copies, no graph) and prints its mean launch time; it is the
-command the ncu captures are taken on.
+command the ncu captures are taken on.  `--grouped T` runs the configs[4]
+layer's (expert, token) pairs for T tokens (Zipf(1.1) top-8 of 256 Q4_0
+experts, H 2048, I 512) on the grouped tensor-core path and on the CUDA-core
+pair programs, W + K calls each, and prints both mean call times; it is the
+command the grouped kernel's ncu captures are taken on.
 
 Workload: the block-quant GEMV format/shape sweep,
 Q4_0, Q5_0 and IQ3_0 at rows x cols in {4096x4096, 14336x4096, 4096x14336,
@@ -805,6 +810,51 @@ def run_case(args, local):
             "GB/s": round(algo_bytes(fmt, rows, cols) / us / 1e3, 1), "copies": len(copies)}
 
 
+def run_grouped(args, local):
+    """configs[4] pairs for T tokens: the grouped tensor-core path
+    (moe_pairs_tc) and the CUDA-core pair programs (moe_pairs), W + K calls
+    each on one stream, timed with CUDA events."""
+    import torch
+    from objeta_b200 import QuantBackend
+    from objeta_b200.ep import moe_pairs, moe_pairs_tc
+    from objeta_b200.moe import MoeLayer
+    T = int(args.grouped)
+    c = C5
+    H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    qb = QuantBackend(local)
+    gen = torch.Generator(device=dev).manual_seed(4242)
+    m = _q4_experts(qb, E, H, I, H, gen, dev)
+    layer = MoeLayer(0, H, I, H, m["gate"], m["up"], m["down"])
+    rng = np.random.default_rng(1000 * T)
+    ids, _ = zipf_routes(T, E, K, c["zipf"], np.random.default_rng(7).permutation(E), rng)
+    flat = ids.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    pe = torch.from_numpy(flat[order].astype(np.int32)).to(dev)
+    pt = torch.from_numpy((order // K).astype(np.int32)).to(dev)
+    po = torch.from_numpy(order.astype(np.int32)).to(dev)
+    x = torch.randn(T, H, device=dev, generator=gen)
+    v = torch.empty(T * K, H, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    res = {"grouped_tokens": T, "pairs": T * K, "distinct_experts": int(len(np.unique(flat))),
+           "unique_expert_bytes": int(len(np.unique(flat)) * Q4_EXPERT_BYTES(H, I))}
+    for name, fn in (("tc", moe_pairs_tc), ("cuda_core", moe_pairs)):
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                fn(layer, pe, pt, x, v, pair_out=po, stream=stream)
+            torch.cuda.synchronize()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for _ in range(args.steps):
+                fn(layer, pe, pt, x, v, pair_out=po, stream=stream)
+            t1.record(stream)
+        torch.cuda.synchronize()
+        res[f"us_{name}"] = round(t0.elapsed_time(t1) * 1e3 / args.steps, 1)
+    return res
+
+
 def main():
     # NCCL's own log lines (e.g. its version banner when NCCL_DEBUG is set)
     # go to stderr, so stdout carries only the result line.
@@ -816,6 +866,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="fmt:RxC, e.g. q4_0:151936x2048 (one GEMV alone)")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE configs reported beside the headline")
+    ap.add_argument("--grouped", type=int, default=None,
+                    help="T: the configs[4] pairs of T tokens on the grouped tensor-core path and the CUDA-core path")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
@@ -823,6 +875,9 @@ def main():
     world, rank, local = dist_env()
     if args.case:
         print(json.dumps(run_case(args, local)), flush=True)
+        return
+    if args.grouped:
+        print(json.dumps(run_grouped(args, local)), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, world, rank)

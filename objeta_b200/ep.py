@@ -397,6 +397,14 @@ class ExpertParallelMoe:
         reads in slot order."""
         import torch
         T, K = ids.shape
+        if T == 1:
+            # one token: the fused single-token launch (the pairs' rows are
+            # bit-identical to it), without the sort and the separate combine
+            out = torch.empty(1, self.out_dim, dtype=torch.float32, device=x.device)
+            self.layer.forward_selected(ids[0].to(torch.int32).contiguous(), w[0].contiguous(), x[0].contiguous(),
+                                        d_out=out[0], swiglu_limit=self.swiglu_limit,
+                                        stream=torch.cuda.current_stream(x.device))
+            return out
         flat = ids.reshape(-1).to(torch.int32)
         key = (T, K, x.device)
         if key not in self._slot_cache:

@@ -195,6 +195,10 @@ def test_ep_single_rank_matches_fused(cuda_device):
             got = ep.forward(x, di, dw)
             torch.cuda.synchronize()
             assert _bits_equal(got, ref)
+        # one token: the fused single-token launch on the device-only path
+        got1 = ep.forward(x[2:3].contiguous(), di[2:3].contiguous(), dw[2:3].contiguous())
+        torch.cuda.synchronize()
+        assert got1.shape == (1, OUT) and _bits_equal(got1[0], ref[2])
 
 
 # ------------------------------------------------------------ two ranks
