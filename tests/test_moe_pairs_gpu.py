@@ -202,7 +202,7 @@ def test_ep_single_rank_matches_fused(cuda_device):
 
 
 # ------------------------------------------------------------ two ranks
-def _ep_rank(rank, world, port, q):
+def _ep_rank(rank, world, port, q, grouped="auto", T=6, K=4):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -215,7 +215,7 @@ def _ep_rank(rank, world, port, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        E, H, I, OUT, K, T = 16, 1024, 512, 1024, 4, 6
+        E, H, I, OUT = 16, 1024, 512, 1024
         full, mats = _q4_layer(O.Q4_0, E, H, I, OUT, seed=61)   # same seed: same experts on every rank
         epr = E // world
         sl = slice(rank * epr, (rank + 1) * epr)
@@ -223,19 +223,22 @@ def _ep_rank(rank, world, port, q):
         ids, ws = _routes(T, E, K, seed=70 + rank)
         x = torch.from_numpy(np.random.default_rng(90 + rank).standard_normal((T, H)).astype(np.float32)).cuda()
         di, dw = torch.from_numpy(ids).cuda(), torch.from_numpy(ws).cuda()
-        ref = _fused_per_token(full, x, di, dw)
+        if grouped == "on":   # one GPU on the grouped path, all experts local
+            ref = ExpertParallelMoe(full, E, K, grouped="on").forward(x, di, dw)
+        else:
+            ref = _fused_per_token(full, x, di, dw)
         # host plan: bit-identical to one GPU
-        ep = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="host")
+        ep = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="host", grouped=grouped)
         ok = _bits_equal(ep.forward(x, di, dw), ref)
         # device exchange: deterministic, within the MoE bound of one GPU
-        epd = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="device")
+        epd = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="device", grouped=grouped)
         g1, g2 = epd.forward(x, di, dw), epd.forward(x, di, dw)
         torch.cuda.synchronize()
         ok = ok and _bits_equal(g1, g2)
         host = [(mats["gate"][e].cpu().numpy(), mats["up"][e].cpu().numpy(), mats["down"][e].cpu().numpy())
                 for e in range(E)]
         xh, r1 = x.cpu().numpy(), ref.cpu().numpy()
-        for t in range(T):
+        for t in range(min(T, 6)):
             sel = list(zip(ids[t].tolist(), ws[t].tolist()))
             bound = moe_bound(q4_matrices(host, H, I, OUT), sel, xh[t], H, I, OUT)
             ok = ok and bool(np.all(np.abs(g1[t].cpu().numpy().astype(np.float64) - r1[t]) <= 2 * bound))
@@ -246,7 +249,11 @@ def _ep_rank(rank, world, port, q):
         q.put((rank, False, repr(exc)))
 
 
-def test_ep_two_ranks_bit_identical_to_single_gpu():
+@pytest.mark.parametrize("grouped", ["auto", "on"])
+def test_ep_two_ranks_bit_identical_to_single_gpu(grouped):
+    """Two NCCL ranks; with grouped="on" every rank runs the tensor-core pair
+    kernel and the host-plan result must equal one GPU's grouped result bit
+    for bit (grouped rows depend only on (expert, token))."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -257,7 +264,8 @@ def test_ep_two_ranks_bit_identical_to_single_gpu():
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    T, K = (40, 8) if grouped == "on" else (6, 4)
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q, grouped, T, K)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
