@@ -320,6 +320,30 @@ int objb_moe_pairs_tc_device(const objb_moe_layer *layer, size_t num_pairs,
                              size_t num_tokens, const float *d_x, float *d_v, size_t v_rows,
                              float swiglu_limit, objb_stream_t stream);
 
+/* The routed experts of execute_selected_moe_official_routed_fp4_cuda
+ * (moe.rs:1393-1548) over (expert, token) pairs on block-scaled tensor cores
+ * (no reference counterpart for many tokens; the reference runs one token
+ * per call).  Same pair arguments as objb_moe_pairs_device; the layer is a
+ * split FP4 E2M1 layer with its E8M0 scale tables, d_x [num_tokens][hidden]
+ * f32.  Per pair: act_quant(x) -> FP8 x FP4 gate and up ->
+ * SwiGLU with only the up value clamped to +-swiglu_limit (deepseek.rs:
+ * 1707-1711) -> act_quant -> FP8 x FP4 down into row d_pair_out[p] of d_v
+ * (unweighted; combine with objb_moe_combine_device).  The FP8 x FP4 dots
+ * run as tcgen05.mma.kind::mxf8f6f4.block_scale: E2M1 weights and E4M3
+ * activations with their UE8M0 block scales multiplied exactly and summed in
+ * f32 by the tensor core, so rows match the CUDA-core official path within
+ * the f32 tolerance (and the re-quantized activation may move by one FP8
+ * step, as between any two orders of summation).  Pairs must be grouped by
+ * expert; up to 128 pairs of an expert share one pass over a weight tile.
+ * hidden and intermediate: multiples of 128. */
+int objb_moe_pairs_official_tc_scratch_bytes(const objb_moe_layer *layer, size_t num_pairs,
+                                             size_t num_tokens, size_t *bytes);
+int objb_moe_pairs_official_tc_device(const objb_moe_layer *layer, size_t num_pairs,
+                                      const int32_t *d_num_pairs, const int32_t *d_pair_expert,
+                                      const int32_t *d_pair_token, const int32_t *d_pair_out,
+                                      size_t num_tokens, const float *d_x, float *d_v,
+                                      size_t v_rows, float swiglu_limit, objb_stream_t stream);
+
 /* The weighted top-k combine (moe.rs:1319-1321) for num_tokens tokens:
  * d_out[t][i] = sum over j = 0..top_k-1, in slot order, of
  * d_weights[t][j] * d_v[d_slot_row[t][j]][i], starting from 0 -- the exact

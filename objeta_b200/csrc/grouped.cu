@@ -43,6 +43,7 @@
 #include "objb_host_launch.cuh"
 #include "objb_launch.h"
 #include "objb_moe.cuh"
+#include "objb_official_launch.h"
 #include "objb_tc.cuh"
 
 namespace objb {
@@ -256,7 +257,7 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp
 }
 
 __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restrict__ pe, int P, const int32_t* count,
-                                                         int32_t* __restrict__ run_start,
+                                                         int nvp, int unit, int32_t* __restrict__ run_start,
                                                          int32_t* __restrict__ slice_start,
                                                          int32_t* __restrict__ slice_len,
                                                          int32_t* __restrict__ slice_unit,
@@ -284,9 +285,9 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
   int lunits = 0;
   for (int r = a; r < b; ++r) {
     const int s0 = run_start[r], s1 = r + 1 < nruns ? run_start[r + 1] : P;
-    for (int q = s0; q < s1; q += kTcNvp) {
+    for (int q = s0; q < s1; q += nvp) {
       ++local;
-      lunits += (min(kTcNvp, s1 - q) + kTcUnit - 1) / kTcUnit;
+      lunits += (min(nvp, s1 - q) + unit - 1) / unit;
     }
   }
   int total = 0, total_units = 0;
@@ -294,12 +295,12 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
   int upos = block_exclusive_scan(lunits, &total_units, warp_tot);
   for (int r = a; r < b; ++r) {
     const int s0 = run_start[r], s1 = r + 1 < nruns ? run_start[r + 1] : P;
-    for (int q = s0; q < s1; q += kTcNvp) {
-      const int len = min(kTcNvp, s1 - q);
+    for (int q = s0; q < s1; q += nvp) {
+      const int len = min(nvp, s1 - q);
       slice_start[pos] = q;
       slice_len[pos] = len;
       slice_unit[pos] = upos;
-      upos += (len + kTcUnit - 1) / kTcUnit;
+      upos += (len + unit - 1) / unit;
       ++pos;
     }
   }
@@ -674,6 +675,352 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
   }
 }
 
+
+// ======================================================================
+// The official DeepSeek FP8 x FP4 contraction on block-scaled MMAs.
+// Weights are split FP4 E2M1 [R][C/2] with E8M0 scales per 32 columns;
+// activations are act_quant output: E4M3 codes [nvec][C] with E8M0 scales per
+// 128 columns.  tcgen05.mma.kind::mxf8f6f4.block_scale multiplies them
+// directly: A = the weight tile (E2M1; under this kind a 16-value group sits
+// in 16 bytes of shared memory: 8 packed bytes, then 8 bytes of padding),
+// B = the slice's activation codes (E4M3), the UE8M0 scale factors of both
+// in tensor memory (CUTLASS's K-major scale atom: 128 rows x 4 blocks in 512
+// bytes, row m = m0 + 32 m1 at byte m0 * 16 + m1 * 4 + block, copied with
+// tcgen05.cp 32x128b.warpx4).  The products are exact and the f32 sum of a
+// whole row stays in tensor memory: one epilogue per work item, none per
+// block.  Work item = (slice of up to 128 pairs of one expert, 128-row tile);
+// a step is 128 columns (4 MMAs, one scale atom).
+constexpr int kMxKB = 4;                           // 32-column blocks per step
+constexpr int kMxStepCols = kMxKB * 32;            // 128
+constexpr int kMxNvp = 128;                        // pairs per slice (at most)
+constexpr int kMxRawRow = kMxStepCols / 2;         // packed FP4 bytes of one row per step
+constexpr int kMxKch = kMxStepCols / 16;           // 16-byte K columns of a staged operand
+constexpr int kMxStages = 3, kMxAbuf = 2, kMxDslots = 2;
+constexpr int kMxUnitBBytes = kTcUnit * kMxStepCols;  // 16 activation rows of one step
+constexpr int kMxSfAtom = 512;
+constexpr int kMxDCols = 128;                      // tensor-memory columns of one accumulator slot
+constexpr int kMxSfaCol = 256, kMxSfbCol = 272;    // scale-factor columns (4 per buffer)
+constexpr int kMxProducerWarp = 0, kMxMmaWarp = 1, kMxUnpackWarp0 = 2, kMxEpiWarp0 = 6, kMxEpiWarps = 4;
+constexpr int kMxThreads = 32 * (kMxEpiWarp0 + kMxEpiWarps);
+
+struct MxSmem {
+  alignas(1024) uint8_t a[kMxAbuf][kTcRows * kMxStepCols];
+  alignas(1024) uint8_t b[kMxStages][kMxNvp * kMxStepCols];
+  alignas(128) uint8_t raw[kMxStages][kTcRows * kMxRawRow];
+  alignas(128) uint8_t sfa[kMxAbuf][kMxSfAtom];
+  alignas(128) uint8_t sfb[kMxStages][kMxSfAtom];
+  alignas(128) CUtensorMap tmap[kMxStages];
+  alignas(8) uint64_t full[kMxStages], empty[kMxStages], a_full[kMxAbuf], a_empty[kMxAbuf];
+  uint64_t d_full[kMxDslots], d_empty[kMxDslots];
+  uint32_t tmem_base;
+};
+static_assert(sizeof(MxSmem) <= 227 * 1024, "block-scaled kernel shared memory");
+static_assert(kMxDslots * kMxDCols <= kMxSfaCol && kMxSfbCol + 4 * kMxStages <= 512, "tensor-memory columns");
+
+// Block-scaled instruction descriptor: A E2M1, B E4M3, UE8M0 scales, M 128,
+// K 32; scale-factor byte `kb` of both operands.
+__device__ __forceinline__ uint32_t mx_idesc(int n, int kb) {
+  return (static_cast<uint32_t>(kb) << 4) | (5u << 7) | (0u << 10) | ((static_cast<uint32_t>(n) >> 3) << 17) |
+         (1u << 23) | ((static_cast<uint32_t>(kTcRows) >> 4) << 24) | (static_cast<uint32_t>(kb) << 29);
+}
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t sfa_tmem, uint32_t sfb_tmem, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u), "r"(sfa_tmem), "r"(sfb_tmem));
+}
+// 32 rows x 16 bytes of shared memory -> 4 tensor-memory columns of every lane quarter.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, const void* smem_atom) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr),
+               "l"(umma_desc_kmajor(smem_addr(smem_atom), 128, 128)));
+}
+
+// Slice images of the block-scaled path: for slice sl, step c, the B rows i
+// (activation codes of the slice's vector i; zero past the slice's length)
+// in core-matrix order, nv = 16 * ceil(len / 16) rows, and the B scale atom
+// (vector i's E8M0 scale of the step's 128 columns in all four blocks).
+__global__ void __launch_bounds__(256) mx_image_kernel(const int32_t* __restrict__ slice_start,
+                                                       const int32_t* __restrict__ slice_len,
+                                                       const int32_t* __restrict__ slice_unit,
+                                                       const int32_t* __restrict__ nslices,
+                                                       const uint8_t* __restrict__ codes,
+                                                       const uint8_t* __restrict__ scales,
+                                                       const int32_t* __restrict__ slot_vec, int nvec, int C,
+                                                       uint8_t* __restrict__ bimg, uint8_t* __restrict__ sfimg) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int nchunks = C / kMxStepCols;
+  const int total = *nslices * nchunks;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    const int sl = w / nchunks, c = w % nchunks;
+    const int s0 = slice_start[sl], ns = min(slice_len[sl], kMxNvp);
+    const int units = (ns + kTcUnit - 1) / kTcUnit, nv = units * kTcUnit;
+    uint8_t* bdst = bimg + (static_cast<size_t>(slice_unit[sl]) * nchunks + static_cast<size_t>(c) * units) * kMxUnitBBytes;
+    for (int q = threadIdx.x; q < nv * kMxKch; q += blockDim.x) {
+      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
+      const int row = 8 * (cm / kMxKch) + r, p = cm % kMxKch;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (row < ns) {
+        int v = slot_vec ? slot_vec[s0 + row] : s0 + row;
+        v = (v < 0 || v >= nvec) ? 0 : v;
+        val = *reinterpret_cast<const uint4*>(codes + static_cast<size_t>(v) * C + c * kMxStepCols + p * 16);
+      }
+      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) = val;
+    }
+    uint32_t* sdst = reinterpret_cast<uint32_t*>(sfimg + (static_cast<size_t>(sl) * nchunks + c) * kMxSfAtom);
+    for (int q = threadIdx.x; q < kMxSfAtom / 4; q += blockDim.x) {
+      // word q = row (q / 4) % 32 + 32 * (q % 4), all four blocks
+      const int row = (q >> 2) + 32 * (q & 3);
+      uint32_t val = 0u;
+      if (row < ns) {
+        int v = slot_vec ? slot_vec[s0 + row] : s0 + row;
+        v = (v < 0 || v >= nvec) ? 0 : v;
+        val = static_cast<uint32_t>(scales[static_cast<size_t>(v) * (C / 128) + c]) * 0x01010101u;
+      }
+      sdst[q] = val;
+    }
+  }
+}
+
+// SwiGLU of the official path (only the up value clamped, deepseek.rs:1707-1711)
+// over the pairs' gate / up rows, in place into the gate rows.
+__global__ void __launch_bounds__(256) mx_swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, size_t n,
+                                                        const int32_t* count, int I, float limit) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) n = min(n, static_cast<size_t>(max(*count, 0)) * I);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    g[i] = swiglu(g[i], u[i], limit, false);
+}
+
+struct MxArgs {
+  const uint8_t* const* W;    // packed E2M1 weights [R][C/2]
+  const uint8_t* const* WS;   // E8M0 scales [R][C/32]
+  const uint8_t* const* W2;   // second matrix (gate + up in one launch), or null
+  const uint8_t* const* WS2;
+  int num_experts, R, C;
+  const int32_t* pe;
+  const int32_t* slot_vec;
+  const int32_t* slot_out;
+  const int32_t* slice_start;
+  const int32_t* slice_len;
+  const int32_t* slice_unit;
+  const int32_t* nslices;
+  const uint8_t* bimg;
+  const uint8_t* sfimg;
+  CUtensorMap* gmaps;
+  int box_rows;
+  int nvec;
+  float* out;
+  float* out2;
+  int out_rows;
+  unsigned* err;
+};
+
+struct MxItem {
+  const uint8_t* w;
+  const uint8_t* ws;
+  float* dst;
+  int tile, s0, ns, units, unit, sl;
+};
+
+__device__ __forceinline__ MxItem mx_item(const MxArgs& A, int w, int tiles, int mats) {
+  MxItem it;
+  const int mat = w % mats, rest = w / mats;
+  it.sl = rest / tiles;
+  it.tile = rest % tiles;
+  it.s0 = A.slice_start[it.sl];
+  it.ns = min(max(A.slice_len[it.sl], 1), kMxNvp);
+  it.units = (it.ns + kTcUnit - 1) / kTcUnit;
+  it.unit = A.slice_unit[it.sl];
+  int e = A.pe[it.s0];
+  if (e < 0 || e >= A.num_experts) e = 0;  // flagged by the epilogue
+  it.w = mat ? A.W2[e] : A.W[e];
+  it.ws = mat ? A.WS2[e] : A.WS[e];
+  it.dst = mat ? A.out2 : A.out;
+  return it;
+}
+
+__global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs A,
+                                                                   const __grid_constant__ CUtensorMap tmpl) {
+  extern __shared__ __align__(1024) uint8_t mx_smem_raw[];
+  MxSmem& sm = *reinterpret_cast<MxSmem*>(mx_smem_raw);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < kMxStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1 + kTcUnpackWarps);
+    }
+    for (int i = 0; i < kMxAbuf; ++i) {
+      mbar_init(&sm.a_full[i], 32 * kTcUnpackWarps);
+      mbar_init(&sm.a_empty[i], 1);
+    }
+    for (int i = 0; i < kMxDslots; ++i) {
+      mbar_init(&sm.d_full[i], 1);
+      mbar_init(&sm.d_empty[i], kMxEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (tid < kMxStages * 8) {
+    const uint4* src = reinterpret_cast<const uint4*>(&tmpl);
+    reinterpret_cast<uint4*>(&sm.tmap[tid / 8])[tid % 8] = src[tid % 8];
+  }
+  if (warp == kMxMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  const int nchunks = A.C / kMxStepCols;
+  const int tiles = (A.R + kTcRows - 1) / kTcRows;
+  const int mats = A.W2 ? 2 : 1;
+  const int total = *A.nslices * tiles * mats;
+  const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int nsteps = my_items * nchunks;
+  auto item_at = [&](int s) { return mx_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
+
+  if (warp == kMxProducerWarp) {
+    CUtensorMap* gmaps = A.gmaps + static_cast<size_t>(blockIdx.x) * kMxStages;
+    const uint8_t* map_addr[kMxStages] = {nullptr, nullptr, nullptr};
+    MxItem it{};
+#pragma unroll 1
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kMxStages, chunk = s % nchunks;
+      if (chunk == 0) it = item_at(s);
+      bool ok = s < kMxStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err);
+      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+      const uint8_t* cur = st == 0 ? map_addr[0] : (st == 1 ? map_addr[1] : map_addr[2]);
+      if (cur != it.w) {
+        if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
+        __syncwarp();
+        tc_tmap_publish(&gmaps[st], &sm.tmap[st]);
+        if (lane == 0) tc_tmap_acquire(&gmaps[st]);
+        if (st == 0) map_addr[0] = it.w;
+        else if (st == 1) map_addr[1] = it.w;
+        else map_addr[2] = it.w;
+      }
+      if (lane == 0) {
+        const uint32_t bbytes = it.units * kMxUnitBBytes;
+        const size_t uoff = static_cast<size_t>(it.unit) * nchunks + static_cast<size_t>(chunk) * it.units;
+        mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kMxRawRow + bbytes + kMxSfAtom);
+        tc_tma_2d(sm.raw[st], &gmaps[st], chunk * kMxRawRow, it.tile * kTcRows, &sm.full[st]);
+        tc_bulk(sm.b[st], A.bimg + uoff * kMxUnitBBytes, bbytes, &sm.full[st]);
+        tc_bulk(sm.sfb[st], A.sfimg + (static_cast<size_t>(it.sl) * nchunks + chunk) * kMxSfAtom, kMxSfAtom,
+                &sm.full[st]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == kMxMmaWarp) {
+    if (lane == 0) {
+      int n = kTcUnit, item = -1, slot = 0;
+#pragma unroll 1
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kMxStages, ab = s % kMxAbuf, chunk = s % nchunks;
+        if (chunk == 0) {
+          n = item_at(s).units * kTcUnit;
+          ++item;
+          slot = item % kMxDslots;
+          if (item >= kMxDslots && !tc_spin(&sm.d_empty[slot], ((item / kMxDslots) - 1) & 1, A.err)) break;
+        }
+        if (!tc_spin(&sm.a_full[ab], (s / kMxAbuf) & 1, A.err) || !tc_spin(&sm.full[st], (s / kMxStages) & 1, A.err))
+          break;
+        fence_async_shared();  // codes and weight scales written by the unpack threads
+        tc_fence_after_sync();
+        const uint32_t t_sfa = tmem + kMxSfaCol + 4 * ab, t_sfb = tmem + kMxSfbCol + 4 * st;
+        tmem_cp_sf(t_sfa, sm.sfa[ab]);
+        tmem_cp_sf(t_sfb, sm.sfb[st]);
+#pragma unroll
+        for (int kb = 0; kb < kMxKB; ++kb) {
+          const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * kb * 128), 128, kMxKch * 128);
+          const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * kb * 128), 128, kMxKch * 128);
+          umma_mx(tmem + slot * kMxDCols, da, db, mx_idesc(n, kb), t_sfa, t_sfb, chunk > 0 || kb > 0);
+        }
+        umma_commit(&sm.a_empty[ab]);
+        umma_commit(&sm.empty[st]);
+        if (chunk == nchunks - 1) umma_commit(&sm.d_full[slot]);
+      }
+    }
+  } else if (warp < kMxEpiWarp0) {
+    const int r = tid - 32 * kMxUnpackWarp0;
+    MxItem it{};
+#pragma unroll 1
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kMxStages, ab = s % kMxAbuf, chunk = s % nchunks;
+      if (chunk == 0) it = item_at(s);
+      const int row = it.tile * kTcRows + r;
+      // this row's four E8M0 block scales of the step (rows past the matrix: 2^-127, zero weights)
+      const uint32_t wsc = row < A.R ? *reinterpret_cast<const uint32_t*>(
+                                           it.ws + static_cast<size_t>(row) * (A.C / 32) + chunk * kMxKB)
+                                     : 0u;
+      if (!tc_wait(&sm.full[st], (s / kMxStages) & 1, A.err)) break;
+      if (s >= kMxAbuf && !tc_wait(&sm.a_empty[ab], ((s / kMxAbuf) - 1) & 1, A.err)) break;
+      const uint8_t* src = sm.raw[st] + r * kMxRawRow;
+      uint8_t* dst = sm.a[ab] + (r >> 3) * kMxKch * 128 + (r & 7) * 16;
+#pragma unroll
+      for (int q = 0; q < kMxRawRow / 16; ++q) {
+        const uint4 x = *reinterpret_cast<const uint4*>(src + 16 * q);
+        // 16 values = 8 packed bytes, then 8 bytes of padding
+        *reinterpret_cast<uint4*>(dst + (2 * q) * 128) = make_uint4(x.x, x.y, 0u, 0u);
+        *reinterpret_cast<uint4*>(dst + (2 * q + 1) * 128) = make_uint4(x.z, x.w, 0u, 0u);
+      }
+      *reinterpret_cast<uint32_t*>(sm.sfa[ab] + (r & 31) * 16 + (r >> 5) * 4) = wsc;
+      fence_async_shared();  // read by the MMAs and the scale copy
+      mbar_arrive(&sm.a_full[ab]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty[st]);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int trow = 32 * quarter + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
+#pragma unroll 1
+    for (int i = 0; i < my_items; ++i) {
+      const MxItem it = item_at(i * nchunks);
+      const int slot = i % kMxDslots;
+      if (!tc_wait(&sm.d_full[slot], (i / kMxDslots) & 1, A.err)) break;
+      tc_fence_after_sync();
+      const int grow = it.tile * kTcRows + trow;
+#pragma unroll 1
+      for (int c0 = 0; c0 < it.units * kTcUnit; c0 += 16) {
+        uint32_t rv[16];
+        tmem_ld16(tmem + lane_addr + slot * kMxDCols + c0, rv);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int vi = c0 + j;
+          if (vi < it.ns && grow < A.R) {
+            const int p = it.s0 + vi;
+            const int o = A.slot_out ? A.slot_out[p] : p;
+            if (o >= 0 && o < A.out_rows) it.dst[static_cast<size_t>(o) * A.R + grow] = __uint_as_float(rv[j]);
+          }
+        }
+      }
+      if (quarter == 0) {
+        for (int vi = lane; vi < it.ns; vi += 32) {
+          const int p = it.s0 + vi;
+          const int o = A.slot_out ? A.slot_out[p] : p;
+          const int v = A.slot_vec ? A.slot_vec[p] : p;
+          const int e = A.pe[p];
+          if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) && A.err)
+            atomicOr(A.err, kErrBadExpertId);
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.d_empty[slot]);
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == kMxMmaWarp) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+}
+
 }  // namespace dev
 
 namespace {
@@ -741,7 +1088,8 @@ int validate_tc(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens) {
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against the driver library).
-int tc_encode_tiled(CUtensorMap* map, void* base, size_t row_bytes, size_t rows, int box_rows) {
+int tc_encode_tiled(CUtensorMap* map, void* base, size_t row_bytes, size_t rows, int box_rows,
+                    int box_inner = dev::kTcRawRow) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -754,7 +1102,7 @@ int tc_encode_tiled(CUtensorMap* map, void* base, size_t row_bytes, size_t rows,
   if (!fn) return OBJB_FAIL(OBJB_ERR_DRIVER, "grouped Q4_0 MoE pairs", "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(dev::kTcRawRow), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -833,8 +1181,9 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   OBJB_TRY(ensure_smem_attr(dev::tc_q4_grouped_kernel, device, smem));
   const int img_grid = 2 * props.sm_count;
 
-  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, run_start, slice_start, slice_len,
-                      slice_unit, nslices, static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
+  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, dev::kTcUnit, run_start,
+                      slice_start, slice_len, slice_unit, nslices,
+                      static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
                       static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
@@ -886,6 +1235,191 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   return OBJB_OK;
 }
 
+
+// ---------------------------------------------------------------- official FP8 x FP4 pairs (block-scaled)
+namespace {
+
+struct MxLayout {
+  size_t codes_x, scales_x, g, u, codes_a, scales_a, run_start, slice_start, slice_len, slice_unit, nslices, bimg,
+      sfimg, gmaps, total;
+};
+
+// Image units (16 vectors) of a pair list grouped by expert: sum ceil(len / 16)
+// <= P / 16 + slices, slices <= P / 128 + distinct experts.  The scale atoms
+// are sized by units too (every slice has at least one unit).
+size_t mx_max_units(size_t P, size_t E) { return P / 16 + P / 128 + std::min(P, E) + 2; }
+
+MxLayout mx_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_count) {
+  MxLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  const size_t units = mx_max_units(P, E), nchunks = std::max(H, I) / dev::kMxStepCols;
+  L.codes_x = take(T * H);
+  L.scales_x = take(T * (H / 128));
+  L.g = take(P * I * 4);
+  L.u = take(P * I * 4);
+  L.codes_a = take(P * I);
+  L.scales_a = take(P * (I / 128));
+  L.run_start = take(P * 4);
+  L.slice_start = take(P * 4);
+  L.slice_len = take(P * 4);
+  L.slice_unit = take(P * 4);
+  L.nslices = take(4);
+  L.bimg = take(units * nchunks * dev::kMxUnitBBytes);
+  L.sfimg = take(units * nchunks * dev::kMxSfAtom);
+  L.gmaps = take(2 * static_cast<size_t>(sm_count) * dev::kMxStages * sizeof(CUtensorMap));
+  L.total = off;
+  return L;
+}
+
+int validate_mx(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens) {
+  const char* act = "official FP8 x FP4 MoE pairs";
+  if (!l) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "null layer");
+  if (l->fmt != OBJB_FP4_E2M1 || !l->d_gate_scale || !l->d_up_scale || !l->d_down_scale)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, act, "needs a split FP4 E2M1 layer (weights + E8M0 scale tables)");
+  if ((l->flags & OBJB_MOE_UNALIGNED) != 0)
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, act, "expert tensors must be 16-byte aligned");
+  if (!l->d_gate || !l->d_up || !l->d_down || l->num_experts == 0 || l->num_experts > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "missing expert tables");
+  if (l->hidden == 0 || l->intermediate == 0 || l->out_dim == 0 || l->hidden > (1u << 20) ||
+      l->intermediate > (1u << 20) || l->out_dim > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "shape out of range");
+  if (l->hidden % 128 || l->intermediate % 128)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "hidden and intermediate must be multiples of 128 (act_quant blocks)");
+  if (num_pairs == 0 || num_pairs > (1u << 20) || num_tokens == 0 || num_tokens > (1u << 20))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "need 1 <= num_pairs, num_tokens <= 2^20");
+  if (num_pairs * std::max(l->intermediate, l->out_dim) > (1u << 30) || num_tokens * l->hidden > (1ull << 34))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "num_pairs * rows too large");
+  return OBJB_OK;
+}
+
+}  // namespace
+
+int moe_pairs_official_tc_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out) {
+  OBJB_TRY(validate_mx(l, num_pairs, num_tokens));
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  *out = mx_layout(num_pairs, num_tokens, l->hidden, l->intermediate, l->num_experts, props.sm_count).total;
+  return OBJB_OK;
+}
+
+// The routed experts of the official path over (expert, token) pairs:
+// act_quant of the tokens, slices, slice images, gate and up on block-scaled
+// MMAs, the official SwiGLU, act_quant of the activations, their images,
+// and down into v[pair_out[p]] (unweighted).
+int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, const int32_t* pt,
+                          const int32_t* po, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
+                          cudaStream_t stream, void* scratch, size_t scratch_bytes, const int32_t* d_count) {
+  const char* act = "official FP8 x FP4 MoE pairs";
+  OBJB_TRY(validate_mx(l, num_pairs, num_tokens));
+  if (!pe || !pt || !x || !v || !scratch) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "null device pointer");
+  if (v_rows < (po ? 1 : num_pairs) || v_rows > (1u << 30))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act, "v_rows cannot hold the pair outputs");
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  const MxLayout L = mx_layout(num_pairs, num_tokens, l->hidden, l->intermediate, l->num_experts, props.sm_count);
+  if (scratch_bytes < L.total)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, act,
+                     "scratch of " + std::to_string(scratch_bytes) + " bytes < needed " + std::to_string(L.total));
+  unsigned* err = nullptr;
+  OBJB_TRY(device_error_word(device, &err));
+  uint8_t* sc = static_cast<uint8_t*>(scratch);
+  uint8_t* codes_x = sc + L.codes_x;
+  uint8_t* scales_x = sc + L.scales_x;
+  float* g = reinterpret_cast<float*>(sc + L.g);
+  float* u = reinterpret_cast<float*>(sc + L.u);
+  uint8_t* codes_a = sc + L.codes_a;
+  uint8_t* scales_a = sc + L.scales_a;
+  int32_t* run_start = reinterpret_cast<int32_t*>(sc + L.run_start);
+  int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
+  int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
+  int32_t* slice_unit = reinterpret_cast<int32_t*>(sc + L.slice_unit);
+  int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
+  uint8_t* bimg = sc + L.bimg;
+  uint8_t* sfimg = sc + L.sfimg;
+  CUtensorMap* gmaps = reinterpret_cast<CUtensorMap*>(sc + L.gmaps);
+  const int P = static_cast<int>(num_pairs), T = static_cast<int>(num_tokens);
+  const int H = static_cast<int>(l->hidden), I = static_cast<int>(l->intermediate), O = static_cast<int>(l->out_dim);
+  CUtensorMap tm_gu, tm_dn;
+  OBJB_TRY(tc_encode_tiled(&tm_gu, scratch, static_cast<size_t>(H / 2), static_cast<size_t>(I),
+                           std::min(dev::kTcRows, I), dev::kMxRawRow));
+  OBJB_TRY(tc_encode_tiled(&tm_dn, scratch, static_cast<size_t>(I / 2), static_cast<size_t>(O),
+                           std::min(dev::kTcRows, O), dev::kMxRawRow));
+  const size_t smem = sizeof(dev::MxSmem);
+  OBJB_TRY(ensure_smem_attr(dev::mx_grouped_kernel, device, smem));
+  const int img_grid = 2 * props.sm_count;
+
+  OBJB_TRY(act_quant(x, num_tokens, l->hidden, codes_x, scales_x, stream, "act_quant hidden"));
+  OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kMxNvp, dev::kTcUnit, run_start,
+                      slice_start, slice_len, slice_unit, nslices,
+                      static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err));
+  OBJB_TRY(launch_pdl(dev::mx_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
+                      static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
+                      static_cast<const int32_t*>(nslices), static_cast<const uint8_t*>(codes_x),
+                      static_cast<const uint8_t*>(scales_x), pt, T, H, bimg, sfimg));
+  dev::MxArgs a{};
+  a.W = reinterpret_cast<const uint8_t* const*>(l->d_gate);
+  a.WS = reinterpret_cast<const uint8_t* const*>(l->d_gate_scale);
+  a.W2 = reinterpret_cast<const uint8_t* const*>(l->d_up);
+  a.WS2 = reinterpret_cast<const uint8_t* const*>(l->d_up_scale);
+  a.num_experts = static_cast<int>(l->num_experts);
+  a.R = I;
+  a.C = H;
+  a.pe = pe;
+  a.slot_vec = pt;
+  a.slot_out = nullptr;
+  a.slice_start = slice_start;
+  a.slice_len = slice_len;
+  a.slice_unit = slice_unit;
+  a.nslices = nslices;
+  a.bimg = bimg;
+  a.sfimg = sfimg;
+  a.gmaps = gmaps;
+  a.box_rows = std::min(dev::kTcRows, I);
+  a.nvec = T;
+  a.out = g;
+  a.out2 = u;
+  a.out_rows = P;
+  a.err = err;
+  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a, tm_gu));
+  {
+    const size_t n = static_cast<size_t>(P) * I;
+    const int sg = static_cast<int>(std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 8ull * props.sm_count)));
+    OBJB_TRY(launch_pdl(dev::mx_swiglu_kernel, sg, 256, 0, stream, g, static_cast<const float*>(u), n, d_count, I,
+                        limit));
+  }
+  OBJB_TRY(act_quant(g, num_pairs, l->intermediate, codes_a, scales_a, stream, "act_quant intermediate"));
+  OBJB_TRY(launch_pdl(dev::mx_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
+                      static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
+                      static_cast<const int32_t*>(nslices), static_cast<const uint8_t*>(codes_a),
+                      static_cast<const uint8_t*>(scales_a), static_cast<const int32_t*>(nullptr), P, I, bimg,
+                      sfimg));
+  a.W = reinterpret_cast<const uint8_t* const*>(l->d_down);
+  a.WS = reinterpret_cast<const uint8_t* const*>(l->d_down_scale);
+  a.W2 = nullptr;
+  a.WS2 = nullptr;
+  a.R = O;
+  a.C = I;
+  a.box_rows = std::min(dev::kTcRows, O);
+  a.slot_vec = nullptr;
+  a.slot_out = po;
+  a.nvec = P;
+  a.out = v;
+  a.out2 = nullptr;
+  a.out_rows = static_cast<int>(v_rows);
+  a.gmaps = gmaps + static_cast<size_t>(props.sm_count) * dev::kMxStages;
+  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a, tm_dn));
+  return OBJB_OK;
+}
+
 }  // namespace objb
 
 extern "C" {
@@ -913,4 +1447,29 @@ int objb_moe_pairs_tc_device(const objb_moe_layer* layer, size_t num_pairs, cons
                             swiglu_limit, stream, ws, need, nullptr, d_num_pairs);
 }
 
+int objb_moe_pairs_official_tc_scratch_bytes(const objb_moe_layer* layer, size_t num_pairs, size_t num_tokens,
+                                             size_t* bytes) {
+  objb::clear_error();
+  if (!bytes)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_moe_pairs_official_tc_scratch_bytes", "null output pointer");
+  return objb::moe_pairs_official_tc_scratch_bytes(layer, num_pairs, num_tokens, bytes);
+}
+
+int objb_moe_pairs_official_tc_device(const objb_moe_layer* layer, size_t num_pairs, const int32_t* d_num_pairs,
+                                      const int32_t* d_pair_expert, const int32_t* d_pair_token,
+                                      const int32_t* d_pair_out, size_t num_tokens, const float* d_x, float* d_v,
+                                      size_t v_rows, float swiglu_limit, objb_stream_t stream_) {
+  objb::clear_error();
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  size_t need = 0;
+  OBJB_TRY(objb::moe_pairs_official_tc_scratch_bytes(layer, num_pairs, num_tokens, &need));
+  int device = 0;
+  OBJB_TRY(objb::current_device(&device));
+  void* ws = nullptr;
+  OBJB_TRY(objb::workspace_get(device, stream, need, &ws));
+  return objb::moe_pairs_official_tc(layer, num_pairs, d_pair_expert, d_pair_token, d_pair_out, num_tokens, d_x, d_v,
+                                     v_rows, swiglu_limit, stream, ws, need, d_num_pairs);
+}
+
 }  // extern "C"
+

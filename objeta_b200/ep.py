@@ -44,6 +44,9 @@ _lib.register_signatures({
     "objb_moe_pairs_tc_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
     "objb_moe_pairs_tc_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_size,
                                          c_void_p, c_void_p, c_size, ctypes.c_float, c_void_p]),
+    "objb_moe_pairs_official_tc_scratch_bytes": (c_int, [c_void_p, c_size, c_size, ctypes.POINTER(c_size)]),
+    "objb_moe_pairs_official_tc_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_size,
+                                                  c_void_p, c_void_p, c_size, ctypes.c_float, c_void_p]),
     "objb_moe_combine_device": (c_int, [c_void_p, c_size, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p,
                                         c_void_p]),
     "objb_router_topk_batched_device": (c_int, [c_void_p, c_size, c_size, c_size, c_int, c_void_p, c_void_p,
@@ -150,6 +153,22 @@ def moe_pairs_tc(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu
     P = pair_expert.numel()
     T = d_x.shape[0]
     _lib.call("objb_moe_pairs_tc_device", ctypes.byref(layer._c), P,
+              _dev_ptr(d_count) if d_count is not None else None, _dev_ptr(pair_expert), _dev_ptr(pair_token),
+              _dev_ptr(pair_out) if pair_out is not None else None, T, _dev_ptr(d_x), _dev_ptr(d_v), d_v.shape[0],
+              float(swiglu_limit), _lib.stream_handle(stream))
+    return d_v
+
+
+def moe_pairs_official_tc(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 10.0,
+                          stream=None, d_count=None):
+    """The official DeepSeek routed experts (act_quant -> FP8 x FP4 gate/up ->
+    SwiGLU clamping up only -> act_quant -> FP8 x FP4 down) over (expert,
+    token) pairs on block-scaled tensor-core MMAs; layer: a split FP4
+    ``MoeLayer`` with scale tables.  Same pair arguments as ``moe_pairs``;
+    pairs grouped by expert; rows unweighted."""
+    P = pair_expert.numel()
+    T = d_x.shape[0]
+    _lib.call("objb_moe_pairs_official_tc_device", ctypes.byref(layer._c), P,
               _dev_ptr(d_count) if d_count is not None else None, _dev_ptr(pair_expert), _dev_ptr(pair_token),
               _dev_ptr(pair_out) if pair_out is not None else None, T, _dev_ptr(d_x), _dev_ptr(d_v), d_v.shape[0],
               float(swiglu_limit), _lib.stream_handle(stream))
