@@ -4,6 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --case q4_0:151936x2048 [--steps K] [--warmup W]
     python bench.py --grouped 256 [--steps K] [--warmup W]
+    python bench.py --official 1,16,256 [--experts E] [--steps K] [--warmup W]
 
 `--case` runs one GEMV of the sweep alone (W + K plain launches, rotating
 over its weight copies, no graph) and prints its mean launch time; it is the
@@ -11,7 +12,11 @@ command the ncu captures are taken on.  `--grouped T` runs the configs[4]
 layer's (expert, token) pairs for T tokens (Zipf(1.1) top-8 of 256 Q4_0
 experts, H 2048, I 512) on the grouped tensor-core path and on the CUDA-core
 pair programs, W + K calls each, and prints both mean call times; it is the
-command the grouped kernel's ncu captures are taken on.
+command the grouped kernel's ncu captures are taken on.  `--official T,..`
+runs the official DeepSeek routed experts (configs[3] shapes: split FP4
+experts, H 4096, I 2048, top-8 of 256 by default; act_quant FP8 activations)
+for T tokens: the pairs on block-scaled tensor cores (moe_pairs_official_tc +
+combine) against the CUDA-core official launch once per token.
 
 Workload: the block-quant GEMV format/shape sweep,
 Q4_0, Q5_0 and IQ3_0 at rows x cols in {4096x4096, 14336x4096, 4096x14336,
@@ -855,6 +860,71 @@ def run_grouped(args, local):
     return res
 
 
+def run_official(args, local):
+    """Official routed experts for T tokens: grouped block-scaled pairs vs the
+    per-token CUDA-core launch (objb_moe_official_selected_device)."""
+    import torch
+    from objeta_b200.ep import moe_combine, moe_pairs_official_tc
+    from objeta_b200.moe import MoeLayer
+    c = C4
+    H, I, K = c["hidden"], c["inter"], c["top_k"]
+    E = int(args.experts or c["experts"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(77)
+    t = {n: [] for n in ("gw", "gs", "uw", "us", "dw", "ds")}
+    for _ in range(E):
+        for wn, sn, r, cc in (("gw", "gs", I, H), ("uw", "us", I, H), ("dw", "ds", H, I)):
+            t[wn].append(torch.randint(0, 256, (r * cc // 2,), device=dev, dtype=torch.uint8, generator=gen))
+            t[sn].append(torch.randint(119, 124, (r * cc // 32,), device=dev, dtype=torch.uint8, generator=gen))
+    layer = MoeLayer(3, H, I, H, t["gw"], t["uw"], t["dw"], t["gs"], t["us"], t["ds"])
+    ebytes = 3 * (I * H // 2 + I * H // 32)
+    res = {"config": f"official routed experts: {E} split FP4 experts, H {H}, I {I}, top-{K}, Zipf(1.1) over a "
+                     "seeded permutation, act_quant FP8 activations", "expert_bytes": ebytes}
+    stream = torch.cuda.Stream(device=dev)
+    for T in (int(v) for v in str(args.official).split(",")):
+        rng = np.random.default_rng(3000 + T)
+        ids, w = zipf_routes(T, E, K, 1.1, np.random.default_rng(7).permutation(E), rng)
+        flat = ids.reshape(-1)
+        order = np.argsort(flat, kind="stable")
+        pe = torch.from_numpy(flat[order].astype(np.int32)).to(dev)
+        pt = torch.from_numpy((order // K).astype(np.int32)).to(dev)
+        po = torch.from_numpy(order.astype(np.int32)).to(dev)
+        x = torch.randn(T, H, device=dev, generator=gen)
+        dw = torch.from_numpy(w).to(dev)
+        di = torch.from_numpy(ids.astype(np.int32)).to(dev)
+        v = torch.empty(T * K, H, device=dev)
+        out = torch.empty(T, H, device=dev)
+        slot = torch.arange(T * K, dtype=torch.int32, device=dev).reshape(T, K)
+
+        def grouped():
+            moe_pairs_official_tc(layer, pe, pt, x, v, pair_out=po, stream=stream)
+            moe_combine(v, slot, dw, out, stream=stream)
+
+        def per_token():
+            for i in range(T):
+                layer.forward_official_selected(di[i], dw[i], x[i], d_out=out[i], stream=stream)
+
+        row = {"distinct_experts": int(len(np.unique(flat))), "unique_expert_bytes": int(len(np.unique(flat)) * ebytes)}
+        for name, fn in (("tc_grouped", grouped), ("cuda_core_per_token", per_token)):
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    fn()
+                torch.cuda.synchronize()
+                t0 = torch.cuda.Event(enable_timing=True)
+                t1 = torch.cuda.Event(enable_timing=True)
+                t0.record(stream)
+                for _ in range(args.steps):
+                    fn()
+                t1.record(stream)
+            torch.cuda.synchronize()
+            us = t0.elapsed_time(t1) * 1e3 / args.steps
+            row[f"us_{name}"] = round(us, 1)
+            row[f"tokens_per_s_{name}"] = round(T * 1e6 / us, 1)
+        res[f"T{T}"] = row
+    return res
+
+
 def main():
     # NCCL's own log lines (e.g. its version banner when NCCL_DEBUG is set)
     # go to stderr, so stdout carries only the result line.
@@ -866,6 +936,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--case", default=None, help="fmt:RxC, e.g. q4_0:151936x2048 (one GEMV alone)")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE configs reported beside the headline")
+    ap.add_argument("--official", default=None,
+                    help="T[,T..]: official routed experts, grouped block-scaled pairs vs the per-token launch")
+    ap.add_argument("--experts", type=int, default=None, help="expert count for --official (default configs[3])")
     ap.add_argument("--grouped", type=int, default=None,
                     help="T: the configs[4] pairs of T tokens on the grouped tensor-core path and the CUDA-core path")
     args = ap.parse_args()
@@ -878,6 +951,9 @@ def main():
         return
     if args.grouped:
         print(json.dumps(run_grouped(args, local)), flush=True)
+        return
+    if args.official:
+        print(json.dumps(run_official(args, local)), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, world, rank)

@@ -695,7 +695,7 @@ constexpr int kMxStepCols = kMxKB * 32;            // 128
 constexpr int kMxNvp = 128;                        // pairs per slice (at most)
 constexpr int kMxRawRow = kMxStepCols / 2;         // packed FP4 bytes of one row per step
 constexpr int kMxKch = kMxStepCols / 16;           // 16-byte K columns of a staged operand
-constexpr int kMxStages = 3, kMxAbuf = 2, kMxDslots = 2;
+constexpr int kMxStages = 6, kMxAbuf = 2, kMxDslots = 2;  // six steps in flight cover the DRAM latency
 constexpr int kMxUnitBBytes = kTcUnit * kMxStepCols;  // 16 activation rows of one step
 constexpr int kMxSfAtom = 512;
 constexpr int kMxDCols = 128;                      // tensor-memory columns of one accumulator slot
@@ -884,7 +884,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
 
   if (warp == kMxProducerWarp) {
     CUtensorMap* gmaps = A.gmaps + static_cast<size_t>(blockIdx.x) * kMxStages;
-    const uint8_t* map_addr[kMxStages] = {nullptr, nullptr, nullptr};
+    const uint8_t* map_addr[kMxStages] = {};
     MxItem it{};
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
@@ -892,15 +892,12 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
       if (chunk == 0) it = item_at(s);
       bool ok = s < kMxStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err);
       if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
-      const uint8_t* cur = st == 0 ? map_addr[0] : (st == 1 ? map_addr[1] : map_addr[2]);
-      if (cur != it.w) {
+      if (map_addr[st] != it.w) {
         if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
         __syncwarp();
         tc_tmap_publish(&gmaps[st], &sm.tmap[st]);
         if (lane == 0) tc_tmap_acquire(&gmaps[st]);
-        if (st == 0) map_addr[0] = it.w;
-        else if (st == 1) map_addr[1] = it.w;
-        else map_addr[2] = it.w;
+        map_addr[st] = it.w;
       }
       if (lane == 0) {
         const uint32_t bbytes = it.units * kMxUnitBBytes;
