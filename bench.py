@@ -610,23 +610,14 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
         plans = [ep.plan(ids[i]) for i in range(S)]
         uniq = sum(len(np.unique(plans[i % S].pair_expert)) for i in range(n))
         nvb = sum(sum(plans[i % S].exchange_bytes(H, H).values()) for i in range(n))
-        if world == 1:
-            # one rank: the step has no host round trip, so it is captured
-            stream = torch.cuda.Stream(device=dev)
-            ms = _graph_time(stream, [(lambda i=i: ep.forward(xs[i], ids[i], ws[i])) for i in range(S)], n, warmup)
-        else:
-            for i in range(warmup):
-                ep.forward(xs[i % S], ids[i % S], ws[i % S])
-            torch.cuda.synchronize()
+        # the step has no host round trip (one rank: device sort; several: the
+        # device exchange, its NCCL all-gathers and all-to-all on the step's
+        # stream), so every rank captures it in CUDA graphs and replays them;
+        # the graphs are released before the process group is destroyed
+        stream = torch.cuda.Stream(device=dev)
+        if world > 1:
             dist.barrier(group=group)
-            t0 = torch.cuda.Event(enable_timing=True)
-            t1 = torch.cuda.Event(enable_timing=True)
-            t0.record()
-            for i in range(n):
-                ep.forward(xs[i % S], ids[i % S], ws[i % S])
-            t1.record()
-            torch.cuda.synchronize()
-            ms = t0.elapsed_time(t1)
+        ms = _graph_time(stream, [(lambda i=i: ep.forward(xs[i], ids[i], ws[i])) for i in range(S)], n, warmup)
         stats = torch.tensor([ms, uniq * Q4_EXPERT_BYTES(H, I), nvb], dtype=torch.float64, device=dev)
         if world > 1:
             mx = stats.clone()
@@ -645,9 +636,10 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
     torch.cuda.empty_cache()
     return {"config": f"configs[4] EP layer, experts resident: 256 Q4_0 experts / {world} rank(s), H 2048, I 512, "
                       "top-8 Zipf(1.1), T tokens per rank",
-            "scaling": "weak (T tokens per rank)", "timer": "CUDA events around whole steps, max over ranks; one rank: "
-            "device-only step (sort + pairs + combine) replayed as CUDA graphs; several: host dispatch plan + "
-            "2 NCCL all-to-alls per step", **res}
+            "scaling": "weak (T tokens per rank)", "timer": "CUDA events around whole steps, max over ranks; the "
+            "device-only step replayed as CUDA graphs (one rank: sort + pairs + combine; several: NCCL all-gathers "
+            "of routing table, weights and token rows, device-built pair list, pairs, partial combine, NCCL "
+            "all-to-all, ordered sum)", **res}
 
 
 def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
