@@ -319,17 +319,27 @@ static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* _
   weights += static_cast<size_t>(blockIdx.x) * top_k;
   extern __shared__ float sp[];  // [n] exp values, then probs
   __shared__ float s_max, s_sum;
+  __shared__ float s_wmax[32];
+  // the maximum is exact in any order: a block reduction
+  float m = -__int_as_float(0x7F800000);
+  for (int e = threadIdx.x; e < n; e += blockDim.x) m = fmaxf(m, logits[e]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+  if ((threadIdx.x & 31) == 0) s_wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
   if (threadIdx.x == 0) {
-    float m = -__int_as_float(0x7F800000);
-    for (int e = 0; e < n; ++e) m = fmaxf(m, logits[e]);
-    s_max = m;
+    float mm = s_wmax[0];
+    for (int w = 1; w < static_cast<int>((blockDim.x + 31) >> 5); ++w) mm = fmaxf(mm, s_wmax[w]);
+    s_max = mm;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < n; e += blockDim.x)
     sp[e] = __double2float_rn(exp(static_cast<double>(__fsub_rn(logits[e], s_max))));
   __syncthreads();
   if (threadIdx.x == 0) {
+    // the sum keeps the reference's sequential f32 order (from shared memory)
     float s = 0.0f;
+#pragma unroll 8
     for (int e = 0; e < n; ++e) s = __fadd_rn(s, sp[e]);
     s_sum = s;
   }
