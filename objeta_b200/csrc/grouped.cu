@@ -145,7 +145,8 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, unsigned
 }
 
 // Bounded wait without suspending the thread between polls (lowest wake-up
-// latency; for the single MMA-issuing thread).
+// latency; for the MMA-issuing warp, every lane of which polls so that the
+// lane elect.sync picks has itself observed the phase).
 __device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned* err) {
   for (uint32_t i = 0; i < 64u * kMaxSpins; ++i) {
     uint32_t done;
@@ -161,6 +162,9 @@ __device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned
   }
   if (err) atomicOr(err, kErrFullWaitTimeout);
   return false;
+}
+__device__ __forceinline__ bool tc_spin_warp(uint64_t* bar, uint32_t parity, unsigned* err) {
+  return __all_sync(0xFFFFFFFFu, tc_spin(bar, parity, err));
 }
 
 // Instruction descriptor of kind::i8 with both operands signed.
@@ -523,39 +527,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       __syncwarp();
     }
   } else if (warp == kTcMmaWarp) {
-    if (lane == 0) {
-      uint32_t idesc = 0;
+    // the whole warp walks the steps (warp-uniform operands); one lane issues
+    uint32_t idesc = 0;
 #pragma unroll 1
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % kTcStages, ab = s % kTcAbuf;
-        if (s % nchunks == 0) idesc = umma_idesc_s8s8(kTcRows, 3 * item_at(s).nv);
-        if (!tc_spin(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
-            !tc_spin(&sm.full[st], (s / kTcStages) & 1, A.err))
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kTcStages, ab = s % kTcAbuf;
+      if (s % nchunks == 0) idesc = umma_idesc_s8s8(kTcRows, 3 * item_at(s).nv);
+      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
+          !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err))
+        break;
+      fence_async_shared();  // codes written by the unpack threads, read by the MMAs
+      tc_fence_after_sync();
+      bool ok = true;
+#pragma unroll 1
+      for (int g = 0; g < kTcKB / 2; ++g) {
+        const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
+        if (G >= kTcSlots && !tc_spin_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err)) {
+          ok = false;
           break;
-        fence_async_shared();  // codes written by the unpack threads, read by the MMAs
-        tc_fence_after_sync();
-        bool ok = true;
-#pragma unroll 1
-        for (int g = 0; g < kTcKB / 2; ++g) {
-          const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
-          if (G >= kTcSlots && !tc_spin(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-#pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int j = 2 * g + jj;
-            const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
-            const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
-            umma_i8(tmem + slot * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
-          }
-          umma_commit(&sm.t_full[slot]);
         }
-        if (!ok) break;
-        umma_commit(&sm.a_empty[ab]);
-        umma_commit(&sm.empty[st]);
+        tc_fence_after_sync();
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * g + jj;
+          const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
+          const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
+          umma_i8(tmem + slot * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
+        }
+        umma_commit(&sm.t_full[slot]);
       }
+      if (!ok) break;
+      umma_commit(&sm.a_empty[ab]);
+      umma_commit(&sm.empty[st]);
     }
   } else if (warp < kTcEpiWarp0) {
     const int r = tid - 32 * kTcUnpackWarp0;
@@ -726,13 +729,15 @@ __device__ __forceinline__ uint32_t mx_idesc(int n, int kb) {
 __device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                         uint32_t sfa_tmem, uint32_t sfb_tmem, bool accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u), "r"(sfa_tmem), "r"(sfb_tmem));
 }
-// 32 rows x 16 bytes of shared memory -> 4 tensor-memory columns of every lane quarter.
+// 32 rows x 16 bytes of shared memory -> 4 tensor-memory columns of every lane
+// quarter (a converged warp executes it; the elected lane issues).
 __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, const void* smem_atom) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr),
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+               "@e tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;\n\t}" ::"r"(taddr),
                "l"(umma_desc_kmajor(smem_addr(smem_atom), 128, 128)));
 }
 
@@ -911,34 +916,33 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
       __syncwarp();
     }
   } else if (warp == kMxMmaWarp) {
-    if (lane == 0) {
-      int n = kTcUnit, item = -1, slot = 0;
+    // the whole warp walks the steps (warp-uniform operands); one lane issues
+    int n = kTcUnit, item = -1, slot = 0;
 #pragma unroll 1
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % kMxStages, ab = s % kMxAbuf, chunk = s % nchunks;
-        if (chunk == 0) {
-          n = item_at(s).units * kTcUnit;
-          ++item;
-          slot = item % kMxDslots;
-          if (item >= kMxDslots && !tc_spin(&sm.d_empty[slot], ((item / kMxDslots) - 1) & 1, A.err)) break;
-        }
-        if (!tc_spin(&sm.a_full[ab], (s / kMxAbuf) & 1, A.err) || !tc_spin(&sm.full[st], (s / kMxStages) & 1, A.err))
-          break;
-        fence_async_shared();  // codes and weight scales written by the unpack threads
-        tc_fence_after_sync();
-        const uint32_t t_sfa = tmem + kMxSfaCol + 4 * ab, t_sfb = tmem + kMxSfbCol + 4 * st;
-        tmem_cp_sf(t_sfa, sm.sfa[ab]);
-        tmem_cp_sf(t_sfb, sm.sfb[st]);
-#pragma unroll
-        for (int kb = 0; kb < kMxKB; ++kb) {
-          const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * kb * 128), 128, kMxKch * 128);
-          const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * kb * 128), 128, kMxKch * 128);
-          umma_mx(tmem + slot * kMxDCols, da, db, mx_idesc(n, kb), t_sfa, t_sfb, chunk > 0 || kb > 0);
-        }
-        umma_commit(&sm.a_empty[ab]);
-        umma_commit(&sm.empty[st]);
-        if (chunk == nchunks - 1) umma_commit(&sm.d_full[slot]);
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kMxStages, ab = s % kMxAbuf, chunk = s % nchunks;
+      if (chunk == 0) {
+        n = item_at(s).units * kTcUnit;
+        ++item;
+        slot = item % kMxDslots;
+        if (item >= kMxDslots && !tc_spin_warp(&sm.d_empty[slot], ((item / kMxDslots) - 1) & 1, A.err)) break;
       }
+      if (!tc_spin_warp(&sm.a_full[ab], (s / kMxAbuf) & 1, A.err) || !tc_spin_warp(&sm.full[st], (s / kMxStages) & 1, A.err))
+        break;
+      fence_async_shared();  // codes and weight scales written by the unpack threads
+      tc_fence_after_sync();
+      const uint32_t t_sfa = tmem + kMxSfaCol + 4 * ab, t_sfb = tmem + kMxSfbCol + 4 * st;
+      tmem_cp_sf(t_sfa, sm.sfa[ab]);
+      tmem_cp_sf(t_sfb, sm.sfb[st]);
+#pragma unroll
+      for (int kb = 0; kb < kMxKB; ++kb) {
+        const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * kb * 128), 128, kMxKch * 128);
+        const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * kb * 128), 128, kMxKch * 128);
+        umma_mx(tmem + slot * kMxDCols, da, db, mx_idesc(n, kb), t_sfa, t_sfb, chunk > 0 || kb > 0);
+      }
+      umma_commit(&sm.a_empty[ab]);
+      umma_commit(&sm.empty[st]);
+      if (chunk == nchunks - 1) umma_commit(&sm.d_full[slot]);
     }
   } else if (warp < kMxEpiWarp0) {
     const int r = tid - 32 * kMxUnpackWarp0;
