@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(256) ffn_generic_out_kernel(const float* __res
 namespace {
 
 bool plan_bf16(int rows, int cols, bool dual, RowLayoutHost* L) {
-  return plan_rows(rows, cols, cols * 2, 0, 2, dual, dev::kMaxConsumerWarps, L);
+  return plan_rows(rows, cols, cols * 2, 0, 2, dual, dev::kMaxConsumerWarps, L, kMoeSmemBudget);
 }
 
 int even_split(int rows, int sms, int* grid) {

@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(256) gemv_fp4_split_fallback_kernel(
 static_assert(sizeof(RowLayoutHost) == sizeof(dev::RowLayout), "layout mirror mismatch");
 
 bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
-               int max_consumer_warps, RowLayoutHost* L) {
+               int max_consumer_warps, RowLayoutHost* L, int smem_budget) {
   if (rows <= 0 || cols <= 0 || cols % 32) return false;
   const int nblocks = cols / 32;
   if (row_bytes % 16 || srow_bytes % 16) return false;
@@ -59,18 +59,9 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
   const int ngrp = std::max(1, max_consumer_warps / nseg);
   int per_row = row_bytes + srow_bytes;
   if (dual) per_row *= 2;
-#ifndef OBJB_STAGE_TARGET
-#define OBJB_STAGE_TARGET (48 * 1024)
-#endif
-#ifndef OBJB_SMEM_BUDGET
-#define OBJB_SMEM_BUDGET (200 * 1024)
-#endif
-#ifndef OBJB_STAGE_MAX
-#define OBJB_STAGE_MAX (OBJB_SMEM_BUDGET / 2 - 4096)
-#endif
-  constexpr int kStageTarget = OBJB_STAGE_TARGET;
-  constexpr int kSmemBudget = OBJB_SMEM_BUDGET;
-  constexpr int kStageMax = OBJB_STAGE_MAX;
+  constexpr int kStageTarget = 48 * 1024;
+  const int kSmemBudget = std::min(smem_budget, 227 * 1024);
+  const int kStageMax = kSmemBudget / 2 - 4096;
   // One stage gives every row group one 4-row batch when that fits; small rows
   // get several batches per stage.
   const int quantum = ngrp * 4;

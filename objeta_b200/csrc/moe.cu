@@ -172,8 +172,8 @@ MoePlan<RD> plan_moe(const MoeShape& s, int fmt, bool split, bool aligned) {
   const int P = 2;
   const bool blocks_ok = split || ((s.H / 32) % P == 0 && (s.I / 32) % P == 0);
   p.fast = aligned && blocks_ok &&
-           plan_rows(s.I, s.H, rbh, srbh, P, true, dev::kMaxConsumerWarps, &p.lg) &&
-           plan_rows(s.O, s.I, rbi, srbi, P, false, dev::kMaxConsumerWarps, &p.ld);
+           plan_rows(s.I, s.H, rbh, srbh, P, true, dev::kMaxConsumerWarps, &p.lg, kMoeSmemBudget) &&
+           plan_rows(s.O, s.I, rbi, srbi, P, false, dev::kMaxConsumerWarps, &p.ld, kMoeSmemBudget);
   if (p.fast) {
     p.imgx_quads = ximage_quads<RD>(p.lg);
     p.imga_quads = ximage_quads<RD>(p.ld);

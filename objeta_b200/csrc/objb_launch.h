@@ -39,8 +39,13 @@ int current_device(int* dev);
 // `row_bytes` (+ `srow_bytes` of split scales) long, with lane tiles covering
 // `blocks_per_lane` blocks.  `dual` doubles the per-stage bytes (two matrices
 // per stage).  Returns false when the shape cannot use the bulk-copy path.
+// `smem_budget` bounds the stage ring: plain GEMVs (one matrix per call, calls
+// back to back) keep the default; the MoE and FFN programs take the larger
+// budget, where a third stage of wide rows shortens each expert's ramp.
+constexpr int kGemvSmemBudget = 200 * 1024;
+constexpr int kMoeSmemBudget = 226 * 1024;
 bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
-               int max_consumer_warps, RowLayoutHost* L);
+               int max_consumer_warps, RowLayoutHost* L, int smem_budget = kGemvSmemBudget);
 
 size_t pipe_smem_bytes(const RowLayoutHost& L);
 

@@ -230,7 +230,7 @@ int launch_ximage_fp8(const RowLayoutHost& L, const uint8_t* codes, const uint8_
 }
 
 bool plan_fp8_fp4(int rows, int cols, bool dual, RowLayoutHost* L) {
-  return plan_rows(rows, cols, cols / 2, cols / 32, 2, dual, dev::kMaxConsumerWarps, L);
+  return plan_rows(rows, cols, cols / 2, cols / 32, 2, dual, dev::kMaxConsumerWarps, L, kMoeSmemBudget);
 }
 
 namespace {
