@@ -89,6 +89,7 @@ int gemv_bf16(const void* w, const float* x, float* y, int rows, int cols, cudaS
   dev::GemvProg prog;
   prog.src = dev::StageSource{static_cast<const uint8_t*>(w), nullptr, nullptr, nullptr};
   prog.ximg = img;
+  prog.x = nullptr;
   prog.y = y;
   prog.rows = rows;
   prog.rows_per_cta = even_split(rows, props.sm_count, &grid);

@@ -76,7 +76,7 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
   T = std::min(T, dev::kMaxRowsPerStage);
   const int stage_bytes = ((T * per_row) + 127) / 128 * 128;
   const int red_bytes = dev::kMaxSlots * T * nseg * 2 * 4;
-  const int fixed = 2 * dev::kMaxSlots * 8 + red_bytes + 128;
+  const int fixed = dev::kPipeBarrierWords * 8 + red_bytes + 128;
   int slots = std::min(dev::kMaxSlots, (kSmemBudget - fixed) / stage_bytes);
   if (slots < 2) return false;
   L->rows = rows;
@@ -95,7 +95,7 @@ bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per
 }
 
 size_t pipe_smem_bytes(const RowLayoutHost& L) {
-  size_t off = 2 * dev::kMaxSlots * sizeof(uint64_t) +
+  size_t off = dev::kPipeBarrierWords * sizeof(uint64_t) +
                static_cast<size_t>(L.nslots) * L.tstage * L.nseg * 2 * sizeof(float);
   off = (off + 127) & ~static_cast<size_t>(127);
   return off + static_cast<size_t>(L.nslots) * L.stage_bytes;
@@ -124,10 +124,21 @@ int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s,
                      float* y, cudaStream_t stream, int device, const DeviceProps& props) {
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
-  void* ws = nullptr;
-  OBJB_TRY(workspace_get(device, stream, ximage_quads<RD>(L) * 16, &ws));
-  uint4* img = static_cast<uint4*>(ws);
-  OBJB_TRY(launch_ximage<RD>(L, x, 0, 1, img, 0, stream));
+  // The kernel forms its x registers itself when x is 16-byte aligned; a
+  // digit image only up to 128 blocks (4096 columns), where building it in
+  // every CTA hides under the first stage's copy, and when it fits in one
+  // ring slot.  Otherwise an ximage launch goes first.
+  constexpr int kInlineDigitBlocks = 128;
+  const bool inline_x = aligned16(x) && (!dev::IsDigitRD<RD>::value ||
+                                         (L.nblocks <= kInlineDigitBlocks && L.nslots >= 2 &&
+                                          ximage_quads<RD>(L) * 16 <= static_cast<size_t>(L.stage_bytes)));
+  uint4* img = nullptr;
+  if (!inline_x) {
+    void* ws = nullptr;
+    OBJB_TRY(workspace_get(device, stream, ximage_quads<RD>(L) * 16, &ws));
+    img = static_cast<uint4*>(ws);
+    OBJB_TRY(launch_ximage<RD>(L, x, 0, 1, img, 0, stream));
+  }
   // Rows split evenly over the SMs in whole 4-row batches (a CTA's last
   // stage may be short), so every SM streams the same number of bytes.
   int per_cta = (L.rows + props.sm_count - 1) / props.sm_count;
@@ -136,6 +147,7 @@ int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s,
   dev::GemvProg prog;
   prog.src = dev::StageSource{w, s, nullptr, nullptr};
   prog.ximg = img;
+  prog.x = inline_x ? x : nullptr;
   prog.y = y;
   prog.rows = L.rows;
   prog.rows_per_cta = per_cta;

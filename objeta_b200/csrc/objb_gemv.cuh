@@ -14,6 +14,8 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
+#include <utility>
 
 #include "objb_decode.cuh"
 #include "objb_pipe.cuh"
@@ -43,17 +45,23 @@ struct RowLayout {
 struct SmemPlan {
   uint64_t* full;
   uint64_t* empty;
+  uint64_t* img_done;  // every consumer warp holds its x registers (in-kernel x images)
   float* red;      // [nslots][tstage][nseg][2]
   uint8_t* stage;  // [nslots][stage_bytes]
 };
+
+// 64-bit barrier words at the start of the pipelined kernel's shared memory
+// (full and empty per slot, img_done, one word of padding).
+constexpr int kPipeBarrierWords = 2 * kMaxSlots + 2;
 
 __device__ __forceinline__ SmemPlan carve_smem(uint8_t* base, const RowLayout& L, int nred) {
   SmemPlan p;
   p.full = reinterpret_cast<uint64_t*>(base);
   p.empty = p.full + kMaxSlots;
-  p.red = reinterpret_cast<float*>(base + 2 * kMaxSlots * sizeof(uint64_t));
+  p.img_done = p.empty + kMaxSlots;
+  p.red = reinterpret_cast<float*>(base + kPipeBarrierWords * sizeof(uint64_t));
   size_t red_bytes = static_cast<size_t>(L.nslots) * L.tstage * L.nseg * nred * sizeof(float);
-  size_t off = 2 * kMaxSlots * sizeof(uint64_t) + red_bytes;
+  size_t off = kPipeBarrierWords * sizeof(uint64_t) + red_bytes;
   off = (off + 127) & ~static_cast<size_t>(127);
   p.stage = base + off;
   return p;
@@ -251,6 +259,132 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
   }
 }
 
+// In-kernel x images.  A plain GEMV whose x is 16-byte aligned forms its x
+// registers inside the pipelined kernel, after its griddepcontrol.wait,
+// instead of behind a separate ximage launch: one grid completion less on the
+// path of every call.  Float tiles load their quads straight from x.  Digit
+// tiles are built by the consumer threads together, four threads per 32-value
+// block, to the same bits as ximage_digits_kernel, into the shared memory of
+// the ring's last slot; the producer
+// holds that slot's first copy until every consumer warp has its registers.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Quarter Q of block B of lane tile lt (groups 2Q, 2Q + 1 of the block: 8 of
+// its elements; the four quarters of a block are consecutive lanes of one
+// warp, `gmask` those four lanes).  For a block of finite values, x * 2^(20-E)
+// is one or two exact power-of-two products and the rounding to an integer
+// (|value| < 2^21) one magic-number addition, both equal to ldexpf and
+// __float2int_rn; a block holding NaN or Inf takes those functions as is.
+template <int FMT>
+__device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool live, int B, int Q, unsigned gmask,
+                                              int lt, int ntp, uint32_t* img) {
+  using T = Tile<FMT>;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = live ? __ldg(xb + T::elem(B, 2 * Q + (i >> 2), i & 3)) : 0.0f;
+  float m = fabsf(v[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = max_nan(m, fabsf(v[i]));
+  m = max_nan(m, __shfl_xor_sync(gmask, m, 1));
+  m = max_nan(m, __shfl_xor_sync(gmask, m, 2));
+  int X[8];
+  int E = 0;
+  if (m < INFINITY) {  // no NaN (max.NaN would carry it) and no Inf in the block
+    frexpf(m, &E);     // m < 2^E (E = 0 for m = 0)
+    const int k = 20 - E, k1 = min(k, 127);
+    const float s1 = __int_as_float((k1 + 127) << 23), s2 = __int_as_float((k - k1 + 127) << 23);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) X[i] = __float_as_int((v[i] * s1) * s2 + 12582912.0f) - 0x4B400000;
+  } else {
+    m = fabsf(v[0]);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(gmask, m, 2));
+    frexpf(m, &E);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) X[i] = __float2int_rn(ldexpf(v[i], 20 - E));
+  }
+  uint32_t sx = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sx += static_cast<uint32_t>(X[i]);
+  sx += __shfl_xor_sync(gmask, sx, 1);
+  sx += __shfl_xor_sync(gmask, sx, 2);
+  auto put = [&](int widx, uint32_t val) { img[(static_cast<size_t>(widx >> 2) * ntp + lt) * 4 + (widx & 3)] = val; };
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int Xe = X[4 * h + j];
+      const int d0 = ((Xe + 64) & 127) - 64;
+      const int X1 = (Xe - d0) / 128;
+      const int d1 = ((X1 + 64) & 127) - 64;
+      const int d2 = (X1 - d1) / 128;
+      w0 |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * j);
+      w1 |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * j);
+      w2 |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * j);
+    }
+    put(dg_word(B, 2 * Q + h, 0), w0);
+    put(dg_word(B, 2 * Q + h, 1), w1);
+    put(dg_word(B, 2 * Q + h, 2), w2);
+  }
+  if (Q == 0) {
+    put(48 + B, __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000)));
+    put(50 + B, static_cast<uint32_t>(-T::kOffset) * sx);
+  }
+}
+
+// Item i (< ntp * 8) of a digit image: quarter i % 4 of block i / 4.
+template <int FMT>
+__device__ __forceinline__ void build_digit_item(const float* __restrict__ x, int item, int nblocks, int ntp,
+                                                 uint32_t* img) {
+  static_assert(Tile<FMT>::P == 2, "digit tiles hold two blocks");
+  const int gb = item >> 2, lt = gb >> 1;
+  const bool live = gb < nblocks;
+  const float* xb = x + static_cast<size_t>(live ? gb : 0) * 32;
+  const unsigned gmask = 0xFu << (threadIdx.x & 28);
+  digit_quarter<FMT>(xb, live, gb & 1, item & 3, gmask, lt, ntp, img);
+}
+
+// Float tiles: quad q of lane tile lt is x[c .. c + 3], c = RD::quad_col.
+template <class RD, class XR>
+__device__ __forceinline__ void load_x_direct(const RowLayout& L, const float* __restrict__ x, int lt, XR& xr) {
+#pragma unroll
+  for (int q = 0; q < XR::kQuads; ++q) {
+    const int c = RD::quad_col(L, lt, q);
+    xr.q[q] = c >= 0 ? __ldg(reinterpret_cast<const uint4*>(x + c)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <class RD, class = void>
+struct HasQuadCol : std::false_type {};
+template <class RD>
+struct HasQuadCol<RD, std::void_t<decltype(&RD::quad_col)>> : std::true_type {};
+
+template <class XR>
+__device__ __forceinline__ void load_ximage_shared(const uint32_t* img, int ntp, int lt, XR& xr) {
+#pragma unroll
+  for (int q = 0; q < XR::kQuads; ++q) xr.q[q] = *reinterpret_cast<const uint4*>(img + (q * ntp + lt) * 4);
+}
+
+// Programs whose x registers the kernel forms itself name the vector in a
+// member `x` (nullptr: the images come from a preceding ximage launch).
+template <class P, class = void>
+struct ProgInlineX {
+  static constexpr bool value = false;
+  __device__ __forceinline__ static const float* get(const P&) { return nullptr; }
+};
+template <class P>
+struct ProgInlineX<P, std::void_t<decltype(std::declval<const P&>().x)>> {
+  static constexpr bool value = true;
+  __device__ __forceinline__ static const float* get(const P& p) { return p.x; }
+};
+
 // Reduces NV per-lane values over the 32 lanes of a warp with a transposed
 // butterfly: log2(NV) exchange steps that halve the value set, then plain
 // xor-shuffle steps.  Afterwards v[0] of lane L holds the full sum of value
@@ -356,11 +490,17 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
       mbar_init(&sp.full[i], 1);
       mbar_init(&sp.empty[i], ncw);
     }
+    mbar_init(sp.img_done, ncw);
     fence_mbar_init();
   }
   __syncthreads();
 
   const int njobs = prog.njobs(cta);
+  // (row formats whose x registers are x quads or a digit image only)
+  constexpr bool kInlineX = ProgInlineX<Prog>::value && (IsDigitRD<RD>::value || HasQuadCol<RD>::value);
+  const float* xin = kInlineX ? ProgInlineX<Prog>::get(prog) : nullptr;
+  // in-kernel digit image: built in the last slot before that slot's first copy
+  const bool img_in_ring = xin != nullptr && IsDigitRD<RD>::value;
 
   if (warp == ncw) {
     // ---------------- producer: one elected thread issues every stage.
@@ -374,6 +514,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
           const int slot = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S)) {
             if (!mbar_wait_bounded(&sp.empty[slot], ((it / S) - 1) & 1u, err, kErrEmptyWaitTimeout)) {
+              ok = false;
+              break;
+            }
+          } else if (img_in_ring && it == static_cast<uint32_t>(S - 1)) {
+            if (!mbar_wait_bounded(sp.img_done, 0u, err, kErrEmptyWaitTimeout)) {
               ok = false;
               break;
             }
@@ -406,12 +551,31 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
   rd.init(L, seg, lane);
   typename RD::XRegs xr;
   const int part = slot_part_bytes(L);
-  // x images are written by the preceding ximage_kernel (programmatic launch).
+  // x (or its image, written by the preceding ximage launch) may come from
+  // the kernel this one was launched behind (programmatic launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (kInlineX) {
+    if (xin != nullptr) {
+      const int ntp = L.nseg * 32;
+      if constexpr (IsDigitRD<RD>::value) {
+        uint32_t* img = reinterpret_cast<uint32_t*>(sp.stage + static_cast<size_t>(S - 1) * L.stage_bytes);
+        for (int item = threadIdx.x; item < ntp * 8; item += nthr)
+          build_digit_item<IsDigitRD<RD>::fmt>(xin, item, L.nblocks, ntp, img);
+        named_bar_sync(1, nthr);
+        load_ximage_shared(img, ntp, seg * 32 + lane, xr);
+        // the slot's bulk copies (async proxy) come after these accesses
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sp.img_done);
+      } else if constexpr (HasQuadCol<RD>::value) {
+        load_x_direct<RD>(L, xin, seg * 32 + lane, xr);
+      }
+    }
+  }
 
   for (int j = 0; j < njobs; ++j) {
     const Job J = prog.job(cta, j);
-    load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
+    if (xin == nullptr) load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
       if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout);
@@ -454,10 +618,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
   prog.finalize(cta, threadIdx.x, nthr);
 }
 
-// Plain GEMV: each CTA owns `rows_per_cta` consecutive rows.
+// Plain GEMV: each CTA owns `rows_per_cta` consecutive rows.  x != nullptr:
+// the kernel forms its x registers from x itself (ximg unused).
 struct GemvProg {
   StageSource src;
   const uint4* ximg;
+  const float* x;
   float* y;
   int rows;
   int rows_per_cta;

@@ -259,6 +259,7 @@ int gemv_fp8_fp4(const uint8_t* act, const uint8_t* act_s, const uint8_t* w, con
   dev::GemvProg prog;
   prog.src = dev::StageSource{w, ws, nullptr, nullptr};
   prog.ximg = img;
+  prog.x = nullptr;
   prog.y = y;
   prog.rows = rows;
   prog.rows_per_cta = per;

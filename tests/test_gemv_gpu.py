@@ -198,6 +198,44 @@ def test_fallback_misaligned_and_ragged(cuda_device, fmt):
         assert q.size == rows * cols // 32 * bb
 
 
+@pytest.mark.parametrize("fmt", FORMATS + ["split"])
+def test_inline_x_matches_ximage_launch(cuda_device, fmt):
+    """With x 16-byte aligned the GEMV kernel forms its x registers itself
+    (digit images built in shared memory, float quads loaded from x); with x
+    misaligned an ximage launch builds them first.  Both give the same bits,
+    including blocks of zeros, tiny and huge magnitudes, Inf and NaN."""
+    torch = _torch()
+    from objeta_b200.quant import gemv_device, gemv_fp4_split_device
+    for rows, cols in [(4096, 4096), (300, 14336), (64, 2048), (7, 96)]:
+        rng = np.random.default_rng(rows + cols)
+        x = rng.standard_normal(cols).astype(np.float32)
+        x[32:64] = 0.0
+        x[64:96] *= 1e-39
+        if cols >= 512:
+            x[96:128] *= 1e30
+            x[130] = np.inf
+            x[200] = np.nan
+        if fmt == "split":
+            w = torch.from_numpy(rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)).cuda()
+            sc = torch.from_numpy(rng.integers(119, 124, rows * cols // 32, dtype=np.uint8)).cuda()
+            run = lambda xv, y: gemv_fp4_split_device(w, sc, xv, y, rows, cols)
+        else:
+            m = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+            q = torch.from_numpy(O.quantize_matrix(fmt, m, rows, cols)).cuda()
+            run = lambda xv, y: gemv_device(fmt, q, xv, y, rows, cols)
+        xa = torch.from_numpy(x).cuda()
+        assert xa.data_ptr() % 16 == 0
+        buf = torch.zeros(cols + 4, device="cuda")
+        buf[1:1 + cols] = xa
+        xm = buf[1:1 + cols]
+        ya = torch.empty(rows, device="cuda")
+        ym = torch.empty(rows, device="cuda")
+        run(xa, ya)
+        run(xm, ym)
+        torch.cuda.synchronize()
+        assert torch.equal(ya.view(torch.int32), ym.view(torch.int32)), (fmt, rows, cols)
+
+
 def test_gemv_is_deterministic(cuda_device):
     torch = _torch()
     dq, dx, dy = _device_case(O.Q4_0, 14336, 4096, seed=5)
