@@ -81,15 +81,19 @@ int gemv_bf16(const void* w, const float* x, float* y, int rows, int cols, cudaS
   }
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
-  void* ws = nullptr;
-  OBJB_TRY(workspace_get(device, stream, ximage_quads<dev::RowDotBf16>(L) * 16, &ws));
-  uint4* img = static_cast<uint4*>(ws);
-  OBJB_TRY(launch_ximage<dev::RowDotBf16>(L, x, 0, 1, img, 0, stream));
+  const bool x_inline = inline_x_ok<dev::RowDotBf16>(L, x);
+  uint4* img = nullptr;
+  if (!x_inline) {
+    void* ws = nullptr;
+    OBJB_TRY(workspace_get(device, stream, ximage_quads<dev::RowDotBf16>(L) * 16, &ws));
+    img = static_cast<uint4*>(ws);
+    OBJB_TRY(launch_ximage<dev::RowDotBf16>(L, x, 0, 1, img, 0, stream));
+  }
   int grid = 0;
   dev::GemvProg prog;
   prog.src = dev::StageSource{static_cast<const uint8_t*>(w), nullptr, nullptr, nullptr};
   prog.ximg = img;
-  prog.x = nullptr;
+  prog.x = x_inline ? x : nullptr;
   prog.y = y;
   prog.rows = rows;
   prog.rows_per_cta = even_split(rows, props.sm_count, &grid);
@@ -142,12 +146,16 @@ int ffn_bf16(const void* gate, const void* up, const void* down, int H, int I, i
   }
   uint4* imgx = reinterpret_cast<uint4*>(sc + act_bytes);
   uint4* imga = imgx + ximage_quads<dev::RowDotBf16>(lg);
-  OBJB_TRY(launch_ximage<dev::RowDotBf16>(lg, x, 0, 1, imgx, 0, stream));
+  // the kernels read x and the activation row directly (float quads) when aligned
+  const bool x_inline = inline_x_ok<dev::RowDotBf16>(lg, x);
+  const bool act_inline = inline_x_ok<dev::RowDotBf16>(ld, act);
+  if (!x_inline) OBJB_TRY(launch_ximage<dev::RowDotBf16>(lg, x, 0, 1, imgx, 0, stream));
   {
     int grid = 0;
     dev::FfnGateUpProg prog;
     prog.src = dev::StageSource{static_cast<const uint8_t*>(gate), nullptr, static_cast<const uint8_t*>(up), nullptr};
     prog.ximg = imgx;
+    prog.x = x_inline ? x : nullptr;
     prog.act = act;
     prog.I = I;
     prog.rows_per_cta = even_split(I, props.sm_count, &grid);
@@ -160,12 +168,13 @@ int ffn_bf16(const void* gate, const void* up, const void* down, int H, int I, i
     std::memcpy(&dl, &lg, sizeof(dl));
     OBJB_TRY(launch_pdl(kernel, grid, (lg.nseg * lg.ngrp + 1) * 32, smem, stream, dl, prog));
   }
-  OBJB_TRY(launch_ximage<dev::RowDotBf16>(ld, act, 0, 1, imga, 0, stream));
+  if (!act_inline) OBJB_TRY(launch_ximage<dev::RowDotBf16>(ld, act, 0, 1, imga, 0, stream));
   {
     int grid = 0;
     dev::FfnDownProg prog;
     prog.src = dev::StageSource{static_cast<const uint8_t*>(down), nullptr, nullptr, nullptr};
     prog.ximg = imga;
+    prog.x = act_inline ? act : nullptr;
     prog.out = out;
     prog.O = O;
     prog.rows_per_cta = even_split(O, props.sm_count, &grid);

@@ -124,14 +124,9 @@ int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s,
                      float* y, cudaStream_t stream, int device, const DeviceProps& props) {
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
-  // The kernel forms its x registers itself when x is 16-byte aligned; a
-  // digit image only up to 128 blocks (4096 columns), where building it in
-  // every CTA hides under the first stage's copy, and when it fits in one
-  // ring slot.  Otherwise an ximage launch goes first.
-  constexpr int kInlineDigitBlocks = 128;
-  const bool inline_x = aligned16(x) && (!dev::IsDigitRD<RD>::value ||
-                                         (L.nblocks <= kInlineDigitBlocks && L.nslots >= 2 &&
-                                          ximage_quads<RD>(L) * 16 <= static_cast<size_t>(L.stage_bytes)));
+  // The kernel forms its x registers itself where that pays; otherwise an
+  // ximage launch goes first.
+  const bool inline_x = inline_x_ok<RD>(L, x);
   uint4* img = nullptr;
   if (!inline_x) {
     void* ws = nullptr;

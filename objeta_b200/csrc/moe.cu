@@ -212,8 +212,9 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
   }
   uint4* imgx = reinterpret_cast<uint4*>(sc + p.act_bytes);
   uint4* imga = imgx + p.imgx_quads;
-  // gate/up
-  OBJB_TRY(launch_ximage<RD>(p.lg, x, 0, 1, imgx, 0, stream));
+  // gate/up (the kernel forms the x registers itself where that pays)
+  const bool x_inline = inline_x_ok<RD>(p.lg, x);
+  if (!x_inline) OBJB_TRY(launch_ximage<RD>(p.lg, x, 0, 1, imgx, 0, stream));
   {
     const int total = s.K * s.I;
     const int T = p.lg.tstage;
@@ -224,6 +225,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     prog.t = t;
     prog.ids = ids;
     prog.ximg = imgx;
+    prog.x = x_inline ? x : nullptr;
     prog.act = act;
     prog.K = s.K;
     prog.I = s.I;
@@ -238,8 +240,9 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
   }
   if (mid) OBJB_CUDA(cudaEventRecord(mid, stream), "record gate/up end");
-  // down + combine
-  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), s.K, imga, p.imga_quads, stream));
+  // down + combine (float-quad rows read the activations directly)
+  const bool act_direct = direct_x_ok<RD>(act, static_cast<size_t>(s.I));
+  if (!act_direct) OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), s.K, imga, p.imga_quads, stream));
   {
     const int T = p.ld.tstage;
     int R = (s.O + props.sm_count - 1) / props.sm_count;
@@ -251,6 +254,8 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     prog.weights = weights;
     prog.ximg = imga;
     prog.img_stride = p.imga_quads;
+    prog.xf = act_direct ? act : nullptr;
+    prog.xf_stride = static_cast<size_t>(s.I);
     prog.out = out;
     prog.K = s.K;
     prog.O = s.O;
@@ -306,7 +311,10 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
   }
   uint4* imgx = reinterpret_cast<uint4*>(sc + p.act_bytes);
   uint4* imga = imgx + p.imgx_quads * T;
-  OBJB_TRY(launch_ximage<RD>(p.lg, x, static_cast<size_t>(s.H), T, imgx, p.imgx_quads, stream));
+  // float-quad rows read the token and activation rows directly
+  const bool x_direct = direct_x_ok<RD>(x, static_cast<size_t>(s.H));
+  const bool act_direct = direct_x_ok<RD>(act, static_cast<size_t>(s.I));
+  if (!x_direct) OBJB_TRY(launch_ximage<RD>(p.lg, x, static_cast<size_t>(s.H), T, imgx, p.imgx_quads, stream));
   {
     const int total = P * s.I;
     int R = (total + props.sm_count - 1) / props.sm_count;
@@ -319,6 +327,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.pair_token = pair_token;
     prog.ximg = imgx;
     prog.img_stride = p.imgx_quads;
+    prog.xf = x_direct ? x : nullptr;
+    prog.xf_stride = static_cast<size_t>(s.H);
     prog.act = act;
     prog.P = P;
     prog.I = s.I;
@@ -334,7 +344,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     std::memcpy(&dl, &p.lg, sizeof(dl));
     OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
   }
-  OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream, d_count));
+  if (!act_direct)
+    OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream, d_count));
   {
     const int total = P * s.O;
     int R = (total + props.sm_count - 1) / props.sm_count;
@@ -346,6 +357,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.pair_out = pair_out;
     prog.ximg = imga;
     prog.img_stride = p.imga_quads;
+    prog.xf = act_direct ? act : nullptr;
+    prog.xf_stride = static_cast<size_t>(s.I);
     prog.v = v;
     prog.P = P;
     prog.O = s.O;

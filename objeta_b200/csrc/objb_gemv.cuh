@@ -366,6 +366,29 @@ struct HasQuadCol : std::false_type {};
 template <class RD>
 struct HasQuadCol<RD, std::void_t<decltype(&RD::quad_col)>> : std::true_type {};
 
+// Row formats whose x registers are plain float quads of x.
+template <class RD>
+struct IsFloatRD {
+  static constexpr bool value = HasQuadCol<RD>::value && !IsDigitRD<RD>::value;
+};
+
+// Float-quad rows whose direct x loads are near-coalesced (neighbouring lanes
+// read quads at most 32 bytes apart): worth reading a fresh vector per job.
+template <class RD>
+struct NearCoalescedQuads : std::false_type {};
+template <>
+struct NearCoalescedQuads<RowDotBf16> : std::true_type {};
+
+// Float-quad rows for which one direct read of x per CTA beats an image
+// launch (measured on B200): bf16 rows and interleaved FP4 tiles; split FP4
+// rows read 128-byte-strided quads and keep the image launch.
+template <class RD>
+struct DirectQuadsOnce : std::false_type {};
+template <>
+struct DirectQuadsOnce<RowDotBf16> : std::true_type {};
+template <>
+struct DirectQuadsOnce<RowDot<OBJB_FP4_E2M1>> : std::true_type {};
+
 template <class XR>
 __device__ __forceinline__ void load_ximage_shared(const uint32_t* img, int ntp, int lt, XR& xr) {
 #pragma unroll
@@ -457,6 +480,7 @@ struct Job {
   StageSource src;
   const uint4* ximg;  // x image of this job's vector
   int row_begin, row_end;
+  const float* x = nullptr;  // float-quad rows: this job's vector, read directly (ximg unused)
 };
 
 // Consumer warps: nseg * ngrp (<= kMaxConsumerWarps); one producer warp more.
@@ -575,7 +599,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
 
   for (int j = 0; j < njobs; ++j) {
     const Job J = prog.job(cta, j);
-    if (xin == nullptr) load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
+    if constexpr (IsFloatRD<RD>::value) {
+      if (J.x != nullptr) load_x_direct<RD>(L, J.x, seg * 32 + lane, xr);
+      else if (xin == nullptr) load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
+    } else if (xin == nullptr) {
+      load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
+    }
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
       if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout);
@@ -623,7 +652,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
 struct GemvProg {
   StageSource src;
   const uint4* ximg;
-  const float* x;
+  const float* x = nullptr;
   float* y;
   int rows;
   int rows_per_cta;

@@ -68,6 +68,30 @@ size_t ximage_quads(const RowLayoutHost& L) {
   return static_cast<size_t>(RD::XRegs::kQuads) * L.nseg * 32;
 }
 
+// Whether the pipelined kernel forms the x registers of ONE vector x itself
+// (a program-level x): float quads straight from x (16-byte aligned) for the
+// row formats where that beats the image launch, or a digit image built in
+// every CTA, which only pays up to 128 blocks (4096 columns: it hides under
+// the first stage's copy) and must fit one ring slot.
+template <class RD>
+bool inline_x_ok(const RowLayoutHost& L, const float* x) {
+  constexpr int kInlineDigitBlocks = 128;
+  if (!aligned16(x)) return false;
+  if (dev::IsFloatRD<RD>::value) return dev::DirectQuadsOnce<RD>::value;
+  return dev::IsDigitRD<RD>::value && L.nblocks <= kInlineDigitBlocks && L.nslots >= 2 &&
+         ximage_quads<RD>(L) * 16 <= static_cast<size_t>(L.stage_bytes);
+}
+
+// Whether each job may read its own float vector base + i * stride directly:
+// float-quad rows whose lanes read near-coalesced quads (for the others a
+// per-job read costs more than the image launch it saves), every vector
+// 16-byte aligned.
+template <class RD>
+bool direct_x_ok(const float* base, size_t stride_floats) {
+  return dev::IsFloatRD<RD>::value && dev::NearCoalescedQuads<RD>::value && aligned16(base) &&
+         stride_floats % 4 == 0;
+}
+
 
 
 }  // namespace objb

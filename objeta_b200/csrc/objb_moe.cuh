@@ -55,6 +55,7 @@ struct GateUpProg {
   ExpertTables t;
   const int32_t* ids;
   const uint4* ximg;
+  const float* x = nullptr;  // != nullptr: the kernel forms the x registers itself (ximg unused)
   float* act;  // [K][I]
   int K, I;
   int rows_per_cta;
@@ -101,6 +102,8 @@ struct DownProg {
   const float* weights;
   const uint4* ximg;  // K images, img_stride quads apart
   size_t img_stride;
+  const float* xf = nullptr;  // float-quad rows: the K activations, xf_stride floats apart
+  size_t xf_stride = 0;
   float* out;
   int K, O;
   int rows_per_cta;
@@ -115,6 +118,7 @@ struct DownProg {
     J.src.wb = nullptr;
     J.src.sb = nullptr;
     J.ximg = ximg + j * img_stride;
+    J.x = xf ? xf + static_cast<size_t>(j) * xf_stride : nullptr;
     J.row_begin = cta * rows_per_cta;
     J.row_end = min(O, J.row_begin + rows_per_cta);
     return J;
@@ -154,6 +158,8 @@ struct GateUpPairsProg {
   const int32_t* pair_token;
   const uint4* ximg;  // T token images, img_stride quads apart
   size_t img_stride;
+  const float* xf = nullptr;  // float-quad rows: the T tokens, xf_stride floats apart
+  size_t xf_stride = 0;
   float* act;  // [P][I]
   int P, I, T;
   int rows_per_cta;  // 0: derived in the kernel from *count
@@ -182,6 +188,7 @@ struct GateUpPairsProg {
     J.src.sa = t.gate_scale ? t.gate_scale[e] : nullptr;
     J.src.sb = t.up_scale ? t.up_scale[e] : nullptr;
     J.ximg = ximg + static_cast<size_t>(tok) * img_stride;
+    J.x = xf ? xf + static_cast<size_t>(tok) * xf_stride : nullptr;
     J.row_begin = max(a, p * I) - p * I;
     J.row_end = min(b, (p + 1) * I) - p * I;
     return J;
@@ -200,6 +207,8 @@ struct DownPairsProg {
   const int32_t* pair_out;  // nullptr: row p
   const uint4* ximg;        // P activation images, img_stride quads apart
   size_t img_stride;
+  const float* xf = nullptr;  // float-quad rows: the P activations, xf_stride floats apart
+  size_t xf_stride = 0;
   float* v;                 // [v_rows][O]
   int P, O, v_rows;
   int rows_per_cta;         // 0: derived in the kernel from *count
@@ -226,6 +235,7 @@ struct DownPairsProg {
     J.src.wb = nullptr;
     J.src.sb = nullptr;
     J.ximg = ximg + static_cast<size_t>(p) * img_stride;
+    J.x = xf ? xf + static_cast<size_t>(p) * xf_stride : nullptr;
     J.row_begin = max(a, p * O) - p * O;
     J.row_end = min(b, (p + 1) * O) - p * O;
     return J;
@@ -261,6 +271,7 @@ static __global__ void __launch_bounds__(256) combine_kernel(const float* __rest
 struct FfnGateUpProg {
   StageSource src;  // wa = gate, wb = up
   const uint4* ximg;
+  const float* x = nullptr;  // != nullptr: the kernel forms the x registers itself (ximg unused)
   float* act;
   int I;
   int rows_per_cta;
@@ -284,6 +295,7 @@ struct FfnGateUpProg {
 struct FfnDownProg {
   StageSource src;  // wa = down
   const uint4* ximg;
+  const float* x = nullptr;  // != nullptr: the kernel forms the x registers itself (ximg unused)
   float* out;
   int O;
   int rows_per_cta;
