@@ -120,12 +120,13 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
   return __int2float_rn(T) * (scale * __uint_as_float(xr.w(48 + b)));
 }
 
-// Four bits (positions 0, 2, 4, 6 of hb) to the low bit of four bytes: the
-// product puts bit 2j at 8j; the other partial products land off the byte
-// boundaries and never carry into them.
-__device__ __forceinline__ uint32_t spread_even4(uint32_t hb) {
-  return ((hb & 0x55u) * 0x41041u) & 0x01010101u;
-}
+// Q5_0 high bits onto bit 4 of the code bytes: bits 0, 2, 4, 6 of hb (the
+// low-nibble elements) -> bits 4, 12, 20, 28, and bits 1, 3, 5, 7 (the
+// high-nibble elements) -> the same positions.  One multiply each: the
+// partial products off the targets never carry into them (checked for every
+// hb), and the mask keeps the targets only.
+__device__ __forceinline__ uint32_t q5_high_even(uint32_t hb) { return ((hb & 0x55u) * 0x410410u) & 0x10101010u; }
+__device__ __forceinline__ uint32_t q5_high_odd(uint32_t hb) { return ((hb & 0xAAu) * 0x208208u) & 0x10101010u; }
 // 16 bits to the even bits of a word (bit i -> bit 2i).
 __device__ __forceinline__ uint32_t spread2_16(uint32_t v) {
   v &= 0xFFFFu;
@@ -221,8 +222,8 @@ struct Tile<OBJB_Q5_0> {
         // high bits of the 8 elements of this decode word, element order
         const uint32_t hb = (b == 0 && uu == 0) ? __funnelshift_r(qh[0], qh[0], 28)
                                                 : (qh[b] >> (b == 0 ? 4 + 8 * (uu - 1) : 8 * uu));
-        qb[2 * uu] = (d & 0x0F0F0F0Fu) + (spread_even4(hb) << 4);
-        qb[2 * uu + 1] = ((d >> 4) & 0x0F0F0F0Fu) + (spread_even4(hb >> 1) << 4);
+        qb[2 * uu] = (d & 0x0F0F0F0Fu) | q5_high_even(hb);
+        qb[2 * uu + 1] = ((d >> 4) & 0x0F0F0F0Fu) | q5_high_odd(hb);
       }
       r += digit_block(qb, xr, b, b ? s1 : s0);
     }
