@@ -127,15 +127,6 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
 // hb), and the mask keeps the targets only.
 __device__ __forceinline__ uint32_t q5_high_even(uint32_t hb) { return ((hb & 0x55u) * 0x410410u) & 0x10101010u; }
 __device__ __forceinline__ uint32_t q5_high_odd(uint32_t hb) { return ((hb & 0xAAu) * 0x208208u) & 0x10101010u; }
-// 16 bits to the even bits of a word (bit i -> bit 2i).
-__device__ __forceinline__ uint32_t spread2_16(uint32_t v) {
-  v &= 0xFFFFu;
-  v = (v | (v << 8)) & 0x00FF00FFu;
-  v = (v | (v << 4)) & 0x0F0F0F0Fu;
-  v = (v | (v << 2)) & 0x33333333u;
-  v = (v | (v << 1)) & 0x55555555u;
-  return v;
-}
 
 // Nibble formats (Q4_0 / Q5_0) share the decode-word layout: in a tile the
 // eight decode words are m = [qs0[14], qs0[15], qs0[0], qs0[1]] (a byte
@@ -237,9 +228,10 @@ struct Tile<OBJB_Q5_0> {
 //   w0 = [s0, L0 b0 b1]  w1 = L0 b2..b5  w2 = [L0 b6 b7, H0 b0 b1]
 //   w3 = [H0 b2 b3, s1]  w4, w5 = L1  w6 = H1
 // A 32-bit word of lows holds 16 elements; (lw >> 2c) & 0x03030303 are
-// elements 4j + c.  The highs are first spread to even bits (element e at
-// bit 2e) so the same shift brings them next to their lows.  Group
-// g = 4 * hh + c (hh: which 16 elements).
+// elements 4j + c.  The 16 highs of those elements are first moved nibble by
+// nibble into bytes (elements 4j .. 4j + 3 in bits 0..3 of byte j: one byte
+// permute and one shift-or), so (hs >> c) & 0x01010101 are the highs of
+// elements 4j + c.  Group g = 4 * hh + c (hh: which 16 elements).
 template <>
 struct Tile<OBJB_IQ3_0> {
   static constexpr int P = 2;
@@ -263,13 +255,11 @@ struct Tile<OBJB_IQ3_0> {
       uint32_t qb[8];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t h2 = spread2_16(H[b] >> (16 * hh));  // element e's high at bit 2e
+        const uint32_t v = __byte_perm(H[b], 0u, hh ? 0x4342u : 0x4140u);  // [h b0, 0, h b1, 0] of this half
+        const uint32_t hs = (v | (v << 4)) & 0x0F0F0F0Fu;                    // elements 4j..4j+3 in byte j
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          // high of element 4j + c sits at bit 8j + 2c; move it to bit 8j + 2
-          const uint32_t hc = c == 0 ? (h2 << 2) : (h2 >> (2 * c - 2));
-          qb[4 * hh + c] = ((L[b][hh] >> (2 * c)) & 0x03030303u) | (hc & 0x04040404u);
-        }
+        for (int c = 0; c < 4; ++c)
+          qb[4 * hh + c] = ((L[b][hh] >> (2 * c)) & 0x03030303u) | (((hs >> c) & 0x01010101u) << 2);
       }
       r += digit_block(qb, xr, b, b ? s1 : s0);
     }
