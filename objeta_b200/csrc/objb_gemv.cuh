@@ -259,14 +259,17 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
   }
 }
 
-// In-kernel x images.  A plain GEMV whose x is 16-byte aligned forms its x
-// registers inside the pipelined kernel, after its griddepcontrol.wait,
-// instead of behind a separate ximage launch: one grid completion less on the
-// path of every call.  Float tiles load their quads straight from x.  Digit
-// tiles are built by the consumer threads together, four threads per 32-value
-// block, to the same bits as ximage_digits_kernel, into the shared memory of
-// the ring's last slot; the producer
-// holds that slot's first copy until every consumer warp has its registers.
+// In-kernel x images.  Where the host allows it (inline_x_ok / direct_x_ok)
+// the pipelined kernel forms its x registers itself, after its
+// griddepcontrol.wait, instead of behind a separate ximage launch: one grid
+// completion less on the path of every call.  Float tiles load their quads
+// straight from x.  Digit tiles are built by the consumer threads together,
+// four threads per 32-value block, to the same bits as ximage_digits_kernel,
+// into the shared memory of the ring's last slot; the producer holds that
+// slot's first copy until every consumer warp has its registers.
+
+// max with NaN propagation (PTX max.NaN): a block holding a NaN is detected
+// by the result alone.
 __device__ __forceinline__ float max_nan(float a, float b) {
   float r;
   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
