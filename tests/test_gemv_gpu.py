@@ -201,9 +201,12 @@ def test_fallback_misaligned_and_ragged(cuda_device, fmt):
 @pytest.mark.parametrize("fmt", FORMATS + ["split"])
 def test_inline_x_matches_ximage_launch(cuda_device, fmt):
     """With x 16-byte aligned the GEMV kernel forms its x registers itself
-    (digit images built in shared memory, float quads loaded from x); with x
-    misaligned an ximage launch builds them first.  Both give the same bits,
-    including blocks of zeros, tiny and huge magnitudes, Inf and NaN."""
+    (digit images up to 4096 columns built in shared memory, interleaved FP4
+    quads loaded from x); with x misaligned an ximage launch builds them
+    first.  Both give the same bits, including blocks of zeros, tiny and huge
+    magnitudes, Inf and NaN.  The 14336-column digit shapes and split FP4 rows
+    take the image launch either way (the case still checks alignment does not
+    change their bits)."""
     torch = _torch()
     from objeta_b200.quant import gemv_device, gemv_fp4_split_device
     for rows, cols in [(4096, 4096), (300, 14336), (64, 2048), (7, 96)]:
