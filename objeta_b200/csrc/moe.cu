@@ -152,6 +152,21 @@ void row_bytes(int fmt, bool split, int cols, int* rb, int* srb) {
   }
 }
 
+// Row format of the down matrix.  Split FP4 down rows take one block per
+// lane: the CTAs of the down launch own few rows per expert (O / SMs), and one
+// block per lane puts two warps on each row, so every consumer warp has a
+// batch in every stage instead of half of them idling at the stage barrier.
+template <class RD>
+struct DownRowFormat {
+  using type = RD;
+  static constexpr int kBlocksPerLane = 2;
+};
+template <>
+struct DownRowFormat<dev::RowDotSplitFp4> {
+  using type = dev::RowDotSplitFp4T<1>;
+  static constexpr int kBlocksPerLane = 1;
+};
+
 template <class RD>
 struct MoePlan {
   bool fast = false;
@@ -169,15 +184,14 @@ MoePlan<RD> plan_moe(const MoeShape& s, int fmt, bool split, bool aligned) {
   int rbh, srbh, rbi, srbi;
   row_bytes(fmt, split, s.H, &rbh, &srbh);
   row_bytes(fmt, split, s.I, &rbi, &srbi);
-  const int P = 2;
+  const int P = 2, Pd = DownRowFormat<RD>::kBlocksPerLane;
   const bool blocks_ok = split || ((s.H / 32) % P == 0 && (s.I / 32) % P == 0);
   p.fast = aligned && blocks_ok &&
            plan_rows(s.I, s.H, rbh, srbh, P, true, dev::kMaxConsumerWarps, &p.lg, kMoeSmemBudget) &&
-           plan_rows(s.O, s.I, rbi, srbi, P, false, dev::kMaxConsumerWarps, &p.ld, kMoeSmemBudget);
+           plan_rows(s.O, s.I, rbi, srbi, Pd, false, dev::kMaxConsumerWarps, &p.ld, kMoeSmemBudget);
   if (p.fast) {
     p.imgx_quads = ximage_quads<RD>(p.lg);
-    p.imga_quads = ximage_quads<RD>(p.ld);
-    p.imga_quads *= 1;  // per vector; K vectors below
+    p.imga_quads = ximage_quads<typename DownRowFormat<RD>::type>(p.ld);  // per vector
   }
   return p;
 }
@@ -241,8 +255,9 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
   }
   if (mid) OBJB_CUDA(cudaEventRecord(mid, stream), "record gate/up end");
   // down + combine (float-quad rows read the activations directly)
-  const bool act_direct = direct_x_ok<RD>(act, static_cast<size_t>(s.I));
-  if (!act_direct) OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), s.K, imga, p.imga_quads, stream));
+  using RDd = typename DownRowFormat<RD>::type;
+  const bool act_direct = direct_x_ok<RDd>(act, static_cast<size_t>(s.I));
+  if (!act_direct) OBJB_TRY(launch_ximage<RDd>(p.ld, act, static_cast<size_t>(s.I), s.K, imga, p.imga_quads, stream));
   {
     const int T = p.ld.tstage;
     int R = (s.O + props.sm_count - 1) / props.sm_count;
@@ -262,7 +277,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     prog.rows_per_cta = R;
     prog.err = err;
     const size_t smem = pipe_smem_bytes(p.ld);
-    auto kernel = dev::pipe_kernel<RD, dev::DownProg, false>;
+    auto kernel = dev::pipe_kernel<RDd, dev::DownProg, false>;
     OBJB_TRY(ensure_smem_attr(kernel, device, smem));
     dev::RowLayout dl;
     std::memcpy(&dl, &p.ld, sizeof(dl));
@@ -313,7 +328,8 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
   uint4* imga = imgx + p.imgx_quads * T;
   // float-quad rows read the token and activation rows directly
   const bool x_direct = direct_x_ok<RD>(x, static_cast<size_t>(s.H));
-  const bool act_direct = direct_x_ok<RD>(act, static_cast<size_t>(s.I));
+  using RDd = typename DownRowFormat<RD>::type;
+  const bool act_direct = direct_x_ok<RDd>(act, static_cast<size_t>(s.I));
   if (!x_direct) OBJB_TRY(launch_ximage<RD>(p.lg, x, static_cast<size_t>(s.H), T, imgx, p.imgx_quads, stream));
   {
     const int total = P * s.I;
@@ -345,7 +361,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     OBJB_TRY(launch_pdl(kernel, grid, (p.lg.nseg * p.lg.ngrp + 1) * 32, smem, stream, dl, prog));
   }
   if (!act_direct)
-    OBJB_TRY(launch_ximage<RD>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream, d_count));
+    OBJB_TRY(launch_ximage<RDd>(p.ld, act, static_cast<size_t>(s.I), P, imga, p.imga_quads, stream, d_count));
   {
     const int total = P * s.O;
     int R = (total + props.sm_count - 1) / props.sm_count;
@@ -367,7 +383,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.count = d_count;
     prog.err = err;
     const size_t smem = pipe_smem_bytes(p.ld);
-    auto kernel = dev::pipe_kernel<RD, dev::DownPairsProg, false>;
+    auto kernel = dev::pipe_kernel<RDd, dev::DownPairsProg, false>;
     OBJB_TRY(ensure_smem_attr(kernel, device, smem));
     dev::RowLayout dl;
     std::memcpy(&dl, &p.ld, sizeof(dl));

@@ -317,24 +317,14 @@ struct Tile<OBJB_FP4_E2M1> {
 
 // ------------------------------------------------------ FP4 E2M1, split
 // DeepSeek layout (moe.rs:27-35, quant.rs:368-408): weight [rows, cols/2],
-// scale [rows, cols/32].  A lane owns blocks (seg * lpr * P + j * lpr + ll),
+// scale [rows, cols/32].  A lane owns P blocks (seg * 32 * P + j * 32 + lane),
 // j < P, so consecutive lanes read consecutive 16-byte blocks (conflict-free
-// 128-bit shared loads).
-struct SplitFp4 {
-  static constexpr int P = 2;
-  using XRegs = Words<16>;
-
-  __device__ __forceinline__ static void load_x(const float* __restrict__ x, int b0, int stride,
-                                                int nblocks, XRegs& xr) {
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      const int b = b0 + j * stride;
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-        xr.set_f2(j * 16 + e, b < nblocks ? make_float2(__ldg(x + b * 32 + 2 * e), __ldg(x + b * 32 + 2 * e + 1))
-                                          : make_float2(0.f, 0.f));
-    }
-  }
+// 128-bit shared loads).  P = 2 by default; P = 1 spreads a row over twice the
+// warps (the MoE down rows, whose CTAs own few rows per expert).
+template <int P_>
+struct SplitFp4T {
+  static constexpr int P = P_;
+  using XRegs = Words<8 * P>;
 
   __device__ __forceinline__ static float dot(const uint8_t* wrow, const uint8_t* srow, int b0,
                                               int stride, int nblocks, const XRegs& xr) {
@@ -358,6 +348,7 @@ struct SplitFp4 {
     return total;
   }
 };
+using SplitFp4 = SplitFp4T<2>;
 
 // ------------------------------------------- generic block dot (fallback)
 // Reads one block straight from global memory (any alignment) and returns

@@ -103,22 +103,26 @@ struct IsDigitRD<RowDot<FMT>> {
   static constexpr int fmt = FMT;
 };
 
-struct RowDotSplitFp4 {
-  using XRegs = SplitFp4::XRegs;
+template <int P>
+struct RowDotSplitFp4T {
+  using D = SplitFp4T<P>;
+  using XRegs = typename D::XRegs;
+  static constexpr int kBlocksPerLane = P;
   int b0, nblocks;
   __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
-    b0 = seg * 32 * SplitFp4::P + lane;
+    b0 = seg * 32 * P + lane;
     nblocks = L.nblocks;
   }
   __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
     const int seg = lt / 32, lane = lt % 32;
-    const int b = seg * 32 * SplitFp4::P + lane + (q / 8) * 32;
+    const int b = seg * 32 * P + lane + (q / 8) * 32;
     return b < L.nblocks ? b * 32 + 4 * (q % 8) : -1;
   }
   __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t* srow, const XRegs& xr) const {
-    return SplitFp4::dot(wrow, srow, b0, 32, nblocks, xr);
+    return D::dot(wrow, srow, b0, 32, nblocks, xr);
   }
 };
+using RowDotSplitFp4 = RowDotSplitFp4T<2>;
 
 // Dense bf16 rows (the shared expert of a DeepSeek-style layer; not a
 // reference QuantFormat).  A lane reads 16-byte chunks (8 columns) c0 + 32 i,
