@@ -528,6 +528,21 @@ def bench_c3(qb, dev, gen, steps, warmup, peak):
             "steps": steps}
 
 
+def run_moe_config(args, local):
+    """One MoE config alone (configs[2] or configs[3]), timed as in the full
+    bench line."""
+    import torch
+    from objeta_b200 import QuantBackend
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(1234)
+    peak, _ = read_peaks()
+    steps = max(3, min(args.steps, 20))
+    if args.moe_config == "c3":
+        return {"c3_q4_stack": bench_c3(QuantBackend(local), dev, gen, steps, args.warmup, peak)}
+    return {"c4_fp4_shared": bench_c4(dev, gen, steps, args.warmup, peak)}
+
+
 def bench_c4(dev, gen, steps, warmup, peak):
     """256 split-FP4 experts (codes uniform, E8M0 scales
     2^-8..2^-4), H 4096, I 2048, router top-8 (renormalised), plus one bf16
@@ -943,6 +958,8 @@ def main():
     ap.add_argument("--experts", type=int, default=None, help="expert count for --official (default configs[3])")
     ap.add_argument("--grouped", type=int, default=None,
                     help="T: the configs[4] pairs of T tokens on the grouped tensor-core path and the CUDA-core path")
+    ap.add_argument("--moe-config", default=None, choices=["c3", "c4"],
+                    help="run one MoE config alone (a few GB on the device: small enough for an ncu capture)")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
@@ -956,6 +973,9 @@ def main():
         return
     if args.official:
         print(json.dumps(run_official(args, local)), flush=True)
+        return
+    if args.moe_config:
+        print(json.dumps(run_moe_config(args, local)), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, world, rank)
