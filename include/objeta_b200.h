@@ -171,6 +171,19 @@ int objb_gemv_fp4_split_device(const void *d_weight, const void *d_scale,
                                const float *d_x, float *d_y, size_t rows,
                                size_t cols, objb_stream_t stream);
 
+/* Diagnostics (no reference counterpart; host arithmetic only, no GPU needed):
+ * how the pipelined kernel streams a rows x cols matrix of `fmt` (split_fp4:
+ * the DeepSeek split layout) with `blocks_per_lane` 32-column blocks per lane
+ * (2; 1 for split FP4 rows), one matrix or a gate/up pair (dual), as a plain
+ * GEMV (moe_program 0) or inside the MoE / FFN programs (1).  out[0..8] =
+ * column segments (warps per row), row groups, rows per stage, ring slots,
+ * bytes per slot, dynamic shared memory, rows per stage that keep every row
+ * group busy, 1 if a 16-byte aligned x (one vector per launch) is formed
+ * inside the kernel instead of by an x-image launch, the ring budget in bytes.
+ * OBJB_ERR_UNSUPPORTED: the shape takes the fallback kernel. */
+int objb_pipe_plan_info(int fmt, int split_fp4, size_t rows, size_t cols, int blocks_per_lane, int dual,
+                        int moe_program, int32_t *out, int nout);
+
 /* Dense bf16 GEMV (no QuantFormat in the reference; the shared expert of a
  * DeepSeek-style layer): y[rows] = W x with W bf16 [rows, cols] row-major,
  * widened to f32 as the reference's bf16 conversion does (objeta-parser

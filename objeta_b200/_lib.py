@@ -88,6 +88,8 @@ _SIGS = {
     "objb_gemv_fp4_split_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size, c_size,
                                            c_void_p]),
     "objb_gemv_bf16_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_void_p]),
+    "objb_pipe_plan_info": (c_int, [c_int, c_int, c_size, c_size, c_int, c_int, c_int,
+                                    ctypes.POINTER(ctypes.c_int32), c_int]),
     "objb_compare_outputs": (c_int, [c_void_p, c_size, c_void_p, c_size, c_void_p]),
     "objb_act_quant_device": (c_int, [c_void_p, c_size, c_size, c_void_p, c_void_p, c_void_p]),
     "objb_gemv_fp8_fp4_device": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size, c_size,

@@ -280,6 +280,38 @@ int objb_gemv_fp4_split_device(const void* d_weight, const void* d_scale, const 
                                      static_cast<cudaStream_t>(stream));
 }
 
+int objb_pipe_plan_info(int fmt, int split_fp4, size_t rows, size_t cols, int blocks_per_lane, int dual,
+                        int moe_program, int32_t* out, int nout) {
+  objb::clear_error();
+  if (!out || nout < 9) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_pipe_plan_info", "output needs 9 entries");
+  if (!objb::valid_format(fmt) || (split_fp4 && fmt != OBJB_FP4_E2M1))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_pipe_plan_info", "unknown format");
+  if (blocks_per_lane != 2 && !(blocks_per_lane == 1 && split_fp4))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_pipe_plan_info",
+                     "blocks_per_lane is 2 (1 only for split FP4 rows)");
+  if (rows == 0 || cols == 0 || cols % 32 || rows > (1u << 30) || cols > (1u << 24))
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_pipe_plan_info", "shape outside the pipelined kernel's range");
+  const int r = static_cast<int>(rows), c = static_cast<int>(cols);
+  const int rb = split_fp4 ? c / 2 : c / 32 * objb::block_bytes(fmt), srb = split_fp4 ? c / 32 : 0;
+  const int budget = moe_program ? objb::kMoeSmemBudget : objb::kGemvSmemBudget;
+  objb::RowLayoutHost L;
+  if (!objb::plan_rows(r, c, rb, srb, blocks_per_lane, dual != 0, objb::dev::kMaxConsumerWarps, &L, budget))
+    return OBJB_FAIL(OBJB_ERR_UNSUPPORTED, "objb_pipe_plan_info", "the shape cannot use the bulk-copy path");
+  // would a 16-byte aligned vector be formed in-kernel (one vector per launch)?
+  const float* aligned = reinterpret_cast<const float*>(static_cast<uintptr_t>(256));
+  bool inl = false;
+  if (split_fp4) inl = blocks_per_lane == 2 ? objb::inline_x_ok<objb::dev::RowDotSplitFp4>(L, aligned)
+                                            : objb::inline_x_ok<objb::dev::RowDotSplitFp4T<1>>(L, aligned);
+  else if (fmt == OBJB_Q4_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_Q4_0>>(L, aligned);
+  else if (fmt == OBJB_Q5_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_Q5_0>>(L, aligned);
+  else if (fmt == OBJB_IQ3_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_IQ3_0>>(L, aligned);
+  else inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_FP4_E2M1>>(L, aligned);
+  const int32_t v[9] = {L.nseg, L.ngrp, L.tstage, L.nslots, L.stage_bytes,
+                        static_cast<int32_t>(objb::pipe_smem_bytes(L)), L.ngrp * 4, inl ? 1 : 0, budget};
+  for (int i = 0; i < 9; ++i) out[i] = v[i];
+  return OBJB_OK;
+}
+
 int objb_quant_backend_new(int device, objb_quant_backend** out) {
   objb::clear_error();
   if (!out) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_quant_backend_new", "null output pointer");

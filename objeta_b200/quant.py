@@ -248,6 +248,20 @@ def gemv_bf16_device(d_w, d_x, d_y, rows, cols, stream=None):
               _lib.stream_handle(stream))
 
 
+def pipe_plan_info(fmt, rows, cols, split_fp4=False, blocks_per_lane=2, dual=False, moe_program=False):
+    """How the pipelined kernel streams a rows x cols matrix (host arithmetic,
+    no GPU): warps per row, row groups, rows per stage, ring slots, bytes per
+    slot, dynamic shared memory, the rows per stage that keep every row group
+    busy, whether an aligned x is formed in-kernel, and the ring budget."""
+    import ctypes
+    out = (ctypes.c_int32 * 9)()
+    _lib.call("objb_pipe_plan_info", int(QuantFormat(fmt)), int(bool(split_fp4)), int(rows), int(cols),
+              int(blocks_per_lane), int(bool(dual)), int(bool(moe_program)), out, 9)
+    keys = ("nseg", "ngrp", "rows_per_stage", "slots", "slot_bytes", "smem_bytes", "busy_quantum",
+            "x_in_kernel", "ring_budget")
+    return {k: int(v) for k, v in zip(keys, out)}
+
+
 def gemv_fp4_split_device(d_weight, d_scale, d_x, d_y, rows, cols, stream=None):
     _lib.call("objb_gemv_fp4_split_device", _dev_ptr(d_weight), _dev_ptr(d_scale), _dev_ptr(d_x),
               _dev_ptr(d_y), rows, cols, _lib.stream_handle(stream))
