@@ -423,10 +423,22 @@ int objb_expert_cache_insert(objb_expert_cache *cache, const objb_expert_cache_k
                              const void **d_ptr, int *resident);
 
 /* The README's get_or_insert (README.md:121-124): get, and on a miss insert;
- * counters move exactly as the executor's inline get/insert (moe.rs:508-518). */
+ * counters move exactly as the executor's inline get/insert (moe.rs:508-518).
+ * *hit = 1 on a hit (host_src is then not read). */
 int objb_expert_cache_get_or_insert(objb_expert_cache *cache, const objb_expert_cache_key *key,
                                     const void *host_src, size_t bytes, objb_stream_t stream,
                                     const void **d_ptr, int *hit);
+
+/* The same with the README's lazy `load_fn` (README.md:121-124): `load` runs
+ * only on a miss and hands back the host bytes to upload (it must keep them
+ * valid until the call returns); a nonzero return from it is passed through
+ * as this call's status with nothing inserted.  `load` runs without the
+ * cache's lock held, but the cache is externally synchronised (one owning
+ * thread): `load` must not use this cache. */
+typedef int (*objb_expert_load_fn)(void *user, const void **host_src, size_t *bytes);
+int objb_expert_cache_get_or_load(objb_expert_cache *cache, const objb_expert_cache_key *key,
+                                  objb_expert_load_fn load, void *user, objb_stream_t stream,
+                                  const void **d_ptr, int *hit);
 
 /* touch / evict_lru / pin / insert_pinned / clear / reset_counters
  * (moe.rs:156-226). evict_lru reports the evicted key in *evicted. */

@@ -300,6 +300,32 @@ int objb_expert_cache_get_or_insert(objb_expert_cache* c, const objb_expert_cach
   return insert(c, k, host_src, bytes, static_cast<cudaStream_t>(stream), d_ptr, nullptr);
 }
 
+int objb_expert_cache_get_or_load(objb_expert_cache* c, const objb_expert_cache_key* key, objb_expert_load_fn load,
+                                  void* user, objb_stream_t stream, const void** d_ptr, int* hit) {
+  CACHE_CHECK(c);
+  if (!key || !d_ptr || !load)
+    return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_expert_cache_get_or_load", "null argument");
+  const Cache::Key k = to_key(key);
+  {
+    std::lock_guard<std::mutex> lk(c->mu);
+    OBJB_TRY(get(c, k, d_ptr));
+  }
+  if (*d_ptr) {
+    if (hit) *hit = 1;
+    return OBJB_OK;
+  }
+  if (hit) *hit = 0;
+  const void* src = nullptr;
+  size_t bytes = 0;
+  const int rc = load(user, &src, &bytes);
+  if (rc != 0) return rc;
+  if (!src && bytes) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_expert_cache_get_or_load", "load gave no bytes");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g;
+  OBJB_TRY(g.enter(c->device));
+  return insert(c, k, src, bytes, static_cast<cudaStream_t>(stream), d_ptr, nullptr);
+}
+
 int objb_expert_cache_touch(objb_expert_cache* c, const objb_expert_cache_key* key) {
   CACHE_CHECK(c);
   if (!key) return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "objb_expert_cache_touch", "null key");

@@ -143,6 +143,7 @@ int launch_gemv_pipe(const RowLayoutHost& L, const uint8_t* w, const uint8_t* s,
   prog.src = dev::StageSource{w, s, nullptr, nullptr};
   prog.ximg = img;
   prog.x = inline_x ? x : nullptr;
+  prog.xd = x;
   prog.y = y;
   prog.rows = L.rows;
   prog.rows_per_cta = per_cta;

@@ -82,6 +82,7 @@ struct TcSmem {
   alignas(8) uint64_t full[kTcStages], empty[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
   uint64_t t_full[kTcSlots], t_empty[kTcSlots], x_full, x_empty;
   uint32_t tmem_base;
+  uint32_t abort;  // a wait of this CTA timed out
 };
 static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
 static_assert(kTcNp <= kTcBlockCols && kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
@@ -131,23 +132,28 @@ __device__ __forceinline__ void tc_tmap_acquire(const CUtensorMap* gmem_map) {
                : "memory");
 }
 
-// Bounded wait that gives up early only when another wait of the launch
-// already timed out (other error bits, e.g. a flagged index, do not stop it).
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
+// Bounded wait.  On timeout it records kErrFullWaitTimeout in the device
+// error word and raises the CTA's abort word (shared memory); it gives up
+// early only when another wait of this CTA already raised it (the device
+// word keeps codes of earlier launches, and other codes such as a flagged
+// index, so it never cuts a wait short).
+__device__ __forceinline__ void tc_raise(unsigned* err, uint32_t* abort) {
+  if (err) atomicOr(err, kErrFullWaitTimeout);
+  *reinterpret_cast<volatile uint32_t*>(abort) = 1u;
+}
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
   for (uint32_t i = 0; i < kMaxSpins; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (err && (i & 1023u) == 1023u &&
-        (*reinterpret_cast<volatile unsigned*>(err) & (kErrFullWaitTimeout | kErrEmptyWaitTimeout)) != 0u)
-      return false;
+    if ((i & 1023u) == 1023u && *reinterpret_cast<volatile uint32_t*>(abort) != 0u) return false;
   }
-  if (err) atomicOr(err, kErrFullWaitTimeout);
+  tc_raise(err, abort);
   return false;
 }
 
 // Bounded wait without suspending the thread between polls (lowest wake-up
 // latency; for the MMA-issuing warp, every lane of which polls so that the
 // lane elect.sync picks has itself observed the phase).
-__device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned* err) {
+__device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
   for (uint32_t i = 0; i < 64u * kMaxSpins; ++i) {
     uint32_t done;
     asm volatile(
@@ -156,15 +162,13 @@ __device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned
         : "r"(smem_addr(bar)), "r"(parity)
         : "memory");
     if (done) return true;
-    if (err && (i & 4095u) == 4095u &&
-        (*reinterpret_cast<volatile unsigned*>(err) & (kErrFullWaitTimeout | kErrEmptyWaitTimeout)) != 0u)
-      return false;
+    if ((i & 4095u) == 4095u && *reinterpret_cast<volatile uint32_t*>(abort) != 0u) return false;
   }
-  if (err) atomicOr(err, kErrFullWaitTimeout);
+  tc_raise(err, abort);
   return false;
 }
-__device__ __forceinline__ bool tc_spin_warp(uint64_t* bar, uint32_t parity, unsigned* err) {
-  return __all_sync(0xFFFFFFFFu, tc_spin(bar, parity, err));
+__device__ __forceinline__ bool tc_spin_warp(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
+  return __all_sync(0xFFFFFFFFu, tc_spin(bar, parity, err, abort));
 }
 
 // Instruction descriptor of kind::i8 with both operands signed.
@@ -176,15 +180,23 @@ __host__ __device__ constexpr uint32_t umma_idesc_s8s8(int m, int n) {
 // Digit planes of one 32-value block of vector v (one warp, one value per
 // lane): X = rint(x * 2^(20-E)), E the block's frexp exponent, split in three
 // signed 7-bit digits; plane k at planes[(v * 3 + k) * C + col]; per block
-// 2^(E-20) (NaN when the block is not finite).
-__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc) {
+// 2^(E-20) (NaN when the block is not finite).  A wide block (block_is_wide:
+// its largest value dwarfs most of the others) gets zero digits, so the MMAs
+// add nothing for it, and wflag[v * C/32 + b] = 1: its terms are added in
+// fp32 by tc_add_wide_rows (gate / up) and tc_wide_down_kernel (down).
+__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc,
+                                                uint8_t* wflag) {
   const int lane = threadIdx.x & 31, nb = C / 32;
   float m = fabsf(xe);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   int E = 0;
   frexpf(m, &E);
-  const int X = __float2int_rn(ldexpf(xe, 20 - E));
+  const float ax = fabsf(xe), thr = ldexpf(m, -kWideShift);
+  const int nsmall = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax < thr));
+  const int nbig = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax >= thr));
+  const bool wide = isfinite(m) && block_is_wide(nsmall, nbig);
+  const int X = wide ? 0 : __float2int_rn(ldexpf(xe, 20 - E));
   const int d0 = ((X + 64) & 127) - 64;
   const int X1 = (X - d0) / 128;
   const int d1 = ((X1 + 64) & 127) - 64;
@@ -193,15 +205,17 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   p[0] = static_cast<int8_t>(d0);
   p[C] = static_cast<int8_t>(d1);
   p[2 * C] = static_cast<int8_t>(d2);
-  if (lane == 0)
+  if (lane == 0) {
     xsc[static_cast<size_t>(v) * nb + b] = isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000);
+    wflag[static_cast<size_t>(v) * nb + b] = wide ? 1 : 0;
+  }
 }
 
 // Digit planes of `nvec` vectors (rows of x, x_stride apart); one warp per
 // (vector, block).
 __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict__ x, size_t x_stride, int nvec,
                                                         const int32_t* count, int C, int8_t* __restrict__ planes,
-                                                        float* __restrict__ xsc) {
+                                                        float* __restrict__ xsc, uint8_t* __restrict__ wflag) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count) nvec = min(max(*count, 0), nvec);
@@ -209,25 +223,113 @@ __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict_
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb; wi += warps) {
     const int v = wi / nb, b = wi % nb;
-    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, planes, xsc);
+    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, planes, xsc, wflag);
   }
 }
 
+// Adds to `acc` (this lane's row r of a Q4_0 matrix, row_bytes apart) the
+// fp32 terms of the wide blocks of vector xv (flags wf[0 .. nb)), rounded as
+// the reference's dot rows round them (quant.rs:950-970):
+// ((q - 8) * scale) * x per element, in element order.  Warp-uniform loop
+// over the flagged blocks; x is read once per block (one value per lane) and
+// broadcast by shuffles.  `row` must point at a readable row for every lane
+// (a lane that is not `live` keeps acc).
+__device__ __forceinline__ float tc_add_wide_rows(float acc, const uint8_t* __restrict__ row,
+                                                  const float* __restrict__ xv, const uint8_t* __restrict__ wf,
+                                                  int nb, bool live) {
+  const int lane = threadIdx.x & 31;
+  for (int b0 = 0; b0 < nb; b0 += 32) {
+    uint32_t m = __ballot_sync(0xFFFFFFFFu, b0 + lane < nb && wf[b0 + lane] != 0);
+    while (m) {
+      const int b = b0 + __ffs(m) - 1;
+      m &= m - 1;
+      // every lane runs the shuffles; `row` is a valid row even for a lane
+      // that is not live, whose sum is dropped
+      const float xl = __ldg(xv + b * 32 + lane);
+      const uint8_t* blk = row + static_cast<size_t>(b) * 18;
+      const float sc = f16_bits_to_f32(blk[0] | (static_cast<uint32_t>(blk[1]) << 8));
+      float t = 0.0f;
+      for (int k = 0; k < 32; ++k) {
+        const float xk = __shfl_sync(0xFFFFFFFFu, xl, k);
+        t = __fadd_rn(t, __fmul_rn(__fmul_rn(qf(block_code<OBJB_Q4_0>(blk, k), 8.0f), sc), xk));
+      }
+      if (live) acc = __fadd_rn(acc, t);
+    }
+  }
+  return acc;
+}
+
 // act = SwiGLU(g, u) of every pair (rows of I floats) straight into digit
-// planes; one warp per (pair, block).
-__global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(const float* __restrict__ g,
+// planes; one warp per (pair, block).  First the gate / up rows get the fp32
+// terms of their token's wide blocks (the grouped launch added nothing for
+// them); act is also stored over g, for the down rows' wide-block terms.
+__global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(float* __restrict__ g,
                                                                const float* __restrict__ u, int P,
                                                                const int32_t* count, int I, float limit,
-                                                               int8_t* __restrict__ planes, float* __restrict__ xsc) {
+                                                               int8_t* __restrict__ planes, float* __restrict__ xsc,
+                                                               uint8_t* __restrict__ wflag_a, const int32_t* pe,
+                                                               const int32_t* pt, int T, const float* __restrict__ x,
+                                                               int H, const uint8_t* __restrict__ wflag_x,
+                                                               const uint8_t* const* gate_w,
+                                                               const uint8_t* const* up_w, int num_experts) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count) P = min(max(*count, 0), P);
-  const int nb = I / 32, lane = threadIdx.x & 31;
+  const int nb = I / 32, nbh = H / 32, lane = threadIdx.x & 31;
+  const size_t row_bytes = static_cast<size_t>(nbh) * 18;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < P * nb; wi += warps) {
     const int p = wi / nb, b = wi % nb;
     const size_t i = static_cast<size_t>(p) * I + b * 32 + lane;
-    tc_block_digits(swiglu(g[i], u[i], limit), p, b, I, planes, xsc);
+    float gv = g[i], uv = u[i];
+    int t = pt[p], e = pe[p];
+    const bool ok = t >= 0 && t < T && e >= 0 && e < num_experts;
+    if (!ok) {  // the grouped launch flagged it already; no wide terms
+      t = 0;
+      e = 0;
+    }
+    const uint8_t* wf = wflag_x + static_cast<size_t>(t) * nbh;
+    const float* xv = x + static_cast<size_t>(t) * H;
+    const size_t roff = static_cast<size_t>(b * 32 + lane) * row_bytes;
+    gv = tc_add_wide_rows(gv, gate_w[e] + roff, xv, wf, nbh, ok);
+    uv = tc_add_wide_rows(uv, up_w[e] + roff, xv, wf, nbh, ok);
+    const float a = swiglu(gv, uv, limit);
+    g[i] = a;
+    tc_block_digits(a, p, b, I, planes, xsc, wflag_a);
+  }
+}
+
+// The down rows' terms of the activations' wide blocks: v[slot(p)][r] +=
+// sum over the wide blocks of pair p's activation (act rows of I floats) of
+// ((q - 8) * scale) * act.  One warp per (pair, 32 output rows); a pair with
+// no wide block costs one flag read.
+__global__ void __launch_bounds__(256) tc_wide_down_kernel(const float* __restrict__ act, int P, const int32_t* count,
+                                                           int I, int O, const uint8_t* __restrict__ wflag_a,
+                                                           const int32_t* pe, const int32_t* po, int v_rows,
+                                                           const uint8_t* const* down_w, int num_experts,
+                                                           float* __restrict__ v) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) P = min(max(*count, 0), P);
+  const int nb = I / 32, nrb = (O + 31) / 32, lane = threadIdx.x & 31;
+  const size_t row_bytes = static_cast<size_t>(nb) * 18;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < P * nrb; wi += warps) {
+    const int p = wi / nrb, rb = wi % nrb;
+    const uint8_t* wf = wflag_a + static_cast<size_t>(p) * nb;
+    bool any = false;
+    for (int b0 = 0; b0 < nb; b0 += 32) any |= __any_sync(0xFFFFFFFFu, b0 + lane < nb && wf[b0 + lane] != 0);
+    if (!any) continue;
+    const int e = pe[p], o = po ? po[p] : p;
+    if (e < 0 || e >= num_experts || o < 0 || o >= v_rows) continue;  // flagged by the grouped launch
+    const int r = rb * 32 + lane;
+    const bool live = r < O;
+    const size_t roff = static_cast<size_t>(live ? r : 0) * row_bytes;
+    const float add = tc_add_wide_rows(0.0f, down_w[e] + roff, act + static_cast<size_t>(p) * I, wf, nb, live);
+    if (live) {
+      float* dst = v + static_cast<size_t>(o) * O + r;
+      *dst = __fadd_rn(*dst, add);
+    }
   }
 }
 
@@ -474,6 +576,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     }
     mbar_init(&sm.x_full, kTcXFullCount);
     mbar_init(&sm.x_empty, kTcXEmptyCount);
+    sm.abort = 0u;
     fence_mbar_init();
   }
   if (tid < kTcStages * 8) {  // the tensor-map template into each stage's shared copy
@@ -502,7 +605,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kTcStages, chunk = s % nchunks;
       if (chunk == 0) it = item_at(s);
-      bool ok = s < kTcStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err);
+      bool ok = s < kTcStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort);
       if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
       // the stage's tensor map follows the item's matrix (its last copy has landed: the stage is empty)
       const uint8_t* cur = st == 0 ? map_addr[0] : (st == 1 ? map_addr[1] : map_addr[2]);
@@ -533,8 +636,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kTcStages, ab = s % kTcAbuf;
       if (s % nchunks == 0) idesc = umma_idesc_s8s8(kTcRows, 3 * item_at(s).nv);
-      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err) ||
-          !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err))
+      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort) ||
+          !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort))
         break;
       fence_async_shared();  // codes written by the unpack threads, read by the MMAs
       tc_fence_after_sync();
@@ -542,7 +645,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
 #pragma unroll 1
       for (int g = 0; g < kTcKB / 2; ++g) {
         const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
-        if (G >= kTcSlots && !tc_spin_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err)) {
+        if (G >= kTcSlots && !tc_spin_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err, &sm.abort)) {
           ok = false;
           break;
         }
@@ -565,8 +668,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kTcStages, ab = s % kTcAbuf;
-      if (!tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err)) break;
-      if (s >= kTcAbuf && !tc_wait(&sm.a_empty[ab], ((s / kTcAbuf) - 1) & 1, A.err)) break;
+      if (!tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort)) break;
+      if (s >= kTcAbuf && !tc_wait(&sm.a_empty[ab], ((s / kTcAbuf) - 1) & 1, A.err, &sm.abort)) break;
       tc_unpack(sm, st, ab, r);
       fence_async_shared();  // codes written here, read by the MMAs
       mbar_arrive(&sm.a_full[ab]);
@@ -591,11 +694,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       if (chunk == 0) it = item_at(s);
       const int nvg = (it.ns + 7) >> 3;
       // block scales (bulk copy) and row scales (unpack) of this step are read below
-      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err) && tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err);
+      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort) && tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort);
 #pragma unroll 1
       for (int g = 0; g < kTcKB / 2 && ok; ++g) {
         const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
-        if (!tc_wait(&sm.t_full[slot], (G / kTcSlots) & 1, A.err)) {
+        if (!tc_wait(&sm.t_full[slot], (G / kTcSlots) & 1, A.err, &sm.abort)) {
           ok = false;
           break;
         }
@@ -636,12 +739,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       if (chunk == nchunks - 1) {
         // odd-block partial sums through shared memory, then one store per live pair
         if (half == 1) {
-          if (items_done > 0 && !tc_wait(&sm.x_empty, (items_done - 1) & 1, A.err)) break;
+          if (items_done > 0 && !tc_wait(&sm.x_empty, (items_done - 1) & 1, A.err, &sm.abort)) break;
 #pragma unroll
           for (int i = 0; i < kTcUnit; ++i) sm.xchg[kTcUnit * vh + i][trow] = acc[i];
           mbar_arrive(&sm.x_full);
         } else {
-          if (!tc_wait(&sm.x_full, items_done & 1, A.err)) break;
+          if (!tc_wait(&sm.x_full, items_done & 1, A.err, &sm.abort)) break;
           const int grow = it.tile * kTcRows + trow;
 #pragma unroll
           for (int i = 0; i < kTcUnit; ++i) {
@@ -716,6 +819,7 @@ struct MxSmem {
   alignas(8) uint64_t full[kMxStages], empty[kMxStages], a_full[kMxAbuf], a_empty[kMxAbuf];
   uint64_t d_full[kMxDslots], d_empty[kMxDslots];
   uint32_t tmem_base;
+  uint32_t abort;  // a wait of this CTA timed out
 };
 static_assert(sizeof(MxSmem) <= 227 * 1024, "block-scaled kernel shared memory");
 static_assert(kMxDslots * kMxDCols <= kMxSfaCol && kMxSfbCol + 4 * kMxStages <= 512, "tensor-memory columns");
@@ -867,6 +971,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
       mbar_init(&sm.d_full[i], 1);
       mbar_init(&sm.d_empty[i], kMxEpiWarps);
     }
+    sm.abort = 0u;
     fence_mbar_init();
   }
   if (tid < kMxStages * 8) {
@@ -895,7 +1000,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kMxStages, chunk = s % nchunks;
       if (chunk == 0) it = item_at(s);
-      bool ok = s < kMxStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err);
+      bool ok = s < kMxStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err, &sm.abort);
       if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
       if (map_addr[st] != it.w) {
         if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
@@ -925,9 +1030,9 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
         n = item_at(s).units * kTcUnit;
         ++item;
         slot = item % kMxDslots;
-        if (item >= kMxDslots && !tc_spin_warp(&sm.d_empty[slot], ((item / kMxDslots) - 1) & 1, A.err)) break;
+        if (item >= kMxDslots && !tc_spin_warp(&sm.d_empty[slot], ((item / kMxDslots) - 1) & 1, A.err, &sm.abort)) break;
       }
-      if (!tc_spin_warp(&sm.a_full[ab], (s / kMxAbuf) & 1, A.err) || !tc_spin_warp(&sm.full[st], (s / kMxStages) & 1, A.err))
+      if (!tc_spin_warp(&sm.a_full[ab], (s / kMxAbuf) & 1, A.err, &sm.abort) || !tc_spin_warp(&sm.full[st], (s / kMxStages) & 1, A.err, &sm.abort))
         break;
       fence_async_shared();  // codes and weight scales written by the unpack threads
       tc_fence_after_sync();
@@ -956,8 +1061,8 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
       const uint32_t wsc = row < A.R ? *reinterpret_cast<const uint32_t*>(
                                            it.ws + static_cast<size_t>(row) * (A.C / 32) + chunk * kMxKB)
                                      : 0u;
-      if (!tc_wait(&sm.full[st], (s / kMxStages) & 1, A.err)) break;
-      if (s >= kMxAbuf && !tc_wait(&sm.a_empty[ab], ((s / kMxAbuf) - 1) & 1, A.err)) break;
+      if (!tc_wait(&sm.full[st], (s / kMxStages) & 1, A.err, &sm.abort)) break;
+      if (s >= kMxAbuf && !tc_wait(&sm.a_empty[ab], ((s / kMxAbuf) - 1) & 1, A.err, &sm.abort)) break;
       const uint8_t* src = sm.raw[st] + r * kMxRawRow;
       uint8_t* dst = sm.a[ab] + (r >> 3) * kMxKch * 128 + (r & 7) * 16;
 #pragma unroll
@@ -981,7 +1086,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
     for (int i = 0; i < my_items; ++i) {
       const MxItem it = item_at(i * nchunks);
       const int slot = i % kMxDslots;
-      if (!tc_wait(&sm.d_full[slot], (i / kMxDslots) & 1, A.err)) break;
+      if (!tc_wait(&sm.d_full[slot], (i / kMxDslots) & 1, A.err, &sm.abort)) break;
       tc_fence_after_sync();
       const int grow = it.tile * kTcRows + trow;
 #pragma unroll 1
@@ -1027,8 +1132,8 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
 namespace {
 
 struct TcLayout {
-  size_t planes_x, xsc_x, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit, nslices, bimg, ximg,
-      gmaps, total;
+  size_t planes_x, xsc_x, wflag_x, wflag_a, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit,
+      nslices, bimg, ximg, gmaps, total;
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -1050,6 +1155,8 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   const size_t units = tc_max_units(P, E), nchunks = std::max(H, I) / (dev::kTcKB * 32);
   L.planes_x = take(T * 3 * H);
   L.xsc_x = take(T * (H / 32) * 4);
+  L.wflag_x = take(T * (H / 32));
+  L.wflag_a = take(P * (I / 32));
   L.g = take(P * I * 4);
   L.u = take(P * I * 4);
   L.planes_a = take(P * 3 * I);
@@ -1156,6 +1263,8 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   uint8_t* sc = static_cast<uint8_t*>(scratch);
   int8_t* planes_x = reinterpret_cast<int8_t*>(sc + L.planes_x);
   float* xsc_x = reinterpret_cast<float*>(sc + L.xsc_x);
+  uint8_t* wflag_x = sc + L.wflag_x;
+  uint8_t* wflag_a = sc + L.wflag_a;
   float* g = reinterpret_cast<float*>(sc + L.g);
   float* u = reinterpret_cast<float*>(sc + L.u);
   int8_t* planes_a = reinterpret_cast<int8_t*>(sc + L.planes_a);
@@ -1186,7 +1295,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
                       slice_start, slice_len, slice_unit, nslices,
                       static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
-                      static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x));
+                      static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x, wflag_x));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_x),
@@ -1214,8 +1323,9 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out_rows = P;
   a.err = err;
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_gu));
-  OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, static_cast<const float*>(g),
-                      static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a));
+  OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, g,
+                      static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a, wflag_a, pe, pt, T, x, H,
+                      static_cast<const uint8_t*>(wflag_x), a.W, a.W2, a.num_experts));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_a),
@@ -1233,6 +1343,9 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out_rows = static_cast<int>(v_rows);
   a.gmaps = gmaps + static_cast<size_t>(props.sm_count) * dev::kTcStages;
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_dn));
+  OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, std::max(O, 32)), 256, 0, stream,
+                      static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a), pe, po,
+                      static_cast<int>(v_rows), a.W, a.num_experts, v));
   return OBJB_OK;
 }
 

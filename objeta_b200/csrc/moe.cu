@@ -240,6 +240,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     prog.ids = ids;
     prog.ximg = imgx;
     prog.x = x_inline ? x : nullptr;
+    prog.xd = x;
     prog.act = act;
     prog.K = s.K;
     prog.I = s.I;
@@ -271,6 +272,7 @@ int run_moe(const objb_moe_layer& l, const MoeShape& s, const int32_t* ids, cons
     prog.img_stride = p.imga_quads;
     prog.xf = act_direct ? act : nullptr;
     prog.xf_stride = static_cast<size_t>(s.I);
+    prog.xd = act;
     prog.out = out;
     prog.K = s.K;
     prog.O = s.O;
@@ -345,6 +347,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.img_stride = p.imgx_quads;
     prog.xf = x_direct ? x : nullptr;
     prog.xf_stride = static_cast<size_t>(s.H);
+    prog.xd = x;
     prog.act = act;
     prog.P = P;
     prog.I = s.I;
@@ -375,6 +378,7 @@ int run_pairs(const objb_moe_layer& l, const MoeShape& s, int T, const int32_t* 
     prog.img_stride = p.imga_quads;
     prog.xf = act_direct ? act : nullptr;
     prog.xf_stride = static_cast<size_t>(s.I);
+    prog.xd = act;
     prog.v = v;
     prog.P = P;
     prog.O = s.O;

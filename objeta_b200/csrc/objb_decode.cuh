@@ -120,6 +120,46 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
   return __int2float_rn(T) * (scale * __uint_as_float(xr.w(48 + b)));
 }
 
+// ------------------------------------------------ wide blocks (exact path)
+// A block whose largest |x| dwarfs most of its other nonzero values ("wide":
+// at least one nonzero value, and no more values at or above 2^-8 of the
+// largest than below it) would lose those small values to the 2^-21 grid of
+// the largest one, and the rows whose weight is zero at the large value would
+// then miss the reference's 1e-5 * sum|w x| bound.  Its digit words and block
+// sum are zero in the image (it adds nothing to the integer path), its
+// 2^(E-20) word holds kWideMark, and the consumer warp adds the block's terms
+// in fp32 instead, one element per lane: ((q_l - off) * scale) * x_l.
+constexpr int kWideShift = 8;
+constexpr uint32_t kWideMark = 0x80000000u;  // -0.0f: a zero block sum times it stays zero
+
+// Whether a finite block is wide, from its value counts: `small` nonzero
+// values below 2^-kWideShift of the largest |x|, `big` values at or above it.
+__device__ __forceinline__ bool block_is_wide(int small, int big) { return small > 0 && small >= big; }
+
+// Code q (unsigned, before the offset) of element l of one block in the
+// reference byte layouts (quant.rs:814-879), read with byte loads.
+template <int FMT>
+__device__ __forceinline__ uint32_t block_code(const uint8_t* blk, int l) {
+  if constexpr (FMT == OBJB_Q4_0) {
+    return (blk[2 + (l >> 1)] >> ((l & 1) * 4)) & 0xFu;
+  } else if constexpr (FMT == OBJB_Q5_0) {
+    const uint32_t lo = (blk[6 + (l >> 1)] >> ((l & 1) * 4)) & 0xFu;
+    return lo | (((blk[2 + (l >> 3)] >> (l & 7)) & 1u) << 4);
+  } else {
+    const uint32_t lo = (blk[2 + (l >> 2)] >> (2 * (l & 3))) & 3u;
+    return lo | (((blk[10 + (l >> 3)] >> (l & 7)) & 1u) << 2);
+  }
+}
+
+// Lane l's fp32 term of a wide block, rounded as the reference's dot rows
+// round it (quant.rs:950-1019): w = (q_l - off) * scale, then w * x_l.
+template <int FMT>
+__device__ __forceinline__ float wide_term(const uint8_t* blk, int l, float xl) {
+  constexpr float off = FMT == OBJB_Q4_0 ? 8.0f : FMT == OBJB_Q5_0 ? 16.0f : 4.0f;
+  const float s = f16_bits_to_f32(blk[0] | (static_cast<uint32_t>(blk[1]) << 8));
+  return __fmul_rn(__fmul_rn(qf(block_code<FMT>(blk, l), off), s), xl);
+}
+
 // Q5_0 high bits onto bit 4 of the code bytes: bits 0, 2, 4, 6 of hb (the
 // low-nibble elements) -> bits 4, 12, 20, 28, and bits 1, 3, 5, 7 (the
 // high-nibble elements) -> the same positions.  One multiply each: the

@@ -46,12 +46,13 @@ struct SmemPlan {
   uint64_t* full;
   uint64_t* empty;
   uint64_t* img_done;  // every consumer warp holds its x registers (in-kernel x images)
+  unsigned* abort;     // CTA-local: a wait of this CTA gave up or a stage was completed without data
   float* red;      // [nslots][tstage][nseg][2]
   uint8_t* stage;  // [nslots][stage_bytes]
 };
 
 // 64-bit barrier words at the start of the pipelined kernel's shared memory
-// (full and empty per slot, img_done, one word of padding).
+// (full and empty per slot, img_done, the abort word).
 constexpr int kPipeBarrierWords = 2 * kMaxSlots + 2;
 
 __device__ __forceinline__ SmemPlan carve_smem(uint8_t* base, const RowLayout& L, int nred) {
@@ -59,6 +60,7 @@ __device__ __forceinline__ SmemPlan carve_smem(uint8_t* base, const RowLayout& L
   p.full = reinterpret_cast<uint64_t*>(base);
   p.empty = p.full + kMaxSlots;
   p.img_done = p.empty + kMaxSlots;
+  p.abort = reinterpret_cast<unsigned*>(p.img_done + 1);
   p.red = reinterpret_cast<float*>(base + kPipeBarrierWords * sizeof(uint64_t));
   size_t red_bytes = static_cast<size_t>(L.nslots) * L.tstage * L.nseg * nred * sizeof(float);
   size_t off = kPipeBarrierWords * sizeof(uint64_t) + red_bytes;
@@ -205,7 +207,8 @@ __global__ void __launch_bounds__(256) ximage_f32_kernel(const RowLayout L, cons
 // its three signed 7-bit digits and sum X; lanes 0..23 then assemble the 24
 // digit words of the block (group g, digit k -> word (b*8 + g)*3 + k, byte j
 // = element Tile::elem(b, g, j)) and lanes 24 / 25 the block's 2^(E-20) and
-// -offset * sum X.
+// -offset * sum X.  A wide block (block_is_wide) gets zero digits and sum and
+// kWideMark in place of 2^(E-20).
 template <int FMT>
 __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, const float* __restrict__ x,
                                                             size_t x_stride, int nvec, uint4* __restrict__ img,
@@ -227,7 +230,11 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
     int E = 0;
     frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
-    const int X = __float2int_rn(ldexpf(xe, 20 - E));
+    const float ax = fabsf(xe), thr = ldexpf(m, -kWideShift);
+    const int nsmall = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax < thr));
+    const int nbig = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax >= thr));
+    const bool wide = isfinite(m) && block_is_wide(nsmall, nbig);
+    const int X = wide ? 0 : __float2int_rn(ldexpf(xe, 20 - E));
     const int d0 = ((X + 64) & 127) - 64;
     const int X1 = (X - d0) / 128;
     const int d1 = ((X1 + 64) & 127) - 64;
@@ -254,7 +261,7 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
       val = word;
     } else if (lane == 24) {
       widx = 48 + b;
-      val = __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000));
+      val = wide ? kWideMark : __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000));
     } else if (lane == 25) {
       widx = 50 + b;
       val = static_cast<uint32_t>(-T::kOffset * sx);
@@ -286,6 +293,7 @@ __device__ __forceinline__ float max_nan(float a, float b) {
 // is one or two exact power-of-two products and the rounding to an integer
 // (|value| < 2^21) one magic-number addition, both equal to ldexpf and
 // __float2int_rn; a block holding NaN or Inf takes those functions as is.
+// Wide blocks are marked as ximage_digits_kernel marks them.
 template <int FMT>
 __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool live, int B, int Q, unsigned gmask,
                                               int lt, int ntp, uint32_t* img) {
@@ -300,12 +308,25 @@ __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool
   m = max_nan(m, __shfl_xor_sync(gmask, m, 2));
   int X[8];
   int E = 0;
+  bool wide = false;
   if (m < INFINITY) {  // no NaN (max.NaN would carry it) and no Inf in the block
     frexpf(m, &E);     // m < 2^E (E = 0 for m = 0)
+    const float thr = ldexpf(m, -kWideShift);
+    int ns = 0, nb = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = fabsf(v[i]);
+      ns += a != 0.0f && a < thr;
+      nb += a != 0.0f && a >= thr;
+    }
+    const int cnt = ns | (nb << 8);  // both counts <= 32: one packed sum over the quarters
+    int c = cnt + __shfl_xor_sync(gmask, cnt, 1);
+    c += __shfl_xor_sync(gmask, c, 2);
+    wide = block_is_wide(c & 0xFF, c >> 8);
     const int k = 20 - E, k1 = min(k, 127);
     const float s1 = __int_as_float((k1 + 127) << 23), s2 = __int_as_float((k - k1 + 127) << 23);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) X[i] = __float_as_int((v[i] * s1) * s2 + 12582912.0f) - 0x4B400000;
+    for (int i = 0; i < 8; ++i) X[i] = wide ? 0 : __float_as_int((v[i] * s1) * s2 + 12582912.0f) - 0x4B400000;
   } else {
     m = fabsf(v[0]);
 #pragma unroll
@@ -341,7 +362,7 @@ __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool
     put(dg_word(B, 2 * Q + h, 2), w2);
   }
   if (Q == 0) {
-    put(48 + B, __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000)));
+    put(48 + B, wide ? kWideMark : __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000)));
     put(50 + B, static_cast<uint32_t>(-T::kOffset) * sx);
   }
 }
@@ -461,6 +482,7 @@ __device__ __forceinline__ void issue_stage(const RowLayout& L, const SmemPlan& 
                          (dual ? (reinterpret_cast<uintptr_t>(src.wb) | reinterpret_cast<uintptr_t>(src.sb)) : 0)) & 15u;
   if (mis || src.wa == nullptr || (dual && src.wb == nullptr)) {
     if (err) atomicOr(err, kErrMisaligned);
+    *reinterpret_cast<volatile unsigned*>(sp.abort) = 1u;  // the rows of this launch come out NaN
     mbar_arrive(&sp.full[slot]);
     return;
   }
@@ -488,7 +510,38 @@ struct Job {
   const uint4* ximg;  // x image of this job's vector
   int row_begin, row_end;
   const float* x = nullptr;  // float-quad rows: this job's vector, read directly (ximg unused)
+  const float* xd = nullptr;  // digit rows: this job's vector as floats, for the terms of wide blocks
 };
+
+// The fp32 terms of the wide blocks of a digit image (flagged kWideMark):
+// w0 / w1 are the lanes of this warp whose tile block 0 / 1 is wide.  For
+// each such block every lane adds its element's term to its partial of each
+// of the batch's rows, so the warp's row reduction sums the block with the
+// rest of the row.
+template <int FMT, int RB, bool DUAL, int NV>
+__device__ __forceinline__ void add_wide_terms(float (&v)[NV], uint32_t w0, uint32_t w1, int seg, int lane,
+                                               const uint8_t* stg, int part, int row_bytes, int bt, int nr,
+                                               const float* __restrict__ xd) {
+  using T = Tile<FMT>;
+#pragma unroll 1
+  for (int b = 0; b < 2; ++b) {
+    uint32_t m = b ? w1 : w0;
+#pragma unroll 1
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const int lt = seg * 32 + src;
+      const int boff = lt * T::TB + b * T::BB;
+      const float xl = __ldg(xd + static_cast<size_t>(lt * T::P + b) * 32 + lane);
+#pragma unroll
+      for (int i = 0; i < RB; ++i) {
+        const int t = min(bt + i, nr - 1);
+        v[i] += wide_term<FMT>(stg + t * row_bytes + boff, lane, xl);
+        if constexpr (DUAL) v[RB + i] += wide_term<FMT>(stg + part + t * row_bytes + boff, lane, xl);
+      }
+    }
+  }
+}
 
 // Consumer warps: nseg * ngrp (<= kMaxConsumerWarps); one producer warp more.
 constexpr int kPipeThreads = (kMaxConsumerWarps + 1) * 32;
@@ -522,6 +575,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
       mbar_init(&sp.empty[i], ncw);
     }
     mbar_init(sp.img_done, ncw);
+    *sp.abort = 0u;
     fence_mbar_init();
   }
   __syncthreads();
@@ -544,12 +598,12 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
         for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
           const int slot = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S)) {
-            if (!mbar_wait_bounded(&sp.empty[slot], ((it / S) - 1) & 1u, err, kErrEmptyWaitTimeout)) {
+            if (!mbar_wait_bounded(&sp.empty[slot], ((it / S) - 1) & 1u, err, kErrEmptyWaitTimeout, sp.abort)) {
               ok = false;
               break;
             }
           } else if (img_in_ring && it == static_cast<uint32_t>(S - 1)) {
-            if (!mbar_wait_bounded(sp.img_done, 0u, err, kErrEmptyWaitTimeout)) {
+            if (!mbar_wait_bounded(sp.img_done, 0u, err, kErrEmptyWaitTimeout, sp.abort)) {
               ok = false;
               break;
             }
@@ -612,9 +666,19 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
     } else if (xin == nullptr) {
       load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     }
+    // digit rows: lanes whose tile block 0 / 1 is wide (warp-uniform masks)
+    uint32_t wide0 = 0u, wide1 = 0u;
+    if constexpr (IsDigitRD<RD>::value) {
+      wide0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
+      wide1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
+      if ((wide0 | wide1) != 0u && J.xd == nullptr) {
+        if (lane == 0 && err) atomicOr(err, kErrNoWideSource);
+        wide0 = wide1 = 0u;
+      }
+    }
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
-      if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout);
+      if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout, sp.abort);
       const int nr = min(T, J.row_end - r0);
       const uint8_t* stg = sp.stage + static_cast<size_t>(slot) * L.stage_bytes;
       const uint8_t* sca = stg + static_cast<size_t>(T) * L.row_bytes;
@@ -629,6 +693,11 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
             v[RB + i] = rd.dot(stg + part + t * L.row_bytes,
                                stg + part + static_cast<size_t>(T) * L.row_bytes + t * L.srow_bytes, xr);
         }
+        if constexpr (IsDigitRD<RD>::value) {
+          if ((wide0 | wide1) != 0u)
+            add_wide_terms<IsDigitRD<RD>::fmt, RB, DUAL>(v, wide0, wide1, seg, lane, stg, part, L.row_bytes, bt, nr,
+                                                         J.xd);
+        }
         butterfly<NV>(v, lane);
         if ((lane & (W - 1)) == 0) {
           const int idx = lane / W;
@@ -639,12 +708,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
       __syncwarp();
       if (lane == 0) mbar_arrive(&sp.empty[slot]);
       named_bar_sync(1, nthr);
+      // a stage that never landed (or landed without data) yields NaN rows,
+      // not values reduced from stale shared memory
+      const bool aborted = *reinterpret_cast<volatile unsigned*>(sp.abort) != 0u;
       for (int t = threadIdx.x; t < nr; t += nthr) {
         float va = 0.0f, vb = 0.0f;
         for (int s2 = 0; s2 < L.nseg; ++s2) {
           va += red[(t * L.nseg + s2) * 2];
           if constexpr (DUAL) vb += red[(t * L.nseg + s2) * 2 + 1];
         }
+        if (aborted) va = vb = __int_as_float(0x7FC00000);
         prog.epilogue(cta, j, r0 + t, va, vb);
       }
       ++it;
@@ -660,6 +733,7 @@ struct GemvProg {
   StageSource src;
   const uint4* ximg;
   const float* x = nullptr;
+  const float* xd = nullptr;  // the vector, for the terms of wide digit blocks
   float* y;
   int rows;
   int rows_per_cta;
@@ -669,6 +743,7 @@ struct GemvProg {
     Job J;
     J.src = src;
     J.ximg = ximg;
+    J.xd = xd;
     J.row_begin = cta * rows_per_cta;
     J.row_end = min(rows, J.row_begin + rows_per_cta);
     return J;

@@ -56,6 +56,7 @@ struct GateUpProg {
   const int32_t* ids;
   const uint4* ximg;
   const float* x = nullptr;  // != nullptr: the kernel forms the x registers itself (ximg unused)
+  const float* xd = nullptr;  // the token vector, for the terms of wide digit blocks
   float* act;  // [K][I]
   int K, I;
   int rows_per_cta;
@@ -81,6 +82,7 @@ struct GateUpProg {
     J.src.sa = t.gate_scale ? t.gate_scale[e] : nullptr;
     J.src.sb = t.up_scale ? t.up_scale[e] : nullptr;
     J.ximg = ximg;
+    J.xd = xd;
     J.row_begin = max(a, k * I) - k * I;
     J.row_end = min(b, (k + 1) * I) - k * I;
     return J;
@@ -104,6 +106,7 @@ struct DownProg {
   size_t img_stride;
   const float* xf = nullptr;  // float-quad rows: the K activations, xf_stride floats apart
   size_t xf_stride = 0;
+  const float* xd = nullptr;  // digit rows: the K activations (wide-block terms), xf_stride floats apart
   float* out;
   int K, O;
   int rows_per_cta;
@@ -119,6 +122,7 @@ struct DownProg {
     J.src.sb = nullptr;
     J.ximg = ximg + j * img_stride;
     J.x = xf ? xf + static_cast<size_t>(j) * xf_stride : nullptr;
+    J.xd = xd ? xd + static_cast<size_t>(j) * xf_stride : nullptr;
     J.row_begin = cta * rows_per_cta;
     J.row_end = min(O, J.row_begin + rows_per_cta);
     return J;
@@ -160,6 +164,7 @@ struct GateUpPairsProg {
   size_t img_stride;
   const float* xf = nullptr;  // float-quad rows: the T tokens, xf_stride floats apart
   size_t xf_stride = 0;
+  const float* xd = nullptr;  // digit rows: the T tokens (wide-block terms), xf_stride floats apart
   float* act;  // [P][I]
   int P, I, T;
   int rows_per_cta;  // 0: derived in the kernel from *count
@@ -189,6 +194,7 @@ struct GateUpPairsProg {
     J.src.sb = t.up_scale ? t.up_scale[e] : nullptr;
     J.ximg = ximg + static_cast<size_t>(tok) * img_stride;
     J.x = xf ? xf + static_cast<size_t>(tok) * xf_stride : nullptr;
+    J.xd = xd ? xd + static_cast<size_t>(tok) * xf_stride : nullptr;
     J.row_begin = max(a, p * I) - p * I;
     J.row_end = min(b, (p + 1) * I) - p * I;
     return J;
@@ -209,6 +215,7 @@ struct DownPairsProg {
   size_t img_stride;
   const float* xf = nullptr;  // float-quad rows: the P activations, xf_stride floats apart
   size_t xf_stride = 0;
+  const float* xd = nullptr;  // digit rows: the P activations (wide-block terms), xf_stride floats apart
   float* v;                 // [v_rows][O]
   int P, O, v_rows;
   int rows_per_cta;         // 0: derived in the kernel from *count
@@ -236,6 +243,7 @@ struct DownPairsProg {
     J.src.sb = nullptr;
     J.ximg = ximg + static_cast<size_t>(p) * img_stride;
     J.x = xf ? xf + static_cast<size_t>(p) * xf_stride : nullptr;
+    J.xd = xd ? xd + static_cast<size_t>(p) * xf_stride : nullptr;
     J.row_begin = max(a, p * O) - p * O;
     J.row_end = min(b, (p + 1) * O) - p * O;
     return J;

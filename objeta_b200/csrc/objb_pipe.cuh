@@ -18,6 +18,7 @@ constexpr unsigned kErrEmptyWaitTimeout = 2u;
 constexpr unsigned kErrDrainTimeout = 4u;
 constexpr unsigned kErrBadExpertId = 8u;
 constexpr unsigned kErrMisaligned = 16u;
+constexpr unsigned kErrNoWideSource = 32u;  // a wide digit block met a program without its float vector
 
 // mbarrier.try_wait may suspend the thread for a hardware time slice, so the
 // wall-clock bound is kMaxSpins times that slice (well under a few seconds).
@@ -59,17 +60,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on phase `parity`.  Gives up early when another thread has
-// already recorded an error in *err, and on timeout ORs `code` into *err;
-// returns false in both cases.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  unsigned* err, unsigned code) {
+// Bounded wait on phase `parity`.  On timeout ORs `code` into the device
+// error word *err and raises the launch's CTA-local abort word *abort
+// (shared memory); gives up early when another thread of the CTA has already
+// raised *abort.  Returns false in both cases.  The device error word only
+// records: it keeps codes of earlier launches until objb_device_error_take,
+// so it never cuts a wait short.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err,
+                                                  unsigned code, unsigned* abort = nullptr) {
   for (uint32_t i = 0; i < kMaxSpins; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (err && (i & 1023u) == 1023u && *reinterpret_cast<volatile unsigned*>(err) != 0u)
-      return false;
+    if (abort && (i & 1023u) == 1023u && *reinterpret_cast<volatile unsigned*>(abort) != 0u) return false;
   }
   if (err) atomicOr(err, code);
+  if (abort) *reinterpret_cast<volatile unsigned*>(abort) = 1u;
   return false;
 }
 

@@ -133,6 +133,9 @@ class _LayerC(ctypes.Structure):
                 ("d_down_scale", c_void_p)]
 
 
+# objb_expert_load_fn: int (*)(void* user, const void** host_src, size_t* bytes)
+_LOAD_FN = ctypes.CFUNCTYPE(c_int, c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_size))
+
 _lib.register_signatures({
     "objb_expert_cache_new": (c_int, [c_int, c_size, ctypes.POINTER(c_void_p)]),
     "objb_expert_cache_free": (None, [c_void_p]),
@@ -141,6 +144,8 @@ _lib.register_signatures({
                                          ctypes.POINTER(c_void_p), ctypes.POINTER(c_int)]),
     "objb_expert_cache_get_or_insert": (c_int, [c_void_p, ctypes.POINTER(_KeyC), c_void_p, c_size, c_void_p,
                                                 ctypes.POINTER(c_void_p), ctypes.POINTER(c_int)]),
+    "objb_expert_cache_get_or_load": (c_int, [c_void_p, ctypes.POINTER(_KeyC), _LOAD_FN, c_void_p, c_void_p,
+                                              ctypes.POINTER(c_void_p), ctypes.POINTER(c_int)]),
     "objb_expert_cache_touch": (c_int, [c_void_p, ctypes.POINTER(_KeyC)]),
     "objb_expert_cache_evict_lru": (c_int, [c_void_p, ctypes.POINTER(_KeyC), ctypes.POINTER(c_int)]),
     "objb_expert_cache_pin": (c_int, [c_void_p, ctypes.POINTER(_KeyC)]),
@@ -253,11 +258,40 @@ class CudaExpertCache:
         return p.value
 
     def get_or_insert(self, key: ExpertCacheKey, load_fn, stream=None):
-        """README.md:121-124: get, else insert(load_fn()).  Returns (ptr, hit)."""
-        p = self.get(key)
-        if p is not None:
-            return p, True
-        return self.insert(key, load_fn(), stream), False
+        """README.md:121-124: get, else insert(load_fn()).  Returns (ptr, hit).
+
+        ``load_fn`` is a callable returning the host bytes, run only on a miss
+        (objb_expert_cache_get_or_load), or the bytes themselves
+        (objb_expert_cache_get_or_insert).  Counters move as the executor's
+        inline get / insert (moe.rs:508-518)."""
+        p, hit = c_void_p(), c_int()
+        if not callable(load_fn):
+            a = _host_u8(load_fn)
+            _lib.call("objb_expert_cache_get_or_insert", self._h, ctypes.byref(_key_c(key)), a.ctypes.data, a.size,
+                      _lib.stream_handle(stream), ctypes.byref(p), ctypes.byref(hit))
+            return p.value, bool(hit.value)
+        held = []
+        failure = []
+
+        def load(_user, src, nbytes):
+            try:
+                a = _host_u8(load_fn())
+            except Exception as exc:  # reported after the C call returns
+                failure.append(exc)
+                return 7  # OBJB_ERR_INTERNAL + 1
+            held.append(a)
+            src[0] = a.ctypes.data
+            nbytes[0] = a.size
+            return 0
+
+        cb = _LOAD_FN(load)
+        rc = _lib.load().objb_expert_cache_get_or_load(self._h, ctypes.byref(_key_c(key)), cb, None,
+                                                         _lib.stream_handle(stream), ctypes.byref(p),
+                                                         ctypes.byref(hit))
+        if failure:
+            raise failure[0]
+        _lib.check(rc)
+        return p.value, bool(hit.value)
 
     def touch(self, key: ExpertCacheKey) -> None:
         _lib.call("objb_expert_cache_touch", self._h, ctypes.byref(_key_c(key)))

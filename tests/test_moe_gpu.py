@@ -257,6 +257,91 @@ def test_cache_matches_model_random_ops(cuda_device):
         assert [(q.layer_id, q.expert_id, int(q.tensor_kind)) for q in c.lru_keys()] == m.order, step
 
 
+@pytest.mark.parametrize("lazy", [True, False])
+def test_get_or_insert_matches_model(cuda_device, lazy):
+    """CudaExpertCache.get_or_insert through objb_expert_cache_get_or_load
+    (lazy load_fn) and objb_expert_cache_get_or_insert (bytes at hand) on the
+    reference's cache sequences (moe.rs:1891-2226, tensor by tensor as the
+    executor looks them up, moe.rs:508-518), then random operations: hit
+    flags, every counter and the LRU order after each step equal the
+    restated cache (oracle/cache_model.py); the loader runs on misses only."""
+    from objeta_b200 import QuantFormat
+    from objeta_b200.moe import CudaExpertCache, ExpertCacheKey, ExpertTensorKind
+    gate, down = 512 * 8 * 18, 256 * 16 * 18
+    expert = 2 * gate + down
+    sizes = {0: gate, 1: gate, 2: down}
+
+    def K(k):
+        return ExpertCacheKey(k[0], k[1], ExpertTensorKind(k[2]), QuantFormat.Q4_0)
+
+    def step(c, m, k, nbytes, where):
+        loads = []
+        data = np.full(nbytes, (k[1] * 3 + k[2]) % 251, np.uint8)
+
+        def load():
+            loads.append(k)
+            return data
+        p, hit = c.get_or_insert(K(k), load if lazy else data)
+        want_hit, _ = m.get_or_insert(k, nbytes)
+        assert hit == want_hit and p is not None, where
+        if lazy:
+            assert len(loads) == (0 if hit else 1), where
+        s = c.stats()
+        for name, v in m.counters().items():
+            assert s[name] == v, (where, name, s[name], v)
+        assert [(q.layer_id, q.expert_id, int(q.tensor_kind)) for q in c.lru_keys()] == m.order, where
+
+    sequences = [
+        (1000 * 1024, [0, 1, 0, 1]),       # moe.rs:1950-2000: 6 misses then 6 hits
+        (4 * expert, [0, 1, 2, 3]),        # moe.rs:2002-2025: no eviction
+        (expert, [0, 1, 0]),               # moe.rs:2027-2082: eviction, reload
+        (2 * expert, [0, 1, 0, 2, 0, 1]),  # moe.rs:2084-2166: LRU touch order
+        (gate - 1, [0, 1]),                # moe.rs:2170-2226: oversized tensors bypass
+    ]
+    for cap, experts in sequences:
+        c, m = CudaExpertCache(cap, cuda_device), CacheModel(cap)
+        for i, e in enumerate(experts):
+            for kind in (0, 1, 2):
+                step(c, m, (0, e, kind), sizes[kind], (cap, i, kind))
+            c.release()
+    rng = random.Random(11)
+    cap = 10_000
+    c, m = CudaExpertCache(cap, cuda_device), CacheModel(cap)
+    keys = [(layer, e, kind) for layer in range(2) for e in range(5) for kind in (0, 1, 2)]
+    ksize = {k: rng.choice([512, 1024, 2048, 3000, 12_000]) for k in keys}
+    for i in range(300):
+        k = rng.choice(keys)
+        r = rng.random()
+        if r < 0.7:
+            step(c, m, k, ksize[k], ("random", i))
+        elif r < 0.8:
+            c.touch(K(k))
+            m.touch(k)
+        elif r < 0.9:
+            c.release()
+        elif r < 0.95:
+            c.pin(K(k))
+            m.pin(k)
+        else:
+            c.reset_counters()
+            m.reset_counters()
+
+
+def test_get_or_insert_loader_error_inserts_nothing(cuda_device):
+    from objeta_b200 import QuantFormat
+    from objeta_b200.moe import CudaExpertCache, ExpertCacheKey, ExpertTensorKind
+    c = CudaExpertCache(10_000, cuda_device)
+    k = ExpertCacheKey(0, 1, ExpertTensorKind.Gate, QuantFormat.Q4_0)
+
+    def bad():
+        raise IOError("expert file missing")
+    with pytest.raises(IOError):
+        c.get_or_insert(k, bad)
+    s = c.stats()
+    assert (s["miss_count"], s["cache_insert_attempt_count"], s["resident_bytes"]) == (1, 0, 0)
+    assert not c.contains(k)
+
+
 def test_cache_data_roundtrip(cuda_device):
     """Resident bytes equal the uploaded host bytes, across slot reuse."""
     import ctypes
@@ -377,6 +462,34 @@ def test_device_layer_fp4_baseline_shape(cuda_device):
         bound = moe_bound(fp4_matrices({e: host[e] for e, _ in sel}, hidden, inter, hidden), sel, x, hidden, inter,
                           hidden)
         _check(out.cpu().numpy(), ref, bound, f"fp4 layer token {tok}")
+
+
+def test_bad_expert_id_leaves_later_calls_exact(cuda_device):
+    """A call with an out-of-range expert id records code 8 in the device
+    error word; later calls on the regular entry point, made without
+    objb_device_error_take, still wait for every stage and return the same
+    bits as before (their bounded waits stop early only on a timeout of their
+    own CTA, never on an older code in the device word)."""
+    import torch
+    from objeta_b200.moe import MoeLayer
+    from objeta_b200.quant import device_error_take
+    H_, I_, O_, E_ = 4096, 14336, 4096, 3
+    mats = _device_q4_layer(O.Q4_0, E_, H_, I_, O_, seed=77)
+    layer = MoeLayer(O.Q4_0, H_, I_, O_, mats["gate"], mats["up"], mats["down"])
+    x = torch.randn(H_, device="cuda")
+    ids = torch.tensor([2, 0], dtype=torch.int32, device="cuda")
+    w = torch.tensor([0.75, 0.25], device="cuda")
+    device_error_take(cuda_device)
+    ref = layer.forward_selected(ids, w, x).clone()
+    torch.cuda.synchronize()
+    assert device_error_take(cuda_device) == 0
+    layer.forward_selected(torch.tensor([2, 9], dtype=torch.int32, device="cuda"), w, x)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        out = layer.forward_selected(ids, w, x)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert device_error_take(cuda_device) == 8
 
 
 def test_no_device_errors_recorded(cuda_device):
