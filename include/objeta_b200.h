@@ -594,6 +594,28 @@ int objb_ep_partial_combine_device(const int32_t *d_ids_all, const float *d_w_al
 int objb_ep_sum_partials_device(const float *d_parts, size_t world, size_t tokens,
                                 size_t out_dim, float *d_out, objb_stream_t stream);
 
+/* The same step with ONE all-gather instead of three (no reference
+ * counterpart).  A rank packs its step into a buffer of
+ * objb_ep_packed_rows(T, top_k, H) rows of H floats: its T token rows, then
+ * its routing ids (int32 bits) and weights, zero-padded
+ * (objb_ep_pack_device).  After an all-gather of those buffers into d_recv
+ * [G][rows][H], the pair builder and the partial combine read ids, weights
+ * and token rows straight from it: pair_token is then a row of d_recv seen
+ * as [G*rows][H] (pass it to objb_moe_pairs_device with num_tokens =
+ * G*rows); pair_out and the partials are as above. */
+size_t objb_ep_packed_rows(size_t tokens, size_t top_k, size_t hidden);
+int objb_ep_pack_device(const float *d_x, const int32_t *d_ids, const float *d_w, size_t tokens,
+                        size_t top_k, size_t hidden, float *d_send, objb_stream_t stream);
+int objb_ep_build_pairs_packed_device(const float *d_recv, size_t world, size_t tokens,
+                                      size_t top_k, size_t hidden, size_t num_experts, size_t rank,
+                                      int32_t *d_pair_expert, int32_t *d_pair_token,
+                                      int32_t *d_pair_out, int32_t *d_num_pairs,
+                                      objb_stream_t stream);
+int objb_ep_partial_combine_packed_device(const float *d_recv, const float *d_v, size_t world,
+                                          size_t tokens, size_t top_k, size_t hidden,
+                                          size_t num_experts, size_t rank, size_t out_dim,
+                                          float *d_partial, objb_stream_t stream);
+
 /* cpu_gate_ref (dsl_moe.rs:768-881), the DeepSeek V4 gate, for num_tokens
  * tokens (one CTA each): logits = W h with W f32 [num_experts][hidden_size]
  * (sequential f32 sums, bit-identical to the reference); scores by

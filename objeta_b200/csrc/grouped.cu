@@ -1,12 +1,14 @@
 // grouped.cu -- the multi-token ("grouped expert") MoE contraction on the
 // tensor cores: for Q4_0 experts, each 128-row tile of an expert's matrix is
 // multiplied with the digit planes of up to 32 vectors routed to that expert
-// by tcgen05 kind::i8 MMAs (unsigned 4-bit codes x signed 7-bit digits, S32
-// in tensor memory), one MMA per 32-column block; the epilogue combines the
-// three digit products into the exact integer block sum and applies the
-// block's f16 row scale and the vector's block scale in f32:
-//   y[v][r] = sum_b d[r][b] * 2^(E[v][b]-20) * (sum_i q[r][b][i] X[v][b][i] - 8 sum_i X[v][b][i])
+// by tcgen05 kind::i8 MMAs (signed codes q - 8 x signed 7-bit digits, both
+// s8, S32 in tensor memory), one MMA per 32-column block; the epilogue
+// combines the three digit products into the exact integer block sum and
+// applies the block's f16 row scale and the vector's block scale in f32:
+//   y[v][r] = sum_b d[r][b] * 2^(E[v][b]-20) * sum_i (q[r][b][i] - 8) X[v][b][i]
 // -- the arithmetic of the CUDA-core row programs, summed in another order.
+// Wide blocks of a vector (objb_decode.cuh) have zero digits here and are
+// added in fp32 by the SwiGLU and wide-down kernels.
 //
 // A launch works on pairs sorted by expert: "slices" (pieces of at most 32
 // pairs of one expert) are found on the device (no host round trip), and

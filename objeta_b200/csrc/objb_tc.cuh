@@ -29,13 +29,6 @@ __device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t saddr, uint32_t lb
   return d;
 }
 
-// Instruction descriptor of kind::i8: S32 accumulator, A unsigned 8-bit,
-// B signed 8-bit, both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_u8s8(int m, int n) {
-  return (2u << 4) | (0u << 7) | (1u << 10) | ((static_cast<uint32_t>(n) >> 3) << 17) |
-         ((static_cast<uint32_t>(m) >> 4) << 24);
-}
-
 // One warp allocates `ncols` (a power of two >= 32) tensor-memory columns;
 // the base address is written to *dst (shared memory).
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {

@@ -56,6 +56,12 @@ _lib.register_signatures({
     "objb_ep_partial_combine_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_size,
                                                c_size, c_size, c_void_p, c_void_p]),
     "objb_ep_sum_partials_device": (c_int, [c_void_p, c_size, c_size, c_size, c_void_p, c_void_p]),
+    "objb_ep_packed_rows": (c_size, [c_size, c_size, c_size]),
+    "objb_ep_pack_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_size, c_size, c_void_p, c_void_p]),
+    "objb_ep_build_pairs_packed_device": (c_int, [c_void_p, c_size, c_size, c_size, c_size, c_size, c_size,
+                                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "objb_ep_partial_combine_packed_device": (c_int, [c_void_p, c_void_p, c_size, c_size, c_size, c_size, c_size,
+                                                      c_size, c_size, c_void_p, c_void_p]),
     "objb_deepseek_gate_device": (c_int, [c_void_p, c_void_p, c_void_p, c_size, c_void_p, c_void_p, c_size, c_size,
                                           c_size, c_size, c_int, ctypes.c_float, c_void_p, c_void_p, c_void_p]),
 })
@@ -117,6 +123,44 @@ def ep_sum_partials(parts, stream=None):
     out = torch.empty(T, O_, dtype=torch.float32, device=parts.device)
     _lib.call("objb_ep_sum_partials_device", _dev_ptr(parts), G, T, O_, _dev_ptr(out), _lib.stream_handle(stream))
     return out
+
+
+def ep_packed_rows(tokens: int, top_k: int, hidden: int) -> int:
+    """Rows of H floats in one rank's packed exchange buffer: its T token rows,
+    then its ids and weights (objb_ep_packed_rows)."""
+    return int(_lib.load().objb_ep_packed_rows(tokens, top_k, hidden))
+
+
+def ep_pack(x, ids, w, send, stream=None):
+    """Packs this rank's step (x [T, H] f32, ids [T, k] int32, w [T, k] f32)
+    into send [ep_packed_rows(T, k, H), H] for the one all-gather."""
+    T, H = x.shape
+    K = ids.shape[1]
+    _lib.call("objb_ep_pack_device", _dev_ptr(x), _dev_ptr(ids), _dev_ptr(w), T, K, H, _dev_ptr(send),
+              _lib.stream_handle(stream))
+    return send
+
+
+def ep_build_pairs_packed(recv, world: int, tokens: int, top_k: int, rank: int, num_experts: int, stream=None):
+    """ep_build_pairs reading the ids from the all-gathered packed buffers
+    recv [G * rows, H]; pair_token indexes the rows of recv."""
+    import torch
+    n = world * tokens * top_k
+    buf = torch.empty(3 * n + 1, dtype=torch.int32, device=recv.device)
+    pe, pt, po, cnt = buf[:n], buf[n:2 * n], buf[2 * n:3 * n], buf[3 * n:]
+    _lib.call("objb_ep_build_pairs_packed_device", _dev_ptr(recv), world, tokens, top_k, recv.shape[1], num_experts,
+              rank, _dev_ptr(pe), _dev_ptr(pt), _dev_ptr(po), _dev_ptr(cnt), _lib.stream_handle(stream))
+    return pe, pt, po, cnt
+
+
+def ep_partial_combine_packed(recv, v, world: int, tokens: int, top_k: int, rank: int, num_experts: int,
+                              out_dim: int, stream=None):
+    """ep_partial_combine reading ids and weights from the packed buffers."""
+    import torch
+    part = torch.empty(world, tokens, out_dim, dtype=torch.float32, device=v.device)
+    _lib.call("objb_ep_partial_combine_packed_device", _dev_ptr(recv), _dev_ptr(v), world, tokens, top_k,
+              recv.shape[1], num_experts, rank, out_dim, _dev_ptr(part), _lib.stream_handle(stream))
+    return part
 
 
 def router_topk_batched(d_logits, top_k: int, renormalize: bool = False, stream=None):
@@ -352,6 +396,7 @@ class ExpertParallelMoe:
             raise ValueError("grouped='on' needs a Q4_0 layer with hidden, intermediate multiples of 256")
         self.grouped = grouped
         self.last_plan = None
+        self.phase_events = None  # a list: forward() appends (phase, CUDA event) boundaries to it
         self._pin = None     # pinned int32 staging for plan arrays (grow-only)
         self._dmeta = None   # device copy (grow-only)
         self._slot_cache = {}
@@ -429,38 +474,60 @@ class ExpertParallelMoe:
         if key not in self._slot_cache:
             self._slot_cache[key] = torch.arange(T * K, dtype=torch.int32, device=x.device).view(T, K)
         slot = self._slot_cache[key]
+        stream = torch.cuda.current_stream(x.device)
+        self._mark("start", stream)
         _, perm = torch.sort(flat, stable=True)
         perm = perm.to(torch.int32)
         pair_expert = flat.index_select(0, perm)
         pair_token = torch.div(perm, K, rounding_mode="floor").to(torch.int32)
-        stream = torch.cuda.current_stream(x.device)
+        self._mark("sort", stream)
         v = torch.empty(T * K, self.out_dim, dtype=torch.float32, device=x.device)
         self._pairs_fn(T * K)(self.layer, pair_expert, pair_token, x.contiguous(), v, pair_out=perm,
                               swiglu_limit=self.swiglu_limit, stream=stream)
+        self._mark("pairs", stream)
         out = torch.empty(T, self.out_dim, dtype=torch.float32, device=x.device)
-        return moe_combine(v, slot, w.contiguous(), out, stream=stream)
+        moe_combine(v, slot, w.contiguous(), out, stream=stream)
+        self._mark("combine", stream)
+        return out
+
+    def _mark(self, name, stream):
+        """Records a phase boundary when the step is instrumented."""
+        if self.phase_events is not None:
+            import torch
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            self.phase_events.append((name, ev))
 
     def _forward_device_exchange(self, x, ids, w):
+        """One all-gather of every rank's packed step (token rows, ids,
+        weights), the pair list built from it on the device, the pairs, a
+        per-rank partial combine and one all-to-all of the partials."""
         import torch
         import torch.distributed as dist
         G, (T, K) = self.world, ids.shape
+        H = x.shape[1]
         dev = x.device
         stream = torch.cuda.current_stream(dev)
-        ids = ids.to(torch.int32).contiguous()
-        ids_all = torch.empty(G, T, K, dtype=torch.int32, device=dev)
-        w_all = torch.empty(G, T, K, dtype=torch.float32, device=dev)
-        x_all = torch.empty(G * T, x.shape[1], dtype=x.dtype, device=dev)
-        dist.all_gather_into_tensor(ids_all, ids, group=self.group)
-        dist.all_gather_into_tensor(w_all, w.contiguous(), group=self.group)
-        dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
-        pe, pt, po, cnt = ep_build_pairs(ids_all, self.rank, self.num_experts, stream=stream)
+        rows = ep_packed_rows(T, K, H)
+        send = torch.empty(rows, H, dtype=torch.float32, device=dev)
+        self._mark("start", stream)
+        ep_pack(x.contiguous(), ids.to(torch.int32).contiguous(), w.contiguous(), send, stream=stream)
+        recv = torch.empty(G * rows, H, dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        self._mark("pack+all_gather", stream)
+        pe, pt, po, cnt = ep_build_pairs_packed(recv, G, T, K, self.rank, self.num_experts, stream=stream)
         v = torch.empty(G * T * K, self.out_dim, dtype=torch.float32, device=dev)
-        self._pairs_fn(T * K)(self.layer, pe, pt, x_all, v, pair_out=po, swiglu_limit=self.swiglu_limit,
+        self._pairs_fn(T * K)(self.layer, pe, pt, recv, v, pair_out=po, swiglu_limit=self.swiglu_limit,
                               stream=stream, d_count=cnt)
-        part = ep_partial_combine(ids_all, w_all, v, self.rank, self.num_experts, self.out_dim, stream=stream)
-        recv = torch.empty_like(part)
-        dist.all_to_all_single(recv, part, group=self.group)
-        return ep_sum_partials(recv, stream=stream)
+        self._mark("build_pairs+pairs", stream)
+        part = ep_partial_combine_packed(recv, v, G, T, K, self.rank, self.num_experts, self.out_dim, stream=stream)
+        self._mark("partial_combine", stream)
+        got = torch.empty_like(part)
+        dist.all_to_all_single(got, part, group=self.group)
+        self._mark("all_to_all", stream)
+        out = ep_sum_partials(got, stream=stream)
+        self._mark("sum", stream)
+        return out
 
     # ---- the layer
     def plan(self, ids) -> DispatchPlan:

@@ -344,3 +344,49 @@ def test_ep_device_exchange_emulated_ranks(cuda_device):
             bound = moe_bound(q4_matrices(host, H, I, OUT), sel, xh[t], H, I, OUT)
             err = np.abs(a[s][t].cpu().numpy().astype(np.float64) - ref[t].astype(np.float64))
             assert np.all(err <= 2 * bound), f"rank {s} token {t}: max err {err.max()}"
+
+
+@pytest.mark.parametrize("G,T,K,tc", [(3, 5, 4, False), (2, 40, 8, True), (4, 1, 8, False)])
+def test_ep_packed_exchange_emulated_ranks(cuda_device, G, T, K, tc):
+    """The one-all-gather exchange (objb_ep_pack_device, then the pair builder
+    and partial combine reading the packed buffers) emulated on one GPU: the
+    concatenated packed buffers stand in for the all-gather.  Every rank's
+    partials equal, bit for bit, those of the three-all-gather layout."""
+    import torch
+    from objeta_b200.ep import (ep_build_pairs, ep_build_pairs_packed, ep_pack, ep_packed_rows, ep_partial_combine,
+                                ep_partial_combine_packed, moe_pairs, moe_pairs_tc)
+    from objeta_b200.moe import MoeLayer
+    from objeta_b200.quant import device_error_take
+    E, H, I, OUT = 8 * G, 1024, 512, 768
+    _, mats = _q4_layer(O.Q4_0, E, H, I, OUT, seed=91 + G)
+    epr = E // G
+    shards = [MoeLayer(O.Q4_0, H, I, OUT, mats["gate"][r * epr:(r + 1) * epr], mats["up"][r * epr:(r + 1) * epr],
+                       mats["down"][r * epr:(r + 1) * epr]) for r in range(G)]
+    routes = [_routes(T, E, K, seed=300 + r) for r in range(G)]
+    ids = [torch.from_numpy(r[0].astype(np.int32)).cuda() for r in routes]
+    ws = [torch.from_numpy(r[1]).cuda() for r in routes]
+    xs = [torch.randn(T, H, device="cuda") for _ in range(G)]
+    rows = ep_packed_rows(T, K, H)
+    assert rows == T + -(-2 * T * K // H)
+    sends = [ep_pack(xs[r], ids[r], ws[r], torch.full((rows, H), float("nan"), device="cuda")) for r in range(G)]
+    recv = torch.cat(sends)
+    ids_all, w_all, x_all = torch.stack(ids), torch.stack(ws), torch.cat(xs)
+    pairs = moe_pairs_tc if tc else moe_pairs
+    device_error_take(cuda_device)
+    for r in range(G):
+        pe, pt, po, cnt = ep_build_pairs_packed(recv, G, T, K, r, E)
+        v = torch.zeros(G * T * K, OUT, device="cuda")
+        pairs(shards[r], pe, pt, recv, v, pair_out=po, d_count=cnt)
+        got = ep_partial_combine_packed(recv, v, G, T, K, r, E, OUT)
+        pe0, pt0, po0, cnt0 = ep_build_pairs(ids_all, r, E)
+        v0 = torch.zeros(G * T * K, OUT, device="cuda")
+        pairs(shards[r], pe0, pt0, x_all, v0, pair_out=po0, d_count=cnt0)
+        want = ep_partial_combine(ids_all, w_all, v0, r, E, OUT)
+        torch.cuda.synchronize()
+        assert int(cnt.item()) == int(cnt0.item())
+        n = int(cnt.item())
+        rows_tok = pt[:n].cpu().numpy()
+        assert np.all(rows_tok % rows < T)                            # token rows only, never the packed ids
+        assert sorted(zip(pe[:n].tolist(), po[:n].tolist())) == sorted(zip(pe0[:n].tolist(), po0[:n].tolist()))
+        assert _bits_equal(got, want), f"rank {r}"
+    assert device_error_take(cuda_device) == 0
