@@ -149,6 +149,68 @@ def read_traffic(kernel_key):
 
 
 # --------------------------------------------------------------- our arm
+def sweep_config(world):
+    """The `config` of the bench line, identical in both arms."""
+    return {"workload": "configs[1] GEMV sweep, batch 1", "formats": ["q4_0", "q5_0", "iq3_0"],
+            "shapes": [f"{r}x{c}" for r, c in SHAPES], "global_batch": 1 * world,
+            "parallelism": f"replicas x{world} (no exchange)",
+            "l2_defeat": "weights rotated over >= 4x L2 per case (GPU); CPU: matrices far above the LLC",
+            "bytes_per_step": sum(algo_bytes(f, r, c) for f in HEADLINE_FORMATS for r, c in SHAPES)}
+
+
+def cpu_sweep_inputs(seed=1234):
+    """The configs[1] sweep for the CPU leg, packed by the oracle's packers
+    (the C restatement of quantize_matrix_cpu): a 64-row tile of
+    N(0, 0.02^2) weights per case, repeated to the full matrix (packing the
+    full 1.3 G weights on the CPU would take longer than the timing), and
+    x ~ N(0, 1).  Both CPU legs (the GPU arm's cpu_baseline and --impl
+    reference) time these same bytes."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    inputs = []
+    for fmt in HEADLINE_FORMATS:
+        for rows, cols in SHAPES:
+            nb = rows * (cols // 32) * BLOCK_BYTES[fmt]
+            m = (rng.standard_normal(64 * cols) * 0.02).astype(np.float32)
+            q = np.resize(O.quantize_matrix(fmt, m, 64, cols), nb)
+            x = rng.standard_normal(cols).astype(np.float32)
+            inputs.append((fmt, rows, cols, q, x))
+    return inputs
+
+
+def time_cpu_sweep(inputs, threads, passes, warmup):
+    """Seconds per pass of the oracle's gemv_cpu over the sweep (row-parallel
+    over `threads` threads; 1 = the reference's single-threaded loop), after
+    `warmup` untimed passes."""
+    from oracle import oracle as O
+    for _ in range(warmup):
+        for f, r, c, q, x in inputs:
+            O.gemv(f, q, x, r, c, threads=threads)
+    t = time.perf_counter()
+    for _ in range(passes):
+        for f, r, c, q, x in inputs:
+            O.gemv(f, q, x, r, c, threads=threads)
+    return (time.perf_counter() - t) / passes
+
+
+def cpu_legs(steps, warmup):
+    """Both CPU figures on the same packed sweep: all host threads (`steps`
+    passes after `warmup`) and one thread (one pass after one warm-up, a
+    bounded sample of about 5 s)."""
+    inputs = cpu_sweep_inputs()
+    step_bytes = sum(algo_bytes(f, r, c) for f, r, c, _, _ in inputs)
+    threads = os.cpu_count() or 1
+    t_all = time_cpu_sweep(inputs, threads, steps, warmup)
+    t_one = time_cpu_sweep(inputs, 1, 1, 1)
+    return {"value": round(step_bytes / t_all / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"the full configs[1] sweep (12 GEMVs, {step_bytes} bytes) per pass; {steps} passes after "
+                      f"{warmup} warm-up on {threads} threads (row-parallel), 1 pass after 1 warm-up on one thread; "
+                      "C restatement of gemv_cpu (quant.rs:627-1019), the Rust reference cannot be built here",
+            "single_thread": {"value": round(step_bytes / t_one / 1e9, 3), "unit": "GB/s", "cores": 1,
+                              "seconds_per_pass": round(t_one, 3)},
+            "seconds_per_pass": round(t_all, 4), "passes": steps}
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -317,18 +379,15 @@ def run_ours(args, world, rank, local):
             "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32-accumulate (u4/u5/u3 codes, f16 scales)",
             "data": "synthetic: weights ~N(0,0.02^2) packed on device, x ~N(0,1), seeded",
-            "config": {"workload": "configs[1] GEMV sweep, batch 1", "formats": ["q4_0", "q5_0", "iq3_0"],
-                       "shapes": [f"{r}x{c}" for r, c in SHAPES], "global_batch": 1 * world,
-                       "parallelism": f"replicas x{world} (no exchange)",
-                       "l2_defeat": "weights rotated over >= 4x L2 per case",
-                       "bytes_per_step": step_bytes, "cuda_graph": True,
-                       "timing": "headline: graph replays of the 12 GEMVs back to back; per case: event pairs"},
+            "config": sweep_config(world),
+            "timing": "headline: CUDA-graph replays of the 12 GEMVs back to back; per case: event pairs",
             "roofline": roofline, "cases": case_out, "e2e": e2e, "moe": moe,
             "gpu_launches": args.steps * sum(gemv_launches(c["cols"]) for c in headline),
             "clocks": sampler.summary(),
         }
-        cb = cpu_baseline(cases, headline, args)
-        result["cpu_baseline"] = cb
+        result["cpu_baseline"] = cpu_legs(max(3, min(args.steps, 10)), 2)
+        if "c5_ep_resident" in moe:
+            result["ep"] = ep_summary(moe["c5_ep_resident"], world)
     if world > 1:
         dist.barrier()
         del graphs, xgraphs, plain
@@ -410,30 +469,6 @@ def run_e2e(qb, cases, headline, args, world, rank, dev):
             "h2d_bytes_per_step": h2d // steps, "d2h_bytes_per_step": d2h // steps,
             "steps": steps, "api": "QuantBackend.gemv (objb_gemv_host): H2D weights+x, kernel, D2H y per call",
             "timer": "host wall clock (perf_counter), each call synchronous like the reference"}
-
-
-def cpu_baseline(cases, headline, args):
-    """The reference CPU path (C restatement of gemv_cpu) on the host cores,
-    on a bounded sample: every headline case on its first rows_sample rows."""
-    from oracle import oracle as O
-    threads = os.cpu_count() or 1
-    frac = 1.0
-    samples = []
-    for c in headline:
-        rows = max(1, int(c["rows"] * frac))
-        q = c["copies"][0][: rows * (c["cols"] // 32) * BLOCK_BYTES[c["fmt"]]].cpu().numpy()
-        x = c["x"].cpu().numpy()
-        samples.append((c, rows, q, x))
-    O.gemv(0, samples[0][2][: samples[0][3].size // 32 * 18], samples[0][3], 1, samples[0][3].size)
-    t = time.perf_counter()
-    nbytes = 0
-    for c, rows, q, x in samples:
-        O.gemv(c["fmt"], q, x, rows, c["cols"], threads=threads)
-        nbytes += algo_bytes(c["fmt"], rows, c["cols"])
-    el = time.perf_counter() - t
-    return {"value": round(nbytes / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"one pass of the 12 configs[1] GEMVs (full size), row-parallel over {threads} threads, "
-                      f"{el:.2f} s", "seconds": round(el, 2)}
 
 
 # ------------------------------------------------------------ MoE configs
@@ -607,7 +642,7 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
     Zipf(1.1) routing, T tokens per rank, NCCL all-to-all dispatch/combine."""
     import torch
     import torch.distributed as dist
-    from objeta_b200.ep import ExpertParallelMoe
+    from objeta_b200.ep import ExpertParallelMoe, ep_packed_rows
     from objeta_b200.moe import MoeLayer
     c = C5
     H, I, E, K = c["hidden"], c["inter"], c["experts"], c["top_k"]
@@ -630,11 +665,11 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
         ids = [torch.from_numpy(r[0]).to(dev) for r in routes]
         ws = [torch.from_numpy(r[1]).to(dev) for r in routes]
         n = max(3, min(steps, 10))
-        # bytes each step must move: this rank's distinct experts, and rows
-        # sent to other ranks (from the dispatch plans, outside the timing)
+        # weight bytes each step must read: this rank's distinct experts
+        # (host dispatch plans, outside the timing)
         plans = [ep.plan(ids[i]) for i in range(S)]
         uniq = sum(len(np.unique(plans[i % S].pair_expert)) for i in range(n))
-        nvb = sum(sum(plans[i % S].exchange_bytes(H, H).values()) for i in range(n))
+        nvb = 0
         # the step has no host round trip (one rank: device sort; several: the
         # device exchange, its NCCL all-gathers and all-to-all on the step's
         # stream), so every rank captures it in CUDA graphs and replays them;
@@ -651,20 +686,76 @@ def bench_c5_resident(qb, dev, gen, world, rank, group, steps, warmup, peak):
             ms = float(mx[0])
         per_step = ms / n
         wbytes = float(stats[1]) / n
-        nv = float(stats[2]) / n
         gbs = wbytes / (per_step / 1e3) / 1e9
+        phases = ep_phases(ep, xs, ids, ws, dev, group, world)
+        # bytes each rank receives over NVLink per step: the packed buffers of
+        # the G - 1 other ranks (one all-gather) and their partials (one
+        # all-to-all); nothing at one rank
+        rows = ep_packed_rows(T, K, H)
+        nv_rank = (world - 1) * (rows * H + T * H) * 4
+        coll_us = phases.get("pack+all_gather", 0.0) + phases.get("all_to_all", 0.0)
         res[f"T{T}"] = {"tokens_per_s": round(T * world * 1e3 / per_step, 1), "us_per_step": round(per_step * 1e3, 1),
                         "unique_expert_bytes_per_step_all_ranks": int(wbytes), "GB/s_all_ranks": round(gbs, 1),
                         "frac_of_aggregate_hbm": round(gbs / (peak * world), 4),
-                        "nvlink_bytes_per_step_all_ranks": int(nv), "steps": n}
+                        "nvlink_bytes_per_step_all_ranks": int(nv_rank * world),
+                        "nvlink_GB/s_per_gpu_over_step": round(nv_rank / (per_step / 1e3) / 1e9, 2),
+                        "nvlink_GB/s_per_gpu_in_collectives": round(nv_rank / (coll_us / 1e6) / 1e9, 2)
+                        if coll_us > 0 and nv_rank else 0.0,
+                        "nvlink_frac_of_peer_copy_in_collectives": round(nv_rank / (coll_us / 1e6) / 1e9 / NVLINK_GBS, 4)
+                        if coll_us > 0 and nv_rank else 0.0,
+                        "phases_us": phases, "steps": n}
     del ep, layer
     torch.cuda.empty_cache()
     return {"config": f"configs[4] EP layer, experts resident: 256 Q4_0 experts / {world} rank(s), H 2048, I 512, "
                       "top-8 Zipf(1.1), T tokens per rank",
             "scaling": "weak (T tokens per rank)", "timer": "CUDA events around whole steps, max over ranks; the "
-            "device-only step replayed as CUDA graphs (one rank: sort + pairs + combine; several: NCCL all-gathers "
-            "of routing table, weights and token rows, device-built pair list, pairs, partial combine, NCCL "
-            "all-to-all, ordered sum)", **res}
+            "device-only step replayed as CUDA graphs (one rank: sort + pairs + combine; several: one NCCL "
+            "all-gather of the packed token rows, ids and weights, device-built pair list, pairs, partial "
+            "combine, one NCCL all-to-all, ordered sum); phases_us from CUDA events at the phase boundaries "
+            "of 3 eager steps", **res}
+
+
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (nominal 900)
+
+
+def ep_phases(ep, xs, ids, ws, dev, group, world, reps=3):
+    """Mean device time (us) of each phase of an expert-parallel step, from
+    CUDA events the layer records at its phase boundaries during `reps`
+    eager (not graph) steps; max over ranks."""
+    import torch
+    import torch.distributed as dist
+    sums = {}
+    for i in range(reps):
+        ep.phase_events = []
+        ep.forward(xs[i % len(xs)], ids[i % len(ids)], ws[i % len(ws)])
+        torch.cuda.synchronize()
+        evs = ep.phase_events
+        for (_, a), (name, b) in zip(evs, evs[1:]):
+            sums[name] = sums.get(name, 0.0) + a.elapsed_time(b) * 1e3 / reps
+    ep.phase_events = None
+    names = sorted(sums)
+    t = torch.tensor([sums[k] for k in names], dtype=torch.float64, device=dev)
+    if world > 1 and names:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return {k: round(float(v), 1) for k, v in zip(names, t.tolist())}
+
+
+def ep_summary(c5, world):
+    """The expert-parallel numbers lifted to the top of the bench line."""
+    out = {"config": c5["config"], "ranks": world, "scaling": c5["scaling"]}
+    for key in ("T1", "T16", "T256"):
+        r = c5.get(key)
+        if not r:
+            continue
+        ph = r.get("phases_us", {})
+        out[key] = {k: r[k] for k in ("tokens_per_s", "us_per_step", "frac_of_aggregate_hbm",
+                                       "nvlink_bytes_per_step_all_ranks", "nvlink_GB/s_per_gpu_over_step",
+                                       "nvlink_GB/s_per_gpu_in_collectives",
+                                       "nvlink_frac_of_peer_copy_in_collectives")}
+        out[key]["phases_us"] = ph
+        if ph:
+            out[key]["largest_phase"] = max(ph, key=ph.get)
+    return out
 
 
 def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
@@ -754,45 +845,20 @@ def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
 
 # --------------------------------------------------------- reference arm
 def run_reference(args, world, rank):
+    """The reference's CPU path on the host cores: the oracle's C restatement
+    of gemv_cpu over the configs[1] sweep, all host threads, `steps` passes
+    after `warmup` (rank 0 only; other ranks exit without work)."""
     if rank != 0:
         return None
-    import torch
-    from oracle import oracle as O
-    rng = np.random.default_rng(1234)
-    threads = os.cpu_count() or 1
-    inputs = []
-    for fmt in HEADLINE_FORMATS:
-        for rows, cols in SHAPES:
-            nb = rows * (cols // 32) * BLOCK_BYTES[fmt]
-            # packed bytes: quantize on CPU would dominate the setup; use random
-            # codes with realistic f16 / E8M0 scales via the oracle packer on a
-            # small matrix tiled to the full size (the timed work is the GEMV)
-            m = (rng.standard_normal(64 * cols) * 0.02).astype(np.float32)
-            tile = O.quantize_matrix(fmt, m, 64, cols)
-            q = np.resize(tile, nb)
-            x = rng.standard_normal(cols).astype(np.float32)
-            inputs.append((fmt, rows, cols, q, x))
-    step_bytes = sum(algo_bytes(f, r, c) for f, r, c, _, _ in inputs)
-    for _ in range(args.warmup):
-        for f, r, c, q, x in inputs[:1]:
-            O.gemv(f, q, x, r, c, threads=threads)
-    t = time.perf_counter()
-    for _ in range(args.steps):
-        for f, r, c, q, x in inputs:
-            O.gemv(f, q, x, r, c, threads=threads)
-    el = time.perf_counter() - t
-    value = step_bytes * args.steps / el / 1e9
-    return {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+    legs = cpu_legs(args.steps, args.warmup)
+    value = legs["value"]
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(el * 1e3 / args.steps, 2), "higher_is_better": True,
+            "ms_per_step": round(legs["seconds_per_pass"] * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic, seeded",
-            "config": {"workload": "configs[1] GEMV sweep, batch 1", "formats": ["q4_0", "q5_0", "iq3_0"],
-                       "shapes": [f"{r}x{c}" for r, c in SHAPES]},
-            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"full configs[1] sweep per step, row-parallel over {threads} threads "
-                                       "(C restatement of gemv_cpu; the Rust reference cannot be built here)"},
-            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "config": sweep_config(world),
+            "cpu_baseline": legs,
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def run_case(args, local):

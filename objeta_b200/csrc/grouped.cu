@@ -309,9 +309,10 @@ __global__ void __launch_bounds__(256) tc_wide_down_kernel(const float* __restri
                                                            int I, int O, const uint8_t* __restrict__ wflag_a,
                                                            const int32_t* pe, const int32_t* po, int v_rows,
                                                            const uint8_t* const* down_w, int num_experts,
-                                                           float* __restrict__ v) {
+                                                           const int32_t* nslices, float* __restrict__ v) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (*nslices <= 0) return;  // the launch ran nothing (a pair list not grouped by expert): v stays as it was
   if (count) P = min(max(*count, 0), P);
   const int nb = I / 32, nrb = (O + 31) / 32, lane = threadIdx.x & 31;
   const size_t row_bytes = static_cast<size_t>(nb) * 18;
@@ -1347,7 +1348,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_dn));
   OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, std::max(O, 32)), 256, 0, stream,
                       static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a), pe, po,
-                      static_cast<int>(v_rows), a.W, a.num_experts, v));
+                      static_cast<int>(v_rows), a.W, a.num_experts, static_cast<const int32_t*>(nslices), v));
   return OBJB_OK;
 }
 

@@ -513,31 +513,45 @@ struct Job {
   const float* xd = nullptr;  // digit rows: this job's vector as floats, for the terms of wide blocks
 };
 
-// The fp32 terms of the wide blocks of a digit image (flagged kWideMark):
-// w0 / w1 are the lanes of this warp whose tile block 0 / 1 is wide.  For
-// each such block every lane adds its element's term to its partial of each
-// of the batch's rows, so the warp's row reduction sums the block with the
-// rest of the row.
-template <int FMT, int RB, bool DUAL, int NV>
-__device__ __forceinline__ void add_wide_terms(float (&v)[NV], uint32_t w0, uint32_t w1, int seg, int lane,
-                                               const uint8_t* stg, int part, int row_bytes, int bt, int nr,
-                                               const float* __restrict__ xd) {
+// The fp32 terms of the wide blocks of a digit image (flagged kWideMark),
+// added after a stage's integer row dots: w0 / w1 are the lanes of this warp
+// whose tile block 0 / 1 is wide.  For each of the warp's rows of the stage
+// every lane forms its element's term of every wide block, the warp sums
+// them, and lane 0 adds the sum to the row's partial of this column segment
+// (the slot the row dot wrote in `red`).  Runs only when the vector has a
+// wide block, outside the integer loop, so that loop keeps its registers.
+template <int FMT, bool DUAL>
+__device__ __forceinline__ void add_wide_terms(float* red, const uint8_t* stg, int part, int row_bytes, int nseg,
+                                            int seg, int grp, int ngrp, int nr, uint32_t w0, uint32_t w1,
+                                            const float* __restrict__ xd) {
   using T = Tile<FMT>;
+  const int lane = threadIdx.x & 31;
+  for (int t = grp * 4; t < nr; t += ngrp * 4) {
+    const int tend = min(nr, t + 4);
+    for (int r = t; r < tend; ++r) {
+      float sa = 0.0f, sb = 0.0f;
 #pragma unroll 1
-  for (int b = 0; b < 2; ++b) {
-    uint32_t m = b ? w1 : w0;
+      for (int b = 0; b < 2; ++b) {
+        uint32_t m = b ? w1 : w0;
 #pragma unroll 1
-    while (m) {
-      const int src = __ffs(m) - 1;
-      m &= m - 1;
-      const int lt = seg * 32 + src;
-      const int boff = lt * T::TB + b * T::BB;
-      const float xl = __ldg(xd + static_cast<size_t>(lt * T::P + b) * 32 + lane);
+        while (m) {
+          const int src = __ffs(m) - 1;
+          m &= m - 1;
+          const int lt = seg * 32 + src;
+          const int boff = lt * T::TB + b * T::BB;
+          const float xl = __ldg(xd + static_cast<size_t>(lt * T::P + b) * 32 + lane);
+          sa += wide_term<FMT>(stg + r * row_bytes + boff, lane, xl);
+          if constexpr (DUAL) sb += wide_term<FMT>(stg + part + r * row_bytes + boff, lane, xl);
+        }
+      }
 #pragma unroll
-      for (int i = 0; i < RB; ++i) {
-        const int t = min(bt + i, nr - 1);
-        v[i] += wide_term<FMT>(stg + t * row_bytes + boff, lane, xl);
-        if constexpr (DUAL) v[RB + i] += wide_term<FMT>(stg + part + t * row_bytes + boff, lane, xl);
+      for (int o = 16; o > 0; o >>= 1) {
+        sa += __shfl_xor_sync(0xFFFFFFFFu, sa, o);
+        if constexpr (DUAL) sb += __shfl_xor_sync(0xFFFFFFFFu, sb, o);
+      }
+      if (lane == 0) {
+        red[(r * nseg + seg) * 2] += sa;
+        if constexpr (DUAL) red[(r * nseg + seg) * 2 + 1] += sb;
       }
     }
   }
@@ -666,16 +680,6 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
     } else if (xin == nullptr) {
       load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     }
-    // digit rows: lanes whose tile block 0 / 1 is wide (warp-uniform masks)
-    uint32_t wide0 = 0u, wide1 = 0u;
-    if constexpr (IsDigitRD<RD>::value) {
-      wide0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
-      wide1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
-      if ((wide0 | wide1) != 0u && J.xd == nullptr) {
-        if (lane == 0 && err) atomicOr(err, kErrNoWideSource);
-        wide0 = wide1 = 0u;
-      }
-    }
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
       if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout, sp.abort);
@@ -693,16 +697,25 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
             v[RB + i] = rd.dot(stg + part + t * L.row_bytes,
                                stg + part + static_cast<size_t>(T) * L.row_bytes + t * L.srow_bytes, xr);
         }
-        if constexpr (IsDigitRD<RD>::value) {
-          if ((wide0 | wide1) != 0u)
-            add_wide_terms<IsDigitRD<RD>::fmt, RB, DUAL>(v, wide0, wide1, seg, lane, stg, part, L.row_bytes, bt, nr,
-                                                         J.xd);
-        }
         butterfly<NV>(v, lane);
         if ((lane & (W - 1)) == 0) {
           const int idx = lane / W;
           const int t = bt + (idx % RB);
           if (t < nr) red[(t * L.nseg + seg) * 2 + idx / RB] = v[0];
+        }
+      }
+      if constexpr (IsDigitRD<RD>::value) {
+        // wide blocks of the vector (warp-uniform masks, from the registers)
+        const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
+        const uint32_t w1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
+        if ((w0 | w1) != 0u) {
+          __syncwarp();
+          const float* xd = prog.job(cta, j).xd;
+          if (xd != nullptr)
+            add_wide_terms<IsDigitRD<RD>::fmt, DUAL>(red, stg, part, L.row_bytes, L.nseg, seg, grp, L.ngrp, nr, w0,
+                                                     w1, xd);
+          else if (lane == 0 && err)
+            atomicOr(err, kErrNoWideSource);
         }
       }
       __syncwarp();

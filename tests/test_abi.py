@@ -107,3 +107,12 @@ def test_compare_outputs_matches_reference_definition():
         raise AssertionError("length mismatch accepted")
     except CudaError as e:
         assert e.kind == "InvalidInput" and "reference len 1000 != actual len 999" in e.source_message
+
+
+def test_integration_binding_covers_the_header():
+    """INTEGRATION.md's Rust extern block declares every function of
+    include/*.h, so a maintainer can bind the whole ABI from it."""
+    text = (ROOT / "INTEGRATION.md").read_text()
+    block = text[text.index("## Rust FFI block"):text.index("## Status")]
+    missing = [n for n in header_functions() if f"pub fn {n}(" not in block]
+    assert not missing, f"not in the Rust block: {missing}"
