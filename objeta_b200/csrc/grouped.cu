@@ -183,7 +183,7 @@ __host__ __device__ constexpr uint32_t umma_idesc_s8s8(int m, int n) {
 // lane): X = rint(x * 2^(20-E)), E the block's frexp exponent, split in three
 // signed 7-bit digits; plane k at planes[(v * 3 + k) * C + col]; per block
 // 2^(E-20) (NaN when the block is not finite).  A wide block (block_is_wide:
-// its largest value dwarfs most of the others) gets zero digits, so the MMAs
+// its largest value dwarfs the others) gets zero digits, so the MMAs
 // add nothing for it, and wflag[v * C/32 + b] = 1: its terms are added in
 // fp32 by tc_add_wide_rows (gate / up) and tc_wide_down_kernel (down).
 __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc,
@@ -194,11 +194,13 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   int E = 0;
   frexpf(m, &E);
-  const float ax = fabsf(xe), thr = ldexpf(m, -kWideShift);
-  const int nsmall = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax < thr));
-  const int nbig = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax >= thr));
-  const bool wide = isfinite(m) && block_is_wide(nsmall, nbig);
-  const int X = wide ? 0 : __float2int_rn(ldexpf(xe, 20 - E));
+  const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
+  const int r = X0 != 0 ? kWideUnit : __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+  const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
+  const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
+  const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
+  const bool wide = isfinite(m) && block_is_wide(nnz, esum, capped);
+  const int X = wide ? 0 : X0;
   const int d0 = ((X + 64) & 127) - 64;
   const int X1 = (X - d0) / 128;
   const int d1 = ((X1 + 64) & 127) - 64;

@@ -121,20 +121,31 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
 }
 
 // ------------------------------------------------ wide blocks (exact path)
-// A block whose largest |x| dwarfs most of its other nonzero values ("wide":
-// at least one nonzero value, and no more values at or above 2^-8 of the
-// largest than below it) would lose those small values to the 2^-21 grid of
-// the largest one, and the rows whose weight is zero at the large value would
-// then miss the reference's 1e-5 * sum|w x| bound.  Its digit words and block
-// sum are zero in the image (it adds nothing to the integer path), its
-// 2^(E-20) word holds kWideMark, and the consumer warp adds the block's terms
-// in fp32 instead, one element per lane: ((q_l - off) * scale) * x_l.
-constexpr int kWideShift = 8;
+// Rounding X = rint(x * 2^(20-E)) moves an element by at most half a grid
+// step 2^(E-20); a value below half a step rounds to 0 and moves by itself.
+// That is harmless while the block's values are comparable, and not when a
+// few of them dwarf the rest: an outlier channel of 1e3 among N(0,1) values
+// leaves the others only ~10 bits (and at 1e7 none), and the rows that weigh
+// the outliers by zero then miss the reference's 1e-5 * sum|w x| bound.
+// Per block, in integers (so every image builder agrees bit for bit):
+//   e = sum_l r_l,  r_l = 2^10 if X_l != 0, else rint(|x_l| * 2^(31-E))
+//       (the rounding error bound in units of 2^-11 grid steps, <= 2^10),
+//   R = sum_l min(|X_l|, 2^15)   (the values, each capped at 2^-5 of 2^E),
+// and the block is "wide" when at least two x are nonzero and 8 e > R, i.e.
+// its possible rounding error exceeds 2^-14 of its capped mass.  Up to 8
+// outliers of up to ~1e6 times the block's ordinary values qualify (beyond
+// that an outlier's capped mass hides the others'); an N(0,1) block sits
+// about 4x below the line, and values far below the grid (silu of a large
+// negative gate) count only by their size.  A wide block's digit words and block sum are
+// zero in the image (it adds nothing to the integer path), its 2^(E-20) word
+// holds kWideMark, and the consumer warp adds the block's terms in fp32
+// instead, one element per lane: ((q_l - off) * scale) * x_l.
+constexpr int kWideCap = 1 << 15;
+constexpr int kWideUnit = 1 << 10;
 constexpr uint32_t kWideMark = 0x80000000u;  // -0.0f: a zero block sum times it stays zero
 
-// Whether a finite block is wide, from its value counts: `small` nonzero
-// values below 2^-kWideShift of the largest |x|, `big` values at or above it.
-__device__ __forceinline__ bool block_is_wide(int small, int big) { return small > 0 && small >= big; }
+// The wide test from n = #{x != 0}, e and R (above).
+__device__ __forceinline__ bool block_is_wide(int n, int e, int R) { return n >= 2 && 8 * e > R; }
 
 // Code q (unsigned, before the offset) of element l of one block in the
 // reference byte layouts (quant.rs:814-879), read with byte loads.

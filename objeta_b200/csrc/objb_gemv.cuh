@@ -230,11 +230,13 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
     int E = 0;
     frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
-    const float ax = fabsf(xe), thr = ldexpf(m, -kWideShift);
-    const int nsmall = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax < thr));
-    const int nbig = __popc(__ballot_sync(0xFFFFFFFFu, ax != 0.0f && ax >= thr));
-    const bool wide = isfinite(m) && block_is_wide(nsmall, nbig);
-    const int X = wide ? 0 : __float2int_rn(ldexpf(xe, 20 - E));
+    const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
+    const int r = X0 != 0 ? kWideUnit : __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+    const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
+    const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
+    const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
+    const bool wide = isfinite(m) && block_is_wide(nnz, esum, capped);
+    const int X = wide ? 0 : X0;
     const int d0 = ((X + 64) & 127) - 64;
     const int X1 = (X - d0) / 128;
     const int d1 = ((X1 + 64) & 127) - 64;
@@ -311,22 +313,28 @@ __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool
   bool wide = false;
   if (m < INFINITY) {  // no NaN (max.NaN would carry it) and no Inf in the block
     frexpf(m, &E);     // m < 2^E (E = 0 for m = 0)
-    const float thr = ldexpf(m, -kWideShift);
-    int ns = 0, nb = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = fabsf(v[i]);
-      ns += a != 0.0f && a < thr;
-      nb += a != 0.0f && a >= thr;
-    }
-    const int cnt = ns | (nb << 8);  // both counts <= 32: one packed sum over the quarters
-    int c = cnt + __shfl_xor_sync(gmask, cnt, 1);
-    c += __shfl_xor_sync(gmask, c, 2);
-    wide = block_is_wide(c & 0xFF, c >> 8);
     const int k = 20 - E, k1 = min(k, 127);
     const float s1 = __int_as_float((k1 + 127) << 23), s2 = __int_as_float((k - k1 + 127) << 23);
+    int nnz = 0, esum = 0, capped = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) X[i] = wide ? 0 : __float_as_int((v[i] * s1) * s2 + 12582912.0f) - 0x4B400000;
+    for (int i = 0; i < 8; ++i) {
+      const float y = (v[i] * s1) * s2;  // exact: x * 2^(20-E)
+      X[i] = __float_as_int(y + 12582912.0f) - 0x4B400000;
+      nnz += v[i] != 0.0f;
+      esum += X[i] != 0 ? kWideUnit : __float2int_rn(fabsf(y) * 2048.0f);
+      capped += min(abs(X[i]), kWideCap);
+    }
+    // over the block's four quarters: nnz (<= 32) and esum (<= 2^15) packed
+    int c = esum | (nnz << 24);
+    c += __shfl_xor_sync(gmask, c, 1);
+    c += __shfl_xor_sync(gmask, c, 2);
+    capped += __shfl_xor_sync(gmask, capped, 1);
+    capped += __shfl_xor_sync(gmask, capped, 2);
+    wide = block_is_wide(c >> 24, c & 0xFFFFFF, capped);
+    if (wide) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) X[i] = 0;
+    }
   } else {
     m = fabsf(v[0]);
 #pragma unroll
@@ -680,6 +688,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
     } else if (xin == nullptr) {
       load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     }
+    // digit rows: whether this warp's tiles hold a wide block (warp-uniform)
+    bool wide_any = false;
+    if constexpr (IsDigitRD<RD>::value)
+      wide_any = __any_sync(0xFFFFFFFFu, xr.w(48) == kWideMark || xr.w(49) == kWideMark);
     for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
       const int slot = static_cast<int>(it % S);
       if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout, sp.abort);
@@ -705,10 +717,10 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
         }
       }
       if constexpr (IsDigitRD<RD>::value) {
-        // wide blocks of the vector (warp-uniform masks, from the registers)
-        const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
-        const uint32_t w1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
-        if ((w0 | w1) != 0u) {
+        if (wide_any) {
+          // the lanes whose tile block 0 / 1 is wide
+          const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
+          const uint32_t w1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
           __syncwarp();
           const float* xd = prog.job(cta, j).xd;
           if (xd != nullptr)
