@@ -195,7 +195,8 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   int E = 0;
   frexpf(m, &E);
   const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
-  const int r = X0 != 0 ? kWideUnit : __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+  const int f = __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+  const int r = (X0 != 0 || f >= kWideFull) ? kWideUnit : f;
   const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
   const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
   const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));

@@ -128,12 +128,14 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
 // leaves the others only ~10 bits (and at 1e7 none), and the rows that weigh
 // the outliers by zero then miss the reference's 1e-5 * sum|w x| bound.
 // Per block, in integers (so every image builder agrees bit for bit):
-//   e = sum_l r_l,  r_l = 2^10 if X_l != 0, else rint(|x_l| * 2^(31-E))
-//       (the rounding error bound in units of 2^-11 grid steps, <= 2^10),
+//   e = sum_l r_l, the rounding error bound in units of 2^-11 grid steps:
+//       r_l = 2^10 (half a step) if X_l != 0 or f_l >= 8, else f_l, with
+//       f_l = rint(|x_l| * 2^(31-E)) (a value that rounds to 0 moves by
+//       itself; one of at least 2^-28 of the block scale counts in full),
 //   R = sum_l min(|X_l|, 2^15)   (the values, each capped at 2^-5 of 2^E),
 // and the block is "wide" when at least two x are nonzero and 8 e > R, i.e.
-// its possible rounding error exceeds 2^-14 of its capped mass.  Up to 8
-// outliers of up to ~1e6 times the block's ordinary values qualify (beyond
+// its possible rounding error exceeds 2^-14 of its capped mass.  Up to 7
+// outliers of up to ~3e6 times the block's ordinary values qualify (beyond
 // that an outlier's capped mass hides the others'); an N(0,1) block sits
 // about 4x below the line, and values far below the grid (silu of a large
 // negative gate) count only by their size.  A wide block's digit words and block sum are
@@ -142,6 +144,7 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
 // instead, one element per lane: ((q_l - off) * scale) * x_l.
 constexpr int kWideCap = 1 << 15;
 constexpr int kWideUnit = 1 << 10;
+constexpr int kWideFull = 8;  // f_l from which a value that rounds to 0 counts a full unit
 constexpr uint32_t kWideMark = 0x80000000u;  // -0.0f: a zero block sum times it stays zero
 
 // The wide test from n = #{x != 0}, e and R (above).

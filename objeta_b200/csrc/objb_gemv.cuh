@@ -231,7 +231,8 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
     int E = 0;
     frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
     const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
-    const int r = X0 != 0 ? kWideUnit : __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+    const int f = __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
+    const int r = (X0 != 0 || f >= kWideFull) ? kWideUnit : f;
     const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
     const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
     const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
@@ -321,7 +322,8 @@ __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool
       const float y = (v[i] * s1) * s2;  // exact: x * 2^(20-E)
       X[i] = __float_as_int(y + 12582912.0f) - 0x4B400000;
       nnz += v[i] != 0.0f;
-      esum += X[i] != 0 ? kWideUnit : __float2int_rn(fabsf(y) * 2048.0f);
+      const int f = __float2int_rn(fabsf(y) * 2048.0f);
+      esum += (X[i] != 0 || f >= kWideFull) ? kWideUnit : f;
       capped += min(abs(X[i]), kWideCap);
     }
     // over the block's four quarters: nnz (<= 32) and esum (<= 2^15) packed
@@ -529,7 +531,7 @@ struct Job {
 // (the slot the row dot wrote in `red`).  Runs only when the vector has a
 // wide block, outside the integer loop, so that loop keeps its registers.
 template <int FMT, bool DUAL>
-__device__ __forceinline__ void add_wide_terms(float* red, const uint8_t* stg, int part, int row_bytes, int nseg,
+__device__ __noinline__ void add_wide_terms(float* red, const uint8_t* stg, int part, int row_bytes, int nseg,
                                             int seg, int grp, int ngrp, int nr, uint32_t w0, uint32_t w1,
                                             const float* __restrict__ xd) {
   using T = Tile<FMT>;
