@@ -40,7 +40,25 @@ struct DeviceGuard {
 int ensure_side(Cache* c) {
   if (c->side) return OBJB_OK;
   OBJB_CUDA(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking), "create cache upload stream");
+  OBJB_CUDA(cudaEventCreateWithFlags(&c->upload_ev, cudaEventDisableTiming), "create upload event");
   return OBJB_OK;
+}
+
+// The upload stream waits for `ev` (skipped when it just did: the event is
+// kept alive, so its handle cannot have been reused meanwhile).
+int side_wait(Cache* c, const std::shared_ptr<Cache::Event>& ev) {
+  if (!ev || !ev->ev || ev == c->side_waited) return OBJB_OK;
+  OBJB_CUDA(cudaStreamWaitEvent(c->side, ev->ev, 0), "order slot reuse after its last reads");
+  c->side_waited = ev;
+  return OBJB_OK;
+}
+
+// The release event that closed `epoch`, or a later one (still a valid fence)
+// when that one has been dropped from the window.
+std::shared_ptr<Cache::Event> fence_of(Cache* c, uint64_t epoch) {
+  for (auto& e : c->closed)
+    if (e.first >= epoch) return e.second;
+  return nullptr;
 }
 
 // Storage for `bytes`: a free slot of the same class (its reuse fence is
@@ -52,8 +70,7 @@ int alloc_slot(Cache* c, size_t bytes, Cache::Slot* out) {
   if (it != c->free_slots.end() && !it->second.empty()) {
     *out = it->second.back();
     it->second.pop_back();
-    if (out->ready && out->ready->ev)
-      OBJB_CUDA(cudaStreamWaitEvent(c->side, out->ready->ev, 0), "order slot reuse after its last reads");
+    if (out->ready) OBJB_TRY(side_wait(c, out->ready));
     out->ready.reset();
     return OBJB_OK;
   }
@@ -82,8 +99,21 @@ int alloc_slot(Cache* c, size_t bytes, Cache::Slot* out) {
   return OBJB_OK;
 }
 
-void retire_slot(Cache* c, const Cache::Slot& s) {
-  if (s.ptr) c->pending.push_back(s);
+// A slot whose entry was last handed out in `last_epoch`: free at once behind
+// that epoch's release event when the epoch is closed, else pending until the
+// next release point.
+void retire_slot(Cache* c, const Cache::Slot& s, uint64_t last_epoch) {
+  if (!s.ptr) return;
+  if (last_epoch < c->epoch && s.cls != 0) {
+    auto f = fence_of(c, last_epoch);
+    if (f) {
+      Cache::Slot r = s;
+      r.ready = f;
+      c->free_slots[r.cls].push_back(r);
+      return;
+    }
+  }
+  c->pending.push_back(s);
 }
 
 // evict_lru (moe.rs:164-176): removes the first non-pinned key from the LRU
@@ -100,7 +130,7 @@ EvictResult evict_lru_ex(Cache* c, Cache::Key* evicted) {
     if (m != c->map.end()) {
       c->st.resident_bytes -= m->second.size;
       c->st.eviction_count += 1;
-      retire_slot(c, m->second.slot);
+      retire_slot(c, m->second.slot, m->second.last_epoch);
       c->map.erase(m);
       if (evicted) *evicted = k;
       return kEvicted;
@@ -121,16 +151,20 @@ void touch(Cache* c, const Cache::Key& k) {
   }
 }
 
+// The caller's stream waits for the uploads issued so far.
+int flush_uploads(Cache* c, cudaStream_t stream) {
+  if (!c->uploads_pending) return OBJB_OK;
+  OBJB_CUDA(cudaEventRecord(c->upload_ev, c->side), "record uploads");
+  OBJB_CUDA(cudaStreamWaitEvent(stream, c->upload_ev, 0), "order uploads before use");
+  c->uploads_pending = false;
+  return OBJB_OK;
+}
+
 int upload(Cache* c, void* dst, const void* host, size_t bytes, cudaStream_t stream) {
   OBJB_TRY(ensure_side(c));
   if (bytes) OBJB_CUDA(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, c->side), "upload expert tensor");
-  cudaEvent_t ev;
-  OBJB_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "create upload event");
-  cudaError_t e = cudaEventRecord(ev, c->side);
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, ev, 0);
-  cudaEventDestroy(ev);
-  if (e != cudaSuccess) return cuda_status(e, "order upload before use", __FILE__, __LINE__);
-  return OBJB_OK;
+  c->uploads_pending = true;
+  return c->defer_wait ? OBJB_OK : flush_uploads(c, stream);
 }
 
 // insert (moe.rs:124-154).
@@ -152,7 +186,7 @@ int insert(Cache* c, const Cache::Key& k, const void* host, size_t bytes, cudaSt
   auto old = c->map.find(k);
   if (old != c->map.end()) {
     c->st.resident_bytes -= old->second.size;
-    retire_slot(c, old->second.slot);
+    retire_slot(c, old->second.slot, old->second.last_epoch);
     c->map.erase(old);
     for (auto it = c->order.begin(); it != c->order.end(); ++it)
       if (*it == k) {
@@ -167,6 +201,7 @@ int insert(Cache* c, const Cache::Key& k, const void* host, size_t bytes, cudaSt
   }
   Cache::Entry e;
   e.size = bytes;
+  e.last_epoch = c->epoch;
   OBJB_TRY(ensure_side(c));
   OBJB_TRY(alloc_slot(c, bytes, &e.slot));
   OBJB_TRY(upload(c, e.slot.ptr, host, bytes, stream));
@@ -183,6 +218,7 @@ int get(Cache* c, const Cache::Key& k, const void** out) {
   if (it != c->map.end()) {
     c->st.hit_count += 1;
     touch(c, k);
+    it->second.last_epoch = c->epoch;
     *out = it->second.slot.ptr;
   } else {
     c->st.miss_count += 1;
@@ -191,11 +227,16 @@ int get(Cache* c, const Cache::Key& k, const void** out) {
   return OBJB_OK;
 }
 
+// A release point: everything handed out so far is read by work already
+// enqueued on `stream`; closes the epoch.
 int release(Cache* c, cudaStream_t stream) {
-  if (!c->pending.empty()) {
+  {
     auto ev = std::make_shared<Cache::Event>();
     OBJB_CUDA(cudaEventCreateWithFlags(&ev->ev, cudaEventDisableTiming), "create release event");
     OBJB_CUDA(cudaEventRecord(ev->ev, stream), "record release point");
+    c->closed.emplace_back(c->epoch, ev);
+    while (c->closed.size() > 64) c->closed.pop_front();
+    c->epoch += 1;
     for (auto& s : c->pending) {
       if (s.cls == 0) {
         // overflow slots come from cudaMallocAsync: freed in stream order
@@ -221,6 +262,14 @@ int cache_insert(Cache* c, const objb_expert_cache_key* k, const void* host, siz
   return insert(c, to_key(k), host, bytes, stream, out, resident);
 }
 int cache_release(Cache* c, cudaStream_t stream) { return release(c, stream); }
+// A batch of lookups whose uploads the caller's stream waits for once, at
+// cache_end_batch (the executor's chunks).
+void cache_begin_batch(Cache* c) { c->defer_wait = true; }
+int cache_end_batch(Cache* c, cudaStream_t stream) {
+  c->defer_wait = false;
+  if (!c->side) return OBJB_OK;
+  return flush_uploads(c, stream);
+}
 
 }  // namespace objb
 
@@ -260,6 +309,7 @@ void objb_expert_cache_free(objb_expert_cache* c) {
     if (s.cls == 0 && s.ptr) cudaFree(s.ptr);
   for (void* p : c->transients) cudaFree(p);
   if (c->arena) cudaFree(c->arena);
+  if (c->upload_ev) cudaEventDestroy(c->upload_ev);
   if (c->side) cudaStreamDestroy(c->side);
   delete c;
 }
@@ -374,13 +424,14 @@ int objb_expert_cache_insert_pinned(objb_expert_cache* c, const objb_expert_cach
   const Cache::Key k = to_key(key);
   Cache::Entry e;
   e.size = bytes;
+  e.last_epoch = c->epoch;
   OBJB_TRY(ensure_side(c));
   OBJB_TRY(alloc_slot(c, bytes, &e.slot));
   OBJB_TRY(upload(c, e.slot.ptr, host_src, bytes, static_cast<cudaStream_t>(stream)));
   auto old = c->map.find(k);
   if (old != c->map.end()) {
     c->st.resident_bytes -= old->second.size;
-    retire_slot(c, old->second.slot);
+    retire_slot(c, old->second.slot, old->second.last_epoch);
   }
   c->map[k] = e;
   c->st.resident_bytes += bytes;
@@ -394,7 +445,7 @@ int objb_expert_cache_insert_pinned(objb_expert_cache* c, const objb_expert_cach
 int objb_expert_cache_clear(objb_expert_cache* c) {
   CACHE_CHECK(c);
   std::lock_guard<std::mutex> lk(c->mu);
-  for (auto& kv : c->map) retire_slot(c, kv.second.slot);
+  for (auto& kv : c->map) retire_slot(c, kv.second.slot, kv.second.last_epoch);
   c->map.clear();
   c->order.clear();
   c->pinned.clear();

@@ -24,6 +24,8 @@ int cache_get(objb_expert_cache* c, const objb_expert_cache_key* k, const void**
 int cache_insert(objb_expert_cache* c, const objb_expert_cache_key* k, const void* host, size_t bytes,
                  cudaStream_t stream, const void** out, int* resident);
 int cache_release(objb_expert_cache* c, cudaStream_t stream);
+void cache_begin_batch(objb_expert_cache* c);
+int cache_end_batch(objb_expert_cache* c, cudaStream_t stream);
 }  // namespace objb
 
 struct objb_moe_executor {
@@ -391,9 +393,15 @@ int execute(objb_moe_executor* ex, cudaStream_t stream, int fmt, bool split, siz
 }
 
 // Multi-token form: the distinct experts of a pair list are resolved once
-// each (first-appearance order), then every pair runs in one pair launch
-// sequence; x and v stay on the device.  Ends with a stream synchronize like
-// the single-token call (the pinned staging block is reused by the next call).
+// each, in first-appearance order (the cache sees the lookups in that order),
+// and every pair runs on its expert's tensors; x and v stay on the device.
+// With a cache the experts go in chunks of at most half its capacity: a
+// chunk's lookups and uploads (one wait of the stream per chunk), then its
+// pair launches, then a release point -- so the next chunk's uploads, on the
+// cache's side stream, reuse the slots of the chunk before and overlap this
+// chunk's kernels.  A chunk of kTcMinPairs pairs or more on a Q4_0 layer runs
+// on the tensor cores.  Ends with a stream synchronize like the single-token
+// call (the pinned staging block is reused by the next call).
 int execute_pairs(objb_moe_executor* ex, cudaStream_t stream, int fmt, const objb_expert_weights* experts,
                   size_t num_experts, const int32_t* pair_expert, const int32_t* pair_token, const int32_t* pair_out,
                   size_t P, const float* d_x, size_t T, size_t hidden, size_t intermediate, size_t out_dim,
@@ -413,68 +421,128 @@ int execute_pairs(objb_moe_executor* ex, cudaStream_t stream, int fmt, const obj
     }
   }
   const size_t U = uniq.size();
+  // chunks of experts
+  size_t C = U;
+  if (cache && U) {
+    const objb_expert_weights& e0 = experts[uniq[0]];
+    const size_t eb = e0.w_gate_len + e0.w_up_len + e0.w_down_len;
+    const size_t cap = cache->st.capacity_bytes;
+    C = std::max<size_t>(1, std::min(U, eb ? cap / (2 * eb) : U));
+  }
+  const size_t nchunks = U ? (U + C - 1) / C : 0;
+  // pairs ordered by slot (chunks contiguous, grouped by expert; stable)
+  std::vector<size_t> start(U + 1, 0);
+  for (size_t p = 0; p < P; ++p) start[slot_of[pair_expert[p]] + 1] += 1;
+  for (size_t u = 0; u < U; ++u) start[u + 1] += start[u];
+  std::vector<int32_t> order(P);
+  {
+    std::vector<size_t> cur(start.begin(), start.end() - 1);
+    for (size_t p = 0; p < P; ++p) order[cur[slot_of[pair_expert[p]]]++] = static_cast<int32_t>(p);
+  }
+  // one table block per chunk: 3 * U_c pointers, then pe / pt / po of its pairs
+  std::vector<size_t> meta_off(nchunks + 1, 0);
+  for (size_t c = 0; c < nchunks; ++c) {
+    const size_t u0 = c * C, u1 = std::min(U, u0 + C);
+    const size_t pc = start[u1] - start[u0];
+    meta_off[c + 1] = meta_off[c] + ((u1 - u0) * 3 * sizeof(void*) + 3 * pc * sizeof(int32_t) + 255) / 256 * 256;
+  }
+  const bool tc_shape = fmt == OBJB_Q4_0 && hidden % 256 == 0 && intermediate % 256 == 0;
+  int rc = OBJB_OK;
+  size_t need = 0;
+  for (size_t c = 0; c < nchunks && rc == OBJB_OK; ++c) {  // scratch for the largest chunk, grown before any launch
+    const size_t u0 = c * C, u1 = std::min(U, u0 + C);
+    const size_t pc = start[u1] - start[u0];
+    objb_moe_layer probe = {};
+    probe.fmt = fmt;
+    probe.hidden = hidden;
+    probe.intermediate = intermediate;
+    probe.out_dim = out_dim;
+    probe.num_experts = u1 - u0;
+    size_t n = 0;
+    rc = (tc_shape && pc >= kTcMinPairs) ? moe_pairs_tc_scratch_bytes(&probe, pc, T, &n)
+                                         : moe_pairs_scratch_bytes(&probe, pc, T, &n);
+    need = std::max(need, n);
+  }
+  if (rc == OBJB_OK) rc = grow_host(&ex->h_meta, &ex->h_meta_cap, std::max<size_t>(meta_off[nchunks], 64));
+  if (rc == OBJB_OK) rc = grow_dev(&ex->d_meta, &ex->d_meta_cap, std::max<size_t>(meta_off[nchunks], 64), "allocate MoE tables");
+  if (rc == OBJB_OK) rc = grow_dev(&ex->d_scratch, &ex->d_scratch_cap, std::max<size_t>(need, 256), "allocate MoE scratch");
   Resolved res;
   std::vector<const void*> ptrs(U * 3, nullptr);
-  int rc = OBJB_OK;
-  for (size_t u = 0; u < U && rc == OBJB_OK; ++u) {
-    const objb_expert_weights& e = experts[uniq[u]];
-    TensorRef t[3] = {TensorRef{e.w_gate, e.w_gate_len, OBJB_KIND_GATE, false},
-                      TensorRef{e.w_up, e.w_up_len, OBJB_KIND_UP, false},
-                      TensorRef{e.w_down, e.w_down_len, OBJB_KIND_DOWN, false}};
-    rc = resolve_expert(cache, stream, fmt, false, layer_id, static_cast<size_t>(uniq[u]), t, &ptrs[u * 3], &res);
-  }
-  if (rc == OBJB_OK) cudaEventRecord(ev[2], stream);
-  uint32_t flags = 0;
-  for (const void* p : ptrs)
-    if (reinterpret_cast<uintptr_t>(p) & 15u) flags |= OBJB_MOE_UNALIGNED;
-  const size_t meta = U * 3 * sizeof(void*) + 3 * P * sizeof(int32_t) + 64;
-  if (rc == OBJB_OK) rc = grow_host(&ex->h_meta, &ex->h_meta_cap, meta);
-  if (rc == OBJB_OK) rc = grow_dev(&ex->d_meta, &ex->d_meta_cap, meta, "allocate MoE tables");
-  objb_moe_layer layer = {};
-  const int32_t *d_pe = nullptr, *d_pt = nullptr, *d_po = nullptr;
-  if (rc == OBJB_OK) {
-    uint8_t* h = static_cast<uint8_t*>(ex->h_meta);
+  bool first = true;
+  for (size_t c = 0; c < nchunks && rc == OBJB_OK; ++c) {
+    const size_t u0 = c * C, u1 = std::min(U, u0 + C), uc = u1 - u0;
+    if (cache) {
+      std::lock_guard<std::mutex> lk(cache->mu);
+      cache_begin_batch(cache);
+    }
+    for (size_t u = u0; u < u1 && rc == OBJB_OK; ++u) {
+      const objb_expert_weights& e = experts[uniq[u]];
+      TensorRef t[3] = {TensorRef{e.w_gate, e.w_gate_len, OBJB_KIND_GATE, false},
+                        TensorRef{e.w_up, e.w_up_len, OBJB_KIND_UP, false},
+                        TensorRef{e.w_down, e.w_down_len, OBJB_KIND_DOWN, false}};
+      rc = resolve_expert(cache, stream, fmt, false, layer_id, static_cast<size_t>(uniq[u]), t, &ptrs[u * 3], &res);
+    }
+    if (cache) {
+      std::lock_guard<std::mutex> lk(cache->mu);
+      const int r2 = cache_end_batch(cache, stream);  // the stream waits for this chunk's uploads
+      if (rc == OBJB_OK) rc = r2;
+    }
+    if (rc != OBJB_OK) break;
+    uint32_t flags = 0;
+    for (size_t u = u0; u < u1; ++u)
+      for (int i = 0; i < 3; ++i)
+        if (reinterpret_cast<uintptr_t>(ptrs[u * 3 + i]) & 15u) flags |= OBJB_MOE_UNALIGNED;
+    const size_t p0 = start[u0], pc = start[u1] - p0;
+    uint8_t* h = static_cast<uint8_t*>(ex->h_meta) + meta_off[c];
+    uint8_t* d = static_cast<uint8_t*>(ex->d_meta) + meta_off[c];
     const void** tab = reinterpret_cast<const void**>(h);
     for (int i = 0; i < 3; ++i)
-      for (size_t u = 0; u < U; ++u) tab[i * U + u] = ptrs[u * 3 + i];
-    int32_t* pe = reinterpret_cast<int32_t*>(h + U * 3 * sizeof(void*));
-    int32_t* pt = pe + P;
-    int32_t* po = pt + P;
-    for (size_t p = 0; p < P; ++p) {
-      pe[p] = slot_of[pair_expert[p]];
-      pt[p] = pair_token[p];
-      po[p] = pair_out ? pair_out[p] : static_cast<int32_t>(p);
+      for (size_t u = 0; u < uc; ++u) tab[i * uc + u] = ptrs[(u0 + u) * 3 + i];
+    int32_t* pe = reinterpret_cast<int32_t*>(h + uc * 3 * sizeof(void*));
+    int32_t* pt = pe + pc;
+    int32_t* po = pt + pc;
+    for (size_t q = 0; q < pc; ++q) {
+      const int32_t p = order[p0 + q];
+      pe[q] = slot_of[pair_expert[p]] - static_cast<int32_t>(u0);
+      pt[q] = pair_token[p];
+      po[q] = pair_out ? pair_out[p] : p;
     }
-    OBJB_CUDA(cudaMemcpyAsync(ex->d_meta, ex->h_meta, meta, cudaMemcpyHostToDevice, stream), "copy MoE tables");
-    const void* const* dtab = static_cast<const void* const*>(ex->d_meta);
-    d_pe = reinterpret_cast<const int32_t*>(static_cast<uint8_t*>(ex->d_meta) + U * 3 * sizeof(void*));
-    d_pt = d_pe + P;
-    d_po = d_pt + P;
+    const size_t bytes = uc * 3 * sizeof(void*) + 3 * pc * sizeof(int32_t);
+    OBJB_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, stream), "copy MoE tables");
+    const void* const* dtab = reinterpret_cast<const void* const*>(d);
+    const int32_t* d_pe = reinterpret_cast<const int32_t*>(d + uc * 3 * sizeof(void*));
+    objb_moe_layer layer = {};
     layer.fmt = fmt;
     layer.flags = flags;
     layer.hidden = hidden;
     layer.intermediate = intermediate;
     layer.out_dim = out_dim;
-    layer.num_experts = U;
+    layer.num_experts = uc;
     layer.d_gate = dtab;
-    layer.d_up = dtab + U;
-    layer.d_down = dtab + 2 * U;
-  }
-  if (rc == OBJB_OK) {
-    size_t need = 0;
-    rc = moe_pairs_scratch_bytes(&layer, P, T, &need);
-    if (rc == OBJB_OK) rc = grow_dev(&ex->d_scratch, &ex->d_scratch_cap, need, "allocate MoE scratch");
-    if (rc == OBJB_OK) cudaEventRecord(ev[3], stream);
-    if (rc == OBJB_OK)
-      rc = moe_pairs(&layer, P, d_pe, d_pt, d_po, T, d_x, d_v, v_rows, 0.0f, stream, ex->d_scratch,
+    layer.d_up = dtab + uc;
+    layer.d_down = dtab + 2 * uc;
+    if (first) {
+      cudaEventRecord(ev[2], stream);
+      cudaEventRecord(ev[3], stream);
+      first = false;
+    }
+    if (tc_shape && pc >= kTcMinPairs && !(flags & OBJB_MOE_UNALIGNED))
+      rc = moe_pairs_tc(&layer, pc, d_pe, d_pe + pc, d_pe + 2 * pc, T, d_x, d_v, v_rows, 0.0f, stream, ex->d_scratch,
+                        ex->d_scratch_cap, nullptr, nullptr);
+    else
+      rc = moe_pairs(&layer, pc, d_pe, d_pe + pc, d_pe + 2 * pc, T, d_x, d_v, v_rows, 0.0f, stream, ex->d_scratch,
                      ex->d_scratch_cap);
-    if (rc == OBJB_OK) cudaEventRecord(ev[5], stream);
+    if (cache) {  // release point: this chunk's tensors are read by work already enqueued
+      std::lock_guard<std::mutex> lk(cache->mu);
+      const int r2 = cache_release(cache, stream);
+      if (rc == OBJB_OK) rc = r2;
+    }
   }
-  if (cache) {  // release point: everything handed to the kernels is enqueued
-    std::lock_guard<std::mutex> lk(cache->mu);
-    int r2 = cache_release(cache, stream);
-    if (rc == OBJB_OK) rc = r2;
+  if (first) {
+    cudaEventRecord(ev[2], stream);
+    cudaEventRecord(ev[3], stream);
   }
+  cudaEventRecord(ev[5], stream);
   for (void* p : res.transients) cudaFreeAsync(p, stream);
   cudaError_t se = cudaStreamSynchronize(stream);
   if (rc != OBJB_OK) return rc;
@@ -520,8 +588,8 @@ int execute_pairs(objb_moe_executor* ex, cudaStream_t stream, int fmt, const obj
       tel->resident_cache_oversized_expert_bypass_count = s.oversized_expert_bypass_count;
       tel->resident_cache_self_eviction_risk_count = s.self_eviction_risk_count;
     }
-    tel->h2d_ms = h2d;
-    tel->gate_up_qgemv_ms = comp;  // gate/up + SwiGLU + down of all pairs
+    tel->h2d_ms = h2d;               // until the first chunk's uploads landed
+    tel->gate_up_qgemv_ms = comp;  // from there: the pairs of every chunk, overlapped with the later uploads
     tel->total_ms = tot;
     tel->unaccounted_ms = std::max(0.0f, tot - h2d - comp);
     tel->bytes_gate = res.bytes_gate;

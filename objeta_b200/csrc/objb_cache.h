@@ -9,13 +9,20 @@
 // caller's stream waits on an event, so misses stream in asynchronously from
 // pinned host memory.  An evicted slot is not reused until the stream that
 // read it passes a release point (release()), which is what keeps a buffer
-// alive for the rest of a call in the reference (Arc<DeviceBuffer>).
+// alive for the rest of a call in the reference (Arc<DeviceBuffer>).  Release
+// points close "epochs": an entry remembers the epoch it was last handed out
+// in, and when it is evicted after that epoch was closed its slot is free at
+// once, the upload stream waiting (on the device) for that epoch's release
+// event -- so a multi-token call that resolves its experts in chunks, with a
+// release point after each chunk's launches, reuses the slots of chunk i - 1
+// for chunk i + 1 while chunk i computes.
 #pragma once
 
 #include <cuda_runtime.h>
 
 #include <cstddef>
 #include <cstdint>
+#include <deque>
 #include <list>
 #include <map>
 #include <memory>
@@ -58,6 +65,7 @@ struct objb_expert_cache {
   struct Entry {
     Slot slot;
     size_t size = 0;
+    uint64_t last_epoch = 0;  // epoch in which it was last handed out (get hit or insert)
   };
 
   int device = 0;
@@ -75,4 +83,14 @@ struct objb_expert_cache {
   std::vector<void*> transients;                   // bypass buffers of the current epoch
   cudaStream_t side = nullptr;
   size_t overflow_allocations = 0;
+
+  // epochs (release points)
+  uint64_t epoch = 0;
+  std::deque<std::pair<uint64_t, std::shared_ptr<Event>>> closed;  // (epoch, its release event), oldest first
+  std::shared_ptr<Event> side_waited;  // the last fence the upload stream waited on (skip repeats)
+
+  // uploads of a batch: the caller's stream waits once, after the batch
+  bool defer_wait = false;
+  bool uploads_pending = false;
+  cudaEvent_t upload_ev = nullptr;
 };

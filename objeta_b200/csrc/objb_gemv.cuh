@@ -690,64 +690,74 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
     } else if (xin == nullptr) {
       load_ximage(J.ximg, L.nseg * 32, seg * 32 + lane, xr);
     }
-    // digit rows: whether this warp's tiles hold a wide block (warp-uniform)
-    bool wide_any = false;
-    if constexpr (IsDigitRD<RD>::value)
-      wide_any = __any_sync(0xFFFFFFFFu, xr.w(48) == kWideMark || xr.w(49) == kWideMark);
-    for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
-      const int slot = static_cast<int>(it % S);
-      if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout, sp.abort);
-      const int nr = min(T, J.row_end - r0);
-      const uint8_t* stg = sp.stage + static_cast<size_t>(slot) * L.stage_bytes;
-      const uint8_t* sca = stg + static_cast<size_t>(T) * L.row_bytes;
-      float* red = sp.red + static_cast<size_t>(slot) * T * L.nseg * 2;
-      for (int bt = grp * RB; bt < nr; bt += L.ngrp * RB) {
-        float v[NV];
+    // The job's stages, in two instantiations: with the fp32 pass for wide
+    // blocks (digit rows whose vector has one in this warp's tiles) and
+    // without, so ordinary vectors run the integer loop untouched.  Warps of
+    // one CTA may take different ones: both pass the same barriers in the
+    // same order.
+    auto stages = [&](auto wide_tag) {
+      constexpr bool kWide = decltype(wide_tag)::value;
+      for (int r0 = J.row_begin; r0 < J.row_end; r0 += T) {
+        const int slot = static_cast<int>(it % S);
+        if (ok) ok = mbar_wait_bounded(&sp.full[slot], (it / S) & 1u, err, kErrFullWaitTimeout, sp.abort);
+        const int nr = min(T, J.row_end - r0);
+        const uint8_t* stg = sp.stage + static_cast<size_t>(slot) * L.stage_bytes;
+        const uint8_t* sca = stg + static_cast<size_t>(T) * L.row_bytes;
+        float* red = sp.red + static_cast<size_t>(slot) * T * L.nseg * 2;
+        for (int bt = grp * RB; bt < nr; bt += L.ngrp * RB) {
+          float v[NV];
 #pragma unroll
-        for (int i = 0; i < RB; ++i) {
-          const int t = min(bt + i, nr - 1);
-          v[i] = rd.dot(stg + t * L.row_bytes, sca + t * L.srow_bytes, xr);
-          if constexpr (DUAL)
-            v[RB + i] = rd.dot(stg + part + t * L.row_bytes,
-                               stg + part + static_cast<size_t>(T) * L.row_bytes + t * L.srow_bytes, xr);
+          for (int i = 0; i < RB; ++i) {
+            const int t = min(bt + i, nr - 1);
+            v[i] = rd.dot(stg + t * L.row_bytes, sca + t * L.srow_bytes, xr);
+            if constexpr (DUAL)
+              v[RB + i] = rd.dot(stg + part + t * L.row_bytes,
+                                 stg + part + static_cast<size_t>(T) * L.row_bytes + t * L.srow_bytes, xr);
+          }
+          butterfly<NV>(v, lane);
+          if ((lane & (W - 1)) == 0) {
+            const int idx = lane / W;
+            const int t = bt + (idx % RB);
+            if (t < nr) red[(t * L.nseg + seg) * 2 + idx / RB] = v[0];
+          }
         }
-        butterfly<NV>(v, lane);
-        if ((lane & (W - 1)) == 0) {
-          const int idx = lane / W;
-          const int t = bt + (idx % RB);
-          if (t < nr) red[(t * L.nseg + seg) * 2 + idx / RB] = v[0];
-        }
-      }
-      if constexpr (IsDigitRD<RD>::value) {
-        if (wide_any) {
+        if constexpr (kWide) {
           // the lanes whose tile block 0 / 1 is wide
           const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
           const uint32_t w1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
           __syncwarp();
-          const float* xd = prog.job(cta, j).xd;
-          if (xd != nullptr)
+          if (J.xd != nullptr)
             add_wide_terms<IsDigitRD<RD>::fmt, DUAL>(red, stg, part, L.row_bytes, L.nseg, seg, grp, L.ngrp, nr, w0,
-                                                     w1, xd);
+                                                     w1, J.xd);
           else if (lane == 0 && err)
             atomicOr(err, kErrNoWideSource);
         }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sp.empty[slot]);
-      named_bar_sync(1, nthr);
-      // a stage that never landed (or landed without data) yields NaN rows,
-      // not values reduced from stale shared memory
-      const bool aborted = *reinterpret_cast<volatile unsigned*>(sp.abort) != 0u;
-      for (int t = threadIdx.x; t < nr; t += nthr) {
-        float va = 0.0f, vb = 0.0f;
-        for (int s2 = 0; s2 < L.nseg; ++s2) {
-          va += red[(t * L.nseg + s2) * 2];
-          if constexpr (DUAL) vb += red[(t * L.nseg + s2) * 2 + 1];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sp.empty[slot]);
+        named_bar_sync(1, nthr);
+        // a stage that never landed (or landed without data) yields NaN rows,
+        // not values reduced from stale shared memory
+        const bool aborted = *reinterpret_cast<volatile unsigned*>(sp.abort) != 0u;
+        for (int t = threadIdx.x; t < nr; t += nthr) {
+          float va = 0.0f, vb = 0.0f;
+          for (int s2 = 0; s2 < L.nseg; ++s2) {
+            va += red[(t * L.nseg + s2) * 2];
+            if constexpr (DUAL) vb += red[(t * L.nseg + s2) * 2 + 1];
+          }
+          if (aborted) va = vb = __int_as_float(0x7FC00000);
+          prog.epilogue(cta, j, r0 + t, va, vb);
         }
-        if (aborted) va = vb = __int_as_float(0x7FC00000);
-        prog.epilogue(cta, j, r0 + t, va, vb);
+        ++it;
       }
-      ++it;
+    };
+    bool wide_any = false;
+    if constexpr (IsDigitRD<RD>::value)
+      wide_any = __any_sync(0xFFFFFFFFu, xr.w(48) == kWideMark || xr.w(49) == kWideMark);
+    if constexpr (IsDigitRD<RD>::value) {
+      if (wide_any) stages(std::true_type{});
+      else stages(std::false_type{});
+    } else {
+      stages(std::false_type{});
     }
   }
   named_bar_sync(1, nthr);

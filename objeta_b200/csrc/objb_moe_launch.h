@@ -28,6 +28,14 @@ int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_exp
               const int32_t* pair_out, size_t num_tokens, const float* x, float* v, size_t v_rows, float limit,
               cudaStream_t stream, void* scratch, size_t scratch_bytes, unsigned* err_word = nullptr,
               const int32_t* d_num_pairs = nullptr);
+// The same pairs on the tensor cores (Q4_0 layers, hidden / intermediate
+// multiples of 256, pairs grouped by expert), grouped.cu.
+int moe_pairs_tc_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t num_tokens, size_t* out);
+int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, const int32_t* pt, const int32_t* po,
+                 size_t num_tokens, const float* x, float* v, size_t v_rows, float limit, cudaStream_t stream,
+                 void* scratch, size_t scratch_bytes, unsigned* err_word, const int32_t* d_count);
+// Pair count from which the multi-token paths take the tensor cores.
+constexpr size_t kTcMinPairs = 256;
 int moe_combine(const float* v, size_t v_rows, const int32_t* slot_row, const float* weights, size_t num_tokens,
                 size_t top_k, size_t out_dim, float* out, cudaStream_t stream, unsigned* err_word = nullptr);
 int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t top_k, int renorm, int32_t* ids,

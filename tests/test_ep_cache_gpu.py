@@ -91,3 +91,52 @@ def test_execute_pairs_validates_like_the_executor(cuda_device):
         ex.execute_pairs(table, [0], [2], dx, v, H, I, OUT, 0)       # token 2 of 2
     with pytest.raises(CudaError):
         ex.execute_pairs(table, [0], [0], dx, v, H, I, OUT, 0, pair_out=[8])
+
+
+@pytest.mark.parametrize("capacity_experts", [E, 4])
+def test_cached_pairs_chunked_match_oracle_and_model(cuda_device, capacity_experts):
+    """256 tokens through the cache: the executor resolves the distinct
+    experts in chunks of half the cache's capacity, overlapping a chunk's
+    uploads with the previous chunk's kernels (16 experts: two chunks of ~512
+    pairs on the tensor cores; 4 experts: eight chunks on the CUDA-core
+    pairs, evicting the whole time).  Tokens match the oracle MoE within the
+    reference bound, and the cache's counters and LRU order equal the
+    restated cache fed the same lookups (distinct experts in first-appearance
+    order, gate / up / down each)."""
+    import torch
+    from oracle.cache_model import CacheModel
+    from objeta_b200.ep import CachedExpertCompute, ExpertParallelMoe
+    from objeta_b200.moe import CudaExpertCache, MoeExecutor
+    from tests._moe_util import moe_bound, q4_matrices
+    T = 256
+    ew, ids, ws, x = _setup(T, seed=11)
+    expert_bytes = ew[0].w_gate.size + ew[0].w_up.size + ew[0].w_down.size
+    cap = capacity_experts * expert_bytes
+    cache = CudaExpertCache(cap, 0)
+    comp = CachedExpertCompute(MoeExecutor(0), cache, ew, H, I, OUT)
+    ep = ExpertParallelMoe(None, E, K, out_dim=OUT, compute=comp)
+    dx, di, dw = (torch.from_numpy(a).cuda() for a in (x, ids, ws))
+    model = CacheModel(cap)
+    for step in range(2):
+        out = ep.forward(dx, di, dw)
+        torch.cuda.synchronize()
+        seen = []
+        for e in ep.last_plan.pair_expert.tolist():
+            if e not in seen:
+                seen.append(e)
+        for e in seen:
+            for kind, n in ((0, ew[e].w_gate.size), (1, ew[e].w_up.size), (2, ew[e].w_down.size)):
+                model.get_or_insert((0, e, kind), n)
+        s = cache.stats()
+        for name, v in model.counters().items():
+            assert s[name] == v, (step, name, s[name], v)
+        assert [(q.layer_id, q.expert_id, int(q.tensor_kind)) for q in cache.lru_keys()] == model.order
+    got = out.cpu().numpy()
+    host = [(w.w_gate, w.w_up, w.w_down) for w in ew]
+    for t in range(0, T, 37):
+        sel = list(zip(ids[t].tolist(), ws[t].tolist()))
+        ref = O.selected_moe_q4(host, sel, x[t], H, I, OUT)
+        bound = moe_bound(q4_matrices(host, H, I, OUT), sel, x[t], H, I, OUT)
+        err = np.abs(got[t].astype(np.float64) - ref.astype(np.float64))
+        assert np.all(err <= bound), f"token {t}: worst err/bound {np.max(err / bound):.3f}"
+    assert cache.stats()["overflow_allocations"] == 0
