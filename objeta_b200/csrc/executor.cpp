@@ -452,12 +452,14 @@ int execute_pairs(objb_moe_executor* ex, cudaStream_t stream, int fmt, const obj
   for (size_t c = 0; c < nchunks && rc == OBJB_OK; ++c) {  // scratch for the largest chunk, grown before any launch
     const size_t u0 = c * C, u1 = std::min(U, u0 + C);
     const size_t pc = start[u1] - start[u0];
-    objb_moe_layer probe = {};
+    objb_moe_layer probe = {};  // the shape only: the sizes do not read the tables
+    static const void* const kNoTable[1] = {nullptr};
     probe.fmt = fmt;
     probe.hidden = hidden;
     probe.intermediate = intermediate;
     probe.out_dim = out_dim;
     probe.num_experts = u1 - u0;
+    probe.d_gate = probe.d_up = probe.d_down = kNoTable;
     size_t n = 0;
     rc = (tc_shape && pc >= kTcMinPairs) ? moe_pairs_tc_scratch_bytes(&probe, pc, T, &n)
                                          : moe_pairs_scratch_bytes(&probe, pc, T, &n);

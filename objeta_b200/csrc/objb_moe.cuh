@@ -337,7 +337,7 @@ static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* _
   logits += static_cast<size_t>(blockIdx.x) * n;
   ids += static_cast<size_t>(blockIdx.x) * top_k;
   weights += static_cast<size_t>(blockIdx.x) * top_k;
-  extern __shared__ float sp[];  // [n] exp values, then probs
+  extern __shared__ __align__(16) float sp[];  // [n] exp values, then probs
   __shared__ float s_max, s_sum;
   __shared__ float s_wmax[32];
   // the maximum is exact in any order: a block reduction
@@ -357,10 +357,19 @@ static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* _
     sp[e] = __double2float_rn(exp(static_cast<double>(__fsub_rn(logits[e], s_max))));
   __syncthreads();
   if (threadIdx.x == 0) {
-    // the sum keeps the reference's sequential f32 order (from shared memory)
+    // the sum keeps the reference's sequential f32 order; the values come
+    // from shared memory four at a time (the adds, not the loads, are the
+    // dependent chain)
     float s = 0.0f;
-#pragma unroll 8
-    for (int e = 0; e < n; ++e) s = __fadd_rn(s, sp[e]);
+    int e = 0;
+    for (; e + 4 <= n; e += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(sp + e);
+      s = __fadd_rn(s, q.x);
+      s = __fadd_rn(s, q.y);
+      s = __fadd_rn(s, q.z);
+      s = __fadd_rn(s, q.w);
+    }
+    for (; e < n; ++e) s = __fadd_rn(s, sp[e]);
     s_sum = s;
   }
   __syncthreads();

@@ -230,18 +230,21 @@ def _ep_rank(rank, world, port, q, grouped="auto", T=6, K=4):
         # host plan: bit-identical to one GPU
         ep = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="host", grouped=grouped)
         ok = _bits_equal(ep.forward(x, di, dw), ref)
-        # device exchange: deterministic, within the MoE bound of one GPU
+        # device exchange (one all-gather of the packed steps): deterministic,
+        # and within the reference bound of the CPU MoE (only the combine's
+        # association differs from one GPU)
         epd = ExpertParallelMoe(shard, E, K, rank=rank, world=world, exchange="device", grouped=grouped)
         g1, g2 = epd.forward(x, di, dw), epd.forward(x, di, dw)
         torch.cuda.synchronize()
         ok = ok and _bits_equal(g1, g2)
         host = [(mats["gate"][e].cpu().numpy(), mats["up"][e].cpu().numpy(), mats["down"][e].cpu().numpy())
                 for e in range(E)]
-        xh, r1 = x.cpu().numpy(), ref.cpu().numpy()
+        xh = x.cpu().numpy()
         for t in range(min(T, 6)):
             sel = list(zip(ids[t].tolist(), ws[t].tolist()))
+            cpu = O.selected_moe_q4(host, sel, xh[t], H, I, OUT).astype(np.float64)
             bound = moe_bound(q4_matrices(host, H, I, OUT), sel, xh[t], H, I, OUT)
-            ok = ok and bool(np.all(np.abs(g1[t].cpu().numpy().astype(np.float64) - r1[t]) <= 2 * bound))
+            ok = ok and bool(np.all(np.abs(g1[t].cpu().numpy().astype(np.float64) - cpu) <= bound))
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok, None))
