@@ -194,13 +194,11 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
   int E = 0;
   frexpf(m, &E);
-  const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
-  const int f = __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
-  const int r = (X0 != 0 || f >= kWideFull) ? kWideUnit : f;
-  const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
-  const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
+  const float y = ldexpf(xe, 20 - E);
+  const int X0 = __float2int_rn(y);
+  const int cnt = __popc(__ballot_sync(0xFFFFFFFFu, fabsf(y) >= kWideFloor));
   const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
-  const bool wide = isfinite(m) && block_is_wide(nnz, esum, capped);
+  const bool wide = isfinite(m) && block_is_wide(cnt, capped);
   const int X = wide ? 0 : X0;
   const int d0 = ((X + 64) & 127) - 64;
   const int X1 = (X - d0) / 128;

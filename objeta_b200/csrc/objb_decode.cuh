@@ -127,28 +127,27 @@ __device__ __forceinline__ float digit_block(const uint32_t (&qb)[8], const Digi
 // few of them dwarf the rest: an outlier channel of 1e3 among N(0,1) values
 // leaves the others only ~10 bits (and at 1e7 none), and the rows that weigh
 // the outliers by zero then miss the reference's 1e-5 * sum|w x| bound.
-// Per block, in integers (so every image builder agrees bit for bit):
-//   e = sum_l r_l, the rounding error bound in units of 2^-11 grid steps:
-//       r_l = 2^10 (half a step) if X_l != 0 or f_l >= 8, else f_l, with
-//       f_l = rint(|x_l| * 2^(31-E)) (a value that rounds to 0 moves by
-//       itself; one of at least 2^-28 of the block scale counts in full),
+// Per block, with y = x * 2^(20-E) (exact) and in integers, so every image
+// builder agrees bit for bit:
+//   c = #{l : |y_l| >= 2^-8}     (the values whose rounding error, at most
+//                                 half a grid step, is not below 2^-9 of a
+//                                 step -- smaller ones move by less than that),
 //   R = sum_l min(|X_l|, 2^15)   (the values, each capped at 2^-5 of 2^E),
-// and the block is "wide" when at least two x are nonzero and 8 e > R, i.e.
-// its possible rounding error exceeds 2^-14 of its capped mass.  Up to 7
+// and the block is "wide" when c >= 2 and c * 2^13 > R, i.e. the half-step
+// rounding of its c values can exceed 2^-14 of its capped mass.  Up to 7
 // outliers of up to ~3e6 times the block's ordinary values qualify (beyond
 // that an outlier's capped mass hides the others'); an N(0,1) block sits
 // about 4x below the line, and values far below the grid (silu of a large
-// negative gate) count only by their size.  A wide block's digit words and block sum are
+// negative gate) do not count.  A wide block's digit words and block sum are
 // zero in the image (it adds nothing to the integer path), its 2^(E-20) word
 // holds kWideMark, and the consumer warp adds the block's terms in fp32
 // instead, one element per lane: ((q_l - off) * scale) * x_l.
 constexpr int kWideCap = 1 << 15;
-constexpr int kWideUnit = 1 << 10;
-constexpr int kWideFull = 8;  // f_l from which a value that rounds to 0 counts a full unit
+constexpr float kWideFloor = 0.00390625f;  // 2^-8 of a grid step
 constexpr uint32_t kWideMark = 0x80000000u;  // -0.0f: a zero block sum times it stays zero
 
-// The wide test from n = #{x != 0}, e and R (above).
-__device__ __forceinline__ bool block_is_wide(int n, int e, int R) { return n >= 2 && 8 * e > R; }
+// The wide test from c and R (above).
+__device__ __forceinline__ bool block_is_wide(int c, int R) { return c >= 2 && (c << 13) > R; }
 
 // Code q (unsigned, before the offset) of element l of one block in the
 // reference byte layouts (quant.rs:814-879), read with byte loads.
@@ -320,6 +319,23 @@ struct Tile<OBJB_IQ3_0> {
     return r;
   }
 };
+
+// 4 FP4 E2M1 codes (the low 16 bits of u, element order) -> 4 int8 holding
+// 2 * value (exact: 0, +-1, +-2, +-3, +-4, +-6, +-8, +-12) by byte-permute
+// table lookups; checked for all 65536 inputs.
+__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t fp4x4_to_i8x4(uint32_t u) {
+  const uint32_t sel = u & 0x7777u;                      // magnitude index per nibble
+  const uint32_t pos = prmt_b32(0x03020100u, 0x0C080604u, sel);  // 0 1 2 3 4 6 8 12
+  const uint32_t neg = prmt_b32(0xFDFEFF00u, 0xF4F8FAFCu, sel);  // their negatives
+  // sign bits (bit 3 of each nibble) on byte sign positions, replicated
+  const uint32_t sgn = prmt_b32(u, u << 4, 0x9D8Cu);
+  return (pos & ~sgn) | (neg & sgn);
+}
 
 // ------------------------------------------------- FP4 E2M1, interleaved
 // Block = [E8M0 scale (1)][16 packed bytes] (quant.rs:908-926).  Tile = 2

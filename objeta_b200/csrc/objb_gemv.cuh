@@ -230,13 +230,11 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
     int E = 0;
     frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
-    const int X0 = __float2int_rn(ldexpf(xe, 20 - E));
-    const int f = __float2int_rn(fabsf(ldexpf(xe, 31 - E)));
-    const int r = (X0 != 0 || f >= kWideFull) ? kWideUnit : f;
-    const int nnz = __popc(__ballot_sync(0xFFFFFFFFu, xe != 0.0f));
-    const int esum = __reduce_add_sync(0xFFFFFFFFu, r);
+    const float y = ldexpf(xe, 20 - E);
+    const int X0 = __float2int_rn(y);
+    const int cnt = __popc(__ballot_sync(0xFFFFFFFFu, fabsf(y) >= kWideFloor));
     const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
-    const bool wide = isfinite(m) && block_is_wide(nnz, esum, capped);
+    const bool wide = isfinite(m) && block_is_wide(cnt, capped);
     const int X = wide ? 0 : X0;
     const int d0 = ((X + 64) & 127) - 64;
     const int X1 = (X - d0) / 128;
@@ -316,23 +314,17 @@ __device__ __forceinline__ void digit_quarter(const float* __restrict__ xb, bool
     frexpf(m, &E);     // m < 2^E (E = 0 for m = 0)
     const int k = 20 - E, k1 = min(k, 127);
     const float s1 = __int_as_float((k1 + 127) << 23), s2 = __int_as_float((k - k1 + 127) << 23);
-    int nnz = 0, esum = 0, capped = 0;
+    int acc = 0;  // capped sum (< 2^21) and count (<= 32, from bit 24), packed
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float y = (v[i] * s1) * s2;  // exact: x * 2^(20-E)
       X[i] = __float_as_int(y + 12582912.0f) - 0x4B400000;
-      nnz += v[i] != 0.0f;
-      const int f = __float2int_rn(fabsf(y) * 2048.0f);
-      esum += (X[i] != 0 || f >= kWideFull) ? kWideUnit : f;
-      capped += min(abs(X[i]), kWideCap);
+      acc += min(abs(X[i]), kWideCap) + (fabsf(y) >= kWideFloor ? (1 << 24) : 0);
     }
-    // over the block's four quarters: nnz (<= 32) and esum (<= 2^15) packed
-    int c = esum | (nnz << 24);
-    c += __shfl_xor_sync(gmask, c, 1);
-    c += __shfl_xor_sync(gmask, c, 2);
-    capped += __shfl_xor_sync(gmask, capped, 1);
-    capped += __shfl_xor_sync(gmask, capped, 2);
-    wide = block_is_wide(c >> 24, c & 0xFFFFFF, capped);
+    // over the block's four quarters
+    acc += __shfl_xor_sync(gmask, acc, 1);
+    acc += __shfl_xor_sync(gmask, acc, 2);
+    wide = block_is_wide(acc >> 24, acc & 0xFFFFFF);
     if (wide) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) X[i] = 0;

@@ -78,20 +78,7 @@ __device__ __forceinline__ int ceil_log2_ref(float y) {
 // words (j * 8 + g) * 3 + k = digit k of elements 4g .. 4g+3 of block slot j,
 // word 48 + j = act_scale(block) * 2^-10 as f32, word 50 + j = 0.
 
-// 4 FP4 codes (the low 16 bits of u, element order) -> 4 int8 (2 * value).
-__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-__device__ __forceinline__ uint32_t fp4x4_to_i8x4(uint32_t u) {
-  const uint32_t sel = u & 0x7777u;                      // magnitude index per nibble
-  const uint32_t pos = prmt_b32(0x03020100u, 0x0C080604u, sel);  // 0 1 2 3 4 6 8 12
-  const uint32_t neg = prmt_b32(0xFDFEFF00u, 0xF4F8FAFCu, sel);  // their negatives
-  // sign bits (bit 3 of each nibble) on byte sign positions, replicated
-  const uint32_t sgn = prmt_b32(u, u << 4, 0x9D8Cu);
-  return (pos & ~sgn) | (neg & sgn);
-}
+// fp4x4_to_i8x4 (objb_decode.cuh): 4 FP4 codes -> 4 int8 (2 * value).
 
 struct RowDotFp8Fp4 {
   using XRegs = DigitRegs;

@@ -4,9 +4,9 @@ with the 1e-5 * sum|w x| row bound, on vectors with outlier values.
 
 The kernels hold each 32-value block of x as X = rint(x * 2^(20-E)) (2^E above
 the block's largest |x|) and form sum_l (q_l - off) X_l exactly in integers;
-a block whose few largest values dwarf the others ("wide": the bound on its
-rounding error exceeds 2^-14 of its values' mass, each value capped at 2^-5
-of the block scale) is left out of the integer sum and added in fp32
+a block whose few largest values dwarf the others ("wide": the half-step
+rounding of its values can exceed 2^-14 of their mass, each value capped at
+2^-5 of the block scale) is left out of the integer sum and added in fp32
 instead.  This file states
 that arithmetic in numpy (integer sums exact, per-block fp32 products as the
 kernel rounds them, the sum over blocks in f64) so the rule can be judged on
@@ -58,16 +58,15 @@ def digit_X(xb):
 
 
 def wide_blocks(xb):
-    """The kernels' wide-block rule on x blocks [nb, 32] (f32): n nonzero x,
-    f = rint(|x| 2^(31-E)), e = sum (2^10 if X != 0 or f >= 8 else f),
-    R = sum min(|X|, 2^15); wide <=> n >= 2 and 8 e > R."""
+    """The kernels' wide-block rule on x blocks [nb, 32] (f32): with
+    y = x 2^(20-E), c = #{|y| >= 2^-8} and R = sum min(|X|, 2^15),
+    wide <=> c >= 2 and c * 2^13 > R."""
     X, E, m = digit_X(xb)
-    n = (xb != 0).sum(axis=1)
     with np.errstate(invalid="ignore", over="ignore"):
-        fine = np.nan_to_num(np.rint(np.abs(np.ldexp(xb.astype(np.float64), (31 - E)[:, None])))).astype(np.int64)
-    e = np.where((X != 0) | (fine >= 8), 1024, fine).sum(axis=1)
+        y = np.nan_to_num(np.abs(np.ldexp(xb.astype(np.float64), (20 - E)[:, None])))
+    c = (y >= 2.0 ** -8).sum(axis=1)
     R = np.minimum(np.abs(X), 1 << 15).sum(axis=1)
-    return np.isfinite(m) & (n >= 2) & (8 * e > R)
+    return np.isfinite(m) & (c >= 2) & (c * 8192 > R)
 
 
 def digit_gemv(fmt, q, x, rows, cols, wide_rule=True):
