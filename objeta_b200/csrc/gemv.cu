@@ -212,8 +212,8 @@ int gemv_fp4_split_device(const void* w, const void* s, const float* x, float* y
   const uint8_t* sb = static_cast<const uint8_t*>(s);
   RowLayoutHost L;
   const bool fast = aligned16(wb) && aligned16(sb) &&
-                    plan_rows(r, c, c / 2, c / 32, dev::SplitFp4::P, false, dev::kMaxConsumerWarps, &L);
-  if (fast) return launch_gemv_pipe<dev::RowDotSplitFp4>(L, wb, sb, x, y, stream, device, props);
+                    plan_rows(r, c, c / 2, c / 32, dev::RowDotSplitFp4Digit::P, false, dev::kMaxConsumerWarps, &L);
+  if (fast) return launch_gemv_pipe<dev::RowDotSplitFp4Digit>(L, wb, sb, x, y, stream, device, props);
   dev::gemv_fp4_split_fallback_kernel<<<(r + 7) / 8, 256, 0, stream>>>(wb, sb, x, y, r, c);
   OBJB_CUDA(cudaGetLastError(), "launch split FP4 fallback kernel");
   return OBJB_OK;
@@ -301,8 +301,8 @@ int objb_pipe_plan_info(int fmt, int split_fp4, size_t rows, size_t cols, int bl
   // would a 16-byte aligned vector be formed in-kernel (one vector per launch)?
   const float* aligned = reinterpret_cast<const float*>(static_cast<uintptr_t>(256));
   bool inl = false;
-  if (split_fp4) inl = blocks_per_lane == 2 ? objb::inline_x_ok<objb::dev::RowDotSplitFp4>(L, aligned)
-                                            : objb::inline_x_ok<objb::dev::RowDotSplitFp4T<1>>(L, aligned);
+  if (split_fp4) inl = blocks_per_lane == 2 ? objb::inline_x_ok<objb::dev::RowDotSplitFp4Digit>(L, aligned)
+                                            : objb::inline_x_ok<objb::dev::RowDotSplitFp4DigitT<1>>(L, aligned);
   else if (fmt == OBJB_Q4_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_Q4_0>>(L, aligned);
   else if (fmt == OBJB_Q5_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_Q5_0>>(L, aligned);
   else if (fmt == OBJB_IQ3_0) inl = objb::inline_x_ok<objb::dev::RowDot<OBJB_IQ3_0>>(L, aligned);

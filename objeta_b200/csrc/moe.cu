@@ -162,8 +162,8 @@ struct DownRowFormat {
   static constexpr int kBlocksPerLane = 2;
 };
 template <>
-struct DownRowFormat<dev::RowDotSplitFp4> {
-  using type = dev::RowDotSplitFp4T<1>;
+struct DownRowFormat<dev::RowDotSplitFp4Digit> {
+  using type = dev::RowDotSplitFp4DigitT<1>;
   static constexpr int kBlocksPerLane = 1;
 };
 
@@ -437,7 +437,7 @@ int moe_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out) {
     MoePlan<RD> p = plan_moe<RD>(s, l->fmt, split, true);
     need = p.fast ? p.act_bytes + (p.imgx_quads + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
   };
-  if (split) calc(dev::RowDotSplitFp4{});
+  if (split) calc(dev::RowDotSplitFp4Digit{});
   else if (l->fmt == OBJB_Q4_0) calc(dev::RowDot<OBJB_Q4_0>{});
   else if (l->fmt == OBJB_Q5_0) calc(dev::RowDot<OBJB_Q5_0>{});
   else if (l->fmt == OBJB_IQ3_0) calc(dev::RowDot<OBJB_IQ3_0>{});
@@ -459,7 +459,7 @@ int moe_selected(const objb_moe_layer* l, const int32_t* ids, const float* weigh
     return OBJB_FAIL(OBJB_ERR_INVALID_INPUT, "run selected-expert MoE", "null device pointer");
   const bool aligned = (l->flags & OBJB_MOE_UNALIGNED) == 0;
   if (split)
-    return run_moe<dev::RowDotSplitFp4, OBJB_FP4_E2M1, true>(*l, s, ids, weights, x, out, limit, stream, scratch,
+    return run_moe<dev::RowDotSplitFp4Digit, OBJB_FP4_E2M1, true>(*l, s, ids, weights, x, out, limit, stream, scratch,
                                                               scratch_bytes, aligned, mid, err_word);
   switch (l->fmt) {
     case OBJB_Q4_0:
@@ -502,7 +502,7 @@ int moe_pairs_scratch_bytes(const objb_moe_layer* l, size_t num_pairs, size_t nu
     using RD = decltype(tag);
     *out = pairs_need(plan_moe<RD>(s, l->fmt, split, true), s, T);
   };
-  if (split) calc(dev::RowDotSplitFp4{});
+  if (split) calc(dev::RowDotSplitFp4Digit{});
   else if (l->fmt == OBJB_Q4_0) calc(dev::RowDot<OBJB_Q4_0>{});
   else if (l->fmt == OBJB_Q5_0) calc(dev::RowDot<OBJB_Q5_0>{});
   else if (l->fmt == OBJB_IQ3_0) calc(dev::RowDot<OBJB_IQ3_0>{});
@@ -528,7 +528,7 @@ int moe_pairs(const objb_moe_layer* l, size_t num_pairs, const int32_t* pair_exp
 #define OBJB_PAIRS(RDT, F, SP)                                                                                   \
   return run_pairs<RDT, F, SP>(*l, s, T, pair_expert, pair_token, pair_out, d_num_pairs, x, v, VR, limit, stream, \
                                scratch, scratch_bytes, aligned, err_word)
-  if (split) OBJB_PAIRS(dev::RowDotSplitFp4, OBJB_FP4_E2M1, true);
+  if (split) OBJB_PAIRS(dev::RowDotSplitFp4Digit, OBJB_FP4_E2M1, true);
   switch (l->fmt) {
     case OBJB_Q4_0: OBJB_PAIRS(dev::RowDot<OBJB_Q4_0>, OBJB_Q4_0, false);
     case OBJB_Q5_0: OBJB_PAIRS(dev::RowDot<OBJB_Q5_0>, OBJB_Q5_0, false);

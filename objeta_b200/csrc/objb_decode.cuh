@@ -385,40 +385,6 @@ struct Tile<OBJB_FP4_E2M1> {
   }
 };
 
-// ------------------------------------------------------ FP4 E2M1, split
-// DeepSeek layout (moe.rs:27-35, quant.rs:368-408): weight [rows, cols/2],
-// scale [rows, cols/32].  A lane owns P blocks (seg * 32 * P + j * 32 + lane),
-// j < P, so consecutive lanes read consecutive 16-byte blocks (conflict-free
-// 128-bit shared loads).  P = 2 by default; P = 1 spreads a row over twice the
-// warps (the MoE down rows, whose CTAs own few rows per expert).
-template <int P_>
-struct SplitFp4T {
-  static constexpr int P = P_;
-  using XRegs = Words<8 * P>;
-
-  __device__ __forceinline__ static float dot(const uint8_t* wrow, const uint8_t* srow, int b0,
-                                              int stride, int nblocks, const XRegs& xr) {
-    float total = 0.0f;
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      const int b = b0 + j * stride;
-      if (b < nblocks) {
-        const uint4 q = *reinterpret_cast<const uint4*>(wrow + 16 * b);
-        const float s = e8m0_to_f32(srow[b]);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-        float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float2 v = e2m1x2_to_float2((qw[k >> 2] >> ((k & 3) * 8)) & 0xFFu);
-          acc = __ffma2_rn(v, xr.f2(j * 16 + k), acc);
-        }
-        total = fmaf(acc.x + acc.y, s, total);
-      }
-    }
-    return total;
-  }
-};
-using SplitFp4 = SplitFp4T<2>;
 
 // ------------------------------------------- generic block dot (fallback)
 // Reads one block straight from global memory (any alignment) and returns

@@ -105,26 +105,61 @@ struct IsDigitRD<RowDot<FMT>> {
   static constexpr int fmt = FMT;
 };
 
-template <int P>
-struct RowDotSplitFp4T {
-  using D = SplitFp4T<P>;
-  using XRegs = typename D::XRegs;
+
+// Split FP4 E2M1 rows on the integer path: x as the digits of
+// X = rint(x * 2^(20-E)) (the digit image of Q4_0 / Q5_0 / IQ3_0), the codes
+// as 2 * value in int8 (fp4x4_to_i8x4), their products summed exactly by
+// dp4a; one int -> f32 conversion and one FMA by scale * 2^(E-21) per block.
+// A lane owns P blocks b = seg * 32 P + lane + 32 j (j < P): consecutive
+// lanes read consecutive 16-byte blocks (conflict-free 128-bit shared loads);
+// P = 1 spreads a row over twice the warps (the MoE down rows, whose CTAs own
+// few rows per expert).  Its image: words (j * 8 + g) * 3 + k = digit k of
+// elements 4g .. 4g+3 of slot j; word 24 P + j = 2^(E-21) of slot j's block
+// (kWideMark for a wide block, NaN for a block that is not finite).
+template <int P_>
+struct RowDotSplitFp4DigitT {
+  static constexpr int P = P_;
   static constexpr int kBlocksPerLane = P;
+  using XRegs = Words<(25 * P + 3) / 4>;
   int b0, nblocks;
   __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
     b0 = seg * 32 * P + lane;
     nblocks = L.nblocks;
   }
-  __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
-    const int seg = lt / 32, lane = lt % 32;
-    const int b = seg * 32 * P + lane + (q / 8) * 32;
-    return b < L.nblocks ? b * 32 + 4 * (q % 8) : -1;
-  }
+  __device__ __forceinline__ static int scale_word(int j) { return 24 * P + j; }
   __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t* srow, const XRegs& xr) const {
-    return D::dot(wrow, srow, b0, 32, nblocks, xr);
+    float r = 0.0f;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      const int b = b0 + 32 * j;
+      if (b < nblocks) {
+        const uint4 q = *reinterpret_cast<const uint4*>(wrow + 16 * b);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        int a0 = 0, a1 = 0, a2 = 0;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int g = 2 * w + h;
+            const int v = static_cast<int>(fp4x4_to_i8x4(h ? (qw[w] >> 16) : qw[w]));
+            a0 = __dp4a(v, static_cast<int>(xr.w((j * 8 + g) * 3 + 0)), a0);
+            a1 = __dp4a(v, static_cast<int>(xr.w((j * 8 + g) * 3 + 1)), a1);
+            a2 = __dp4a(v, static_cast<int>(xr.w((j * 8 + g) * 3 + 2)), a2);
+          }
+        }
+        const int S = a0 + (a1 + a2 * 128) * 128;
+        r = fmaf(__int2float_rn(S), e8m0_to_f32(srow[b]) * __uint_as_float(xr.w(scale_word(j))), r);
+      }
+    }
+    return r;
   }
 };
-using RowDotSplitFp4 = RowDotSplitFp4T<2>;
+using RowDotSplitFp4Digit = RowDotSplitFp4DigitT<2>;
+
+template <class RD>
+struct IsSplitDigitRD : std::false_type {};
+template <int P>
+struct IsSplitDigitRD<RowDotSplitFp4DigitT<P>> : std::true_type {};
 
 // Dense bf16 rows (the shared expert of a DeepSeek-style layer; not a
 // reference QuantFormat).  A lane reads 16-byte chunks (8 columns) c0 + 32 i,
@@ -266,6 +301,66 @@ __global__ void __launch_bounds__(256) ximage_digits_kernel(const RowLayout L, c
     } else if (lane == 25) {
       widx = 50 + b;
       val = static_cast<uint32_t>(-T::kOffset * sx);
+    }
+    if (widx >= 0) out[(static_cast<size_t>(widx >> 2) * ntp + lt) * 4 + (widx & 3)] = val;
+  }
+}
+
+// Digit images of split FP4 rows (RowDotSplitFp4DigitT<P>): one warp per
+// (vector, block); the block's X, its digits and the wide test as in
+// ximage_digits_kernel; group g of slot j holds elements 4g .. 4g+3, and the
+// slot's scale word is 2^(E-21) (the weights enter as 2 * value).
+template <int P>
+__global__ void __launch_bounds__(256) ximage_split_digits_kernel(const RowLayout L, const float* __restrict__ x,
+                                                                  size_t x_stride, int nvec, uint4* __restrict__ img,
+                                                                  size_t img_stride_quads, const int32_t* count) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // x may be the output of the kernel this one was launched behind.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (count) nvec = min(max(*count, 0), nvec);  // vectors to build (device), at most nvec
+  const int ntp = L.nseg * 32;
+  const int nb_img = ntp * P;  // block slots covered by the image (incl. idle lanes)
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb_img; wi += warps) {
+    const int v = wi / nb_img, b = wi % nb_img;  // slot b covers global block b
+    const float xe = b < L.nblocks ? __ldg(x + v * x_stride + b * 32 + lane) : 0.0f;
+    float m = fabsf(xe);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    int E = 0;
+    frexpf(m, &E);  // m < 2^E (E = 0 for m = 0)
+    const float y = ldexpf(xe, 20 - E);
+    const int X0 = __float2int_rn(y);
+    const int cnt = __popc(__ballot_sync(0xFFFFFFFFu, fabsf(y) >= kWideFloor));
+    const int capped = __reduce_add_sync(0xFFFFFFFFu, min(abs(X0), kWideCap));
+    const bool wide = isfinite(m) && block_is_wide(cnt, capped);
+    const int X = wide ? 0 : X0;
+    const int d0 = ((X + 64) & 127) - 64;
+    const int X1 = (X - d0) / 128;
+    const int d1 = ((X1 + 64) & 127) - 64;
+    const int d2 = (X1 - d1) / 128;
+    const int seg = b / (32 * P), j = (b % (32 * P)) / 32, lt = seg * 32 + b % 32;
+    const int t = lane < 24 ? lane : 0;  // word t = g * 3 + k of this slot
+    const int g = t / 3, k = t % 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int s0 = __shfl_sync(0xFFFFFFFFu, d0, 4 * g + e);
+      const int s1 = __shfl_sync(0xFFFFFFFFu, d1, 4 * g + e);
+      const int s2 = __shfl_sync(0xFFFFFFFFu, d2, 4 * g + e);
+      const int dk = k == 0 ? s0 : (k == 1 ? s1 : s2);
+      word |= (static_cast<uint32_t>(dk) & 0xFFu) << (8 * e);
+    }
+    uint32_t* out = reinterpret_cast<uint32_t*>(img + v * img_stride_quads);
+    int widx = -1;
+    uint32_t val = 0;
+    if (lane < 24) {
+      widx = (j * 8 + g) * 3 + k;
+      val = word;
+    } else if (lane == 24) {
+      widx = RowDotSplitFp4DigitT<P>::scale_word(j);
+      val = wide ? kWideMark : __float_as_uint(isfinite(m) ? ldexpf(1.0f, E - 21) : __int_as_float(0x7FC00000));
     }
     if (widx >= 0) out[(static_cast<size_t>(widx >> 2) * ntp + lt) * 4 + (widx & 3)] = val;
   }
@@ -559,6 +654,126 @@ __device__ __noinline__ void add_wide_terms(float* red, const uint8_t* stg, int 
   }
 }
 
+// The wide-block pass of split FP4 rows (RowDotSplitFp4DigitT<P>): as
+// add_wide_terms, with the slot-j block of lane `src` at global block
+// seg * 32 P + src + 32 j, its 16 code bytes in the row and its E8M0 scale in
+// the stage's scale rows (`srows`, `srow_bytes` apart; the second matrix's
+// weights and scale rows `part` and `sb_part` bytes further).  A term is
+// (value * scale) * x_l, the reference's w * x (decode_deepseek_fp4_to_f32,
+// deepseek.rs:862-918, then a dense dot).
+template <int P, bool DUAL>
+__device__ __noinline__ void add_wide_terms_split(float* red, const uint8_t* stg, const uint8_t* srows, int part,
+                                                  int sb_part, int row_bytes, int srow_bytes, int nseg, int seg,
+                                                  int grp, int ngrp, int nr, uint32_t w0, uint32_t w1,
+                                                  const float* __restrict__ xd) {
+  const int lane = threadIdx.x & 31;
+  for (int t = grp * 4; t < nr; t += ngrp * 4) {
+    const int tend = min(nr, t + 4);
+    for (int r = t; r < tend; ++r) {
+      float sa = 0.0f, sb = 0.0f;
+#pragma unroll 1
+      for (int j = 0; j < P; ++j) {
+        uint32_t m = j ? w1 : w0;
+#pragma unroll 1
+        while (m) {
+          const int src = __ffs(m) - 1;
+          m &= m - 1;
+          const int b = seg * 32 * P + src + 32 * j;
+          const float xl = __ldg(xd + static_cast<size_t>(b) * 32 + lane);
+          const uint32_t byte = stg[r * row_bytes + 16 * b + (lane >> 1)];
+          const uint32_t c = (lane & 1) ? (byte >> 4) : (byte & 0xFu);
+          const int v2 = static_cast<int8_t>(fp4x4_to_i8x4(c) & 0xFFu);  // 2 * value
+          const float scale = e8m0_to_f32(srows[r * srow_bytes + b]);
+          sa += __fmul_rn(static_cast<float>(v2) * (0.5f * scale), xl);
+          if constexpr (DUAL) {
+            const uint32_t byte2 = stg[part + r * row_bytes + 16 * b + (lane >> 1)];
+            const uint32_t c2 = (lane & 1) ? (byte2 >> 4) : (byte2 & 0xFu);
+            const int u2 = static_cast<int8_t>(fp4x4_to_i8x4(c2) & 0xFFu);
+            const float scale2 = e8m0_to_f32(srows[sb_part + r * srow_bytes + b]);
+            sb += __fmul_rn(static_cast<float>(u2) * (0.5f * scale2), xl);
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sa += __shfl_xor_sync(0xFFFFFFFFu, sa, o);
+        if constexpr (DUAL) sb += __shfl_xor_sync(0xFFFFFFFFu, sb, o);
+      }
+      if (lane == 0) {
+        red[(r * nseg + seg) * 2] += sa;
+        if constexpr (DUAL) red[(r * nseg + seg) * 2 + 1] += sb;
+      }
+    }
+  }
+}
+
+// Row formats whose digit images may mark wide blocks, and their fp32 pass.
+template <class RD>
+struct WideTerms {
+  static constexpr bool value = false;
+};
+template <int FMT>
+struct WideTerms<RowDot<FMT>> {
+  static constexpr bool value = IsDigitRD<RowDot<FMT>>::value;
+  static constexpr int kSlots = 2;
+  template <class XR>
+  __device__ __forceinline__ static uint32_t mark_word(const XR& xr, int j) { return xr.w(48 + j); }
+  template <bool DUAL>
+  __device__ __forceinline__ static void add(float* red, const uint8_t* stg, const uint8_t*, int part, int,
+                                             const RowLayout& L, int seg, int grp, int nr, uint32_t w0, uint32_t w1,
+                                             const float* xd) {
+    add_wide_terms<FMT, DUAL>(red, stg, part, L.row_bytes, L.nseg, seg, grp, L.ngrp, nr, w0, w1, xd);
+  }
+};
+template <int P>
+struct WideTerms<RowDotSplitFp4DigitT<P>> {
+  static constexpr bool value = true;
+  static constexpr int kSlots = P;
+  template <class XR>
+  __device__ __forceinline__ static uint32_t mark_word(const XR& xr, int j) {
+    return xr.w(RowDotSplitFp4DigitT<P>::scale_word(j));
+  }
+  template <bool DUAL>
+  __device__ __forceinline__ static void add(float* red, const uint8_t* stg, const uint8_t* srows, int part,
+                                             int sb_part, const RowLayout& L, int seg, int grp, int nr, uint32_t w0,
+                                             uint32_t w1, const float* xd) {
+    add_wide_terms_split<P, DUAL>(red, stg, srows, part, sb_part, L.row_bytes, L.srow_bytes, L.nseg, seg, grp, L.ngrp,
+                                  nr, w0, w1, xd);
+  }
+};
+
+// One stage's wide-block pass of a warp (row formats with WideTerms).
+template <class RD, bool DUAL, class XR>
+__device__ __forceinline__ void wide_stage(const XR& xr, float* red, const uint8_t* stg, const uint8_t* sca, int part,
+                                           const RowLayout& L, int seg, int grp, int nr, const float* xd,
+                                           unsigned* err) {
+  if constexpr (WideTerms<RD>::value) {
+    using WT = WideTerms<RD>;
+    // the lanes whose slot-0 / slot-1 block is wide
+    const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, WT::mark_word(xr, 0) == kWideMark);
+    uint32_t w1 = 0u;
+    if constexpr (WT::kSlots > 1) w1 = __ballot_sync(0xFFFFFFFFu, WT::mark_word(xr, 1) == kWideMark);
+    __syncwarp();
+    if (xd != nullptr)
+      WT::template add<DUAL>(red, stg, sca, part, part, L, seg, grp, nr, w0, w1, xd);
+    else if ((threadIdx.x & 31) == 0 && err)
+      atomicOr(err, kErrNoWideSource);
+  }
+}
+
+// Whether this warp's x registers mark a wide block.
+template <class RD, class XR>
+__device__ __forceinline__ bool warp_has_wide(const XR& xr) {
+  if constexpr (WideTerms<RD>::value) {
+    using WT = WideTerms<RD>;
+    bool mine = WT::mark_word(xr, 0) == kWideMark;
+    if constexpr (WT::kSlots > 1) mine = mine || WT::mark_word(xr, 1) == kWideMark;
+    return __any_sync(0xFFFFFFFFu, mine);
+  } else {
+    return false;
+  }
+}
+
 // Consumer warps: nseg * ngrp (<= kMaxConsumerWarps); one producer warp more.
 constexpr int kPipeThreads = (kMaxConsumerWarps + 1) * 32;
 
@@ -713,17 +928,7 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
             if (t < nr) red[(t * L.nseg + seg) * 2 + idx / RB] = v[0];
           }
         }
-        if constexpr (kWide) {
-          // the lanes whose tile block 0 / 1 is wide
-          const uint32_t w0 = __ballot_sync(0xFFFFFFFFu, xr.w(48) == kWideMark);
-          const uint32_t w1 = __ballot_sync(0xFFFFFFFFu, xr.w(49) == kWideMark);
-          __syncwarp();
-          if (J.xd != nullptr)
-            add_wide_terms<IsDigitRD<RD>::fmt, DUAL>(red, stg, part, L.row_bytes, L.nseg, seg, grp, L.ngrp, nr, w0,
-                                                     w1, J.xd);
-          else if (lane == 0 && err)
-            atomicOr(err, kErrNoWideSource);
-        }
+        if constexpr (kWide) wide_stage<RD, DUAL>(xr, red, stg, sca, part, L, seg, grp, nr, J.xd, err);
         __syncwarp();
         if (lane == 0) mbar_arrive(&sp.empty[slot]);
         named_bar_sync(1, nthr);
@@ -742,11 +947,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) pipe_kernel(const RowLayout L
         ++it;
       }
     };
-    bool wide_any = false;
-    if constexpr (IsDigitRD<RD>::value)
-      wide_any = __any_sync(0xFFFFFFFFu, xr.w(48) == kWideMark || xr.w(49) == kWideMark);
-    if constexpr (IsDigitRD<RD>::value) {
-      if (wide_any) stages(std::true_type{});
+    if constexpr (WideTerms<RD>::value) {
+      if (warp_has_wide<RD>(xr)) stages(std::true_type{});
       else stages(std::false_type{});
     } else {
       stages(std::false_type{});

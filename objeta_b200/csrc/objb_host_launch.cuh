@@ -50,7 +50,12 @@ int launch_ximage(const RowLayoutHost& L, const float* x, size_t x_stride, int n
   // Launched with programmatic serialization: the kernel waits
   // (griddepcontrol.wait) for the preceding grid before reading x, so its
   // launch overlaps that grid's tail.
-  if constexpr (dev::IsDigitRD<RD>::value) {
+  if constexpr (dev::IsSplitDigitRD<RD>::value) {
+    const int warps = L.nseg * 32 * RD::P * nvec;
+    const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
+    return launch_pdl(dev::ximage_split_digits_kernel<RD::P>, grid, 256, 0, stream, dl, x, x_stride, nvec, img,
+                      img_stride_quads, count);
+  } else if constexpr (dev::IsDigitRD<RD>::value) {
     const int warps = L.nseg * 32 * 2 * nvec;
     const int grid = std::max(1, std::min((warps + 7) / 8, 2048));
     return launch_pdl(dev::ximage_digits_kernel<dev::IsDigitRD<RD>::fmt>, grid, 256, 0, stream, dl, x, x_stride,

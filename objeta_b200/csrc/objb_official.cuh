@@ -74,7 +74,7 @@ __device__ __forceinline__ int ceil_log2_ref(float y) {
 // [-12, 12]) by a byte-permute table lookup; dp4a forms sum (2w) A exactly and
 // the block's f32 contribution is S * (w_scale * act_scale * 2^-10).
 //
-// Image of a lane tile (blocks b0 and b0 + 32 of the lane, as RowDotSplitFp4):
+// Image of a lane tile (blocks b0 and b0 + 32 of the lane, as RowDotSplitFp4Digit):
 // words (j * 8 + g) * 3 + k = digit k of elements 4g .. 4g+3 of block slot j,
 // word 48 + j = act_scale(block) * 2^-10 as f32, word 50 + j = 0.
 

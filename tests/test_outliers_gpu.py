@@ -200,3 +200,31 @@ def test_pairs_outliers(cuda_device, path):
             bound = moe_bound(q4_matrices(host, H, I, OUT), sel, xs[t], H, I, OUT)
             err = np.abs(got[t].astype(np.float64) - ref)
             assert np.all(err <= bound), f"{path} token {t}: worst err/bound {np.max(err / bound):.3f}"
+
+
+@pytest.mark.parametrize("rows,cols", [(2048, 4096), (4096, 2048), (512, 7168)])
+def test_split_fp4_gemv_outliers(cuda_device, rows, cols):
+    """Split FP4 rows (objb_gemv_fp4_split_device) on the integer digit path:
+    outliers over zero codes (both zero codes, 0 and 8, appear) against the
+    interleaved-FP4 gemv_cpu of the same bytes."""
+    import torch
+    from objeta_b200.quant import gemv_fp4_split_device
+    rng = np.random.default_rng(rows + 3 * cols)
+    w = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+    s = rng.integers(119, 124, rows * cols // 32, dtype=np.uint8)
+    x, oc = _outlier_x(cols, seed=cols + 1)
+    W = w.reshape(rows, cols // 2)
+    for i, c in enumerate(oc):   # rows [0, rows/2): code 0 or 8 at every outlier column
+        zero = 0x0 if i % 2 else 0x8
+        if c % 2 == 0:
+            W[: rows // 2, c // 2] = (W[: rows // 2, c // 2] & 0xF0) | zero
+        else:
+            W[: rows // 2, c // 2] = (W[: rows // 2, c // 2] & 0x0F) | (zero << 4)
+    dy = torch.empty(rows, device="cuda")
+    gemv_fp4_split_device(torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(x).cuda(), dy,
+                          rows, cols)
+    torch.cuda.synchronize()
+    inter = np.concatenate([s.reshape(rows, cols // 32, 1), w.reshape(rows, cols // 32, 16)], axis=2).reshape(-1)
+    ref = O.gemv(O.FP4_E2M1, inter, x, rows, cols, threads=0)
+    assert_rows_within(dy.cpu().numpy(), ref, O.row_abs_sums(O.FP4_E2M1, inter, x, rows, cols),
+                       what=f"split fp4 {rows}x{cols} outliers")
