@@ -47,8 +47,36 @@ __global__ void __launch_bounds__(256) ffn_generic_out_kernel(const float* __res
 
 namespace {
 
-bool plan_bf16(int rows, int cols, bool dual, RowLayoutHost* L) {
-  return plan_rows(rows, cols, cols * 2, 0, 2, dual, dev::kMaxConsumerWarps, L, kMoeSmemBudget);
+// Row plan of a bf16 matrix with CPL chunks per lane: cols / (256 CPL) warps
+// per row.
+bool plan_bf16_cpl(int cpl, int rows, int cols, bool dual, RowLayoutHost* L) {
+  const int lanes = (cols / 8 + cpl - 1) / cpl;
+  return plan_rows_lanes(rows, cols, cols * 2, 0, lanes, dual, dev::kMaxConsumerWarps, L, kMoeSmemBudget);
+}
+
+// Chunks per lane for a matrix: the most (fewest warps per row) whose stage
+// still gives every row group one 4-row batch; else the fewest (all warps on
+// the rows of a small stage).
+int pick_cpl(int rows, int cols, bool dual) {
+  const int stage_max = std::min(kMoeSmemBudget, 227 * 1024) / 2 - 4096;
+  const size_t per_row = static_cast<size_t>(cols) * 2 * (dual ? 2 : 1);
+  for (int cpl : {8, 4}) {
+    const int nseg = (cols / 8 + 32 * cpl - 1) / (32 * cpl);
+    if (nseg > dev::kMaxConsumerWarps) continue;
+    const int quantum = std::max(1, dev::kMaxConsumerWarps / nseg) * 4;
+    if (static_cast<size_t>(quantum) * per_row <= static_cast<size_t>(stage_max)) return cpl;
+  }
+  (void)rows;
+  return 2;
+}
+
+template <int CPL, class F>
+int with_cpl(int cpl, F&& f) {
+  switch (cpl) {
+    case 8: return f(std::integral_constant<int, 8>{});
+    case 4: return f(std::integral_constant<int, 4>{});
+    default: return f(std::integral_constant<int, 2>{});
+  }
 }
 
 int even_split(int rows, int sms, int* grid) {
@@ -66,28 +94,18 @@ int validate_dense(size_t rows, size_t cols, const char* action) {
   return OBJB_OK;
 }
 
-int gemv_bf16(const void* w, const float* x, float* y, int rows, int cols, cudaStream_t stream) {
-  int device = 0;
-  OBJB_TRY(current_device(&device));
-  DeviceProps props;
-  OBJB_TRY(device_props(device, &props));
-  RowLayoutHost L;
-  const bool fast = aligned16(w) && plan_bf16(rows, cols, false, &L);
-  if (!fast) {
-    dev::gemv_bf16_fallback_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(static_cast<const uint16_t*>(w), x, y, rows,
-                                                                      cols);
-    OBJB_CUDA(cudaGetLastError(), "launch bf16 GEMV fallback");
-    return OBJB_OK;
-  }
+template <class RD>
+int gemv_bf16_pipe(const RowLayoutHost& L, const void* w, const float* x, float* y, int rows, int device,
+                   const DeviceProps& props, cudaStream_t stream) {
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
-  const bool x_inline = inline_x_ok<dev::RowDotBf16>(L, x);
+  const bool x_inline = inline_x_ok<RD>(L, x);
   uint4* img = nullptr;
   if (!x_inline) {
     void* ws = nullptr;
-    OBJB_TRY(workspace_get(device, stream, ximage_quads<dev::RowDotBf16>(L) * 16, &ws));
+    OBJB_TRY(workspace_get(device, stream, ximage_quads<RD>(L) * 16, &ws));
     img = static_cast<uint4*>(ws);
-    OBJB_TRY(launch_ximage<dev::RowDotBf16>(L, x, 0, 1, img, 0, stream));
+    OBJB_TRY(launch_ximage<RD>(L, x, 0, 1, img, 0, stream));
   }
   int grid = 0;
   dev::GemvProg prog;
@@ -99,17 +117,82 @@ int gemv_bf16(const void* w, const float* x, float* y, int rows, int cols, cudaS
   prog.rows_per_cta = even_split(rows, props.sm_count, &grid);
   prog.err = err;
   const size_t smem = pipe_smem_bytes(L);
-  auto kernel = dev::pipe_kernel<dev::RowDotBf16, dev::GemvProg, false>;
+  auto kernel = dev::pipe_kernel<RD, dev::GemvProg, false>;
   OBJB_TRY(ensure_smem_attr(kernel, device, smem));
   dev::RowLayout dl;
   std::memcpy(&dl, &L, sizeof(dl));
   return launch_pdl(kernel, grid, (L.nseg * L.ngrp + 1) * 32, smem, stream, dl, prog);
 }
 
-size_t ffn_scratch(const RowLayoutHost& lg, const RowLayoutHost& ld, int I, bool fast) {
-  const size_t act = (static_cast<size_t>(I) * 4 + 255) / 256 * 256;
-  if (!fast) return 3 * act;  // gate, up, act
-  return act + (ximage_quads<dev::RowDotBf16>(lg) + ximage_quads<dev::RowDotBf16>(ld)) * 16 + 256;
+int gemv_bf16(const void* w, const float* x, float* y, int rows, int cols, cudaStream_t stream) {
+  int device = 0;
+  OBJB_TRY(current_device(&device));
+  DeviceProps props;
+  OBJB_TRY(device_props(device, &props));
+  RowLayoutHost L;
+  const int cpl = pick_cpl(rows, cols, false);
+  const bool fast = aligned16(w) && plan_bf16_cpl(cpl, rows, cols, false, &L);
+  if (!fast) {
+    dev::gemv_bf16_fallback_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(static_cast<const uint16_t*>(w), x, y, rows,
+                                                                      cols);
+    OBJB_CUDA(cudaGetLastError(), "launch bf16 GEMV fallback");
+    return OBJB_OK;
+  }
+  return with_cpl<0>(cpl, [&](auto c) {
+    return gemv_bf16_pipe<dev::RowDotBf16T<decltype(c)::value>>(L, w, x, y, rows, device, props, stream);
+  });
+}
+
+template <class RDg, class RDd>
+int ffn_bf16_pipe(const RowLayoutHost& lg, const RowLayoutHost& ld, const void* gate, const void* up,
+                  const void* down, int I, int O, const float* x, float* out, int accumulate, float limit,
+                  cudaStream_t stream, int device, const DeviceProps& props, uint8_t* sc, unsigned* err) {
+  const size_t act_bytes = (static_cast<size_t>(I) * 4 + 255) / 256 * 256;
+  float* act = reinterpret_cast<float*>(sc);
+  uint4* imgx = reinterpret_cast<uint4*>(sc + act_bytes);
+  uint4* imga = imgx + ximage_quads<RDg>(lg);
+  // the kernels read x and the activation row directly (float quads) when aligned
+  const bool x_inline = inline_x_ok<RDg>(lg, x);
+  const bool act_inline = inline_x_ok<RDd>(ld, act);
+  if (!x_inline) OBJB_TRY(launch_ximage<RDg>(lg, x, 0, 1, imgx, 0, stream));
+  {
+    int grid = 0;
+    dev::FfnGateUpProg prog;
+    prog.src = dev::StageSource{static_cast<const uint8_t*>(gate), nullptr, static_cast<const uint8_t*>(up), nullptr};
+    prog.ximg = imgx;
+    prog.x = x_inline ? x : nullptr;
+    prog.act = act;
+    prog.I = I;
+    prog.rows_per_cta = even_split(I, props.sm_count, &grid);
+    prog.swiglu_limit = limit;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(lg);
+    auto kernel = dev::pipe_kernel<RDg, dev::FfnGateUpProg, true>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &lg, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (lg.nseg * lg.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  if (!act_inline) OBJB_TRY(launch_ximage<RDd>(ld, act, 0, 1, imga, 0, stream));
+  {
+    int grid = 0;
+    dev::FfnDownProg prog;
+    prog.src = dev::StageSource{static_cast<const uint8_t*>(down), nullptr, nullptr, nullptr};
+    prog.ximg = imga;
+    prog.x = act_inline ? act : nullptr;
+    prog.out = out;
+    prog.O = O;
+    prog.rows_per_cta = even_split(O, props.sm_count, &grid);
+    prog.accumulate = accumulate;
+    prog.err = err;
+    const size_t smem = pipe_smem_bytes(ld);
+    auto kernel = dev::pipe_kernel<RDd, dev::FfnDownProg, false>;
+    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
+    dev::RowLayout dl;
+    std::memcpy(&dl, &ld, sizeof(dl));
+    OBJB_TRY(launch_pdl(kernel, grid, (ld.nseg * ld.ngrp + 1) * 32, smem, stream, dl, prog));
+  }
+  return OBJB_OK;
 }
 
 int ffn_bf16(const void* gate, const void* up, const void* down, int H, int I, int O, const float* x, float* out,
@@ -121,13 +204,16 @@ int ffn_bf16(const void* gate, const void* up, const void* down, int H, int I, i
   unsigned* err = nullptr;
   OBJB_TRY(device_error_word(device, &err));
   RowLayoutHost lg, ld;
-  const bool fast = aligned16(gate) && aligned16(up) && aligned16(down) && plan_bf16(I, H, true, &lg) &&
-                    plan_bf16(O, I, false, &ld);
-  const size_t need = ffn_scratch(lg, ld, I, fast);
+  const int cg = pick_cpl(I, H, true), cd = pick_cpl(O, I, false);
+  const bool fast = aligned16(gate) && aligned16(up) && aligned16(down) && plan_bf16_cpl(cg, I, H, true, &lg) &&
+                    plan_bf16_cpl(cd, O, I, false, &ld);
+  const size_t act_bytes = (static_cast<size_t>(I) * 4 + 255) / 256 * 256;
+  // scratch: act, then the two x images (at most 16 quads per lane tile)
+  const size_t need = fast ? act_bytes + (static_cast<size_t>(16) * lg.nseg * 32 + 16 * ld.nseg * 32) * 16 + 256
+                           : 3 * act_bytes;
   void* ws = nullptr;
   OBJB_TRY(workspace_get(device, stream, need, &ws));
   uint8_t* sc = static_cast<uint8_t*>(ws);
-  const size_t act_bytes = (static_cast<size_t>(I) * 4 + 255) / 256 * 256;
   float* act = reinterpret_cast<float*>(sc);
   if (!fast) {
     float* g = reinterpret_cast<float*>(sc + act_bytes);
@@ -144,50 +230,12 @@ int ffn_bf16(const void* gate, const void* up, const void* down, int H, int I, i
     OBJB_CUDA(cudaGetLastError(), "launch FFN output");
     return OBJB_OK;
   }
-  uint4* imgx = reinterpret_cast<uint4*>(sc + act_bytes);
-  uint4* imga = imgx + ximage_quads<dev::RowDotBf16>(lg);
-  // the kernels read x and the activation row directly (float quads) when aligned
-  const bool x_inline = inline_x_ok<dev::RowDotBf16>(lg, x);
-  const bool act_inline = inline_x_ok<dev::RowDotBf16>(ld, act);
-  if (!x_inline) OBJB_TRY(launch_ximage<dev::RowDotBf16>(lg, x, 0, 1, imgx, 0, stream));
-  {
-    int grid = 0;
-    dev::FfnGateUpProg prog;
-    prog.src = dev::StageSource{static_cast<const uint8_t*>(gate), nullptr, static_cast<const uint8_t*>(up), nullptr};
-    prog.ximg = imgx;
-    prog.x = x_inline ? x : nullptr;
-    prog.act = act;
-    prog.I = I;
-    prog.rows_per_cta = even_split(I, props.sm_count, &grid);
-    prog.swiglu_limit = limit;
-    prog.err = err;
-    const size_t smem = pipe_smem_bytes(lg);
-    auto kernel = dev::pipe_kernel<dev::RowDotBf16, dev::FfnGateUpProg, true>;
-    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
-    dev::RowLayout dl;
-    std::memcpy(&dl, &lg, sizeof(dl));
-    OBJB_TRY(launch_pdl(kernel, grid, (lg.nseg * lg.ngrp + 1) * 32, smem, stream, dl, prog));
-  }
-  if (!act_inline) OBJB_TRY(launch_ximage<dev::RowDotBf16>(ld, act, 0, 1, imga, 0, stream));
-  {
-    int grid = 0;
-    dev::FfnDownProg prog;
-    prog.src = dev::StageSource{static_cast<const uint8_t*>(down), nullptr, nullptr, nullptr};
-    prog.ximg = imga;
-    prog.x = act_inline ? act : nullptr;
-    prog.out = out;
-    prog.O = O;
-    prog.rows_per_cta = even_split(O, props.sm_count, &grid);
-    prog.accumulate = accumulate;
-    prog.err = err;
-    const size_t smem = pipe_smem_bytes(ld);
-    auto kernel = dev::pipe_kernel<dev::RowDotBf16, dev::FfnDownProg, false>;
-    OBJB_TRY(ensure_smem_attr(kernel, device, smem));
-    dev::RowLayout dl;
-    std::memcpy(&dl, &ld, sizeof(dl));
-    OBJB_TRY(launch_pdl(kernel, grid, (ld.nseg * ld.ngrp + 1) * 32, smem, stream, dl, prog));
-  }
-  return OBJB_OK;
+  return with_cpl<0>(cg, [&](auto a) {
+    return with_cpl<0>(cd, [&](auto b) {
+      return ffn_bf16_pipe<dev::RowDotBf16T<decltype(a)::value>, dev::RowDotBf16T<decltype(b)::value>>(
+          lg, ld, gate, up, down, I, O, x, out, accumulate, limit, stream, device, props, sc, err);
+    });
+  });
 }
 
 }  // namespace

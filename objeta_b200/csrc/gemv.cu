@@ -48,10 +48,16 @@ static_assert(sizeof(RowLayoutHost) == sizeof(dev::RowLayout), "layout mirror mi
 
 bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
                int max_consumer_warps, RowLayoutHost* L, int smem_budget) {
-  if (rows <= 0 || cols <= 0 || cols % 32) return false;
+  if (rows <= 0 || cols <= 0 || cols % 32 || blocks_per_lane <= 0) return false;
+  const int lanes = (cols / 32 + blocks_per_lane - 1) / blocks_per_lane;
+  return plan_rows_lanes(rows, cols, row_bytes, srow_bytes, lanes, dual, max_consumer_warps, L, smem_budget);
+}
+
+bool plan_rows_lanes(int rows, int cols, int row_bytes, int srow_bytes, int lanes, bool dual, int max_consumer_warps,
+                     RowLayoutHost* L, int smem_budget) {
+  if (rows <= 0 || cols <= 0 || cols % 32 || lanes <= 0) return false;
   const int nblocks = cols / 32;
   if (row_bytes % 16 || srow_bytes % 16) return false;
-  const int lanes = (nblocks + blocks_per_lane - 1) / blocks_per_lane;
   const int nseg = (lanes + 31) / 32;
   if (nseg > max_consumer_warps) return false;
   const int lpr = 32;  // one row per warp; idle lanes when the row is narrow

@@ -162,28 +162,33 @@ template <int P>
 struct IsSplitDigitRD<RowDotSplitFp4DigitT<P>> : std::true_type {};
 
 // Dense bf16 rows (the shared expert of a DeepSeek-style layer; not a
-// reference QuantFormat).  A lane reads 16-byte chunks (8 columns) c0 + 32 i,
-// i < 8, so consecutive lanes read consecutive chunks (conflict-free 128-bit
-// shared loads); its 64 x values are the matching columns, as float pairs.
+// reference QuantFormat).  A lane reads CPL 16-byte chunks (8 columns each)
+// c0 + 32 i, i < CPL, so consecutive lanes read consecutive chunks
+// (conflict-free 128-bit shared loads); its 8 CPL x values are the matching
+// columns, as float pairs.  CPL = 8 puts 2048 columns on a warp; fewer chunks
+// per lane spread a wide row over more warps (a stage then holds few rows,
+// and the host picks the CPL that keeps every warp busy).
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
-struct RowDotBf16 {
-  using XRegs = Words<16>;
+template <int CPL>
+struct RowDotBf16T {
+  static constexpr int kChunksPerLane = CPL;
+  using XRegs = Words<2 * CPL>;
   int c0, nchunks;
   __device__ __forceinline__ void init(const RowLayout& L, int seg, int lane) {
-    c0 = seg * 256 + lane;
+    c0 = seg * 32 * CPL + lane;
     nchunks = L.cols / 8;
   }
   __device__ __forceinline__ static int quad_col(const RowLayout& L, int lt, int q) {
-    const int c = (lt / 32) * 256 + (q / 2) * 32 + lt % 32;
+    const int c = (lt / 32) * 32 * CPL + (q / 2) * 32 + lt % 32;
     return c < L.cols / 8 ? c * 8 + 4 * (q % 2) : -1;
   }
   __device__ __forceinline__ float dot(const uint8_t* wrow, const uint8_t*, const XRegs& xr) const {
     float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < CPL; ++i) {
       const int c = c0 + 32 * i;
       if (c < nchunks) {
         const uint4 v = *reinterpret_cast<const uint4*>(wrow + 16 * c);
@@ -196,6 +201,7 @@ struct RowDotBf16 {
     return (a0.x + a0.y) + (a1.x + a1.y);
   }
 };
+using RowDotBf16 = RowDotBf16T<8>;
 
 template <class XR>
 __device__ __forceinline__ void load_ximage(const uint4* __restrict__ img, int ntp, int lt, XR& xr) {
@@ -501,16 +507,16 @@ struct IsFloatRD {
 // read quads at most 32 bytes apart): worth reading a fresh vector per job.
 template <class RD>
 struct NearCoalescedQuads : std::false_type {};
-template <>
-struct NearCoalescedQuads<RowDotBf16> : std::true_type {};
+template <int CPL>
+struct NearCoalescedQuads<RowDotBf16T<CPL>> : std::true_type {};
 
 // Float-quad rows for which one direct read of x per CTA beats an image
 // launch (measured on B200): bf16 rows and interleaved FP4 tiles; split FP4
 // rows read 128-byte-strided quads and keep the image launch.
 template <class RD>
 struct DirectQuadsOnce : std::false_type {};
-template <>
-struct DirectQuadsOnce<RowDotBf16> : std::true_type {};
+template <int CPL>
+struct DirectQuadsOnce<RowDotBf16T<CPL>> : std::true_type {};
 template <>
 struct DirectQuadsOnce<RowDot<OBJB_FP4_E2M1>> : std::true_type {};
 

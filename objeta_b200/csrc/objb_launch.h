@@ -46,6 +46,9 @@ constexpr int kGemvSmemBudget = 200 * 1024;
 constexpr int kMoeSmemBudget = 226 * 1024;
 bool plan_rows(int rows, int cols, int row_bytes, int srow_bytes, int blocks_per_lane, bool dual,
                int max_consumer_warps, RowLayoutHost* L, int smem_budget = kGemvSmemBudget);
+// The same with the lanes a row spreads over given directly.
+bool plan_rows_lanes(int rows, int cols, int row_bytes, int srow_bytes, int lanes, bool dual, int max_consumer_warps,
+                     RowLayoutHost* L, int smem_budget = kGemvSmemBudget);
 
 size_t pipe_smem_bytes(const RowLayoutHost& L);
 
