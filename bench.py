@@ -377,7 +377,9 @@ def run_ours(args, world, rank, local):
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32-accumulate (u4/u5/u3 codes, f16 scales)",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "u4/u5/u3 codes x int digits of x (21-bit per-block fixed point; outlier blocks in f32): "
+                     "exact int32 block sums, f16 scales, f32 accumulate",
             "data": "synthetic: weights ~N(0,0.02^2) packed on device, x ~N(0,1), seeded",
             "config": sweep_config(world),
             "timing": "headline: CUDA-graph replays of the 12 GEMVs back to back; per case: event pairs",
@@ -388,11 +390,31 @@ def run_ours(args, world, rank, local):
         result["cpu_baseline"] = cpu_legs(max(3, min(args.steps, 10)), 2)
         if "c5_ep_resident" in moe:
             result["ep"] = ep_summary(moe["c5_ep_resident"], world)
+        # last, so that a reader keeping only the line's tail keeps it: every
+        # case's fraction of peak and the MoE configs in a few numbers
+        result["summary"] = line_summary(case_out, moe, result.get("ep"), result["cpu_baseline"])
     if world > 1:
         dist.barrier()
         del graphs, xgraphs, plain
         dist.destroy_process_group()
     return result
+
+
+def line_summary(case_out, moe, ep, cpu):
+    """A compact digest of the line (under ~1.2 KB)."""
+    out = {"case_frac_of_peak": {k: v["frac_of_peak"] for k, v in case_out.items()}}
+    for key, name in (("c3_q4_stack", "c3"), ("c4_fp4_shared", "c4")):
+        if key in moe:
+            out[name] = {"us_per_token": moe[key]["us_per_token"], "frac": moe[key]["frac_of_hbm"]}
+    if ep:
+        out["c5_resident"] = {k: {"tok_s": v["tokens_per_s"], "frac": v["frac_of_aggregate_hbm"],
+                                  "largest_phase": v.get("largest_phase")}
+                              for k, v in ep.items() if k.startswith("T")}
+    if "c5_ep_cache" in moe:
+        out["c5_cache_pcie_GBs"] = {k: v["pcie_GB/s_all_ranks"] for k, v in moe["c5_ep_cache"].items()
+                                    if k.startswith("T")}
+    out["cpu_GBs"] = {"threads": cpu["value"], "one_thread": cpu["single_thread"]["value"]}
+    return out
 
 
 def gemv_launches(cols):
