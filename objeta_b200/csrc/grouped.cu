@@ -18,17 +18,16 @@
 // operand (16 or 32 vectors wide).  A work item walks its K in steps of 8
 // blocks (256 columns):
 //   * one producer thread stages a step with one 2-D TMA copy of the raw
-//     Q4_0 tile (128 rows x 144 bytes; a per-stage tensor map whose global
-//     address is rewritten on the device for each expert, rows past the
-//     matrix end zero-filled) and two bulk copies of the slice image;
+//     Q4_0 tile (128 rows x 144 bytes, rows past the matrix end zero-filled;
+//     every slice's tensor maps are written once per call by
+//     tc_maps_kernel) and two bulk copies of the slice image;
 //   * four unpack warps turn the raw rows into signed code bytes q - 8 in
 //     core-matrix order (K-major, no swizzle) and the row block scales;
-//   * one thread issues the MMAs two blocks at a time into one of two
-//     tensor-memory slots (an MMA of this shape costs about 100 cycles to
-//     issue whatever its N, so the group, not the slot count, sets the pace);
-//   * sixteen epilogue warps (tensor-memory lanes = tile rows; blocks of one
-//     parity and half of the vectors each) fold the exact block sums into
-//     f32 row sums; the two parity halves are added at the item's end.
+//   * one warp issues one MMA per block into one of five tensor-memory
+//     slots (N = 3 x 16 or 3 x 32 columns each);
+//   * sixteen epilogue warps (tensor-memory lanes = tile rows; a quarter of
+//     the slice's vectors each) fold the exact block sums into f32 row sums
+//     and store them at the item's end.
 // Every hand-off is an mbarrier with a bounded wait.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -60,9 +59,12 @@ constexpr int kTcStages = 3;                   // ring of raw tiles + slice-imag
 constexpr int kTcAbuf = 2;                     // unpacked code buffers
 constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
 constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
-constexpr int kTcBlockCols = 128;              // tensor-memory columns of one block's accumulators (>= kTcNp)
-constexpr int kTcSlotCols = 2 * kTcBlockCols;  // one MMA group (two blocks)
-constexpr int kTcSlots = 2;                    // tensor-memory slots
+constexpr int kTcSlotCols = 256;              // tensor-memory columns of one MMA group
+constexpr int kTcSlots = 2;                    // tensor-memory slots (one group each)
+// A group (one wait, one commit) is 4 blocks of a 16-vector slice (48 of 64
+// columns each) or 2 blocks of a 32-vector slice (96 of 128 columns each).
+__device__ __forceinline__ int tc_group_blocks(int nv) { return nv > kTcUnit ? 2 : 4; }
+__device__ __forceinline__ int tc_block_stride(int nv) { return nv > kTcUnit ? 128 : 64; }
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcUnitBBytes = 3 * kTcUnit * kTcKB * 32;  // digit planes of one unit, one step
 constexpr int kTcUnitXFloats = kTcKB * kTcUnit;          // block scales of one unit, one step
@@ -76,28 +78,26 @@ constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 struct TcSmem {
   alignas(1024) uint8_t a[kTcAbuf][kTcRows * kTcKB * 32];   // signed codes q - 8, core-matrix order
   alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // slice image step (digit planes)
-  alignas(128) uint8_t raw[kTcStages][kTcRows * kTcRawRow]; // raw Q4_0 tile step (TMA box)
+  alignas(128) uint8_t raw[kTcStages][kTcRows * kTcRawRow]; // raw Q4_0 rows of a step (bulk copies)
   alignas(16) float xs[kTcStages][kTcKB * kTcNvp];          // vector block scales [block][vector]
-  alignas(16) float d[kTcAbuf][kTcKB][kTcRows];             // row block scales
-  alignas(16) float xchg[kTcNvp][kTcRows];                  // odd-block partial sums
-  alignas(128) CUtensorMap tmap[kTcStages];                 // per-stage tensor maps being rewritten
-  alignas(8) uint64_t full[kTcStages], empty[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
-  uint64_t t_full[kTcSlots], t_empty[kTcSlots], x_full, x_empty;
+  alignas(16) float d[kTcStages][kTcKB][kTcRows];           // row block scales (written by unpack)
+  alignas(8) uint64_t full[kTcStages], empty[kTcStages], d_full[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
+  uint64_t t_full[kTcSlots], t_empty[kTcSlots];
   uint32_t tmem_base;
   uint32_t abort;  // a wait of this CTA timed out
 };
 static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
-static_assert(kTcNp <= kTcBlockCols && kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols), "tensor-memory slots");
+static_assert(kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols) && kTcNp <= 128 && kTcKB % 4 == 0,
+              "tensor-memory slots");
 static_assert(kTcUnpackWarps * 32 == kTcRows && kTcEpiWarps == 16 && kTcNvp == 2 * kTcUnit, "warp roles");
 
 // Arrival counts of the pipeline barriers.
 constexpr uint32_t kTcFullCount = 1;                                  // producer (arrive + transaction bytes)
 constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps + kTcEpiWarps;  // MMA commit, unpack, epilogue
+constexpr uint32_t kTcDFullCount = kTcUnpackWarps;                    // row scales of a step written
 constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;               // every unpack thread
-constexpr uint32_t kTcAEmptyCount = 1 + kTcEpiWarps;                  // MMA commit, epilogue (row scales)
+constexpr uint32_t kTcAEmptyCount = 1;                                // MMA commit
 constexpr uint32_t kTcTEmptyCount = kTcEpiWarps;
-constexpr uint32_t kTcXFullCount = 32 * kTcEpiWarps / 2;              // every odd-block thread
-constexpr uint32_t kTcXEmptyCount = kTcEpiWarps / 2;
 
 // 1-D bulk copy (both addresses 16-byte aligned, bytes a multiple of 16).
 __device__ __forceinline__ void tc_bulk(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
@@ -128,6 +128,17 @@ __device__ __forceinline__ void tc_tmap_publish(CUtensorMap* gmem_map, const CUt
           reinterpret_cast<uint64_t>(gmem_map)),
       "r"(smem_addr(smem_map))
       : "memory");
+}
+// Tensor map in global memory: new global address (generic proxy), and the
+// release fence that makes such writes visible to the tensor-map proxy.
+__device__ __forceinline__ void tc_tmap_set_addr_global(CUtensorMap* gmem_map, const void* addr) {
+  asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(
+                   reinterpret_cast<uint64_t>(gmem_map)),
+               "l"(reinterpret_cast<uint64_t>(addr))
+               : "memory");
+}
+__device__ __forceinline__ void tc_tmap_release() {
+  asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
 }
 __device__ __forceinline__ void tc_tmap_acquire(const CUtensorMap* gmem_map) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(gmem_map))
@@ -470,6 +481,34 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
   }
 }
 
+// The tensor maps of every slice's gate, up and down matrices: maps[3 sl + k]
+// = template k (gate / up share one) with the global address of expert
+// pe[slice_start[sl]]'s matrix.  Written once per call, so the grouped
+// kernels only acquire a map when an item starts (no per-item rewrite).
+__global__ void __launch_bounds__(256) tc_maps_kernel(const __grid_constant__ CUtensorMap t_gu,
+                                                      const __grid_constant__ CUtensorMap t_dn,
+                                                      const int32_t* __restrict__ slice_start,
+                                                      const int32_t* __restrict__ nslices, int max_slices,
+                                                      const int32_t* __restrict__ pe, const uint8_t* const* Wg,
+                                                      const uint8_t* const* Wu, const uint8_t* const* Wd, int E,
+                                                      CUtensorMap* __restrict__ maps) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int n = min(*nslices, max_slices);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 3 * n; i += gridDim.x * blockDim.x) {
+    const int sl = i / 3, k = i % 3;
+    int e = pe[slice_start[sl]];
+    if (e < 0 || e >= E) e = 0;  // flagged by the grouped kernel
+    const uint8_t* w = k == 0 ? Wg[e] : (k == 1 ? Wu[e] : Wd[e]);
+    const uint4* src = reinterpret_cast<const uint4*>(k == 2 ? &t_dn : &t_gu);
+    uint4* dst = reinterpret_cast<uint4*>(&maps[i]);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) dst[q] = src[q];
+    tc_tmap_set_addr_global(&maps[i], w);
+  }
+  tc_tmap_release();
+}
+
 // Operands of one launch of the grouped kernel.
 struct TcArgs {
   const uint8_t* const* W;   // expert matrices [R][C/32 blocks of 18 bytes]
@@ -484,8 +523,9 @@ struct TcArgs {
   const int32_t* nslices;
   const uint8_t* bimg;       // slice images (tc_image_kernel)
   const float* ximg;
-  CUtensorMap* gmaps;        // kTcStages global tensor-map slots per CTA
-  int box_rows;              // rows of the tensor map's box (min(128, R))
+  const CUtensorMap* maps;   // tensor maps of every slice's matrices (tc_maps_kernel): [slice][gate, up, down]
+  int map0;                  // 0: gate (+ up), 2: down
+  int box_rows;              // rows of the maps' box (min(128, R))
   int nvec;
   float* out;                // [out_rows][R]
   float* out2;               // for W2
@@ -494,7 +534,7 @@ struct TcArgs {
 };
 
 struct TcItem {
-  const uint8_t* w;
+  const CUtensorMap* map;
   float* dst;
   int tile, s0, ns, nv, unit;
 };
@@ -508,15 +548,14 @@ __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int
   it.ns = min(max(A.slice_len[sl], 1), kTcNvp);
   it.nv = it.ns > kTcUnit ? 2 * kTcUnit : kTcUnit;
   it.unit = A.slice_unit[sl];
-  int e = A.pe[it.s0];
-  if (e < 0 || e >= A.num_experts) e = 0;  // flagged at the item's end
-  it.w = mat ? A.W2[e] : A.W[e];
+  it.map = A.maps + 3 * sl + A.map0 + mat;
   it.dst = mat ? A.out2 : A.out;
   return it;
 }
 
 // Unpack (four warps, thread = tile row): raw row of ring slot `st` -> signed
-// codes q - 8 in core-matrix order (A buffer `ab`) and the row's block scales.
+// codes q - 8 in core-matrix order (A buffer `ab`) and the row's block scales
+// (beside the stage, so that the A buffer is free once the MMAs have read it).
 __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
   uint32_t w[kTcRawRow / 4];
   const uint8_t* src = sm.raw[st] + r * kTcRawRow;
@@ -550,17 +589,75 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
     uint8_t* dst = sm.a[ab] + ((r >> 3) * kTcKch + 2 * b) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(c[0], c[1], c[2], c[3]);
     *reinterpret_cast<uint4*>(dst + 128) = make_uint4(c[4], c[5], c[6], c[7]);
-    sm.d[ab][b][r] = f16_bits_to_f32(d16);
+    sm.d[st][b][r] = f16_bits_to_f32(d16);
   }
 }
 
 // The grouped contraction of Q4_0 matrices: out[slot_out[p]][r] = y[vector
 // slot_vec[p]][r] of expert pe[p]'s matrix for every pair p.  Needs C a
-// multiple of 256 and the slice images of this launch.  `tmpl`: a 2-D tensor
-// map over one matrix (inner dimension C/32*18 bytes, R rows, box 144 x 128)
-// whose global address is replaced per expert.
-__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A,
-                                                                      const __grid_constant__ CUtensorMap tmpl) {
+// multiple of 256, 16-byte aligned matrices and the slice images of this
+// launch.
+//
+// Roles and hand-offs (every wait bounded):
+//   producer   empty[st] -> raw tile (2-D TMA) + slice image + block scales -> full[st]
+//   unpack     full[st], a_empty[ab] -> codes a[ab], row scales d[st] -> a_full[ab], d_full[st], empty[st]
+//   MMA        a_full[ab], full[st]; per group t_empty[slot] -> 2 or 4 MMAs -> t_full[slot]; then a_empty[ab], empty[st]
+//   epilogue   full[st], d_full[st]; per group t_full[slot] -> tensor-memory loads -> t_empty[slot]; empty[st]
+// A code buffer is released by the MMAs alone, so the unpack of step s + 2
+// overlaps the epilogue of step s.  An MMA of this shape occupies the tensor
+// pipe for about 170 to 230 cycles whatever its N, and a wait + commit adds
+// about 140, so the MMA warp issues a group of blocks (4 of a 16-vector slice,
+// 2 of a 32-vector one) per wait and commit, into one of two tensor-memory
+// slots; it sets the pace.  Epilogue
+// warp (quarter q, set w) owns tile rows 32 q .. 32 q + 31 and vectors
+// w * nv/4 .. (w + 1) * nv/4 - 1 of every block, so its sums need no
+// exchange with other warps; a warp whose vectors are all past the slice's
+// length still waits and arrives, without loading.
+template <int NVW>
+__device__ __forceinline__ void tc_epi_load(uint32_t taddr, int nv, uint32_t (&r)[3][NVW]) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    if constexpr (NVW == 8)
+      tmem_ld8(taddr + k * nv, r[k]);
+    else
+      tmem_ld4(taddr + k * nv, r[k]);
+  }
+}
+template <int NVW>
+__device__ __forceinline__ void tc_epi_fold(const uint32_t (&r)[3][NVW], float dr, const float* xsv, float (&acc)[8]) {
+  float xv[NVW];
+#pragma unroll
+  for (int q = 0; q < NVW / 4; ++q) {
+    const float4 t = *reinterpret_cast<const float4*>(xsv + 4 * q);
+    xv[4 * q] = t.x, xv[4 * q + 1] = t.y, xv[4 * q + 2] = t.z, xv[4 * q + 3] = t.w;
+  }
+#pragma unroll
+  for (int u = 0; u < NVW; u += 2) {
+    const int S0 = static_cast<int>(r[0][u]) + static_cast<int>(r[1][u]) * 128 + static_cast<int>(r[2][u]) * 16384;
+    const int S1 =
+        static_cast<int>(r[0][u + 1]) + static_cast<int>(r[1][u + 1]) * 128 + static_cast<int>(r[2][u + 1]) * 16384;
+    const float2 sc = __fmul2_rn(make_float2(dr, dr), make_float2(xv[u], xv[u + 1]));
+    const float2 a = __ffma2_rn(make_float2(__int2float_rn(S0), __int2float_rn(S1)), sc, make_float2(acc[u], acc[u + 1]));
+    acc[u] = a.x, acc[u + 1] = a.y;
+  }
+}
+// One MMA group of an epilogue warp: tensor-memory loads of its GB blocks
+// (column stride BS), the slot released, then the folds.
+template <int NVW, int GB, int BS>
+__device__ __forceinline__ void tc_epi_group(uint32_t taddr, int nv, const float* dcol, const float* xsv,
+                                             uint64_t* t_empty, float (&acc)[8]) {
+  uint32_t r[GB][3][NVW];
+#pragma unroll
+  for (int b = 0; b < GB; ++b) tc_epi_load<NVW>(taddr + b * BS, nv, r[b]);
+  tmem_wait_ld();
+  tc_fence_before_sync();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(t_empty);
+#pragma unroll
+  for (int b = 0; b < GB; ++b) tc_epi_fold<NVW>(r[b], dcol[b * kTcRows], xsv + b * nv, acc);
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>(tc_smem_raw);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -569,6 +666,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     for (int i = 0; i < kTcStages; ++i) {
       mbar_init(&sm.full[i], kTcFullCount);
       mbar_init(&sm.empty[i], kTcEmptyCount);
+      mbar_init(&sm.d_full[i], kTcDFullCount);
     }
     for (int i = 0; i < kTcAbuf; ++i) {
       mbar_init(&sm.a_full[i], kTcAFullCount);
@@ -578,14 +676,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kTcTEmptyCount);
     }
-    mbar_init(&sm.x_full, kTcXFullCount);
-    mbar_init(&sm.x_empty, kTcXEmptyCount);
     sm.abort = 0u;
     fence_mbar_init();
-  }
-  if (tid < kTcStages * 8) {  // the tensor-map template into each stage's shared copy
-    const uint4* src = reinterpret_cast<const uint4*>(&tmpl);
-    reinterpret_cast<uint4*>(&sm.tmap[tid / 8])[tid % 8] = src[tid % 8];
   }
   if (warp == kTcMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
   __syncthreads();
@@ -602,64 +694,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
   auto item_at = [&](int s) { return tc_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
 
   if (warp == kTcProducerWarp) {
-    CUtensorMap* gmaps = A.gmaps + static_cast<size_t>(blockIdx.x) * kTcStages;
-    const uint8_t* map_addr[kTcStages] = {nullptr, nullptr, nullptr};
-    TcItem it{};
+    if (lane == 0) {
+      TcItem it{};
 #pragma unroll 1
-    for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kTcStages, chunk = s % nchunks;
-      if (chunk == 0) it = item_at(s);
-      bool ok = s < kTcStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort);
-      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
-      // the stage's tensor map follows the item's matrix (its last copy has landed: the stage is empty)
-      const uint8_t* cur = st == 0 ? map_addr[0] : (st == 1 ? map_addr[1] : map_addr[2]);
-      if (cur != it.w) {
-        if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
-        __syncwarp();
-        tc_tmap_publish(&gmaps[st], &sm.tmap[st]);
-        if (lane == 0) tc_tmap_acquire(&gmaps[st]);
-        if (st == 0) map_addr[0] = it.w;
-        else if (st == 1) map_addr[1] = it.w;
-        else map_addr[2] = it.w;
-      }
-      if (lane == 0) {
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kTcStages, chunk = s % nchunks;
+        if (chunk == 0) {
+          it = item_at(s);
+          tc_tmap_acquire(it.map);
+        }
+        if (s >= kTcStages && !tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort)) break;
         const int units = it.nv / kTcUnit;
         const uint32_t bbytes = units * kTcUnitBBytes, xbytes = units * kTcUnitXFloats * 4;
         const size_t uoff = static_cast<size_t>(it.unit) * nchunks + static_cast<size_t>(chunk) * units;
         mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kTcRawRow + bbytes + xbytes);
-        tc_tma_2d(sm.raw[st], &gmaps[st], chunk * kTcRawRow, it.tile * kTcRows, &sm.full[st]);
+        tc_tma_2d(sm.raw[st], it.map, chunk * kTcRawRow, it.tile * kTcRows, &sm.full[st]);
         tc_bulk(sm.b[st], A.bimg + uoff * kTcUnitBBytes, bbytes, &sm.full[st]);
         tc_bulk(sm.xs[st], A.ximg + uoff * kTcUnitXFloats, xbytes, &sm.full[st]);
       }
-      __syncwarp();
     }
   } else if (warp == kTcMmaWarp) {
     // the whole warp walks the steps (warp-uniform operands); one lane issues
     uint32_t idesc = 0;
+    int gb = 4, bstride = 64, G = 0;  // group size, block column stride, groups issued
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
       const int st = s % kTcStages, ab = s % kTcAbuf;
-      if (s % nchunks == 0) idesc = umma_idesc_s8s8(kTcRows, 3 * item_at(s).nv);
+      if (s % nchunks == 0) {
+        const int nv = item_at(s).nv;
+        idesc = umma_idesc_s8s8(kTcRows, 3 * nv);
+        gb = tc_group_blocks(nv);
+        bstride = tc_block_stride(nv);
+      }
+      // (the unpack threads fenced their code stores to the async proxy
+      // before arriving on a_full)
       if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort) ||
           !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort))
         break;
-      fence_async_shared();  // codes written by the unpack threads, read by the MMAs
       tc_fence_after_sync();
       bool ok = true;
 #pragma unroll 1
-      for (int g = 0; g < kTcKB / 2; ++g) {
-        const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
+      for (int j0 = 0; j0 < kTcKB; j0 += gb, ++G) {
+        const int slot = G % kTcSlots;
         if (G >= kTcSlots && !tc_spin_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err, &sm.abort)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
-#pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int j = 2 * g + jj;
+#pragma unroll 1
+        for (int jj = 0; jj < gb; ++jj) {
+          const int j = j0 + jj;
           const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
           const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
-          umma_i8(tmem + slot * kTcSlotCols + jj * kTcBlockCols, da, db, idesc, false);
+          umma_i8(tmem + slot * kTcSlotCols + jj * bstride, da, db, idesc, false);
         }
         umma_commit(&sm.t_full[slot]);
       }
@@ -678,102 +765,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       fence_async_shared();  // codes written here, read by the MMAs
       mbar_arrive(&sm.a_full[ab]);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[st]);
+      if (lane == 0) {
+        mbar_arrive(&sm.d_full[st]);
+        mbar_arrive(&sm.empty[st]);
+      }
     }
   } else {
     const int ew = warp - kTcEpiWarp0;
-    const int quarter = warp & 3;            // tensor-memory lanes 32*quarter ..
-    const int half = (ew >> 2) & 1;          // blocks of this parity
-    const int vh = ew >> 3;                  // vectors 16*vh .. 16*vh+15
+    const int quarter = warp & 3;  // tensor-memory lanes 32*quarter ..
+    const int vset = ew >> 2;      // vectors vset * nv/4 ..
     const int trow = 32 * quarter + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(32 * quarter) << 16;
-    float acc[kTcUnit];
+    float acc[8];
 #pragma unroll
-    for (int i = 0; i < kTcUnit; ++i) acc[i] = 0.0f;
-    int items_done = 0;
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
     TcItem it{};
+    int nvw = 4, v0 = 0, orow = -1, G = 0;
+    bool live = false;
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kTcStages, ab = s % kTcAbuf, chunk = s % nchunks;
-      if (chunk == 0) it = item_at(s);
-      const int nvg = (it.ns + 7) >> 3;
+      const int st = s % kTcStages, chunk = s % nchunks;
+      if (chunk == 0) {
+        it = item_at(s);
+        nvw = it.nv / 4;
+        v0 = vset * nvw;
+        live = v0 < it.ns;
+        // output row of this lane's vector (lane < nvw), read ahead of the stores
+        orow = -1;
+        if (live && lane < nvw && v0 + lane < it.ns) {
+          const int p = it.s0 + v0 + lane;
+          orow = A.slot_out ? A.slot_out[p] : p;
+        }
+      }
       // block scales (bulk copy) and row scales (unpack) of this step are read below
-      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort) && tc_wait(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort);
+      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort) &&
+                tc_wait(&sm.d_full[st], (s / kTcStages) & 1, A.err, &sm.abort);
+      const int gb = tc_group_blocks(it.nv);
 #pragma unroll 1
-      for (int g = 0; g < kTcKB / 2 && ok; ++g) {
-        const int G = (kTcKB / 2) * s + g, slot = G % kTcSlots;
+      for (int j = 0; j < kTcKB && ok; j += gb, ++G) {
+        const int slot = G % kTcSlots;
         if (!tc_wait(&sm.t_full[slot], (G / kTcSlots) & 1, A.err, &sm.abort)) {
           ok = false;
           break;
         }
         tc_fence_after_sync();
-        const int j = 2 * g + half;
-        const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + half * kTcBlockCols;
-        const float dr = sm.d[ab][j][trow];
-        const float* xsj = &sm.xs[st][j * it.nv];
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int vg = 2 * vh + h2;
-          if (vg < nvg) {
-            uint32_t r0[8], r1[8], r2[8];
-            tmem_ld8(taddr + 8 * vg, r0);
-            tmem_ld8(taddr + it.nv + 8 * vg, r1);
-            tmem_ld8(taddr + 2 * it.nv + 8 * vg, r2);
-            tmem_wait_ld();
-            const float4 xa = *reinterpret_cast<const float4*>(xsj + 8 * vg);
-            const float4 xb = *reinterpret_cast<const float4*>(xsj + 8 * vg + 4);
-            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int S = static_cast<int>(r0[u]) + static_cast<int>(r1[u]) * 128 + static_cast<int>(r2[u]) * 16384;
-              acc[8 * h2 + u] = fmaf(__int2float_rn(S), dr * xv[u], acc[8 * h2 + u]);
-            }
-          }
+        if (live) {
+          const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + v0;
+          const float* dcol = &sm.d[st][j][trow];
+          const float* xsv = &sm.xs[st][j * it.nv + v0];
+          if (nvw == 8)
+            tc_epi_group<8, 2, 128>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+          else
+            tc_epi_group<4, 4, 64>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+        } else {
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.t_empty[slot]);
         }
-        tc_fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.t_empty[slot]);
       }
       if (!ok) break;
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&sm.a_empty[ab]);
-        mbar_arrive(&sm.empty[st]);
-      }
+      if (lane == 0) mbar_arrive(&sm.empty[st]);
       if (chunk == nchunks - 1) {
-        // odd-block partial sums through shared memory, then one store per live pair
-        if (half == 1) {
-          if (items_done > 0 && !tc_wait(&sm.x_empty, (items_done - 1) & 1, A.err, &sm.abort)) break;
+        const int grow = it.tile * kTcRows + trow;
+        if (live) {
 #pragma unroll
-          for (int i = 0; i < kTcUnit; ++i) sm.xchg[kTcUnit * vh + i][trow] = acc[i];
-          mbar_arrive(&sm.x_full);
-        } else {
-          if (!tc_wait(&sm.x_full, items_done & 1, A.err, &sm.abort)) break;
-          const int grow = it.tile * kTcRows + trow;
-#pragma unroll
-          for (int i = 0; i < kTcUnit; ++i) {
-            const int vi = kTcUnit * vh + i;
-            if (vi < it.ns) {
-              const int p = it.s0 + vi;
-              const int o = A.slot_out ? A.slot_out[p] : p;
-              if (o >= 0 && o < A.out_rows && grow < A.R)
-                it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i] + sm.xchg[vi][trow];
-            }
+          for (int i = 0; i < 8; ++i) {
+            const int o = __shfl_sync(0xFFFFFFFFu, orow, i);
+            if (i < nvw && v0 + i < it.ns && o >= 0 && o < A.out_rows && grow < A.R)
+              it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i];
           }
-          if (ew == 0 && lane < it.ns) {
-            const int p = it.s0 + lane;
-            const int o = A.slot_out ? A.slot_out[p] : p;
-            const int v = A.slot_vec ? A.slot_vec[p] : p;
-            const int e = A.pe[p];
-            if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) && A.err)
-              atomicOr(A.err, kErrBadExpertId);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.x_empty);
+        }
+        if (ew == 0 && lane < it.ns) {
+          const int p = it.s0 + lane;
+          const int o = A.slot_out ? A.slot_out[p] : p;
+          const int v = A.slot_vec ? A.slot_vec[p] : p;
+          const int e = A.pe[p];
+          if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) && A.err)
+            atomicOr(A.err, kErrBadExpertId);
         }
 #pragma unroll
-        for (int i = 0; i < kTcUnit; ++i) acc[i] = 0.0f;
-        ++items_done;
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
       }
     }
   }
@@ -1137,7 +1209,7 @@ namespace {
 
 struct TcLayout {
   size_t planes_x, xsc_x, wflag_x, wflag_a, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit,
-      nslices, bimg, ximg, gmaps, total;
+      nslices, bimg, ximg, maps, total;
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -1172,7 +1244,7 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   L.nslices = take(4);
   L.bimg = take(units * nchunks * dev::kTcUnitBBytes);
   L.ximg = take(units * nchunks * dev::kTcUnitXFloats * 4);
-  L.gmaps = take(2 * static_cast<size_t>(sm_count) * dev::kTcStages * sizeof(CUtensorMap));
+  L.maps = take(3 * units * sizeof(CUtensorMap));  // slices <= units
   L.total = off;
   return L;
 }
@@ -1280,7 +1352,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
   uint8_t* bimg = sc + L.bimg;
   float* ximg = reinterpret_cast<float*>(sc + L.ximg);
-  CUtensorMap* gmaps = reinterpret_cast<CUtensorMap*>(sc + L.gmaps);
+  CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(sc + L.maps);
   const int P = static_cast<int>(num_pairs), T = static_cast<int>(num_tokens);
   const int H = static_cast<int>(l->hidden), I = static_cast<int>(l->intermediate), O = static_cast<int>(l->out_dim);
   auto warp_grid = [&](int nvec, int C) {
@@ -1291,6 +1363,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   CUtensorMap tm_gu, tm_dn;
   OBJB_TRY(tc_encode_tiled(&tm_gu, scratch, row_gu, static_cast<size_t>(I), std::min(dev::kTcRows, I)));
   OBJB_TRY(tc_encode_tiled(&tm_dn, scratch, row_dn, static_cast<size_t>(O), std::min(dev::kTcRows, O)));
+  const int max_slices = static_cast<int>(tc_max_units(num_pairs, l->num_experts));
   const size_t smem = sizeof(dev::TcSmem);
   OBJB_TRY(ensure_smem_attr(dev::tc_q4_grouped_kernel, device, smem));
   const int img_grid = 2 * props.sm_count;
@@ -1298,6 +1371,11 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
                       static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
+  OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
+                      static_cast<const int32_t*>(slice_start), static_cast<const int32_t*>(nslices), max_slices, pe,
+                      reinterpret_cast<const uint8_t* const*>(l->d_gate),
+                      reinterpret_cast<const uint8_t* const*>(l->d_up),
+                      reinterpret_cast<const uint8_t* const*>(l->d_down), static_cast<int>(l->num_experts), maps));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
                       static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x, wflag_x));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
@@ -1310,7 +1388,6 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.num_experts = static_cast<int>(l->num_experts);
   a.R = I;
   a.C = H;
-  a.box_rows = std::min(dev::kTcRows, I);
   a.pe = pe;
   a.slot_vec = pt;
   a.slot_out = nullptr;
@@ -1320,13 +1397,15 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.nslices = nslices;
   a.bimg = bimg;
   a.ximg = ximg;
-  a.gmaps = gmaps;
+  a.maps = maps;
+  a.map0 = 0;
+  a.box_rows = std::min(dev::kTcRows, I);
   a.nvec = T;
   a.out = g;
   a.out2 = u;
   a.out_rows = P;
   a.err = err;
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_gu));
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, g,
                       static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a, wflag_a, pe, pt, T, x, H,
                       static_cast<const uint8_t*>(wflag_x), a.W, a.W2, a.num_experts));
@@ -1338,6 +1417,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.W2 = nullptr;
   a.R = O;
   a.C = I;
+  a.map0 = 2;
   a.box_rows = std::min(dev::kTcRows, O);
   a.slot_vec = nullptr;
   a.slot_out = po;
@@ -1345,8 +1425,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out = v;
   a.out2 = nullptr;
   a.out_rows = static_cast<int>(v_rows);
-  a.gmaps = gmaps + static_cast<size_t>(props.sm_count) * dev::kTcStages;
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a, tm_dn));
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, std::max(O, 32)), 256, 0, stream,
                       static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a), pe, po,
                       static_cast<int>(v_rows), a.W, a.num_experts, static_cast<const int32_t*>(nslices), v));
