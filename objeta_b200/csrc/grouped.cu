@@ -196,9 +196,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_s8s8(int m, int n) {
 // 2^(E-20) (NaN when the block is not finite).  A wide block (block_is_wide:
 // its largest value dwarfs the others) gets zero digits, so the MMAs
 // add nothing for it, and wflag[v * C/32 + b] = 1: its terms are added in
-// fp32 by tc_add_wide_rows (gate / up) and tc_wide_down_kernel (down).
-__device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc,
-                                                uint8_t* wflag) {
+// fp32 by tc_add_wide_rows (gate / up) and tc_wide_down_kernel (down), and
+// wany[v] = 1 (zeroed by tc_slices_kernel).  Returns whether it is wide.
+__device__ __forceinline__ bool tc_block_digits(float xe, int v, int b, int C, int8_t* planes, float* xsc,
+                                                uint8_t* wflag, uint8_t* wany) {
   const int lane = threadIdx.x & 31, nb = C / 32;
   float m = fabsf(xe);
 #pragma unroll
@@ -222,14 +223,17 @@ __device__ __forceinline__ void tc_block_digits(float xe, int v, int b, int C, i
   if (lane == 0) {
     xsc[static_cast<size_t>(v) * nb + b] = isfinite(m) ? ldexpf(1.0f, E - 20) : __int_as_float(0x7FC00000);
     wflag[static_cast<size_t>(v) * nb + b] = wide ? 1 : 0;
+    if (wide) wany[v] = 1;
   }
+  return wide;
 }
 
 // Digit planes of `nvec` vectors (rows of x, x_stride apart); one warp per
 // (vector, block).
 __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict__ x, size_t x_stride, int nvec,
                                                         const int32_t* count, int C, int8_t* __restrict__ planes,
-                                                        float* __restrict__ xsc, uint8_t* __restrict__ wflag) {
+                                                        float* __restrict__ xsc, uint8_t* __restrict__ wflag,
+                                                        uint8_t* __restrict__ wany) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (count) nvec = min(max(*count, 0), nvec);
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(256) tc_planes_kernel(const float* __restrict_
   const int warps = (gridDim.x * blockDim.x) >> 5;
   for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < nvec * nb; wi += warps) {
     const int v = wi / nb, b = wi % nb;
-    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, planes, xsc, wflag);
+    tc_block_digits(x[static_cast<size_t>(v) * x_stride + b * 32 + lane], v, b, C, planes, xsc, wflag, wany);
   }
 }
 
@@ -276,14 +280,18 @@ __device__ __forceinline__ float tc_add_wide_rows(float acc, const uint8_t* __re
 // act = SwiGLU(g, u) of every pair (rows of I floats) straight into digit
 // planes; one warp per (pair, block).  First the gate / up rows get the fp32
 // terms of their token's wide blocks (the grouped launch added nothing for
-// them); act is also stored over g, for the down rows' wide-block terms.
+// them; a token with none, wany_x[t] == 0, costs one byte read); an
+// activation block that is itself wide is also stored over g, for the down
+// rows' wide-block terms.
 __global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(float* __restrict__ g,
                                                                const float* __restrict__ u, int P,
                                                                const int32_t* count, int I, float limit,
                                                                int8_t* __restrict__ planes, float* __restrict__ xsc,
-                                                               uint8_t* __restrict__ wflag_a, const int32_t* pe,
+                                                               uint8_t* __restrict__ wflag_a,
+                                                               uint8_t* __restrict__ wany_a, const int32_t* pe,
                                                                const int32_t* pt, int T, const float* __restrict__ x,
                                                                int H, const uint8_t* __restrict__ wflag_x,
+                                                               const uint8_t* __restrict__ wany_x,
                                                                const uint8_t* const* gate_w,
                                                                const uint8_t* const* up_w, int num_experts) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -302,48 +310,50 @@ __global__ void __launch_bounds__(256) tc_swiglu_planes_kernel(float* __restrict
       t = 0;
       e = 0;
     }
-    const uint8_t* wf = wflag_x + static_cast<size_t>(t) * nbh;
-    const float* xv = x + static_cast<size_t>(t) * H;
-    const size_t roff = static_cast<size_t>(b * 32 + lane) * row_bytes;
-    gv = tc_add_wide_rows(gv, gate_w[e] + roff, xv, wf, nbh, ok);
-    uv = tc_add_wide_rows(uv, up_w[e] + roff, xv, wf, nbh, ok);
+    if (ok && wany_x[t]) {
+      const uint8_t* wf = wflag_x + static_cast<size_t>(t) * nbh;
+      const float* xv = x + static_cast<size_t>(t) * H;
+      const size_t roff = static_cast<size_t>(b * 32 + lane) * row_bytes;
+      gv = tc_add_wide_rows(gv, gate_w[e] + roff, xv, wf, nbh, true);
+      uv = tc_add_wide_rows(uv, up_w[e] + roff, xv, wf, nbh, true);
+    }
     const float a = swiglu(gv, uv, limit);
-    g[i] = a;
-    tc_block_digits(a, p, b, I, planes, xsc, wflag_a);
+    if (tc_block_digits(a, p, b, I, planes, xsc, wflag_a, wany_a)) g[i] = a;
   }
 }
 
 // The down rows' terms of the activations' wide blocks: v[slot(p)][r] +=
-// sum over the wide blocks of pair p's activation (act rows of I floats) of
-// ((q - 8) * scale) * act.  One warp per (pair, 32 output rows); a pair with
-// no wide block costs one flag read.
+// sum over the wide blocks of pair p's activation (act rows of I floats; the
+// wide blocks' values were stored there) of ((q - 8) * scale) * act.  One
+// warp per pair; a pair with no wide block (wany_a[p] == 0) costs one byte
+// read, one with some walks every 32 output rows.
 __global__ void __launch_bounds__(256) tc_wide_down_kernel(const float* __restrict__ act, int P, const int32_t* count,
                                                            int I, int O, const uint8_t* __restrict__ wflag_a,
-                                                           const int32_t* pe, const int32_t* po, int v_rows,
+                                                           const uint8_t* __restrict__ wany_a, const int32_t* pe,
+                                                           const int32_t* po, int v_rows,
                                                            const uint8_t* const* down_w, int num_experts,
                                                            const int32_t* nslices, float* __restrict__ v) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (*nslices <= 0) return;  // the launch ran nothing (a pair list not grouped by expert): v stays as it was
   if (count) P = min(max(*count, 0), P);
-  const int nb = I / 32, nrb = (O + 31) / 32, lane = threadIdx.x & 31;
+  const int nb = I / 32, lane = threadIdx.x & 31;
   const size_t row_bytes = static_cast<size_t>(nb) * 18;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int wi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; wi < P * nrb; wi += warps) {
-    const int p = wi / nrb, rb = wi % nrb;
-    const uint8_t* wf = wflag_a + static_cast<size_t>(p) * nb;
-    bool any = false;
-    for (int b0 = 0; b0 < nb; b0 += 32) any |= __any_sync(0xFFFFFFFFu, b0 + lane < nb && wf[b0 + lane] != 0);
-    if (!any) continue;
+  for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < P; p += warps) {
+    if (!wany_a[p]) continue;
     const int e = pe[p], o = po ? po[p] : p;
     if (e < 0 || e >= num_experts || o < 0 || o >= v_rows) continue;  // flagged by the grouped launch
-    const int r = rb * 32 + lane;
-    const bool live = r < O;
-    const size_t roff = static_cast<size_t>(live ? r : 0) * row_bytes;
-    const float add = tc_add_wide_rows(0.0f, down_w[e] + roff, act + static_cast<size_t>(p) * I, wf, nb, live);
-    if (live) {
-      float* dst = v + static_cast<size_t>(o) * O + r;
-      *dst = __fadd_rn(*dst, add);
+    const uint8_t* wf = wflag_a + static_cast<size_t>(p) * nb;
+    for (int r0 = 0; r0 < O; r0 += 32) {
+      const int r = r0 + lane;
+      const bool live = r < O;
+      const size_t roff = static_cast<size_t>(live ? r : 0) * row_bytes;
+      const float add = tc_add_wide_rows(0.0f, down_w[e] + roff, act + static_cast<size_t>(p) * I, wf, nb, live);
+      if (live) {
+        float* dst = v + static_cast<size_t>(o) * O + r;
+        *dst = __fadd_rn(*dst, add);
+      }
     }
   }
 }
@@ -383,9 +393,15 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
                                                          int32_t* __restrict__ slice_len,
                                                          int32_t* __restrict__ slice_unit,
                                                          int32_t* __restrict__ nslices, int unit_cap,
-                                                         unsigned* err) {
+                                                         unsigned* err, uint8_t* __restrict__ wany_x, int T,
+                                                         uint8_t* __restrict__ wany_a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ int warp_tot[32];
+  // the any-wide bytes of this call start clear (the planes kernels set them)
+  if (wany_x)
+    for (int i = threadIdx.x; i < T; i += blockDim.x) wany_x[i] = 0;
+  if (wany_a)
+    for (int i = threadIdx.x; i < P; i += blockDim.x) wany_a[i] = 0;
   if (count) P = min(max(*count, 0), P);
   const int nt = blockDim.x, tid = threadIdx.x;
   // 1. run starts
@@ -447,6 +463,8 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
                                                        uint8_t* __restrict__ bimg, float* __restrict__ ximg) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int kImgRow = kTcKB * 32 + 16;
+  __shared__ __align__(16) uint8_t rows[kTcNp * kImgRow];
   const int nchunks = C / (kTcKB * 32), nb = C / 32;
   const int total = *nslices * nchunks;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
@@ -455,18 +473,28 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
     const int nv = ns > kTcUnit ? 2 * kTcUnit : kTcUnit, units = nv / kTcUnit;
     const size_t uoff = static_cast<size_t>(slice_unit[sl]) * nchunks + static_cast<size_t>(c) * units;
     uint8_t* bdst = bimg + uoff * kTcUnitBBytes;
+    // rows gathered with 256-byte coalesced reads into shared memory (rows
+    // 272 bytes apart: the core-matrix reads below hit distinct banks), then
+    // written out in core-matrix order with coalesced stores
     for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
-      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
-      const int brow = 8 * (cm / kTcKch) + r, p = cm % kTcKch;
+      const int brow = q / kTcKch, pc = q % kTcKch;
       const int k = brow / nv, i = brow % nv;
       uint4 val = make_uint4(0u, 0u, 0u, 0u);
       if (i < ns) {
         int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
         v = (v < 0 || v >= nvec) ? 0 : v;
-        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + p * 16);
+        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + pc * 16);
       }
-      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) = val;
+      *reinterpret_cast<uint4*>(rows + brow * kImgRow + pc * 16) = val;
     }
+    __syncthreads();
+    for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
+      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
+      const int brow = 8 * (cm / kTcKch) + r, pc = cm % kTcKch;
+      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) =
+          *reinterpret_cast<const uint4*>(rows + brow * kImgRow + pc * 16);
+    }
+    __syncthreads();
     float* xdst = ximg + uoff * kTcUnitXFloats;
     for (int q = threadIdx.x; q < kTcKB * nv; q += blockDim.x) {
       const int j = q / nv, i = q % nv;
@@ -1208,7 +1236,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
 namespace {
 
 struct TcLayout {
-  size_t planes_x, xsc_x, wflag_x, wflag_a, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit,
+  size_t planes_x, xsc_x, wflag_x, wflag_a, wany_x, wany_a, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit,
       nslices, bimg, ximg, maps, total;
 };
 
@@ -1233,6 +1261,8 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   L.xsc_x = take(T * (H / 32) * 4);
   L.wflag_x = take(T * (H / 32));
   L.wflag_a = take(P * (I / 32));
+  L.wany_x = take(T);
+  L.wany_a = take(P);
   L.g = take(P * I * 4);
   L.u = take(P * I * 4);
   L.planes_a = take(P * 3 * I);
@@ -1341,6 +1371,8 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   float* xsc_x = reinterpret_cast<float*>(sc + L.xsc_x);
   uint8_t* wflag_x = sc + L.wflag_x;
   uint8_t* wflag_a = sc + L.wflag_a;
+  uint8_t* wany_x = sc + L.wany_x;
+  uint8_t* wany_a = sc + L.wany_a;
   float* g = reinterpret_cast<float*>(sc + L.g);
   float* u = reinterpret_cast<float*>(sc + L.u);
   int8_t* planes_a = reinterpret_cast<int8_t*>(sc + L.planes_a);
@@ -1370,14 +1402,14 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
 
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
-                      static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err));
+                      static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err, wany_x, T, wany_a));
   OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
                       static_cast<const int32_t*>(slice_start), static_cast<const int32_t*>(nslices), max_slices, pe,
                       reinterpret_cast<const uint8_t* const*>(l->d_gate),
                       reinterpret_cast<const uint8_t* const*>(l->d_up),
                       reinterpret_cast<const uint8_t* const*>(l->d_down), static_cast<int>(l->num_experts), maps));
   OBJB_TRY(launch_pdl(dev::tc_planes_kernel, warp_grid(T, H), 256, 0, stream, x, static_cast<size_t>(H), T,
-                      static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x, wflag_x));
+                      static_cast<const int32_t*>(nullptr), H, planes_x, xsc_x, wflag_x, wany_x));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_x),
@@ -1407,8 +1439,9 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.err = err;
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, g,
-                      static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a, wflag_a, pe, pt, T, x, H,
-                      static_cast<const uint8_t*>(wflag_x), a.W, a.W2, a.num_experts));
+                      static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a, wflag_a, wany_a, pe, pt, T,
+                      x, H, static_cast<const uint8_t*>(wflag_x), static_cast<const uint8_t*>(wany_x), a.W, a.W2,
+                      a.num_experts));
   OBJB_TRY(launch_pdl(dev::tc_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const int8_t*>(planes_a),
@@ -1426,8 +1459,9 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out2 = nullptr;
   a.out_rows = static_cast<int>(v_rows);
   OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
-  OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, std::max(O, 32)), 256, 0, stream,
-                      static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a), pe, po,
+  OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, 32), 256, 0, stream,
+                      static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a),
+                      static_cast<const uint8_t*>(wany_a), pe, po,
                       static_cast<int>(v_rows), a.W, a.num_experts, static_cast<const int32_t*>(nslices), v));
   return OBJB_OK;
 }
@@ -1557,7 +1591,7 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   OBJB_TRY(act_quant(x, num_tokens, l->hidden, codes_x, scales_x, stream, "act_quant hidden"));
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kMxNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
-                      static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err));
+                      static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err, static_cast<uint8_t*>(nullptr), 0, static_cast<uint8_t*>(nullptr)));
   OBJB_TRY(launch_pdl(dev::mx_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const uint8_t*>(codes_x),
