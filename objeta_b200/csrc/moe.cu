@@ -568,10 +568,8 @@ int router_topk_batched(const float* logits, size_t num_tokens, size_t n, size_t
                      "need 1 <= num_tokens <= 65535 and 1 <= top_k <= num_experts <= 8192 (got top_k " +
                          std::to_string(top_k) + ", num_experts " + std::to_string(n) + ")");
   const int threads = static_cast<int>(std::min<size_t>(1024, (n + 31) / 32 * 32));
-  dev::router_topk_kernel<<<static_cast<unsigned>(num_tokens), threads, n * sizeof(float), stream>>>(
-      logits, static_cast<int>(n), static_cast<int>(top_k), renorm, ids, weights);
-  OBJB_CUDA(cudaGetLastError(), "launch batched router kernel");
-  return OBJB_OK;
+  return launch_pdl(dev::router_topk_kernel, static_cast<int>(num_tokens), threads, n * sizeof(float), stream, logits,
+                    static_cast<int>(n), static_cast<int>(top_k), renorm, ids, weights);
 }
 
 // ---- official DeepSeek routed experts (execute_selected_moe_official_routed_fp4_cuda,
@@ -705,10 +703,8 @@ int router_topk(const float* logits, size_t n, size_t top_k, int renorm, int32_t
                      "need 1 <= top_k <= num_experts <= 8192 (got top_k " + std::to_string(top_k) +
                          ", num_experts " + std::to_string(n) + ")");
   const int threads = static_cast<int>(std::min<size_t>(1024, (n + 31) / 32 * 32));
-  dev::router_topk_kernel<<<1, threads, n * sizeof(float), stream>>>(logits, static_cast<int>(n),
-                                                                     static_cast<int>(top_k), renorm, ids, weights);
-  OBJB_CUDA(cudaGetLastError(), "launch router kernel");
-  return OBJB_OK;
+  return launch_pdl(dev::router_topk_kernel, 1, threads, n * sizeof(float), stream, logits, static_cast<int>(n),
+                    static_cast<int>(top_k), renorm, ids, weights);
 }
 
 }  // namespace objb

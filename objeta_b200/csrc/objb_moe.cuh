@@ -333,6 +333,11 @@ struct FfnDownProg {
 static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int n, int top_k,
                                                            int renorm, int32_t* __restrict__ ids,
                                                            float* __restrict__ weights) {
+  // Launched with programmatic serialization: the next kernel may start its
+  // prologue now; this one waits for the preceding grid (which may write the
+  // logits, or still read ids / weights) before touching memory.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // CTA b routes token b (logits row b, ids / weights row b).
   logits += static_cast<size_t>(blockIdx.x) * n;
   ids += static_cast<size_t>(blockIdx.x) * top_k;
@@ -377,8 +382,15 @@ static __global__ void __launch_bounds__(1024) router_topk_kernel(const float* _
   __syncthreads();
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
     const float pe = sp[e];
-    int rank = 0;
-    for (int j = 0; j < n; ++j) {
+    int rank = 0, j = 0;
+    for (; j + 4 <= n; j += 4) {  // four probabilities per shared load
+      const float4 q = *reinterpret_cast<const float4*>(sp + j);
+      rank += (q.x > pe) || (q.x == pe && j < e);
+      rank += (q.y > pe) || (q.y == pe && j + 1 < e);
+      rank += (q.z > pe) || (q.z == pe && j + 2 < e);
+      rank += (q.w > pe) || (q.w == pe && j + 3 < e);
+    }
+    for (; j < n; ++j) {
       const float pj = sp[j];
       rank += (pj > pe) || (pj == pe && j < e);
     }
