@@ -463,8 +463,6 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
                                                        uint8_t* __restrict__ bimg, float* __restrict__ ximg) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  constexpr int kImgRow = kTcKB * 32 + 16;
-  __shared__ __align__(16) uint8_t rows[kTcNp * kImgRow];
   const int nchunks = C / (kTcKB * 32), nb = C / 32;
   const int total = *nslices * nchunks;
   for (int w = blockIdx.x; w < total; w += gridDim.x) {
@@ -473,28 +471,18 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
     const int nv = ns > kTcUnit ? 2 * kTcUnit : kTcUnit, units = nv / kTcUnit;
     const size_t uoff = static_cast<size_t>(slice_unit[sl]) * nchunks + static_cast<size_t>(c) * units;
     uint8_t* bdst = bimg + uoff * kTcUnitBBytes;
-    // rows gathered with 256-byte coalesced reads into shared memory (rows
-    // 272 bytes apart: the core-matrix reads below hit distinct banks), then
-    // written out in core-matrix order with coalesced stores
     for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
-      const int brow = q / kTcKch, pc = q % kTcKch;
+      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
+      const int brow = 8 * (cm / kTcKch) + r, p = cm % kTcKch;
       const int k = brow / nv, i = brow % nv;
       uint4 val = make_uint4(0u, 0u, 0u, 0u);
       if (i < ns) {
         int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
         v = (v < 0 || v >= nvec) ? 0 : v;
-        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + pc * 16);
+        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + p * 16);
       }
-      *reinterpret_cast<uint4*>(rows + brow * kImgRow + pc * 16) = val;
+      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) = val;
     }
-    __syncthreads();
-    for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
-      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
-      const int brow = 8 * (cm / kTcKch) + r, pc = cm % kTcKch;
-      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) =
-          *reinterpret_cast<const uint4*>(rows + brow * kImgRow + pc * 16);
-    }
-    __syncthreads();
     float* xdst = ximg + uoff * kTcUnitXFloats;
     for (int q = threadIdx.x; q < kTcKB * nv; q += blockDim.x) {
       const int j = q / nv, i = q % nv;
