@@ -434,7 +434,9 @@ int moe_scratch_bytes(const objb_moe_layer* l, size_t top_k, size_t* out) {
   size_t need = 0;
   auto calc = [&](auto tag) {
     using RD = decltype(tag);
-    MoePlan<RD> p = plan_moe<RD>(s, l->fmt, split, true);
+    // planned as moe_selected plans it: an unaligned layer runs the generic
+    // path, which needs only the activations
+    MoePlan<RD> p = plan_moe<RD>(s, l->fmt, split, (l->flags & OBJB_MOE_UNALIGNED) == 0);
     need = p.fast ? p.act_bytes + (p.imgx_quads + p.imga_quads * s.K) * 16 + 256 : p.act_bytes;
   };
   if (split) calc(dev::RowDotSplitFp4Digit{});

@@ -119,3 +119,70 @@ def test_noalloc_device_error_poisons_output_then_recovers(cuda_device):
     torch.cuda.synchronize()
     assert not torch.isnan(out).any()
     assert torch.equal(out, ref)
+
+
+def _q4_layer_offset(hidden, inter, out_dim, num_experts, seed, offset):
+    """A Q4_0 layer whose expert tensors start `offset` bytes into their
+    allocations (offset % 16 != 0 marks the layer unaligned: generic path)."""
+    import torch
+    from objeta_b200 import QGemvShape, QuantBackend, QuantFormat
+    from objeta_b200.moe import MoeLayer
+    qb = QuantBackend(torch.cuda.current_device())
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    mats = {"gate": [], "up": [], "down": []}
+    for _ in range(num_experts):
+        for name, (r, c) in (("gate", (inter, hidden)), ("up", (inter, hidden)), ("down", (out_dim, inter))):
+            m = torch.randn(r, c, device="cuda", generator=g) * 0.02
+            q = qb.quantize_matrix_device(QuantFormat.Q4_0, m, QGemvShape.new(QuantFormat.Q4_0, r, c))
+            buf = torch.zeros(q.numel() + offset, dtype=torch.uint8, device="cuda")
+            buf[offset:].copy_(q)
+            mats[name].append(buf[offset:])
+    return MoeLayer(QuantFormat.Q4_0, hidden, inter, out_dim, mats["gate"], mats["up"], mats["down"])
+
+
+def test_noalloc_unaligned_offset_x_and_side_stream(cuda_device):
+    """The generic (unaligned) path, an x that is not 16-byte aligned (the x
+    image launch) and a side stream: each bit-identical to the regular entry
+    point on the same inputs, which runs the same kernels with other scratch."""
+    import torch
+    hidden, inter, out_dim, E = 1024, 1024, 512, 6
+    sel = torch.tensor([4, 1, 5], dtype=torch.int32, device="cuda")
+    w = torch.tensor([0.5, 0.3, 0.2], device="cuda")
+    x_store = torch.randn(hidden + 1, device="cuda")
+    x_off = x_store[1:]  # data_ptr + 4: not 16-byte aligned
+    aligned, _ = _q4_layer(hidden, inter, out_dim, E, seed=41)
+    unaligned = _q4_layer_offset(hidden, inter, out_dim, E, seed=41, offset=2)
+    assert unaligned._c.flags & 1
+    side = torch.cuda.Stream()
+    for layer, x in ((unaligned, x_store[:hidden]), (aligned, x_off), (unaligned, x_off)):
+        for s in (torch.cuda.current_stream(), side):
+            got = torch.full((out_dim,), float("nan"), device="cuda")
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                ref = layer.forward_selected(sel, w, x, stream=s)
+                layer.forward_selected_noalloc(sel, w, x, got, stream=s)
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref)
+
+
+def test_noalloc_sizes_unaligned_layers_by_their_own_path(cuda_device):
+    """An unaligned layer runs the generic path, which needs only the
+    activations: one whose aligned (fast-path) plan would not fit the fixed
+    array is still accepted."""
+    import torch
+    from objeta_b200._lib import CudaError
+    hidden, inter, out_dim, E, K = 256, 30720, 256, 24, 24
+    ids = torch.arange(K, dtype=torch.int32, device="cuda")
+    w = torch.full((K,), 1.0 / K, device="cuda")
+    x = torch.randn(hidden, device="cuda")
+    aligned, _ = _q4_layer(hidden, inter, out_dim, E, seed=5)
+    assert aligned.scratch_bytes(K) > (4 << 20) - 256
+    with pytest.raises(CudaError):
+        aligned.forward_selected_noalloc(ids, w, x, torch.zeros(out_dim, device="cuda"))
+    unaligned = _q4_layer_offset(hidden, inter, out_dim, E, seed=5, offset=2)
+    assert unaligned.scratch_bytes(K) <= (4 << 20) - 256
+    got = torch.full((out_dim,), float("nan"), device="cuda")
+    unaligned.forward_selected_noalloc(ids, w, x, got)
+    ref = unaligned.forward_selected(ids, w, x)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
