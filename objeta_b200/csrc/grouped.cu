@@ -114,21 +114,6 @@ __device__ __forceinline__ void tc_tma_2d(void* smem_dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
 }
-// Tensor map in shared memory: new global address.
-__device__ __forceinline__ void tc_tmap_set_addr(CUtensorMap* smem_map, const void* addr) {
-  asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(smem_addr(smem_map)),
-               "l"(reinterpret_cast<uint64_t>(addr))
-               : "memory");
-}
-// Copies a tensor map from shared to global memory with a release fence of
-// the tensor-map proxy (whole warp).
-__device__ __forceinline__ void tc_tmap_publish(CUtensorMap* gmem_map, const CUtensorMap* smem_map) {
-  asm volatile(
-      "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::"l"(
-          reinterpret_cast<uint64_t>(gmem_map)),
-      "r"(smem_addr(smem_map))
-      : "memory");
-}
 // Tensor map in global memory: new global address (generic proxy), and the
 // release fence that makes such writes visible to the tensor-map proxy.
 __device__ __forceinline__ void tc_tmap_set_addr_global(CUtensorMap* gmem_map, const void* addr) {
@@ -907,7 +892,6 @@ struct MxSmem {
   alignas(128) uint8_t raw[kMxStages][kTcRows * kMxRawRow];
   alignas(128) uint8_t sfa[kMxAbuf][kMxSfAtom];
   alignas(128) uint8_t sfb[kMxStages][kMxSfAtom];
-  alignas(128) CUtensorMap tmap[kMxStages];
   alignas(8) uint64_t full[kMxStages], empty[kMxStages], a_full[kMxAbuf], a_empty[kMxAbuf];
   uint64_t d_full[kMxDslots], d_empty[kMxDslots];
   uint32_t tmem_base;
@@ -1011,7 +995,8 @@ struct MxArgs {
   const int32_t* nslices;
   const uint8_t* bimg;
   const uint8_t* sfimg;
-  CUtensorMap* gmaps;
+  const CUtensorMap* maps;   // tensor maps of every slice's weight matrices (tc_maps_kernel): [slice][gate, up, down]
+  int map0;                  // 0: gate (+ up), 2: down
   int box_rows;
   int nvec;
   float* out;
@@ -1021,7 +1006,7 @@ struct MxArgs {
 };
 
 struct MxItem {
-  const uint8_t* w;
+  const CUtensorMap* map;
   const uint8_t* ws;
   float* dst;
   int tile, s0, ns, units, unit, sl;
@@ -1038,14 +1023,13 @@ __device__ __forceinline__ MxItem mx_item(const MxArgs& A, int w, int tiles, int
   it.unit = A.slice_unit[it.sl];
   int e = A.pe[it.s0];
   if (e < 0 || e >= A.num_experts) e = 0;  // flagged by the epilogue
-  it.w = mat ? A.W2[e] : A.W[e];
+  it.map = A.maps + 3 * it.sl + A.map0 + mat;
   it.ws = mat ? A.WS2[e] : A.WS[e];
   it.dst = mat ? A.out2 : A.out;
   return it;
 }
 
-__global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs A,
-                                                                   const __grid_constant__ CUtensorMap tmpl) {
+__global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs A) {
   extern __shared__ __align__(1024) uint8_t mx_smem_raw[];
   MxSmem& sm = *reinterpret_cast<MxSmem*>(mx_smem_raw);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1066,10 +1050,6 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
     sm.abort = 0u;
     fence_mbar_init();
   }
-  if (tid < kMxStages * 8) {
-    const uint4* src = reinterpret_cast<const uint4*>(&tmpl);
-    reinterpret_cast<uint4*>(&sm.tmap[tid / 8])[tid % 8] = src[tid % 8];
-  }
   if (warp == kMxMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
   __syncthreads();
   tc_fence_after_sync();
@@ -1085,32 +1065,24 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
   auto item_at = [&](int s) { return mx_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
 
   if (warp == kMxProducerWarp) {
-    CUtensorMap* gmaps = A.gmaps + static_cast<size_t>(blockIdx.x) * kMxStages;
-    const uint8_t* map_addr[kMxStages] = {};
-    MxItem it{};
+    if (lane == 0) {
+      MxItem it{};
 #pragma unroll 1
-    for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kMxStages, chunk = s % nchunks;
-      if (chunk == 0) it = item_at(s);
-      bool ok = s < kMxStages || lane != 0 || tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err, &sm.abort);
-      if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
-      if (map_addr[st] != it.w) {
-        if (lane == 0) tc_tmap_set_addr(&sm.tmap[st], it.w);
-        __syncwarp();
-        tc_tmap_publish(&gmaps[st], &sm.tmap[st]);
-        if (lane == 0) tc_tmap_acquire(&gmaps[st]);
-        map_addr[st] = it.w;
-      }
-      if (lane == 0) {
+      for (int s = 0; s < nsteps; ++s) {
+        const int st = s % kMxStages, chunk = s % nchunks;
+        if (chunk == 0) {
+          it = item_at(s);
+          tc_tmap_acquire(it.map);
+        }
+        if (s >= kMxStages && !tc_wait(&sm.empty[st], ((s / kMxStages) - 1) & 1, A.err, &sm.abort)) break;
         const uint32_t bbytes = it.units * kMxUnitBBytes;
         const size_t uoff = static_cast<size_t>(it.unit) * nchunks + static_cast<size_t>(chunk) * it.units;
         mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kMxRawRow + bbytes + kMxSfAtom);
-        tc_tma_2d(sm.raw[st], &gmaps[st], chunk * kMxRawRow, it.tile * kTcRows, &sm.full[st]);
+        tc_tma_2d(sm.raw[st], it.map, chunk * kMxRawRow, it.tile * kTcRows, &sm.full[st]);
         tc_bulk(sm.b[st], A.bimg + uoff * kMxUnitBBytes, bbytes, &sm.full[st]);
         tc_bulk(sm.sfb[st], A.sfimg + (static_cast<size_t>(it.sl) * nchunks + chunk) * kMxSfAtom, kMxSfAtom,
                 &sm.full[st]);
       }
-      __syncwarp();
     }
   } else if (warp == kMxMmaWarp) {
     // the whole warp walks the steps (warp-uniform operands); one lane issues
@@ -1460,7 +1432,7 @@ namespace {
 
 struct MxLayout {
   size_t codes_x, scales_x, g, u, codes_a, scales_a, run_start, slice_start, slice_len, slice_unit, nslices, bimg,
-      sfimg, gmaps, total;
+      sfimg, maps, total;
 };
 
 // Image units (16 vectors) of a pair list grouped by expert: sum ceil(len / 16)
@@ -1490,7 +1462,7 @@ MxLayout mx_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   L.nslices = take(4);
   L.bimg = take(units * nchunks * dev::kMxUnitBBytes);
   L.sfimg = take(units * nchunks * dev::kMxSfAtom);
-  L.gmaps = take(2 * static_cast<size_t>(sm_count) * dev::kMxStages * sizeof(CUtensorMap));
+  L.maps = take(3 * mx_max_units(P, E) * sizeof(CUtensorMap));  // slices <= units
   L.total = off;
   return L;
 }
@@ -1564,7 +1536,7 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
   uint8_t* bimg = sc + L.bimg;
   uint8_t* sfimg = sc + L.sfimg;
-  CUtensorMap* gmaps = reinterpret_cast<CUtensorMap*>(sc + L.gmaps);
+  CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(sc + L.maps);
   const int P = static_cast<int>(num_pairs), T = static_cast<int>(num_tokens);
   const int H = static_cast<int>(l->hidden), I = static_cast<int>(l->intermediate), O = static_cast<int>(l->out_dim);
   CUtensorMap tm_gu, tm_dn;
@@ -1580,6 +1552,14 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kMxNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
                       static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err, static_cast<uint8_t*>(nullptr), 0, static_cast<uint8_t*>(nullptr)));
+  {
+    const int max_slices = static_cast<int>(mx_max_units(num_pairs, l->num_experts));
+    OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
+                        static_cast<const int32_t*>(slice_start), static_cast<const int32_t*>(nslices), max_slices,
+                        pe, reinterpret_cast<const uint8_t* const*>(l->d_gate),
+                        reinterpret_cast<const uint8_t* const*>(l->d_up),
+                        reinterpret_cast<const uint8_t* const*>(l->d_down), static_cast<int>(l->num_experts), maps));
+  }
   OBJB_TRY(launch_pdl(dev::mx_image_kernel, img_grid, 256, 0, stream, static_cast<const int32_t*>(slice_start),
                       static_cast<const int32_t*>(slice_len), static_cast<const int32_t*>(slice_unit),
                       static_cast<const int32_t*>(nslices), static_cast<const uint8_t*>(codes_x),
@@ -1601,14 +1581,15 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   a.nslices = nslices;
   a.bimg = bimg;
   a.sfimg = sfimg;
-  a.gmaps = gmaps;
+  a.maps = maps;
+  a.map0 = 0;
   a.box_rows = std::min(dev::kTcRows, I);
   a.nvec = T;
   a.out = g;
   a.out2 = u;
   a.out_rows = P;
   a.err = err;
-  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a, tm_gu));
+  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a));
   {
     const size_t n = static_cast<size_t>(P) * I;
     const int sg = static_cast<int>(std::max<size_t>(1, std::min<size_t>((n + 255) / 256, 8ull * props.sm_count)));
@@ -1634,8 +1615,8 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   a.out = v;
   a.out2 = nullptr;
   a.out_rows = static_cast<int>(v_rows);
-  a.gmaps = gmaps + static_cast<size_t>(props.sm_count) * dev::kMxStages;
-  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a, tm_dn));
+  a.map0 = 2;
+  OBJB_TRY(launch_pdl(dev::mx_grouped_kernel, props.sm_count, dev::kMxThreads, smem, stream, a));
   return OBJB_OK;
 }
 
