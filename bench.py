@@ -413,6 +413,8 @@ def line_summary(case_out, moe, ep, cpu):
     if "c5_ep_cache" in moe:
         out["c5_cache_pcie_GBs"] = {k: v["pcie_GB/s_all_ranks"] for k, v in moe["c5_ep_cache"].items()
                                     if k.startswith("T")}
+        out["c5_cache_frac_of_h2d"] = {k: v["pcie_frac_of_measured_h2d"] for k, v in moe["c5_ep_cache"].items()
+                                       if k.startswith("T")}
     out["cpu_GBs"] = {"threads": cpu["value"], "one_thread": cpu["single_thread"]["value"]}
     return out
 
@@ -586,8 +588,8 @@ def bench_c3(qb, dev, gen, steps, warmup, peak):
 
 
 def run_moe_config(args, local):
-    """One MoE config alone (configs[2] or configs[3]), timed as in the full
-    bench line."""
+    """One MoE config alone (configs[2], configs[3], or configs[4] with the
+    expert cache, one rank), timed as in the full bench line."""
     import torch
     from objeta_b200 import QuantBackend
     torch.cuda.set_device(local)
@@ -597,6 +599,8 @@ def run_moe_config(args, local):
     steps = max(3, min(args.steps, 20))
     if args.moe_config == "c3":
         return {"c3_q4_stack": bench_c3(QuantBackend(local), dev, gen, steps, args.warmup, peak)}
+    if args.moe_config == "c5cache":
+        return {"c5_ep_cache": bench_c5_cache(QuantBackend(local), dev, gen, 1, 0, None, steps, args.warmup, peak)}
     return {"c4_fp4_shared": bench_c4(dev, gen, steps, args.warmup, peak)}
 
 
@@ -804,6 +808,21 @@ def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
         host.append(ExpertWeights(*ts))
     del m
     torch.cuda.empty_cache()
+    # this box's pinned host -> device rate at the cache's copy size (one
+    # expert tensor), the same copies the cache issues, back to back
+    tens = [t for e in host for t in (e.w_gate, e.w_up, e.w_down)][:96]
+    dbuf = torch.empty(max(t.nbytes for t in tens), dtype=torch.uint8, device=dev)
+    srcs = [torch.from_numpy(t) for t in tens]
+    h0 = torch.cuda.Event(enable_timing=True)
+    h1 = torch.cuda.Event(enable_timing=True)
+    for rep in range(2):
+        h0.record()
+        for t in srcs:
+            dbuf[:t.numel()].copy_(t, non_blocking=True)
+        h1.record()
+        torch.cuda.synchronize()
+    h2d_gbs = sum(t.numel() for t in srcs) / (h0.elapsed_time(h1) / 1e3) / 1e9
+    del dbuf, srcs
     ebytes = Q4_EXPERT_BYTES(H, I)
     cap_experts = max(1, epr // 4)
     cache = CudaExpertCache(cap_experts * ebytes, rank if world > 1 else torch.cuda.current_device())
@@ -853,6 +872,8 @@ def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
                         "pcie_bytes_per_step_all_ranks": int(float(stats[1]) / n),
                         "cache_reused_bytes_per_step_all_ranks": int(float(stats[2]) / n),
                         "pcie_GB/s_all_ranks": round(float(stats[1]) / n / (per_step / 1e3) / 1e9, 1),
+                        "pcie_frac_of_measured_h2d": round(float(stats[1]) / n / (per_step / 1e3) / 1e9 / world
+                                                           / h2d_gbs, 3),
                         "rank0_tensor_hit_rate": round(hits / max(1, hits + misses), 3), "steps": n}
     for e in host:
         for t in (e.w_gate, e.w_up, e.w_down):
@@ -862,7 +883,10 @@ def bench_c5_cache(qb, dev, gen, world, rank, group, steps, warmup, peak):
     return {"config": f"configs[4] EP layer with expert cache: 256 Q4_0 experts / {world} rank(s) in pinned host "
                       f"memory, cache = {cap_experts} experts per GPU (25%), H 2048, I 512, top-8 Zipf(1.1), "
                       "T tokens per rank",
-            "bound": "PCIe (cache misses) + HBM", "scaling": "weak (T tokens per rank)", **res}
+            "bound": "PCIe (cache misses) + HBM", "scaling": "weak (T tokens per rank)",
+            "h2d_pinned_GB/s_per_gpu": round(h2d_gbs, 1),
+            "h2d_note": "measured on each rank alone: 96 back-to-back copies of one expert tensor (576 KB) from "
+                        "registered host memory; the fraction divides the per-GPU upload rate by it", **res}
 
 
 # --------------------------------------------------------- reference arm
@@ -1046,7 +1070,7 @@ def main():
     ap.add_argument("--experts", type=int, default=None, help="expert count for --official (default configs[3])")
     ap.add_argument("--grouped", type=int, default=None,
                     help="T: the configs[4] pairs of T tokens on the grouped tensor-core path and the CUDA-core path")
-    ap.add_argument("--moe-config", default=None, choices=["c3", "c4"],
+    ap.add_argument("--moe-config", default=None, choices=["c3", "c4", "c5cache"],
                     help="run one MoE config alone (a few GB on the device: small enough for an ncu capture)")
     args = ap.parse_args()
     if args.warmup < 3:
