@@ -50,7 +50,7 @@
 namespace objb {
 namespace dev {
 
-constexpr int kTcRows = 128;                   // M of the MMA: rows per tile
+constexpr int kTcRows = 128;                   // rows per CTA of a 256-row pair tile (M 256 per MMA)
 constexpr int kTcNvp = 32;                     // pairs per slice (at most)
 constexpr int kTcUnit = 16;                    // vectors per slice-image unit; a slice is 1 or 2 units wide
 constexpr int kTcNp = 3 * kTcNvp;              // widest MMA N: three digit planes of kTcNvp vectors
@@ -59,11 +59,12 @@ constexpr int kTcStages = 3;                   // ring of raw tiles + slice-imag
 constexpr int kTcAbuf = 2;                     // unpacked code buffers
 constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
 constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
-constexpr int kTcSlotCols = 256;              // tensor-memory columns of one MMA group
-constexpr int kTcSlots = 2;                    // tensor-memory slots (one group each)
-// A group (one wait, one commit) is 4 blocks of a 16-vector slice (48 of 64
-// columns each) or 2 blocks of a 32-vector slice (96 of 128 columns each).
-__device__ __forceinline__ int tc_group_blocks(int nv) { return nv > kTcUnit ? 2 : 4; }
+constexpr int kTcSlotCols = 512;              // tensor-memory columns of one MMA group
+constexpr int kTcSlots = 1;                    // one slot: a whole step (or half of one) per hand-off
+// A group (one wait, one commit) is 8 blocks of a 16-vector slice (48 of 64
+// columns each: a whole step) or 4 blocks of a 32-vector slice (96 of 128
+// columns each: half a step).
+__device__ __forceinline__ int tc_group_blocks(int nv) { return nv > kTcUnit ? 4 : 8; }
 __device__ __forceinline__ int tc_block_stride(int nv) { return nv > kTcUnit ? 128 : 64; }
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcUnitBBytes = 3 * kTcUnit * kTcKB * 32;  // digit planes of one unit, one step
@@ -82,6 +83,7 @@ struct TcSmem {
   alignas(16) float xs[kTcStages][kTcKB * kTcNvp];          // vector block scales [block][vector]
   alignas(16) float d[kTcStages][kTcKB][kTcRows];           // row block scales (written by unpack)
   alignas(8) uint64_t full[kTcStages], empty[kTcStages], d_full[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
+  uint64_t peer_full[kTcAbuf];  // (even CTA) the odd CTA's codes and slice-image half of a step are in place
   uint64_t t_full[kTcSlots], t_empty[kTcSlots];
   uint32_t tmem_base;
   uint32_t abort;  // a wait of this CTA timed out
@@ -97,7 +99,8 @@ constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps + kTcEpiWarps;  // MMA com
 constexpr uint32_t kTcDFullCount = kTcUnpackWarps;                    // row scales of a step written
 constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;               // every unpack thread
 constexpr uint32_t kTcAEmptyCount = 1;                                // MMA commit
-constexpr uint32_t kTcTEmptyCount = kTcEpiWarps;
+constexpr uint32_t kTcTEmptyCount = 2 * kTcEpiWarps;  // the epilogue warps of both CTAs of the pair
+constexpr uint32_t kTcPeerCount = kTcUnpackWarps;     // the other CTA's unpack warps, codes of a step written
 
 // 1-D bulk copy (both addresses 16-byte aligned, bytes a multiple of 16).
 __device__ __forceinline__ void tc_bulk(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
@@ -167,6 +170,26 @@ __device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, unsigned
 }
 __device__ __forceinline__ bool tc_spin_warp(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
   return __all_sync(0xFFFFFFFFu, tc_spin(bar, parity, err, abort));
+}
+// The same for a barrier the other CTA of the pair arrives on (acquire at
+// cluster scope).
+__device__ __forceinline__ bool tc_spin_cluster(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
+  for (uint32_t i = 0; i < 64u * kMaxSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 4095u) == 4095u && *reinterpret_cast<volatile uint32_t*>(abort) != 0u) return false;
+  }
+  tc_raise(err, abort);
+  return false;
+}
+__device__ __forceinline__ bool tc_spin_cluster_warp(uint64_t* bar, uint32_t parity, unsigned* err, uint32_t* abort) {
+  return __all_sync(0xFFFFFFFFu, tc_spin_cluster(bar, parity, err, abort));
 }
 
 // Instruction descriptor of kind::i8 with both operands signed.
@@ -599,21 +622,31 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
 // multiple of 256, 16-byte aligned matrices and the slice images of this
 // launch.
 //
+// A 2-CTA cluster (a CTA pair on two SMs) works one 256-row tile at a time:
+// each CTA stages its 128 rows and half of the slice image, and the even
+// CTA issues M256 cta_group::2 MMAs (about 35 cycles of issue each, against
+// 170 to 230 for an M128 MMA of one CTA) whose sums land in each CTA's own
+// tensor memory.  Commits are multicast to both CTAs' barriers; the odd
+// CTA's unpack and epilogue warps arrive on the even CTA's barriers.
+//
 // Roles and hand-offs (every wait bounded):
-//   producer   empty[st] -> raw tile (2-D TMA) + slice image + block scales -> full[st]
+//   producer   empty[st] -> raw tile (2-D TMA) + slice-image half + block scales -> full[st]
 //   unpack     full[st], a_empty[ab] -> codes a[ab], row scales d[st] -> a_full[ab], d_full[st], empty[st]
-//   MMA        a_full[ab], full[st]; per group t_empty[slot] -> 2 or 4 MMAs -> t_full[slot]; then a_empty[ab], empty[st]
-//   epilogue   full[st], d_full[st]; per group t_full[slot] -> tensor-memory loads -> t_empty[slot]; empty[st]
+//              (odd CTA: also peer_full[ab] of the even CTA)
+//   MMA        (even CTA) a_full[ab], peer_full[ab], full[st]; per group t_empty -> 4 or 8 MMAs -> t_full
+//              (both CTAs); then a_empty[ab], empty[st] (both CTAs)
+//   epilogue   full[st], d_full[st]; per group t_full -> tensor-memory loads -> t_empty (even CTA); empty[st]
 // A code buffer is released by the MMAs alone, so the unpack of step s + 2
-// overlaps the epilogue of step s.  An MMA of this shape occupies the tensor
-// pipe for about 170 to 230 cycles whatever its N, and a wait + commit adds
-// about 140, so the MMA warp issues a group of blocks (4 of a 16-vector slice,
-// 2 of a 32-vector one) per wait and commit, into one of two tensor-memory
-// slots; it sets the pace.  Epilogue
-// warp (quarter q, set w) owns tile rows 32 q .. 32 q + 31 and vectors
-// w * nv/4 .. (w + 1) * nv/4 - 1 of every block, so its sums need no
-// exchange with other warps; a warp whose vectors are all past the slice's
-// length still waits and arrives, without loading.
+// overlaps the epilogue of step s.  One 512-column tensor-memory slot holds
+// a whole step of a 16-vector slice (half a step of a 32-vector one), so a
+// step crosses between the SMs once: the epilogue loads it in two halves
+// and releases the slot after the second half's loads.  The releases are
+// relaxed cluster arrivals (the tcgen05 fences order the tensor-memory
+// accesses; a release at cluster scope costs the arriving warp hundreds of
+// cycles).  Epilogue warp (quarter q, set w) owns tile rows 32 q .. 32 q + 31
+// of its CTA and vectors w * nv/4 .. (w + 1) * nv/4 - 1 of every block, so its
+// sums need no exchange with other warps; a warp whose vectors are all past
+// the slice's length still waits and arrives, without loading.
 template <int NVW>
 __device__ __forceinline__ void tc_epi_load(uint32_t taddr, int nv, uint32_t (&r)[3][NVW]) {
 #pragma unroll
@@ -643,22 +676,30 @@ __device__ __forceinline__ void tc_epi_fold(const uint32_t (&r)[3][NVW], float d
   }
 }
 // One MMA group of an epilogue warp: tensor-memory loads of its GB blocks
-// (column stride BS), the slot released, then the folds.
+// (column stride BS) in two halves (the registers hold half a group), each
+// half folded as it lands; the slot is released to the pair's MMA warp (in
+// CTA 0) after the second half's loads.
 template <int NVW, int GB, int BS>
 __device__ __forceinline__ void tc_epi_group(uint32_t taddr, int nv, const float* dcol, const float* xsv,
                                              uint64_t* t_empty, float (&acc)[8]) {
-  uint32_t r[GB][3][NVW];
+  constexpr int H = GB / 2;
+  uint32_t r[H][3][NVW];
 #pragma unroll
-  for (int b = 0; b < GB; ++b) tc_epi_load<NVW>(taddr + b * BS, nv, r[b]);
+  for (int b = 0; b < H; ++b) tc_epi_load<NVW>(taddr + b * BS, nv, r[b]);
+  tmem_wait_ld();
+#pragma unroll
+  for (int b = 0; b < H; ++b) tc_epi_fold<NVW>(r[b], dcol[b * kTcRows], xsv + b * nv, acc);
+#pragma unroll
+  for (int b = 0; b < H; ++b) tc_epi_load<NVW>(taddr + (H + b) * BS, nv, r[b]);
   tmem_wait_ld();
   tc_fence_before_sync();
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(t_empty);
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cta_relaxed(t_empty, 0);  // the pair's MMAs are issued by CTA 0
 #pragma unroll
-  for (int b = 0; b < GB; ++b) tc_epi_fold<NVW>(r[b], dcol[b * kTcRows], xsv + b * nv, acc);
+  for (int b = 0; b < H; ++b) tc_epi_fold<NVW>(r[b], dcol[(H + b) * kTcRows], xsv + (H + b) * nv, acc);
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   TcSmem& sm = *reinterpret_cast<TcSmem*>(tc_smem_raw);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -672,6 +713,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     for (int i = 0; i < kTcAbuf; ++i) {
       mbar_init(&sm.a_full[i], kTcAFullCount);
       mbar_init(&sm.a_empty[i], kTcAEmptyCount);
+      mbar_init(&sm.peer_full[i], kTcPeerCount);
     }
     for (int i = 0; i < kTcSlots; ++i) {
       mbar_init(&sm.t_full[i], 1);
@@ -680,19 +722,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
     sm.abort = 0u;
     fence_mbar_init();
   }
-  if (warp == kTcMmaWarp) tmem_alloc(&sm.tmem_base, kTcTmemCols);
+  if (warp == kTcMmaWarp) tmem_alloc_pair(&sm.tmem_base, kTcTmemCols);
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either arrives on the other's
   tc_fence_after_sync();
   const uint32_t tmem = sm.tmem_base;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs of the pair
+  const int pair = static_cast<int>(blockIdx.x) >> 1, npairs = static_cast<int>(gridDim.x) >> 1;
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int nb = A.C / 32, nchunks = nb / kTcKB;
-  const int tiles = (A.R + kTcRows - 1) / kTcRows;
+  const int tiles = (A.R + 2 * kTcRows - 1) / (2 * kTcRows);  // 256-row tiles of the pair
   const int mats = A.W2 ? 2 : 1;
   const int total = *A.nslices * tiles * mats;
-  const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_items = pair < total ? (total - 1 - pair) / npairs + 1 : 0;
   const int nsteps = my_items * nchunks;
-  auto item_at = [&](int s) { return tc_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
+  auto item_at = [&](int s) { return tc_item(A, pair + (s / nchunks) * npairs, tiles, mats); };
+  const int row0 = static_cast<int>(rank) * kTcRows;  // this CTA's rows within a pair tile
 
   if (warp == kTcProducerWarp) {
     if (lane == 0) {
@@ -706,16 +752,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
         }
         if (s >= kTcStages && !tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort)) break;
         const int units = it.nv / kTcUnit;
-        const uint32_t bbytes = units * kTcUnitBBytes, xbytes = units * kTcUnitXFloats * 4;
+        // this CTA's half of the slice image (B rows N/2 * rank ..), all the block scales
+        const uint32_t bhalf = units * kTcUnitBBytes / 2, xbytes = units * kTcUnitXFloats * 4;
         const size_t uoff = static_cast<size_t>(it.unit) * nchunks + static_cast<size_t>(chunk) * units;
-        mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kTcRawRow + bbytes + xbytes);
-        tc_tma_2d(sm.raw[st], it.map, chunk * kTcRawRow, it.tile * kTcRows, &sm.full[st]);
-        tc_bulk(sm.b[st], A.bimg + uoff * kTcUnitBBytes, bbytes, &sm.full[st]);
+        mbar_arrive_expect_tx(&sm.full[st], A.box_rows * kTcRawRow + bhalf + xbytes);
+        tc_tma_2d(sm.raw[st], it.map, chunk * kTcRawRow, it.tile * 2 * kTcRows + row0, &sm.full[st]);
+        tc_bulk(sm.b[st], A.bimg + uoff * kTcUnitBBytes + rank * bhalf, bhalf, &sm.full[st]);
         tc_bulk(sm.xs[st], A.ximg + uoff * kTcUnitXFloats, xbytes, &sm.full[st]);
       }
     }
   } else if (warp == kTcMmaWarp) {
-    // the whole warp walks the steps (warp-uniform operands); one lane issues
+    // the even CTA's whole warp walks the steps (warp-uniform operands); one
+    // lane issues the pair's MMAs; the odd CTA's MMA warp has no steps
+    if (rank != 0) goto tc_done;
     uint32_t idesc = 0;
     int gb = 4, bstride = 64, G = 0;  // group size, block column stride, groups issued
 #pragma unroll 1
@@ -723,13 +772,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       const int st = s % kTcStages, ab = s % kTcAbuf;
       if (s % nchunks == 0) {
         const int nv = item_at(s).nv;
-        idesc = umma_idesc_s8s8(kTcRows, 3 * nv);
+        idesc = umma_idesc_s8s8(2 * kTcRows, 3 * nv);
         gb = tc_group_blocks(nv);
         bstride = tc_block_stride(nv);
       }
       // (the unpack threads fenced their code stores to the async proxy
       // before arriving on a_full)
-      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort) ||
+      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort)) break;
+      if (!tc_spin_cluster_warp(&sm.peer_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort) ||
           !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort))
         break;
       tc_fence_after_sync();
@@ -737,7 +787,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
 #pragma unroll 1
       for (int j0 = 0; j0 < kTcKB; j0 += gb, ++G) {
         const int slot = G % kTcSlots;
-        if (G >= kTcSlots && !tc_spin_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err, &sm.abort)) {
+        if (G >= kTcSlots && !tc_spin_cluster_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err, &sm.abort)) {
           ok = false;
           break;
         }
@@ -747,13 +797,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
           const int j = j0 + jj;
           const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
           const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
-          umma_i8(tmem + slot * kTcSlotCols + jj * bstride, da, db, idesc, false);
+          umma_i8_pair(tmem + slot * kTcSlotCols + jj * bstride, da, db, idesc);
         }
-        umma_commit(&sm.t_full[slot]);
+        umma_commit_pair(&sm.t_full[slot]);
       }
       if (!ok) break;
-      umma_commit(&sm.a_empty[ab]);
-      umma_commit(&sm.empty[st]);
+      umma_commit_pair(&sm.a_empty[ab]);
+      umma_commit_pair(&sm.empty[st]);
     }
   } else if (warp < kTcEpiWarp0) {
     const int r = tid - 32 * kTcUnpackWarp0;
@@ -769,6 +819,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       if (lane == 0) {
         mbar_arrive(&sm.d_full[st]);
         mbar_arrive(&sm.empty[st]);
+        // the even CTA issues the MMAs that read these codes and this CTA's
+        // slice-image half (landed: full[st] was waited above)
+        if (rank != 0) mbar_arrive_cta(&sm.peer_full[ab], 0);
       }
     }
   } else {
@@ -815,20 +868,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
           const float* dcol = &sm.d[st][j][trow];
           const float* xsv = &sm.xs[st][j * it.nv + v0];
           if (nvw == 8)
-            tc_epi_group<8, 2, 128>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+            tc_epi_group<8, 4, 128>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
           else
-            tc_epi_group<4, 4, 64>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+            tc_epi_group<4, 8, 64>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
         } else {
           tc_fence_before_sync();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.t_empty[slot]);
+          if (lane == 0) mbar_arrive_cta_relaxed(&sm.t_empty[slot], 0);
         }
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty[st]);
       if (chunk == nchunks - 1) {
-        const int grow = it.tile * kTcRows + trow;
+        const int grow = it.tile * 2 * kTcRows + row0 + trow;
         if (live) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -850,11 +903,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcAr
       }
     }
   }
+tc_done:
   tc_fence_before_sync();
   __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the other may still read or arrive on its memory
   if (warp == kTcMmaWarp) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem, kTcTmemCols);
+    tmem_dealloc_pair(tmem, kTcTmemCols);
   }
 }
 
@@ -1397,7 +1452,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out2 = u;
   a.out_rows = P;
   a.err = err;
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count / 2 * 2, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_swiglu_planes_kernel, warp_grid(P, I), 256, 0, stream, g,
                       static_cast<const float*>(u), P, d_count, I, limit, planes_a, xsc_a, wflag_a, wany_a, pe, pt, T,
                       x, H, static_cast<const uint8_t*>(wflag_x), static_cast<const uint8_t*>(wany_x), a.W, a.W2,
@@ -1418,7 +1473,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.out = v;
   a.out2 = nullptr;
   a.out_rows = static_cast<int>(v_rows);
-  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count, dev::kTcThreads, smem, stream, a));
+  OBJB_TRY(launch_pdl(dev::tc_q4_grouped_kernel, props.sm_count / 2 * 2, dev::kTcThreads, smem, stream, a));
   OBJB_TRY(launch_pdl(dev::tc_wide_down_kernel, warp_grid(P, 32), 256, 0, stream,
                       static_cast<const float*>(g), P, d_count, I, O, static_cast<const uint8_t*>(wflag_a),
                       static_cast<const uint8_t*>(wany_a), pe, po,
@@ -1672,4 +1727,5 @@ int objb_moe_pairs_official_tc_device(const objb_moe_layer* layer, size_t num_pa
 }
 
 }  // extern "C"
+
 
