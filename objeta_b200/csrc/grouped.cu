@@ -55,8 +55,9 @@ constexpr int kTcNvp = 32;                     // pairs per slice (at most)
 constexpr int kTcUnit = 16;                    // vectors per slice-image unit; a slice is 1 or 2 units wide
 constexpr int kTcNp = 3 * kTcNvp;              // widest MMA N: three digit planes of kTcNvp vectors
 constexpr int kTcKB = 8;                       // 32-column blocks per step
-constexpr int kTcStages = 3;                   // ring of raw tiles + slice-image steps
+constexpr int kTcStages = 4;                   // ring of raw tiles + slice-image steps
 constexpr int kTcAbuf = 2;                     // unpacked code buffers
+constexpr int kTcQ = 4;                        // ring of a step's scales for the epilogue
 constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
 constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
 constexpr int kTcSlotCols = 512;              // tensor-memory columns of one MMA group
@@ -65,7 +66,6 @@ constexpr int kTcSlots = 1;                    // one slot: a whole step (or hal
 // columns each: a whole step) or 4 blocks of a 32-vector slice (96 of 128
 // columns each: half a step).
 __device__ __forceinline__ int tc_group_blocks(int nv) { return nv > kTcUnit ? 4 : 8; }
-__device__ __forceinline__ int tc_block_stride(int nv) { return nv > kTcUnit ? 128 : 64; }
 constexpr uint32_t kTcTmemCols = 512;
 constexpr int kTcUnitBBytes = 3 * kTcUnit * kTcKB * 32;  // digit planes of one unit, one step
 constexpr int kTcUnitXFloats = kTcKB * kTcUnit;          // block scales of one unit, one step
@@ -78,25 +78,30 @@ constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 
 struct TcSmem {
   alignas(1024) uint8_t a[kTcAbuf][kTcRows * kTcKB * 32];   // signed codes q - 8, core-matrix order
-  alignas(1024) uint8_t b[kTcStages][kTcNp * kTcKB * 32];   // slice image step (digit planes)
+  alignas(1024) uint8_t b[kTcStages][kTcNp / 2 * kTcKB * 32];  // this CTA's half of a slice-image step
   alignas(128) uint8_t raw[kTcStages][kTcRows * kTcRawRow]; // raw Q4_0 rows of a step (bulk copies)
-  alignas(16) float xs[kTcStages][kTcKB * kTcNvp];          // vector block scales [block][vector]
-  alignas(16) float d[kTcStages][kTcKB][kTcRows];           // row block scales (written by unpack)
-  alignas(8) uint64_t full[kTcStages], empty[kTcStages], d_full[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
-  uint64_t peer_full[kTcAbuf];  // (even CTA) the odd CTA's codes and slice-image half of a step are in place
+  alignas(16) float xs[kTcStages][kTcKB * kTcNvp];          // vector block scales [block][vector] (bulk copy)
+  // the epilogue's copy of a step's scales (written by unpack), so that a
+  // stage is free once unpacked and multiplied
+  alignas(16) float q_xs[kTcQ][kTcKB * kTcNvp];
+  alignas(16) float q_d[kTcQ][kTcKB][kTcRows];              // row block scales
+  alignas(8) uint64_t full[kTcStages], empty[kTcStages], a_full[kTcAbuf], a_empty[kTcAbuf];
+  uint64_t q_full[kTcQ], q_empty[kTcQ];
   uint64_t t_full[kTcSlots], t_empty[kTcSlots];
   uint32_t tmem_base;
   uint32_t abort;  // a wait of this CTA timed out
 };
 static_assert(sizeof(TcSmem) <= 227 * 1024, "grouped kernel shared memory");
-static_assert(kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols) && kTcNp <= 128 && kTcKB % 4 == 0,
-              "tensor-memory slots");
+static_assert(kTcSlots == 1 && kTcSlotCols == 512 && kTcSlots * kTcSlotCols <= static_cast<int>(kTcTmemCols) &&
+                  kTcNp <= 128 && kTcKB == 8,
+              "tensor-memory slot: 8 blocks x 64 columns or 2 x 4 blocks x 128 columns per step");
 static_assert(kTcUnpackWarps * 32 == kTcRows && kTcEpiWarps == 16 && kTcNvp == 2 * kTcUnit, "warp roles");
 
 // Arrival counts of the pipeline barriers.
 constexpr uint32_t kTcFullCount = 1;                                  // producer (arrive + transaction bytes)
-constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps + kTcEpiWarps;  // MMA commit, unpack, epilogue
-constexpr uint32_t kTcDFullCount = kTcUnpackWarps;                    // row scales of a step written
+constexpr uint32_t kTcEmptyCount = 1 + kTcUnpackWarps;               // MMA commit, unpack
+constexpr uint32_t kTcQFullCount = kTcUnpackWarps;                    // a step's scales written
+constexpr uint32_t kTcQEmptyCount = kTcEpiWarps;                      // a step's scales read
 constexpr uint32_t kTcAFullCount = 32 * kTcUnpackWarps;               // every unpack thread
 constexpr uint32_t kTcAEmptyCount = 1;                                // MMA commit
 constexpr uint32_t kTcTEmptyCount = 2 * kTcEpiWarps;  // the epilogue warps of both CTAs of the pair
@@ -580,7 +585,7 @@ __device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int
 // Unpack (four warps, thread = tile row): raw row of ring slot `st` -> signed
 // codes q - 8 in core-matrix order (A buffer `ab`) and the row's block scales
 // (beside the stage, so that the A buffer is free once the MMAs have read it).
-__device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
+__device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int q, int r) {
   uint32_t w[kTcRawRow / 4];
   const uint8_t* src = sm.raw[st] + r * kTcRawRow;
 #pragma unroll
@@ -613,7 +618,7 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
     uint8_t* dst = sm.a[ab] + ((r >> 3) * kTcKch + 2 * b) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(c[0], c[1], c[2], c[3]);
     *reinterpret_cast<uint4*>(dst + 128) = make_uint4(c[4], c[5], c[6], c[7]);
-    sm.d[st][b][r] = f16_bits_to_f32(d16);
+    sm.q_d[q][b][r] = f16_bits_to_f32(d16);
   }
 }
 
@@ -631,11 +636,12 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int r) {
 //
 // Roles and hand-offs (every wait bounded):
 //   producer   empty[st] -> raw tile (2-D TMA) + slice-image half + block scales -> full[st]
-//   unpack     full[st], a_empty[ab] -> codes a[ab], row scales d[st] -> a_full[ab], d_full[st], empty[st]
-//              (odd CTA: also peer_full[ab] of the even CTA)
-//   MMA        (even CTA) a_full[ab], peer_full[ab], full[st]; per group t_empty -> 4 or 8 MMAs -> t_full
+//   unpack     full[st], a_empty[ab], q_empty[q] -> codes a[ab], scales q_d/q_xs[q] -> a_full[ab], q_full[q],
+//              empty[st]
+//              (odd CTA: also a_full[ab] of the even CTA, one arrival per warp)
+//   MMA        (even CTA) a_full[ab]; per group t_empty -> 4 or 8 MMAs -> t_full
 //              (both CTAs); then a_empty[ab], empty[st] (both CTAs)
-//   epilogue   full[st], d_full[st]; per group t_full -> tensor-memory loads -> t_empty (even CTA); empty[st]
+//   epilogue   q_full[q]; per group t_full -> tensor-memory loads -> t_empty (even CTA); q_empty[q]
 // A code buffer is released by the MMAs alone, so the unpack of step s + 2
 // overlaps the epilogue of step s.  One 512-column tensor-memory slot holds
 // a whole step of a 16-vector slice (half a step of a 32-vector one), so a
@@ -708,12 +714,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
     for (int i = 0; i < kTcStages; ++i) {
       mbar_init(&sm.full[i], kTcFullCount);
       mbar_init(&sm.empty[i], kTcEmptyCount);
-      mbar_init(&sm.d_full[i], kTcDFullCount);
+    }
+    for (int i = 0; i < kTcQ; ++i) {
+      mbar_init(&sm.q_full[i], kTcQFullCount);
+      mbar_init(&sm.q_empty[i], kTcQEmptyCount);
     }
     for (int i = 0; i < kTcAbuf; ++i) {
-      mbar_init(&sm.a_full[i], kTcAFullCount);
+      // the even CTA's also counts the odd CTA's unpack warps (its codes and
+      // slice-image half of the step are in place)
+      mbar_init(&sm.a_full[i], kTcAFullCount + (cluster_ctarank() == 0 ? kTcPeerCount : 0u));
       mbar_init(&sm.a_empty[i], kTcAEmptyCount);
-      mbar_init(&sm.peer_full[i], kTcPeerCount);
     }
     for (int i = 0; i < kTcSlots; ++i) {
       mbar_init(&sm.t_full[i], 1);
@@ -765,64 +775,78 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
     // the even CTA's whole warp walks the steps (warp-uniform operands); one
     // lane issues the pair's MMAs; the odd CTA's MMA warp has no steps
     if (rank != 0) goto tc_done;
-    uint32_t idesc = 0;
-    int gb = 4, bstride = 64, G = 0;  // group size, block column stride, groups issued
+    // Operand descriptors of block j of code buffer ab / image stage st: the
+    // address field (bits 0-13, byte address >> 4; shared memory stays below
+    // 256 KB, so no carry leaves it) of the buffer's base plus 16 per block.
+    const uint64_t da0 = umma_desc_kmajor(smem_addr(sm.a[0]), 128, kTcKch * 128);
+    const uint64_t db0 = umma_desc_kmajor(smem_addr(sm.b[0]), 128, kTcKch * 128);
+    constexpr uint64_t kADesc = sizeof(sm.a[0]) >> 4, kBDesc = sizeof(sm.b[0]) >> 4;
+    int st = 0, ab = 0, G = 0;  // image stage, code buffer, groups issued
+    uint32_t apar = 0;          // a_full parity of buffer ab
 #pragma unroll 1
-    for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kTcStages, ab = s % kTcAbuf;
-      if (s % nchunks == 0) {
-        const int nv = item_at(s).nv;
-        idesc = umma_idesc_s8s8(2 * kTcRows, 3 * nv);
-        gb = tc_group_blocks(nv);
-        bstride = tc_block_stride(nv);
-      }
-      // (the unpack threads fenced their code stores to the async proxy
-      // before arriving on a_full)
-      if (!tc_spin_warp(&sm.a_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort)) break;
-      if (!tc_spin_cluster_warp(&sm.peer_full[ab], (s / kTcAbuf) & 1, A.err, &sm.abort) ||
-          !tc_spin_warp(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort))
-        break;
-      tc_fence_after_sync();
-      bool ok = true;
+    for (int i = 0; i < my_items; ++i) {
+      const int nv = tc_item(A, pair + i * npairs, tiles, mats).nv;
+      const uint32_t idesc = umma_idesc_s8s8(2 * kTcRows, 3 * nv);
+      const bool wide = nv > kTcUnit;
 #pragma unroll 1
-      for (int j0 = 0; j0 < kTcKB; j0 += gb, ++G) {
-        const int slot = G % kTcSlots;
-        if (G >= kTcSlots && !tc_spin_cluster_warp(&sm.t_empty[slot], ((G / kTcSlots) - 1) & 1, A.err, &sm.abort)) {
-          ok = false;
-          break;
-        }
+      for (int c = 0; c < nchunks; ++c) {
+        // One wait covers both CTAs' operands of the step: the unpack
+        // threads of both arrive on this a_full after their own full[st]
+        // wait (the slice-image halves landed) and after fencing their code
+        // stores to the async proxy.
+        if (!tc_spin_cluster_warp(&sm.a_full[ab], apar, A.err, &sm.abort)) goto tc_mma_out;
         tc_fence_after_sync();
-#pragma unroll 1
-        for (int jj = 0; jj < gb; ++jj) {
-          const int j = j0 + jj;
-          const uint64_t da = umma_desc_kmajor(smem_addr(sm.a[ab] + 2 * j * 128), 128, kTcKch * 128);
-          const uint64_t db = umma_desc_kmajor(smem_addr(sm.b[st] + 2 * j * 128), 128, kTcKch * 128);
-          umma_i8_pair(tmem + slot * kTcSlotCols + jj * bstride, da, db, idesc);
+        const uint64_t da = da0 + ab * kADesc, db = db0 + st * kBDesc;
+        if (wide) {  // two groups of 4 blocks, 128 columns each
+#pragma unroll
+          for (int h = 0; h < 2; ++h, ++G) {
+            if (G > 0 && !tc_spin_cluster_warp(&sm.t_empty[0], (G - 1) & 1, A.err, &sm.abort)) goto tc_mma_out;
+            tc_fence_after_sync();
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+              umma_i8_pair(tmem + jj * 128, da + 16 * (4 * h + jj), db + 16 * (4 * h + jj), idesc);
+            umma_commit_pair(&sm.t_full[0]);
+          }
+        } else {  // one group of 8 blocks, 64 columns each
+          if (G > 0 && !tc_spin_cluster_warp(&sm.t_empty[0], (G - 1) & 1, A.err, &sm.abort)) goto tc_mma_out;
+          tc_fence_after_sync();
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) umma_i8_pair(tmem + jj * 64, da + 16 * jj, db + 16 * jj, idesc);
+          umma_commit_pair(&sm.t_full[0]);
+          ++G;
         }
-        umma_commit_pair(&sm.t_full[slot]);
+        umma_commit_pair(&sm.a_empty[ab]);
+        umma_commit_pair(&sm.empty[st]);
+        ab = ab == kTcAbuf - 1 ? 0 : ab + 1;
+        apar ^= static_cast<uint32_t>(ab == 0);
+        st = st == kTcStages - 1 ? 0 : st + 1;
       }
-      if (!ok) break;
-      umma_commit_pair(&sm.a_empty[ab]);
-      umma_commit_pair(&sm.empty[st]);
     }
+  tc_mma_out:;
   } else if (warp < kTcEpiWarp0) {
     const int r = tid - 32 * kTcUnpackWarp0;
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kTcStages, ab = s % kTcAbuf;
+      const int st = s % kTcStages, ab = s % kTcAbuf, q = s % kTcQ;
       if (!tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort)) break;
       if (s >= kTcAbuf && !tc_wait(&sm.a_empty[ab], ((s / kTcAbuf) - 1) & 1, A.err, &sm.abort)) break;
-      tc_unpack(sm, st, ab, r);
+      if (s >= kTcQ && !tc_wait(&sm.q_empty[q], ((s / kTcQ) - 1) & 1, A.err, &sm.abort)) break;
+      tc_unpack(sm, st, ab, q, r);
+      {  // the block scales: 2 of the step's 256 per thread
+        static_assert(kTcKB * kTcNvp == 2 * kTcRows, "block scales per unpack thread");
+        reinterpret_cast<float2*>(sm.q_xs[q])[r] = reinterpret_cast<const float2*>(sm.xs[st])[r];
+      }
       fence_async_shared();  // codes written here, read by the MMAs
       mbar_arrive(&sm.a_full[ab]);
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sm.d_full[st]);
+        mbar_arrive(&sm.q_full[q]);
         mbar_arrive(&sm.empty[st]);
         // the even CTA issues the MMAs that read these codes and this CTA's
         // slice-image half (landed: full[st] was waited above)
-        if (rank != 0) mbar_arrive_cta(&sm.peer_full[ab], 0);
+        if (rank != 0) mbar_arrive_cta(&sm.a_full[ab], 0);
       }
+      __syncwarp();  // the warp unpacks the next step converged
     }
   } else {
     const int ew = warp - kTcEpiWarp0;
@@ -838,7 +862,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
     bool live = false;
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
-      const int st = s % kTcStages, chunk = s % nchunks;
+      const int q = s % kTcQ, chunk = s % nchunks;
       if (chunk == 0) {
         it = item_at(s);
         nvw = it.nv / 4;
@@ -851,9 +875,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
           orow = A.slot_out ? A.slot_out[p] : p;
         }
       }
-      // block scales (bulk copy) and row scales (unpack) of this step are read below
-      bool ok = tc_wait(&sm.full[st], (s / kTcStages) & 1, A.err, &sm.abort) &&
-                tc_wait(&sm.d_full[st], (s / kTcStages) & 1, A.err, &sm.abort);
+      // the step's block and row scales (copied and written by unpack) are read below
+      bool ok = tc_wait(&sm.q_full[q], (s / kTcQ) & 1, A.err, &sm.abort);
       const int gb = tc_group_blocks(it.nv);
 #pragma unroll 1
       for (int j = 0; j < kTcKB && ok; j += gb, ++G) {
@@ -865,8 +888,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
         tc_fence_after_sync();
         if (live) {
           const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + v0;
-          const float* dcol = &sm.d[st][j][trow];
-          const float* xsv = &sm.xs[st][j * it.nv + v0];
+          const float* dcol = &sm.q_d[q][j][trow];
+          const float* xsv = &sm.q_xs[q][j * it.nv + v0];
           if (nvw == 8)
             tc_epi_group<8, 4, 128>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
           else
@@ -879,7 +902,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
       }
       if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.empty[st]);
+      if (lane == 0) mbar_arrive(&sm.q_empty[q]);
       if (chunk == nchunks - 1) {
         const int grow = it.tile * 2 * kTcRows + row0 + trow;
         if (live) {

@@ -99,18 +99,22 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Arrive (release at cluster scope) on the barrier at the same shared-memory
-// offset in CTA `rank` of this cluster.
+// Arrive (release at CTA scope) on the barrier at the same shared-memory
+// offset in CTA `rank` of this cluster.  For the operands of a cta_group::2
+// MMA in this CTA's shared memory: A rows that its threads wrote (fenced to
+// the async proxy before the arrival; only this SM's tensor core reads them)
+// and a B half that a bulk copy wrote (its completion observed on a local
+// barrier before the arrival).  A release at cluster scope costs the
+// arriving thread ~800 cycles.
 __device__ __forceinline__ void mbar_arrive_cta(const uint64_t* bar, uint32_t rank) {
   asm volatile(
       "{\n\t.reg .b32 ra;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_addr(bar)),
+      "mbarrier.arrive.release.cta.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_addr(bar)),
       "r"(rank)
       : "memory");
 }
 // The same with relaxed semantics: for a barrier that only orders tensor-
-// memory accesses, which the tcgen05 fences around it order (a release at
-// cluster scope costs the arriving warp hundreds of cycles).
+// memory accesses, which the tcgen05 fences around it order.
 __device__ __forceinline__ void mbar_arrive_cta_relaxed(const uint64_t* bar, uint32_t rank) {
   asm volatile(
       "{\n\t.reg .b32 ra;\n\tmapa.shared::cluster.u32 ra, %0, %1;\n\t"
