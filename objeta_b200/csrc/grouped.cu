@@ -58,6 +58,7 @@ constexpr int kTcKB = 8;                       // 32-column blocks per step
 constexpr int kTcStages = 4;                   // ring of raw tiles + slice-image steps
 constexpr int kTcAbuf = 2;                     // unpacked code buffers
 constexpr int kTcQ = 4;                        // ring of a step's scales for the epilogue
+constexpr int kTcItemRing = 16;                // ring of work items (read once, by the producer warp)
 constexpr int kTcRawRow = kTcKB * 18;          // raw Q4_0 bytes of one row per step
 constexpr int kTcKch = 2 * kTcKB;              // 16-byte K columns of a staged operand
 constexpr int kTcSlotCols = 512;              // tensor-memory columns of one MMA group
@@ -76,7 +77,19 @@ constexpr int kTcUnpackWarp0 = 2, kTcUnpackWarps = 4;
 constexpr int kTcEpiWarp0 = 6, kTcEpiWarps = 16;
 constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 
+// A work item as the MMA and epilogue warps need it, written by the producer
+// warp after its empty[st] wait for the item's first step.  That wait means
+// the epilogue has finished step s - kTcStages - kTcQ (unpack waited its
+// q_empty before releasing the stage), so with items of one step or more the
+// entry being overwritten (item n - kTcItemRing) has been read.
+struct TcItemSlot {
+  int tile, s0, ns, nv, mat;
+  int orow[kTcNvp];  // output row of the slice's vector i (-1 past its length)
+};
+static_assert(kTcItemRing >= kTcStages + kTcQ, "item ring outlives the producer's lead");
+
 struct TcSmem {
+  TcItemSlot items[kTcItemRing];
   alignas(1024) uint8_t a[kTcAbuf][kTcRows * kTcKB * 32];   // signed codes q - 8, core-matrix order
   alignas(1024) uint8_t b[kTcStages][kTcNp / 2 * kTcKB * 32];  // this CTA's half of a slice-image step
   alignas(128) uint8_t raw[kTcStages][kTcRows * kTcRawRow]; // raw Q4_0 rows of a step (bulk copies)
@@ -463,9 +476,13 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
 }
 
 // The slice images of one contraction: for slice sl, step c, the B operand
-// rows k * nv + i (plane k of the slice's vector i, nv = 16 or 32; zero rows
-// past the slice's length) in core-matrix order, then the block scales
-// [block][vector]; unit offsets from tc_slices_kernel.
+// rows k * nv + i (plane k of the slice's vector i, nv = 16 or 32) in
+// core-matrix order, then the block scales [block][vector]; unit offsets
+// from tc_slices_kernel.  Rows and scales past the slice's length are not
+// written: the MMAs multiply them into columns that the epilogue never reads
+// or stores.  One warp per (slice, vector): one id lookup, then the vector's
+// three digit planes for every step, read contiguously (several loads in
+// flight per lane) and scattered as 16-byte core-matrix rows.
 __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict__ slice_start,
                                                        const int32_t* __restrict__ slice_len,
                                                        const int32_t* __restrict__ slice_unit,
@@ -476,36 +493,44 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
                                                        uint8_t* __restrict__ bimg, float* __restrict__ ximg) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int nchunks = C / (kTcKB * 32), nb = C / 32;
-  const int total = *nslices * nchunks;
-  for (int w = blockIdx.x; w < total; w += gridDim.x) {
-    const int sl = w / nchunks, c = w % nchunks;
-    const int s0 = slice_start[sl], ns = slice_len[sl];
+  constexpr int kBatch = 6;  // loads in flight per lane before their stores
+  const int lane = threadIdx.x & 31;
+  const int nchunks = C / (kTcKB * 32), nb = C / 32, kc = C / 16;  // steps, blocks, 16-byte columns
+  const int nsl = *nslices, total = nsl * kTcNvp;
+  const int nwarps = static_cast<int>(gridDim.x * blockDim.x) >> 5;
+  // vector-major order: the live items (small i, present in most slices)
+  // spread over every block instead of a quarter of them
+  for (int w = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5); w < total; w += nwarps) {
+    const int sl = w % nsl, i = w / nsl;
+    const int ns = slice_len[sl];
+    if (i >= ns) continue;
+    const int s0 = slice_start[sl];
     const int nv = ns > kTcUnit ? 2 * kTcUnit : kTcUnit, units = nv / kTcUnit;
-    const size_t uoff = static_cast<size_t>(slice_unit[sl]) * nchunks + static_cast<size_t>(c) * units;
-    uint8_t* bdst = bimg + uoff * kTcUnitBBytes;
-    for (int q = threadIdx.x; q < 3 * nv * kTcKch; q += blockDim.x) {
-      const int cm = q >> 3, r = q & 7;  // core matrix (row group, K column), row within it
-      const int brow = 8 * (cm / kTcKch) + r, p = cm % kTcKch;
-      const int k = brow / nv, i = brow % nv;
-      uint4 val = make_uint4(0u, 0u, 0u, 0u);
-      if (i < ns) {
-        int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
-        v = (v < 0 || v >= nvec) ? 0 : v;
-        val = *reinterpret_cast<const uint4*>(planes + (static_cast<size_t>(v) * 3 + k) * C + c * (kTcKB * 32) + p * 16);
+    const size_t ubase = static_cast<size_t>(slice_unit[sl]) * nchunks;
+    int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
+    v = (v < 0 || v >= nvec) ? 0 : v;
+    const uint4* src = reinterpret_cast<const uint4*>(planes + static_cast<size_t>(v) * 3 * C);
+    for (int q0 = lane; q0 < 3 * kc; q0 += 32 * kBatch) {
+      uint4 t[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (q0 + 32 * u < 3 * kc) t[u] = src[q0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int q = q0 + 32 * u;
+        if (q >= 3 * kc) break;
+        const int k = q / kc, col = q % kc;            // plane, 16-byte column of the row
+        const int c = col / kTcKch, pk = col % kTcKch;  // step, K column within the step
+        const int brow = k * nv + i;
+        const int cm = (brow >> 3) * kTcKch + pk;       // core matrix
+        uint8_t* dst = bimg + (ubase + static_cast<size_t>(c) * units) * kTcUnitBBytes;
+        *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(cm) * 8 + (brow & 7)) * 16) = t[u];
       }
-      *reinterpret_cast<uint4*>(bdst + static_cast<size_t>(q) * 16) = val;
     }
-    float* xdst = ximg + uoff * kTcUnitXFloats;
-    for (int q = threadIdx.x; q < kTcKB * nv; q += blockDim.x) {
-      const int j = q / nv, i = q % nv;
-      float val = 0.0f;
-      if (i < ns) {
-        int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
-        v = (v < 0 || v >= nvec) ? 0 : v;
-        val = xsc[static_cast<size_t>(v) * nb + c * kTcKB + j];
-      }
-      xdst[q] = val;
+    for (int q = lane; q < nb; q += 32) {
+      const int c = q / kTcKB, j = q % kTcKB;
+      ximg[(ubase + static_cast<size_t>(c) * units) * kTcUnitXFloats + j * nv + i] =
+          xsc[static_cast<size_t>(v) * nb + q];
     }
   }
 }
@@ -751,16 +776,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
   const int row0 = static_cast<int>(rank) * kTcRows;  // this CTA's rows within a pair tile
 
   if (warp == kTcProducerWarp) {
-    if (lane == 0) {
-      TcItem it{};
+    // the whole warp reads each item (its fields, the slice's output rows,
+    // the pair ids checked); lane 0 issues the copies
+    TcItem it{};
 #pragma unroll 1
-      for (int s = 0; s < nsteps; ++s) {
-        const int st = s % kTcStages, chunk = s % nchunks;
-        if (chunk == 0) {
-          it = item_at(s);
-          tc_tmap_acquire(it.map);
+    for (int s = 0; s < nsteps; ++s) {
+      const int st = s % kTcStages, chunk = s % nchunks;
+      bool okw = true;
+      if (lane == 0 && s >= kTcStages) okw = tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort);
+      if (!__shfl_sync(0xFFFFFFFFu, okw, 0)) break;
+      __syncwarp();  // lane 0's wait orders the other lanes' entry writes below
+      if (chunk == 0) {
+        it = item_at(s);
+        TcItemSlot& e = sm.items[(s / nchunks) % kTcItemRing];
+        int o = -1;
+        if (lane < it.ns) {
+          const int p = it.s0 + lane;
+          o = A.slot_out ? A.slot_out[p] : p;
+          const int v = A.slot_vec ? A.slot_vec[p] : p;
+          const int x = A.pe[p];
+          if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || x < 0 || x >= A.num_experts) && A.err)
+            atomicOr(A.err, kErrBadExpertId);
         }
-        if (s >= kTcStages && !tc_wait(&sm.empty[st], ((s / kTcStages) - 1) & 1, A.err, &sm.abort)) break;
+        e.orow[lane] = o;
+        if (lane == 0) {
+          e.tile = it.tile, e.s0 = it.s0, e.ns = it.ns, e.nv = it.nv;
+          e.mat = it.dst == A.out ? 0 : 1;
+        }
+        __syncwarp();  // the entry is published by lane 0's arrival on full[st]
+        if (lane == 0) tc_tmap_acquire(it.map);
+      }
+      if (lane == 0) {
         const int units = it.nv / kTcUnit;
         // this CTA's half of the slice image (B rows N/2 * rank ..), all the block scales
         const uint32_t bhalf = units * kTcUnitBBytes / 2, xbytes = units * kTcUnitXFloats * 4;
@@ -783,19 +829,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
     constexpr uint64_t kADesc = sizeof(sm.a[0]) >> 4, kBDesc = sizeof(sm.b[0]) >> 4;
     int st = 0, ab = 0, G = 0;  // image stage, code buffer, groups issued
     uint32_t apar = 0;          // a_full parity of buffer ab
+    uint32_t idesc = 0;
+    bool wide = false;
 #pragma unroll 1
     for (int i = 0; i < my_items; ++i) {
-      const int nv = tc_item(A, pair + i * npairs, tiles, mats).nv;
-      const uint32_t idesc = umma_idesc_s8s8(2 * kTcRows, 3 * nv);
-      const bool wide = nv > kTcUnit;
 #pragma unroll 1
       for (int c = 0; c < nchunks; ++c) {
         // One wait covers both CTAs' operands of the step: the unpack
         // threads of both arrive on this a_full after their own full[st]
-        // wait (the slice-image halves landed) and after fencing their code
-        // stores to the async proxy.
+        // wait (the slice-image halves landed, the item entry published)
+        // and after fencing their code stores to the async proxy.
         if (!tc_spin_cluster_warp(&sm.a_full[ab], apar, A.err, &sm.abort)) goto tc_mma_out;
         tc_fence_after_sync();
+        if (c == 0) {
+          const int nv = sm.items[i % kTcItemRing].nv;
+          idesc = umma_idesc_s8s8(2 * kTcRows, 3 * nv);
+          wide = nv > kTcUnit;
+        }
         const uint64_t da = da0 + ab * kADesc, db = db0 + st * kBDesc;
         if (wide) {  // two groups of 4 blocks, 128 columns each
 #pragma unroll
@@ -857,27 +907,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    TcItem it{};
-    int nvw = 4, v0 = 0, orow = -1, G = 0;
+    int nv = kTcUnit, ns = 0, tile = 0, nvw = 4, v0 = 0, orow = -1, G = 0;
+    float* dst = A.out;
     bool live = false;
 #pragma unroll 1
     for (int s = 0; s < nsteps; ++s) {
       const int q = s % kTcQ, chunk = s % nchunks;
-      if (chunk == 0) {
-        it = item_at(s);
-        nvw = it.nv / 4;
-        v0 = vset * nvw;
-        live = v0 < it.ns;
-        // output row of this lane's vector (lane < nvw), read ahead of the stores
-        orow = -1;
-        if (live && lane < nvw && v0 + lane < it.ns) {
-          const int p = it.s0 + v0 + lane;
-          orow = A.slot_out ? A.slot_out[p] : p;
-        }
-      }
-      // the step's block and row scales (copied and written by unpack) are read below
+      // the step's block and row scales (copied and written by unpack) are
+      // read below, and at an item's first step its entry
       bool ok = tc_wait(&sm.q_full[q], (s / kTcQ) & 1, A.err, &sm.abort);
-      const int gb = tc_group_blocks(it.nv);
+      if (chunk == 0) {
+        const TcItemSlot& e = sm.items[(s / nchunks) % kTcItemRing];
+        nv = e.nv, ns = e.ns, tile = e.tile;
+        dst = e.mat ? A.out2 : A.out;
+        nvw = nv / 4;
+        v0 = vset * nvw;
+        live = v0 < ns;
+        orow = live && lane < nvw ? e.orow[v0 + lane] : -1;  // this lane's vector's output row
+      }
+      const int gb = tc_group_blocks(nv);
 #pragma unroll 1
       for (int j = 0; j < kTcKB && ok; j += gb, ++G) {
         const int slot = G % kTcSlots;
@@ -889,11 +937,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
         if (live) {
           const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + v0;
           const float* dcol = &sm.q_d[q][j][trow];
-          const float* xsv = &sm.q_xs[q][j * it.nv + v0];
+          const float* xsv = &sm.q_xs[q][j * nv + v0];
           if (nvw == 8)
-            tc_epi_group<8, 4, 128>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+            tc_epi_group<8, 4, 128>(taddr, nv, dcol, xsv, &sm.t_empty[slot], acc);
           else
-            tc_epi_group<4, 8, 64>(taddr, it.nv, dcol, xsv, &sm.t_empty[slot], acc);
+            tc_epi_group<4, 8, 64>(taddr, nv, dcol, xsv, &sm.t_empty[slot], acc);
         } else {
           tc_fence_before_sync();
           __syncwarp();
@@ -904,22 +952,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.q_empty[q]);
       if (chunk == nchunks - 1) {
-        const int grow = it.tile * 2 * kTcRows + row0 + trow;
+        const int grow = tile * 2 * kTcRows + row0 + trow;
         if (live) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int o = __shfl_sync(0xFFFFFFFFu, orow, i);
-            if (i < nvw && v0 + i < it.ns && o >= 0 && o < A.out_rows && grow < A.R)
-              it.dst[static_cast<size_t>(o) * A.R + grow] = acc[i];
+            if (i < nvw && v0 + i < ns && o >= 0 && o < A.out_rows && grow < A.R)
+              dst[static_cast<size_t>(o) * A.R + grow] = acc[i];
           }
-        }
-        if (ew == 0 && lane < it.ns) {
-          const int p = it.s0 + lane;
-          const int o = A.slot_out ? A.slot_out[p] : p;
-          const int v = A.slot_vec ? A.slot_vec[p] : p;
-          const int e = A.pe[p];
-          if ((o < 0 || o >= A.out_rows || v < 0 || v >= A.nvec || e < 0 || e >= A.num_experts) && A.err)
-            atomicOr(A.err, kErrBadExpertId);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
@@ -1436,7 +1476,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   const int max_slices = static_cast<int>(tc_max_units(num_pairs, l->num_experts));
   const size_t smem = sizeof(dev::TcSmem);
   OBJB_TRY(ensure_smem_attr(dev::tc_q4_grouped_kernel, device, smem));
-  const int img_grid = 2 * props.sm_count;
+  const int img_grid = 4 * props.sm_count;
 
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
