@@ -387,6 +387,8 @@ __global__ void __launch_bounds__(256) tc_wide_down_kernel(const float* __restri
 // Work slices of the expert-sorted pair list: runs of equal experts cut into
 // pieces of at most `nvp` pairs -> slice_start / slice_len [0..n), n in
 // *nslices.  One CTA; each thread scans a contiguous slice of the pairs.
+// With slice_order (and nslices of two entries) it also lists the slices
+// wider than one unit first, for the grouped kernel's item assignment.
 __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp_tot) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nt = blockDim.x;
   int incl = v;
@@ -420,7 +422,8 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
                                                          int32_t* __restrict__ slice_unit,
                                                          int32_t* __restrict__ nslices, int unit_cap,
                                                          unsigned* err, uint8_t* __restrict__ wany_x, int T,
-                                                         uint8_t* __restrict__ wany_a) {
+                                                         uint8_t* __restrict__ wany_a,
+                                                         int32_t* __restrict__ slice_order) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ int warp_tot[32];
   // the any-wide bytes of this call start clear (the planes kernels set them)
@@ -466,6 +469,21 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
       upos += (len + unit - 1) / unit;
       ++pos;
     }
+  }
+  // 3. (optional) the slices wider than one unit first, then the others,
+  // each in slice order; nslices[1] = how many are wide
+  if (slice_order) {
+    __syncthreads();  // every slice length written
+    per = (total + nt - 1) / nt;
+    a = min(total, tid * per);
+    b = min(total, a + per);
+    local = 0;
+    for (int q = a; q < b; ++q) local += slice_len[q] > unit;
+    int nwide = 0;
+    int wpos = block_exclusive_scan(local, &nwide, warp_tot);
+    int npos = nwide + (a - wpos);
+    for (int q = a; q < b; ++q) slice_order[slice_len[q] > unit ? wpos++ : npos++] = q;
+    if (tid == 0) nslices[1] = nwide;
   }
   // a pair list not grouped by expert can need more image space than sized
   // for: run nothing and flag it
@@ -574,7 +592,8 @@ struct TcArgs {
   const int32_t* slice_start;
   const int32_t* slice_len;
   const int32_t* slice_unit;
-  const int32_t* nslices;
+  const int32_t* nslices;      // [0] slices, [1] slices wider than one unit
+  const int32_t* slice_order;  // the wide slices first (tc_slices_kernel)
   const uint8_t* bimg;       // slice images (tc_image_kernel)
   const float* ximg;
   const CUtensorMap* maps;   // tensor maps of every slice's matrices (tc_maps_kernel): [slice][gate, up, down]
@@ -593,10 +612,12 @@ struct TcItem {
   int tile, s0, ns, nv, unit;
 };
 
-__device__ __forceinline__ TcItem tc_item(const TcArgs& A, int w, int tiles, int mats) {
+// Item o of the launch's ordered list: (slice slice_order[o / (tiles mats)],
+// tile, matrix), the matrix fastest.
+__device__ __forceinline__ TcItem tc_item(const TcArgs& A, int o, int tiles, int mats) {
   TcItem it;
-  const int mat = w % mats, rest = w / mats;
-  const int sl = rest / tiles;
+  const int mat = o % mats, rest = o / mats;
+  const int sl = A.slice_order[rest / tiles];
   it.tile = rest % tiles;
   it.s0 = A.slice_start[sl];
   it.ns = min(max(A.slice_len[sl], 1), kTcNvp);
@@ -769,10 +790,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
   const int nb = A.C / 32, nchunks = nb / kTcKB;
   const int tiles = (A.R + 2 * kTcRows - 1) / (2 * kTcRows);  // 256-row tiles of the pair
   const int mats = A.W2 ? 2 : 1;
-  const int total = *A.nslices * tiles * mats;
-  const int my_items = pair < total ? (total - 1 - pair) / npairs + 1 : 0;
+  // Static item assignment balanced for cost: a wide slice's item (32
+  // vectors: two tensor-memory hand-offs a step) costs about two narrow
+  // ones.  The wide items go round-robin over the pairs; the narrow ones
+  // round-robin from the first pair that got one fewer wide item.  A pair
+  // takes its wide items first.
+  const int per_slice = tiles * mats;
+  const int total = *A.nslices * per_slice, wide_items = A.nslices[1] * per_slice;
+  const int narrow_items = total - wide_items;
+  const int my_wide = wide_items / npairs + (pair < wide_items % npairs ? 1 : 0);
+  const int nfirst = (pair - wide_items % npairs + npairs) % npairs;  // this pair's first narrow item
+  const int my_items = my_wide + narrow_items / npairs + (nfirst < narrow_items % npairs ? 1 : 0);
   const int nsteps = my_items * nchunks;
-  auto item_at = [&](int s) { return tc_item(A, pair + (s / nchunks) * npairs, tiles, mats); };
+  auto item_at = [&](int s) {
+    const int i = s / nchunks;
+    const int o = i < my_wide ? pair + i * npairs : wide_items + nfirst + (i - my_wide) * npairs;
+    return tc_item(A, o, tiles, mats);
+  };
   const int row0 = static_cast<int>(rank) * kTcRows;  // this CTA's rows within a pair tile
 
   if (warp == kTcProducerWarp) {
@@ -1315,7 +1349,7 @@ namespace {
 
 struct TcLayout {
   size_t planes_x, xsc_x, wflag_x, wflag_a, wany_x, wany_a, g, u, planes_a, xsc_a, run_start, slice_start, slice_len, slice_unit,
-      nslices, bimg, ximg, maps, total;
+      slice_order, nslices, bimg, ximg, maps, total;
 };
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
@@ -1349,7 +1383,8 @@ TcLayout tc_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   L.slice_start = take(P * 4);
   L.slice_len = take(P * 4);
   L.slice_unit = take(P * 4);
-  L.nslices = take(4);
+  L.slice_order = take(P * 4);
+  L.nslices = take(8);
   L.bimg = take(units * nchunks * dev::kTcUnitBBytes);
   L.ximg = take(units * nchunks * dev::kTcUnitXFloats * 4);
   L.maps = take(3 * units * sizeof(CUtensorMap));  // slices <= units
@@ -1459,6 +1494,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
   int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
   int32_t* slice_unit = reinterpret_cast<int32_t*>(sc + L.slice_unit);
+  int32_t* slice_order = reinterpret_cast<int32_t*>(sc + L.slice_order);
   int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
   uint8_t* bimg = sc + L.bimg;
   float* ximg = reinterpret_cast<float*>(sc + L.ximg);
@@ -1480,7 +1516,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
 
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kTcNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
-                      static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err, wany_x, T, wany_a));
+                      static_cast<int>(tc_max_units(num_pairs, l->num_experts)), err, wany_x, T, wany_a, slice_order));
   OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
                       static_cast<const int32_t*>(slice_start), static_cast<const int32_t*>(nslices), max_slices, pe,
                       reinterpret_cast<const uint8_t* const*>(l->d_gate),
@@ -1505,6 +1541,7 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
   a.slice_len = slice_len;
   a.slice_unit = slice_unit;
   a.nslices = nslices;
+  a.slice_order = slice_order;
   a.bimg = bimg;
   a.ximg = ximg;
   a.maps = maps;
@@ -1669,7 +1706,8 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   OBJB_TRY(act_quant(x, num_tokens, l->hidden, codes_x, scales_x, stream, "act_quant hidden"));
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kMxNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
-                      static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err, static_cast<uint8_t*>(nullptr), 0, static_cast<uint8_t*>(nullptr)));
+                      static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err, static_cast<uint8_t*>(nullptr), 0,
+                      static_cast<uint8_t*>(nullptr), static_cast<int32_t*>(nullptr)));
   {
     const int max_slices = static_cast<int>(mx_max_units(num_pairs, l->num_experts));
     OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
