@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(256) tc_wide_down_kernel(const float* __restri
 // pieces of at most `nvp` pairs -> slice_start / slice_len [0..n), n in
 // *nslices.  One CTA; each thread scans a contiguous slice of the pairs.
 // With slice_order (and nslices of two entries) it also lists the slices
-// wider than one unit first, for the grouped kernel's item assignment.
+// widest first, for the grouped kernels' item assignment.
 __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp_tot) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nt = blockDim.x;
   int incl = v;
@@ -470,19 +470,25 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
       ++pos;
     }
   }
-  // 3. (optional) the slices wider than one unit first, then the others,
-  // each in slice order; nslices[1] = how many are wide
+  // 3. (optional) the slices by width in units, widest first, each width in
+  // slice order (a counting sort); nslices[1] = how many are wider than one
+  // unit
   if (slice_order) {
     __syncthreads();  // every slice length written
     per = (total + nt - 1) / nt;
     a = min(total, tid * per);
     b = min(total, a + per);
-    local = 0;
-    for (int q = a; q < b; ++q) local += slice_len[q] > unit;
-    int nwide = 0;
-    int wpos = block_exclusive_scan(local, &nwide, warp_tot);
-    int npos = nwide + (a - wpos);
-    for (int q = a; q < b; ++q) slice_order[slice_len[q] > unit ? wpos++ : npos++] = q;
+    int base = 0, nwide = 0;
+    for (int c = (nvp + unit - 1) / unit; c >= 1; --c) {
+      local = 0;
+      for (int q = a; q < b; ++q) local += (slice_len[q] + unit - 1) / unit == c;
+      int cnt = 0;
+      int at = base + block_exclusive_scan(local, &cnt, warp_tot);
+      for (int q = a; q < b; ++q)
+        if ((slice_len[q] + unit - 1) / unit == c) slice_order[at++] = q;
+      base += cnt;
+      if (c == 2) nwide = base;
+    }
     if (tid == 0) nslices[1] = nwide;
   }
   // a pair list not grouped by expert can need more image space than sized
@@ -1145,6 +1151,7 @@ struct MxArgs {
   const int32_t* slice_len;
   const int32_t* slice_unit;
   const int32_t* nslices;
+  const int32_t* slice_order;  // slices widest first (tc_slices_kernel)
   const uint8_t* bimg;
   const uint8_t* sfimg;
   const CUtensorMap* maps;   // tensor maps of every slice's weight matrices (tc_maps_kernel): [slice][gate, up, down]
@@ -1164,10 +1171,12 @@ struct MxItem {
   int tile, s0, ns, units, unit, sl;
 };
 
-__device__ __forceinline__ MxItem mx_item(const MxArgs& A, int w, int tiles, int mats) {
+// Item o of the launch's ordered list (slices widest first; tile, matrix
+// within a slice, the matrix fastest).
+__device__ __forceinline__ MxItem mx_item(const MxArgs& A, int o, int tiles, int mats) {
   MxItem it;
-  const int mat = w % mats, rest = w / mats;
-  it.sl = rest / tiles;
+  const int mat = o % mats, rest = o / mats;
+  it.sl = A.slice_order[rest / tiles];
   it.tile = rest % tiles;
   it.s0 = A.slice_start[it.sl];
   it.ns = min(max(A.slice_len[it.sl], 1), kMxNvp);
@@ -1211,10 +1220,15 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_grouped_kernel(const MxArgs 
   const int nchunks = A.C / kMxStepCols;
   const int tiles = (A.R + kTcRows - 1) / kTcRows;
   const int mats = A.W2 ? 2 : 1;
-  const int total = *A.nslices * tiles * mats;
-  const int my_items = static_cast<int>(blockIdx.x) < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // Items widest first, dealt in snake order (round r goes over the CTAs
+  // forward when r is even, backward when odd), so each CTA's share of the
+  // costly wide items and of the cheap narrow ones evens out.
+  const int total = *A.nslices * tiles * mats, G = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
+  auto item_o = [&](int r) { return r * G + ((r & 1) ? G - 1 - cta : cta); };
+  const int rounds = (total + G - 1) / G;
+  const int my_items = rounds > 0 && item_o(rounds - 1) >= total ? rounds - 1 : rounds;
   const int nsteps = my_items * nchunks;
-  auto item_at = [&](int s) { return mx_item(A, blockIdx.x + (s / nchunks) * gridDim.x, tiles, mats); };
+  auto item_at = [&](int s) { return mx_item(A, item_o(s / nchunks), tiles, mats); };
 
   if (warp == kMxProducerWarp) {
     if (lane == 0) {
@@ -1586,8 +1600,8 @@ int moe_pairs_tc(const objb_moe_layer* l, size_t num_pairs, const int32_t* pe, c
 namespace {
 
 struct MxLayout {
-  size_t codes_x, scales_x, g, u, codes_a, scales_a, run_start, slice_start, slice_len, slice_unit, nslices, bimg,
-      sfimg, maps, total;
+  size_t codes_x, scales_x, g, u, codes_a, scales_a, run_start, slice_start, slice_len, slice_unit, slice_order, nslices,
+      bimg, sfimg, maps, total;
 };
 
 // Image units (16 vectors) of a pair list grouped by expert: sum ceil(len / 16)
@@ -1614,7 +1628,8 @@ MxLayout mx_layout(size_t P, size_t T, size_t H, size_t I, size_t E, int sm_coun
   L.slice_start = take(P * 4);
   L.slice_len = take(P * 4);
   L.slice_unit = take(P * 4);
-  L.nslices = take(4);
+  L.slice_order = take(P * 4);
+  L.nslices = take(8);
   L.bimg = take(units * nchunks * dev::kMxUnitBBytes);
   L.sfimg = take(units * nchunks * dev::kMxSfAtom);
   L.maps = take(3 * mx_max_units(P, E) * sizeof(CUtensorMap));  // slices <= units
@@ -1688,6 +1703,7 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   int32_t* slice_start = reinterpret_cast<int32_t*>(sc + L.slice_start);
   int32_t* slice_len = reinterpret_cast<int32_t*>(sc + L.slice_len);
   int32_t* slice_unit = reinterpret_cast<int32_t*>(sc + L.slice_unit);
+  int32_t* slice_order = reinterpret_cast<int32_t*>(sc + L.slice_order);
   int32_t* nslices = reinterpret_cast<int32_t*>(sc + L.nslices);
   uint8_t* bimg = sc + L.bimg;
   uint8_t* sfimg = sc + L.sfimg;
@@ -1707,7 +1723,7 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   OBJB_TRY(launch_pdl(dev::tc_slices_kernel, 1, 1024, 0, stream, pe, P, d_count, dev::kMxNvp, dev::kTcUnit, run_start,
                       slice_start, slice_len, slice_unit, nslices,
                       static_cast<int>(mx_max_units(num_pairs, l->num_experts)), err, static_cast<uint8_t*>(nullptr), 0,
-                      static_cast<uint8_t*>(nullptr), static_cast<int32_t*>(nullptr)));
+                      static_cast<uint8_t*>(nullptr), slice_order));
   {
     const int max_slices = static_cast<int>(mx_max_units(num_pairs, l->num_experts));
     OBJB_TRY(launch_pdl(dev::tc_maps_kernel, std::max(1, (3 * max_slices + 255) / 256), 256, 0, stream, tm_gu, tm_dn,
@@ -1735,6 +1751,7 @@ int moe_pairs_official_tc(const objb_moe_layer* l, size_t num_pairs, const int32
   a.slice_len = slice_len;
   a.slice_unit = slice_unit;
   a.nslices = nslices;
+  a.slice_order = slice_order;
   a.bimg = bimg;
   a.sfimg = sfimg;
   a.maps = maps;
