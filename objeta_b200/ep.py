@@ -192,8 +192,8 @@ def moe_pairs(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_li
 def moe_pairs_tc(layer, pair_expert, pair_token, d_x, d_v, pair_out=None, swiglu_limit: float = 0.0, stream=None,
                  d_count=None):
     """moe_pairs for Q4_0 layers on the tensor cores (tcgen05 kind::i8):
-    runs of equal experts are taken 32 pairs at a time per 128-row weight
-    tile.  Same arguments; pairs must be grouped by expert."""
+    runs of equal experts are taken 32 pairs at a time per 256-row weight
+    tile (a CTA pair).  Same arguments; pairs must be grouped by expert."""
     P = pair_expert.numel()
     T = d_x.shape[0]
     _lib.call("objb_moe_pairs_tc_device", ctypes.byref(layer._c), P,
@@ -456,9 +456,11 @@ class ExpertParallelMoe:
 
     def _forward_one_rank(self, x, ids, w):
         """World size 1: no host round trip.  Pairs are the (token, slot)
-        entries sorted by expert on the device (stable, so ties keep token
-        order); pair p's output goes to row t * k + j, which the combine
-        reads in slot order."""
+        entries grouped by expert on the device (objb_ep_build_pairs_device
+        with one rank: a count per expert, a scan, a scatter, one launch;
+        within an expert the order is the atomics', which changes no row, as
+        a pair's row depends on its expert and token alone); pair p's output
+        goes to row t * k + j, which the combine reads in slot order."""
         import torch
         T, K = ids.shape
         if T == 1:
@@ -476,14 +478,11 @@ class ExpertParallelMoe:
         slot = self._slot_cache[key]
         stream = torch.cuda.current_stream(x.device)
         self._mark("start", stream)
-        _, perm = torch.sort(flat, stable=True)
-        perm = perm.to(torch.int32)
-        pair_expert = flat.index_select(0, perm)
-        pair_token = torch.div(perm, K, rounding_mode="floor").to(torch.int32)
+        pair_expert, pair_token, perm, cnt = ep_build_pairs(flat.view(1, T, K), 0, self.num_experts, stream=stream)
         self._mark("sort", stream)
         v = torch.empty(T * K, self.out_dim, dtype=torch.float32, device=x.device)
         self._pairs_fn(T * K)(self.layer, pair_expert, pair_token, x.contiguous(), v, pair_out=perm,
-                              swiglu_limit=self.swiglu_limit, stream=stream)
+                              swiglu_limit=self.swiglu_limit, stream=stream, d_count=cnt)
         self._mark("pairs", stream)
         out = torch.empty(T, self.out_dim, dtype=torch.float32, device=x.device)
         moe_combine(v, slot, w.contiguous(), out, stream=stream)
