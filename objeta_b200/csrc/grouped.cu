@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(1024) tc_slices_kernel(const int32_t* __restri
 }
 
 // The slice images of one contraction: for slice sl, step c, the B operand
-// rows k * nv + i (plane k of the slice's vector i, nv = 16 or 32) in
+// rows 3 i + k (plane k of the slice's vector i, nv = 16 or 32) in
 // core-matrix order, then the block scales [block][vector]; unit offsets
 // from tc_slices_kernel.  Rows and scales past the slice's length are not
 // written: the MMAs multiply them into columns that the epilogue never reads
@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
         if (q >= 3 * kc) break;
         const int k = q / kc, col = q % kc;            // plane, 16-byte column of the row
         const int c = col / kTcKch, pk = col % kTcKch;  // step, K column within the step
-        const int brow = k * nv + i;
+        const int brow = 3 * i + k;
         const int cm = (brow >> 3) * kTcKch + pk;       // core matrix
         uint8_t* dst = bimg + (ubase + static_cast<size_t>(c) * units) * kTcUnitBBytes;
         *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(cm) * 8 + (brow & 7)) * 16) = t[u];
@@ -697,64 +697,74 @@ __device__ __forceinline__ void tc_unpack(TcSmem& sm, int st, int ab, int q, int
 // A code buffer is released by the MMAs alone, so the unpack of step s + 2
 // overlaps the epilogue of step s.  One 512-column tensor-memory slot holds
 // a whole step of a 16-vector slice (half a step of a 32-vector one), so a
-// step crosses between the SMs once: the epilogue loads it in two halves
-// and releases the slot after the second half's loads.  The releases are
+// step crosses between the SMs once: the epilogue loads it in one batch of
+// packed 16-bit loads and releases the slot before folding.  The releases are
 // relaxed cluster arrivals (the tcgen05 fences order the tensor-memory
 // accesses; a release at cluster scope costs the arriving warp hundreds of
 // cycles).  Epilogue warp (quarter q, set w) owns tile rows 32 q .. 32 q + 31
 // of its CTA and vectors w * nv/4 .. (w + 1) * nv/4 - 1 of every block, so its
 // sums need no exchange with other warps; a warp whose vectors are all past
 // the slice's length still waits and arrives, without loading.
+// A block's columns hold, per vector i and digit plane k, the int32 sum
+// r_k(i) = sum over the block's 32 elements of (q - 8) * digit_k at column
+// 3 i + k.  |r_k| <= 32 * 8 * 64 = 16384, so the low 16 bits hold it: the
+// loads take two columns per register (.pack::16b), the 3 NVW columns of a
+// warp's NVW vectors in 3 NVW / 2 registers, in column order.
 template <int NVW>
-__device__ __forceinline__ void tc_epi_load(uint32_t taddr, int nv, uint32_t (&r)[3][NVW]) {
+__device__ __forceinline__ void tc_epi_load(uint32_t taddr, uint32_t (&r)[3 * NVW / 2]) {
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
+  for (int m = 0; m < 3; ++m) {
     if constexpr (NVW == 8)
-      tmem_ld8(taddr + k * nv, r[k]);
+      tmem_ld4_pack16(taddr + m * 8, r[4 * m], r[4 * m + 1], r[4 * m + 2], r[4 * m + 3]);
     else
-      tmem_ld4(taddr + k * nv, r[k]);
+      tmem_ld2_pack16(taddr + m * 4, r[2 * m], r[2 * m + 1]);
   }
 }
+// d = lo16(a) * byte0(b) + hi16(a) * byte1(b) + c, a's halves signed, b's bytes unsigned.
+__device__ __forceinline__ int dp2a_lo_su(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// Block sums of a vector pair (2p, 2p + 1) from its three registers
+// ra = [r0 | r1], rb = [r2 | r0'], rc = [r1' | r2']:
+//   S = r0 + 128 r1 + 16384 r2,  S' = r0' + 128 (r1' + 128 r2'),
+// then acc += f32(S) * (d * xv) as in the block epilogue before.
 template <int NVW>
-__device__ __forceinline__ void tc_epi_fold(const uint32_t (&r)[3][NVW], float dr, const float* xsv, float (&acc)[8]) {
+__device__ __forceinline__ void tc_epi_fold(const uint32_t (&r)[3 * NVW / 2], float dr, const float* xsv,
+                                            float (&acc)[8]) {
   float xv[NVW];
 #pragma unroll
   for (int q = 0; q < NVW / 4; ++q) {
     const float4 t = *reinterpret_cast<const float4*>(xsv + 4 * q);
     xv[4 * q] = t.x, xv[4 * q + 1] = t.y, xv[4 * q + 2] = t.z, xv[4 * q + 3] = t.w;
   }
+  constexpr uint32_t kRadix = 0x8001u;  // bytes 1, 128
 #pragma unroll
   for (int u = 0; u < NVW; u += 2) {
-    const int S0 = static_cast<int>(r[0][u]) + static_cast<int>(r[1][u]) * 128 + static_cast<int>(r[2][u]) * 16384;
-    const int S1 =
-        static_cast<int>(r[0][u + 1]) + static_cast<int>(r[1][u + 1]) * 128 + static_cast<int>(r[2][u + 1]) * 16384;
+    const uint32_t ra = r[3 * (u / 2)], rb = r[3 * (u / 2) + 1], rc = r[3 * (u / 2) + 2];
+    const int S0 = dp2a_lo_su(ra, kRadix, static_cast<int>(rb << 16) >> 2);
+    const int S1 = (static_cast<int>(rb) >> 16) + dp2a_lo_su(rc, kRadix, 0) * 128;
     const float2 sc = __fmul2_rn(make_float2(dr, dr), make_float2(xv[u], xv[u + 1]));
     const float2 a = __ffma2_rn(make_float2(__int2float_rn(S0), __int2float_rn(S1)), sc, make_float2(acc[u], acc[u + 1]));
     acc[u] = a.x, acc[u + 1] = a.y;
   }
 }
 // One MMA group of an epilogue warp: tensor-memory loads of its GB blocks
-// (column stride BS) in two halves (the registers hold half a group), each
-// half folded as it lands; the slot is released to the pair's MMA warp (in
-// CTA 0) after the second half's loads.
+// (column stride BS) in one batch, the slot released to the pair's MMA warp
+// (in CTA 0), then the folds.
 template <int NVW, int GB, int BS>
 __device__ __forceinline__ void tc_epi_group(uint32_t taddr, int nv, const float* dcol, const float* xsv,
                                              uint64_t* t_empty, float (&acc)[8]) {
-  constexpr int H = GB / 2;
-  uint32_t r[H][3][NVW];
+  uint32_t r[GB][3 * NVW / 2];
 #pragma unroll
-  for (int b = 0; b < H; ++b) tc_epi_load<NVW>(taddr + b * BS, nv, r[b]);
-  tmem_wait_ld();
-#pragma unroll
-  for (int b = 0; b < H; ++b) tc_epi_fold<NVW>(r[b], dcol[b * kTcRows], xsv + b * nv, acc);
-#pragma unroll
-  for (int b = 0; b < H; ++b) tc_epi_load<NVW>(taddr + (H + b) * BS, nv, r[b]);
+  for (int b = 0; b < GB; ++b) tc_epi_load<NVW>(taddr + b * BS, r[b]);
   tmem_wait_ld();
   tc_fence_before_sync();
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive_cta_relaxed(t_empty, 0);  // the pair's MMAs are issued by CTA 0
 #pragma unroll
-  for (int b = 0; b < H; ++b) tc_epi_fold<NVW>(r[b], dcol[(H + b) * kTcRows], xsv + (H + b) * nv, acc);
+  for (int b = 0; b < GB; ++b) tc_epi_fold<NVW>(r[b], dcol[b * kTcRows], xsv + b * nv, acc);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4_grouped_kernel(const TcArgs A) {
@@ -975,7 +985,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1) tc_q4
         }
         tc_fence_after_sync();
         if (live) {
-          const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + v0;
+          const uint32_t taddr = tmem + lane_addr + slot * kTcSlotCols + 3 * v0;
           const float* dcol = &sm.q_d[q][j][trow];
           const float* xsv = &sm.q_xs[q][j * nv + v0];
           if (nvw == 8)
