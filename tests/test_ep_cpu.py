@@ -5,7 +5,6 @@ tests; here the plan and the two all-to-alls must deliver every pair output
 to its token owner in slot order, so that the combined result is bit-identical
 to the single-rank result and to the reference CPU MoE (moe.rs:1283-1324)."""
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -156,10 +155,9 @@ def _rank_main(rank, world, port, q):
     import torch.distributed as dist
     from datetime import timedelta
     from objeta_b200.ep import ExpertParallelMoe
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        store = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=timedelta(seconds=60))
+        dist.init_process_group("gloo", store=store, rank=rank, world_size=world, timeout=timedelta(seconds=60))
         experts = _experts()
         x, ids, ws = _inputs(rank)
         ep = ExpertParallelMoe(None, E, K, rank=rank, world=world, out_dim=OUT,
@@ -173,20 +171,21 @@ def _rank_main(rank, world, port, q):
         q.put((rank, repr(exc), None))
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _parent_store():
+    """A rendezvous store held by the test process on a port the OS assigns
+    (no window between choosing a free port and listening on it); the ranks
+    connect to it as clients."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    return dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False, timeout=timedelta(seconds=60))
 
 
 def test_two_gloo_ranks_match_single_rank_and_reference():
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    store = _parent_store()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, store.port, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}

@@ -7,7 +7,6 @@ so a token's combined output must be bit-identical to the fused single-token
 path (objb_moe_selected_device), which the MoE tests check against the
 reference CPU MoE within max |err| <= 1e-5 * sum|w x| propagated."""
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -208,12 +207,12 @@ def _ep_rank(rank, world, port, q, grouped="auto", T=6, K=4):
     from datetime import timedelta
     from objeta_b200.ep import ExpertParallelMoe
     from objeta_b200.moe import MoeLayer
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     try:
         torch.cuda.set_device(rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+        # the parent holds the rendezvous store (an OS-assigned port)
+        store = dist.TCPStore("127.0.0.1", port, is_master=False, timeout=timedelta(seconds=60))
+        dist.init_process_group("nccl", store=store, rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
         E, H, I, OUT = 16, 1024, 512, 1024
         full, mats = _q4_layer(O.Q4_0, E, H, I, OUT, seed=61)   # same seed: same experts on every rank
@@ -261,12 +260,14 @@ def test_ep_two_ranks_bit_identical_to_single_gpu(grouped):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
+    import torch.distributed as dist
+    from datetime import timedelta
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
+    # rendezvous store on a port the OS assigns, held here until the ranks end
+    # (choosing a free port and closing it left a window another bind took)
+    store = dist.TCPStore("127.0.0.1", 0, is_master=True, wait_for_workers=False, timeout=timedelta(seconds=60))
+    port = store.port
     T, K = (40, 8) if grouped == "on" else (6, 4)
     procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q, grouped, T, K)) for r in range(2)]
     for p in procs:
