@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
                                                        uint8_t* __restrict__ bimg, float* __restrict__ ximg) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  constexpr int kBatch = 6;  // loads in flight per lane before their stores
+  constexpr int kBatch = 4;  // steps per plane in flight per lane before their stores
   const int lane = threadIdx.x & 31;
   const int nchunks = C / (kTcKB * 32), nb = C / 32, kc = C / 16;  // steps, blocks, 16-byte columns
   const int nsl = *nslices, total = nsl * kTcNvp;
@@ -533,23 +533,35 @@ __global__ void __launch_bounds__(256) tc_image_kernel(const int32_t* __restrict
     const size_t ubase = static_cast<size_t>(slice_unit[sl]) * nchunks;
     int v = slot_vec ? slot_vec[s0 + i] : s0 + i;
     v = (v < 0 || v >= nvec) ? 0 : v;
+    // a lane copies the 16-byte column pk of steps c = cl, cl + 2, ... of the
+    // three planes: contiguous reads across lanes, and a store address that
+    // is a fixed per-plane row offset plus c times the step's image size
     const uint4* src = reinterpret_cast<const uint4*>(planes + static_cast<size_t>(v) * 3 * C);
-    for (int q0 = lane; q0 < 3 * kc; q0 += 32 * kBatch) {
-      uint4 t[kBatch];
+    const int cl = lane >> 4, pk = lane & 15;
+    const size_t step_bytes = static_cast<size_t>(units) * kTcUnitBBytes;
+    uint8_t* base = bimg + ubase * kTcUnitBBytes;
+    size_t rowoff[3];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u)
-        if (q0 + 32 * u < 3 * kc) t[u] = src[q0 + 32 * u];
+    for (int k = 0; k < 3; ++k) {
+      const int brow = 3 * i + k;
+      rowoff[k] = static_cast<size_t>(((brow >> 3) * kTcKch + pk) * 128 + (brow & 7) * 16);
+    }
+    for (int c0 = cl; c0 < nchunks; c0 += 2 * kBatch) {
+      uint4 t[3][kBatch];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int q = q0 + 32 * u;
-        if (q >= 3 * kc) break;
-        const int k = q / kc, col = q % kc;            // plane, 16-byte column of the row
-        const int c = col / kTcKch, pk = col % kTcKch;  // step, K column within the step
-        const int brow = 3 * i + k;
-        const int cm = (brow >> 3) * kTcKch + pk;       // core matrix
-        uint8_t* dst = bimg + (ubase + static_cast<size_t>(c) * units) * kTcUnitBBytes;
-        *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(cm) * 8 + (brow & 7)) * 16) = t[u];
-      }
+      for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int c = c0 + 2 * u;
+          if (c < nchunks) t[k][u] = src[k * kc + c * kTcKch + pk];
+        }
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int c = c0 + 2 * u;
+          if (c < nchunks) *reinterpret_cast<uint4*>(base + rowoff[k] + static_cast<size_t>(c) * step_bytes) = t[k][u];
+        }
     }
     for (int q = lane; q < nb; q += 32) {
       const int c = q / kTcKB, j = q % kTcKB;
